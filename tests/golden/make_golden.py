@@ -1,0 +1,204 @@
+"""Generate the golden fixtures in this folder by running the REFERENCE's own code.
+
+Run from the repository root in a container that has the reference checkout:
+
+    PYTHONPATH=/root/reference:. python tests/golden/make_golden.py
+
+Only this script reads the reference; the fixtures it writes are committed so the
+tests (CPU and GPU) never need the reference at run time.  Every fixture is
+produced by calling the reference functions named below on seeded inputs:
+
+* ``quant_golden.npz``   — ``ProgressiveKVQuantizer.quantize_to_fp8`` /
+  ``dequantize_fp8`` on bf16 (144, 64) frame-head slices and
+  ``quantize_to_int4(group_size=64)`` / ``dequantize_int4`` on the same slices,
+  plus ``quantize_to_int4`` with its default group of 128 on a ragged flat tensor
+  (``worldserve/optimizations/system_level/kv_cache/progressive_quant.py:113-257``).
+* ``sampler_golden.npz`` — ``DPMSolverPPSampler(order=1,2,3).step`` sequences
+  (``optimizations/model_level/samplers/dpm_solver_pp.py:85-143``) and the DDIM
+  v-prediction updates made by ``worldserve.models.oasis.generate`` around a
+  deterministic stand-in DiT (``worldserve/models/oasis.py:174-235``).
+* ``temporal_attn_golden.npz`` — the reference's restated temporal attention
+  ``PersistentTemporalAxialAttention`` (``kv_cache/oasis_temporal_persistent_wrapper.py``)
+  built around the oracle's ``TemporalAxialAttention`` weights and RoPE, in full
+  and in cached-prefix mode.
+* ``cached_past_golden.npz`` — ``attention_with_cached_past``
+  (``kv_cache/oasis_persistent_kv_theory.py:97-124``).
+"""
+
+from __future__ import annotations
+
+import os
+import sys
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, ROOT)
+
+from worldserve.optimizations.system_level.kv_cache.progressive_quant import ProgressiveKVQuantizer  # noqa: E402
+from worldserve.optimizations.model_level.samplers.dpm_solver_pp import DPMSolverPPSampler  # noqa: E402
+
+
+def _bf16_bits(t: torch.Tensor) -> np.ndarray:
+    return t.contiguous().view(torch.int16).numpy().view(np.uint16).copy()
+
+
+def quant_cases():
+    g = torch.Generator().manual_seed(1234)
+    xs = []
+    for i in range(12):
+        xs.append(torch.randn(144, 64, generator=g) * (0.05 * (i + 1)))
+    xs.append(torch.zeros(144, 64))                              # all zero
+    xs.append(torch.full((144, 64), 0.37))                       # constant
+    x = torch.randn(144, 64, generator=g) * 0.01
+    x[17, 5] = 40.0                                              # single outlier
+    xs.append(x)
+    xs.append(torch.randn(144, 64, generator=g) * 1e-6)          # tiny (FP8 subnormals)
+    xs.append(torch.randn(144, 64, generator=g) * 300.0)         # large
+    x = torch.randn(144, 64, generator=g)
+    x[::3] = -x[::3].abs()                                       # skewed rows
+    xs.append(x)
+    return [z.bfloat16() for z in xs]
+
+
+def make_quant():
+    P = ProgressiveKVQuantizer
+    xs = quant_cases()
+    inp = np.stack([_bf16_bits(x) for x in xs])
+    f8_codes, f8_scale, f8_deq = [], [], []
+    i4_packed, i4_scale, i4_zero, i4_deq = [], [], [], []
+    for x in xs:
+        q, s = P.quantize_to_fp8(x)
+        f8_codes.append(q.view(torch.uint8).numpy().copy())
+        f8_scale.append(_bf16_bits(s.reshape(1))[0])
+        f8_deq.append(_bf16_bits(P.dequantize_fp8(q, s, target_dtype=torch.bfloat16)))
+        p, sc, z = P.quantize_to_int4(x, group_size=64)
+        i4_packed.append(p.numpy().copy())
+        i4_scale.append(sc.numpy().copy())
+        i4_zero.append(z.numpy().copy())
+        d = P.dequantize_int4(p, sc, z, 64, x.numel(), tuple(x.shape), target_dtype=torch.float32)
+        i4_deq.append(d.numpy().copy())
+    g = torch.Generator().manual_seed(99)
+    flat = (torch.randn(1000, generator=g) * 2.0).bfloat16()     # ragged: pads to 1024
+    p, sc, z = P.quantize_to_int4(flat)                          # default group_size=128
+    np.savez_compressed(
+        os.path.join(HERE, "quant_golden.npz"),
+        inp_bf16=inp, fp8_codes=np.stack(f8_codes), fp8_scale_bf16=np.array(f8_scale, np.uint16),
+        fp8_deq_bf16=np.stack(f8_deq), int4_packed=np.stack(i4_packed), int4_scale=np.stack(i4_scale),
+        int4_zero=np.stack(i4_zero), int4_deq_f32=np.stack(i4_deq),
+        flat_bf16=_bf16_bits(flat), flat_packed=p.numpy(), flat_scale=sc.numpy(), flat_zero=z.numpy(),
+    )
+
+
+class _StandInDiT:
+    """Deterministic stand-in with the DiT call signature; records every call."""
+
+    def __init__(self):
+        self.calls = []
+
+    def __call__(self, x, t, actions):
+        v = 0.6 * torch.sin(x) - 0.25 * x + (t.float() / 1000.0)[..., None, None, None]
+        self.calls.append((x.clone(), t.clone(), v.clone()))
+        return v
+
+
+class _StandInVAE:
+    def decode(self, z):
+        return z.unsqueeze(1).expand(-1, 3, -1, -1)
+
+
+def make_sampler():
+    out = {}
+    g = torch.Generator().manual_seed(7)
+    shape = (1, 2, 4, 6, 8)
+    for order in (1, 2, 3):
+        s = DPMSolverPPSampler(order=order)
+        lat = torch.randn(shape, generator=g)
+        ts = torch.linspace(1.0, 0.0, 6)
+        lats, preds = [lat.numpy().copy()], []
+        for i in range(5):
+            v = torch.randn(shape, generator=g)
+            preds.append(v.numpy().copy())
+            lat = s.step(lat, v, ts[i], ts[i + 1])
+            lats.append(lat.numpy().copy())
+        out[f"ab{order}_latents"] = np.stack(lats)
+        out[f"ab{order}_preds"] = np.stack(preds)
+        out[f"ab{order}_ts"] = ts.numpy()
+
+    # load models/oasis.py by path: the worldserve.models package __init__ pulls in
+    # plotting dependencies that this container lacks
+    import importlib.util
+    import worldserve
+    path = os.path.join(os.path.dirname(worldserve.__file__), "models", "oasis.py")
+    spec = importlib.util.spec_from_file_location("_ref_oasis", path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    generate = mod.generate
+    from oracle.sampler_ref import alphas_cumprod
+    ab = torch.from_numpy(alphas_cumprod(1000))
+    dit = _StandInDiT()
+    model = {"dit": dit, "vae": _StandInVAE(), "device": "cpu", "dtype": torch.float32,
+             "alpha_bar_override": ab}
+    generate(model, num_frames=2, num_steps=10, n_prompt=1, seed=5)
+    out["ddim_x_in"] = np.stack([c[0][:, -1, :2].numpy() for c in dit.calls])  # 2 channels suffice
+    out["ddim_t_in"] = np.stack([c[1][:, -1].numpy() for c in dit.calls])
+    out["ddim_v"] = np.stack([c[2][:, -1, :2].numpy() for c in dit.calls])
+    out["ddim_n_calls"] = np.array(len(dit.calls))
+    out["ddim_steps"] = np.array(10)
+    out["alphas_cumprod"] = ab.numpy()
+    np.savez_compressed(os.path.join(HERE, "sampler_golden.npz"), **out)
+
+
+def make_temporal_attn():
+    from oracle.dit_ref import RotaryEmbedding, TemporalAxialAttention
+    from worldserve.optimizations.system_level.kv_cache.oasis_temporal_persistent_wrapper import (
+        PersistentTemporalAxialAttention, TemporalPersistentKVRuntime)
+    torch.manual_seed(11)
+    dim, heads, dh = 128, 2, 64
+    rot = RotaryEmbedding(dh)
+    base = TemporalAxialAttention(dim, heads, dh, rot, is_causal=True)
+    with torch.no_grad():
+        for p in base.parameters():
+            if p.requires_grad:
+                p.normal_(0, 0.05)
+    rt = TemporalPersistentKVRuntime()
+    ref = PersistentTemporalAxialAttention(base, layer_idx=0, runtime=rt)
+    x0 = torch.randn(2, 5, 3, 4, dim)
+    x1 = x0.clone()
+    x1[:, -1] = torch.randn(2, 3, 4, dim)
+    with torch.no_grad():
+        y_full = ref(x0)
+        rt.enable(True)
+        rt.start_frame(4)
+        y_step0 = ref(x0)
+        rt.set_step(1)
+        y_step1 = ref(x1)  # past prefix reused from step 0
+    np.savez_compressed(
+        os.path.join(HERE, "temporal_attn_golden.npz"),
+        w_qkv=base.to_qkv.weight.detach().numpy(), w_out=base.to_out.weight.detach().numpy(),
+        b_out=base.to_out.bias.detach().numpy(), x0=x0.numpy(), x1=x1.numpy(),
+        y_full=y_full.numpy(), y_step0=y_step0.numpy(), y_step1=y_step1.numpy())
+
+
+def make_cached_past():
+    from worldserve.optimizations.system_level.kv_cache.oasis_persistent_kv_theory import (
+        PersistentPastKVCache, attention_with_cached_past)
+    g = torch.Generator().manual_seed(3)
+    q = torch.randn(2, 4, 16, 64, generator=g)
+    k = torch.randn(2, 4, 16 + 12, 64, generator=g)
+    v = torch.randn(2, 4, 16 + 12, 64, generator=g)
+    cache = PersistentPastKVCache()
+    cache.start_frame(1)
+    y = attention_with_cached_past(q, k, v, 12, cache, 0)
+    np.savez_compressed(os.path.join(HERE, "cached_past_golden.npz"),
+                        q=q.numpy(), k=k.numpy(), v=v.numpy(), n_past=np.array(12), y=y.numpy())
+
+
+if __name__ == "__main__":
+    make_quant()
+    make_sampler()
+    make_temporal_attn()
+    make_cached_past()
+    print("golden fixtures written to", HERE)
