@@ -1,0 +1,446 @@
+// Spatial (144-token, non-causal) and temporal (<=32-frame, causal) attention.
+//
+// Both are small, HBM/L2-bound attention problems (head dim 64): a whole
+// sequence fits one tile, so softmax is exact (no online rescaling).  QK^T and PV
+// run on mma.sync m16n8k16 bf16 tensor-core tiles with fp32 accumulation; q and k
+// arrive post-RoPE from the QKV GEMM epilogue.  Temporal K/V may come from the
+// quantised cache: FP8/INT4 codes are dequantised while they are staged into
+// shared memory, so the cache is never materialised in bf16 in HBM.
+#include "launch.cuh"
+
+namespace oasis {
+
+constexpr int kQkvLd = 3 * OASIS_HIDDEN;  // 3072
+constexpr int kSmemStride = 72;           // bf16 per staged row (64 + 8 pad: conflict-free ldmatrix)
+
+// ----------------------------------------------------------------------------------
+// spatial attention: one CTA per (frame, head), 9 warps x 16 query rows
+// ----------------------------------------------------------------------------------
+constexpr int kSpThreads = 288;
+constexpr int kSpSmem = 3 * OASIS_TOKENS * kSmemStride * 2;  // 62,208 B
+
+__global__ void __launch_bounds__(kSpThreads)
+    attn_spatial_kernel(const __nv_bfloat16* __restrict__ qkv, __nv_bfloat16* __restrict__ out,
+                        float scale_log2) {
+  extern __shared__ __align__(16) uint8_t sm_sp[];
+  __nv_bfloat16* sQ = reinterpret_cast<__nv_bfloat16*>(sm_sp);
+  const int f = blockIdx.x;
+  const int h = blockIdx.y;
+  const __nv_bfloat16* base = qkv + static_cast<long long>(f) * OASIS_TOKENS * kQkvLd + h * 64;
+
+  for (int i = threadIdx.x; i < 3 * OASIS_TOKENS * 8; i += kSpThreads) {
+    const int which = i / (OASIS_TOKENS * 8);
+    const int r = (i >> 3) % OASIS_TOKENS;
+    const int c = i & 7;
+    cp_async16(sQ + (which * OASIS_TOKENS + r) * kSmemStride + c * 8,
+               base + static_cast<long long>(r) * kQkvLd + which * OASIS_HIDDEN + c * 8);
+  }
+  cp_async_wait_all();
+  __syncthreads();
+
+  const __nv_bfloat16* sK = sQ + OASIS_TOKENS * kSmemStride;
+  const __nv_bfloat16* sV = sK + OASIS_TOKENS * kSmemStride;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int r0 = warp * 16;
+
+  uint32_t qa[4][4];
+#pragma unroll
+  for (int kk = 0; kk < 4; ++kk)
+    ldsm_x4(smem_u32(sQ + (r0 + (lane & 15)) * kSmemStride + kk * 16 + (lane >> 4) * 8), qa[kk][0],
+            qa[kk][1], qa[kk][2], qa[kk][3]);
+
+  float s[18][4];
+#pragma unroll
+  for (int j = 0; j < 18; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.0f;
+#pragma unroll
+  for (int jp = 0; jp < 9; ++jp) {
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      uint32_t b0, b1, b2, b3;
+      const int key = jp * 16 + (lane & 7) + ((lane >> 4) << 3);
+      const int col = kk * 16 + ((lane >> 3) & 1) * 8;
+      ldsm_x4(smem_u32(sK + key * kSmemStride + col), b0, b1, b2, b3);
+      mma_bf16_16816(s[2 * jp], qa[kk], b0, b1);
+      mma_bf16_16816(s[2 * jp + 1], qa[kk], b2, b3);
+    }
+  }
+
+  float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < 18; ++j) {
+    mx0 = fmaxf(mx0, fmaxf(s[j][0], s[j][1]));
+    mx1 = fmaxf(mx1, fmaxf(s[j][2], s[j][3]));
+  }
+  mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+  mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+  mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+  mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+  const float o0 = mx0 * scale_log2, o1 = mx1 * scale_log2;
+  float sum0 = 0.0f, sum1 = 0.0f;
+#pragma unroll
+  for (int j = 0; j < 18; ++j) {
+    s[j][0] = exp2f(s[j][0] * scale_log2 - o0);
+    s[j][1] = exp2f(s[j][1] * scale_log2 - o0);
+    s[j][2] = exp2f(s[j][2] * scale_log2 - o1);
+    s[j][3] = exp2f(s[j][3] * scale_log2 - o1);
+    sum0 += s[j][0] + s[j][1];
+    sum1 += s[j][2] + s[j][3];
+  }
+  sum0 += __shfl_xor_sync(0xffffffffu, sum0, 1);
+  sum0 += __shfl_xor_sync(0xffffffffu, sum0, 2);
+  sum1 += __shfl_xor_sync(0xffffffffu, sum1, 1);
+  sum1 += __shfl_xor_sync(0xffffffffu, sum1, 2);
+
+  float o[8][4];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.0f;
+#pragma unroll
+  for (int kk = 0; kk < 9; ++kk) {
+    uint32_t pa[4];
+    pa[0] = pack_bf16x2(s[2 * kk][0], s[2 * kk][1]);
+    pa[1] = pack_bf16x2(s[2 * kk][2], s[2 * kk][3]);
+    pa[2] = pack_bf16x2(s[2 * kk + 1][0], s[2 * kk + 1][1]);
+    pa[3] = pack_bf16x2(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+#pragma unroll
+    for (int jd = 0; jd < 8; jd += 2) {
+      uint32_t b0, b1, b2, b3;
+      const int key = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+      const int col = jd * 8 + (lane >> 4) * 8;
+      ldsm_x4_t(smem_u32(sV + key * kSmemStride + col), b0, b1, b2, b3);
+      mma_bf16_16816(o[jd], pa, b0, b1);
+      mma_bf16_16816(o[jd + 1], pa, b2, b3);
+    }
+  }
+
+  const float inv0 = 1.0f / sum0, inv1 = 1.0f / sum1;
+  const int g = lane >> 2, c = lane & 3;
+  __nv_bfloat16* orow0 = out + (static_cast<long long>(f) * OASIS_TOKENS + r0 + g) * OASIS_HIDDEN + h * 64;
+  __nv_bfloat16* orow1 = orow0 + 8 * OASIS_HIDDEN;
+#pragma unroll
+  for (int jd = 0; jd < 8; ++jd) {
+    *reinterpret_cast<uint32_t*>(orow0 + jd * 8 + 2 * c) = pack_bf16x2(o[jd][0] * inv0, o[jd][1] * inv0);
+    *reinterpret_cast<uint32_t*>(orow1 + jd * 8 + 2 * c) = pack_bf16x2(o[jd][2] * inv1, o[jd][3] * inv1);
+  }
+}
+
+// ----------------------------------------------------------------------------------
+// temporal attention: one warp per (session, token, head); CTA = 4 heads of one token
+// ----------------------------------------------------------------------------------
+
+
+constexpr int kTpWarps = 4;
+constexpr int kTpRowsPerMat = 32;
+constexpr int kTpWarpSmem = 3 * kTpRowsPerMat * kSmemStride;  // bf16 elements
+constexpr int kTpSmem = kTpWarps * kTpWarpSmem * 2;             // 55,296 B
+
+// Stage one 64-wide K or V row of cache slot `s` into shared memory as bf16.
+__device__ __forceinline__ void stage_cache_row(const KvView& kv, bool is_v, int b, int layer,
+                                                int s, int p, int h, __nv_bfloat16* dst) {
+  const int kind = kv.kind[s];
+  const int idx = kv.index[s];
+  if (kind == OASIS_KV_BF16) {
+    const long long slot = (static_cast<long long>(b) * kv.layers + layer) * kv.n_bf16 + idx;
+    const uint4* src = reinterpret_cast<const uint4*>(
+        (is_v ? kv.v_bf16 : kv.k_bf16) + (slot * OASIS_TOKENS + p) * OASIS_HIDDEN + h * 64);
+    uint4* d = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) d[i] = src[i];
+  } else if (kind == OASIS_KV_FP8) {
+    const long long slot = (static_cast<long long>(b) * kv.layers + layer) * kv.n_fp8 + idx;
+    const uint4* src = reinterpret_cast<const uint4*>(
+        (is_v ? kv.v_fp8 : kv.k_fp8) + (slot * OASIS_TOKENS + p) * OASIS_HIDDEN + h * 64);
+    const float scale = __bfloat162float((is_v ? kv.v_fp8_scale : kv.k_fp8_scale)[slot * OASIS_HEADS + h]);
+    uint32_t* d = reinterpret_cast<uint32_t*>(dst);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint4 w = src[i];
+      const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint32_t x = words[j];
+        // dequantise exactly as q.to(bf16) * scale in bf16 (one rounding)
+        d[i * 8 + j * 2 + 0] = pack_bf16x2(e4m3_to_float(x & 0xFF) * scale,
+                                           e4m3_to_float((x >> 8) & 0xFF) * scale);
+        d[i * 8 + j * 2 + 1] = pack_bf16x2(e4m3_to_float((x >> 16) & 0xFF) * scale,
+                                           e4m3_to_float(x >> 24) * scale);
+      }
+    }
+  } else {
+    const long long slot = (static_cast<long long>(b) * kv.layers + layer) * kv.n_int4 + idx;
+    const long long grp = (slot * OASIS_TOKENS + p) * OASIS_HEADS + h;
+    const uint4* src = reinterpret_cast<const uint4*>((is_v ? kv.v_int4 : kv.k_int4) + grp * 32);
+    const float scale = __half2float((is_v ? kv.v_i4_scale : kv.k_i4_scale)[grp]);
+    const float zero = __half2float((is_v ? kv.v_i4_zero : kv.k_i4_zero)[grp]);
+    uint32_t* d = reinterpret_cast<uint32_t*>(dst);
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const uint4 w = src[i];
+      const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+#pragma unroll
+        for (int bt = 0; bt < 4; ++bt) {
+          const uint32_t byte = (words[j] >> (8 * bt)) & 0xFFu;  // element 2i high, 2i+1 low
+          const float hi = static_cast<float>(byte >> 4) * scale + zero;
+          const float lo = static_cast<float>(byte & 0xFu) * scale + zero;
+          d[i * 16 + j * 4 + bt] = pack_bf16x2(hi, lo);
+        }
+      }
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kTpWarps * 32)
+    attn_temporal_kernel(const __nv_bfloat16* __restrict__ qkv, __nv_bfloat16* __restrict__ out,
+                         KvView kv, int layer, int q_frames, int q_pos0, int n_past, int n_kv,
+                         float scale_log2) {
+  extern __shared__ __align__(16) uint8_t sm_tp[];
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int p = blockIdx.x;                 // token within frame
+  const int h = blockIdx.y * kTpWarps + warp;
+  const int b = blockIdx.z;                 // session
+  __nv_bfloat16* sQ = reinterpret_cast<__nv_bfloat16*>(sm_tp) + warp * kTpWarpSmem;
+  __nv_bfloat16* sK = sQ + kTpRowsPerMat * kSmemStride;
+  __nv_bfloat16* sV = sK + kTpRowsPerMat * kSmemStride;
+
+  // lane r stages row r of Q, K and V
+  {
+    const int r = lane;
+    uint4* dq = reinterpret_cast<uint4*>(sQ + r * kSmemStride);
+    if (r < q_frames) {
+      const uint4* src = reinterpret_cast<const uint4*>(
+          qkv + (static_cast<long long>(b * q_frames + r) * OASIS_TOKENS + p) * kQkvLd + h * 64);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) dq[i] = src[i];
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) dq[i] = make_uint4(0, 0, 0, 0);
+    }
+    __nv_bfloat16* dk = sK + r * kSmemStride;
+    __nv_bfloat16* dv = sV + r * kSmemStride;
+    if (r < n_past) {
+      stage_cache_row(kv, false, b, layer, r, p, h, dk);
+      stage_cache_row(kv, true, b, layer, r, p, h, dv);
+    } else if (r < n_kv) {
+      const long long row = static_cast<long long>(b * q_frames + (r - n_past)) * OASIS_TOKENS + p;
+      const uint4* srck = reinterpret_cast<const uint4*>(qkv + row * kQkvLd + OASIS_HIDDEN + h * 64);
+      const uint4* srcv = reinterpret_cast<const uint4*>(qkv + row * kQkvLd + 2 * OASIS_HIDDEN + h * 64);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        reinterpret_cast<uint4*>(dk)[i] = srck[i];
+        reinterpret_cast<uint4*>(dv)[i] = srcv[i];
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        reinterpret_cast<uint4*>(dk)[i] = make_uint4(0, 0, 0, 0);
+        reinterpret_cast<uint4*>(dv)[i] = make_uint4(0, 0, 0, 0);
+      }
+    }
+  }
+  __syncwarp();
+
+  const int m_tiles = (q_frames + 15) >> 4;  // 1 or 2
+  const int n_pairs = (n_kv + 15) >> 4;      // key tiles of 16 (1 or 2)
+  const int g = lane >> 2, c = lane & 3;
+
+  for (int mt = 0; mt < m_tiles; ++mt) {
+    uint32_t qa[4][4];
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk)
+      ldsm_x4(smem_u32(sQ + (mt * 16 + (lane & 15)) * kSmemStride + kk * 16 + (lane >> 4) * 8),
+              qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3]);
+    float s[4][4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.0f;
+#pragma unroll
+    for (int jp = 0; jp < 2; ++jp) {
+      if (jp < n_pairs) {
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          uint32_t b0, b1, b2, b3;
+          const int key = jp * 16 + (lane & 7) + ((lane >> 4) << 3);
+          const int col = kk * 16 + ((lane >> 3) & 1) * 8;
+          ldsm_x4(smem_u32(sK + key * kSmemStride + col), b0, b1, b2, b3);
+          mma_bf16_16816(s[2 * jp], qa[kk], b0, b1);
+          mma_bf16_16816(s[2 * jp + 1], qa[kk], b2, b3);
+        }
+      }
+    }
+    // causal mask: query row t at window position q_pos0 + t sees keys 0..q_pos0+t
+    const int qp0 = q_pos0 + mt * 16 + g;
+    const int qp1 = qp0 + 8;
+    float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int key = j * 8 + 2 * c + e;
+        const bool ok = key < n_kv;
+        if (!(ok && key <= qp0)) s[j][e] = -INFINITY;
+        if (!(ok && key <= qp1)) s[j][2 + e] = -INFINITY;
+        mx0 = fmaxf(mx0, s[j][e]);
+        mx1 = fmaxf(mx1, s[j][2 + e]);
+      }
+    }
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+    const float o0 = mx0 * scale_log2, o1 = mx1 * scale_log2;
+    float sum0 = 0.0f, sum1 = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      s[j][0] = exp2f(s[j][0] * scale_log2 - o0);
+      s[j][1] = exp2f(s[j][1] * scale_log2 - o0);
+      s[j][2] = exp2f(s[j][2] * scale_log2 - o1);
+      s[j][3] = exp2f(s[j][3] * scale_log2 - o1);
+      sum0 += s[j][0] + s[j][1];
+      sum1 += s[j][2] + s[j][3];
+    }
+    sum0 += __shfl_xor_sync(0xffffffffu, sum0, 1);
+    sum0 += __shfl_xor_sync(0xffffffffu, sum0, 2);
+    sum1 += __shfl_xor_sync(0xffffffffu, sum1, 1);
+    sum1 += __shfl_xor_sync(0xffffffffu, sum1, 2);
+
+    float o[8][4];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.0f;
+#pragma unroll
+    for (int kk = 0; kk < 2; ++kk) {
+      if (kk < n_pairs) {
+        uint32_t pa[4];
+        pa[0] = pack_bf16x2(s[2 * kk][0], s[2 * kk][1]);
+        pa[1] = pack_bf16x2(s[2 * kk][2], s[2 * kk][3]);
+        pa[2] = pack_bf16x2(s[2 * kk + 1][0], s[2 * kk + 1][1]);
+        pa[3] = pack_bf16x2(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+#pragma unroll
+        for (int jd = 0; jd < 8; jd += 2) {
+          uint32_t b0, b1, b2, b3;
+          const int key = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+          const int col = jd * 8 + (lane >> 4) * 8;
+          ldsm_x4_t(smem_u32(sV + key * kSmemStride + col), b0, b1, b2, b3);
+          mma_bf16_16816(o[jd], pa, b0, b1);
+          mma_bf16_16816(o[jd + 1], pa, b2, b3);
+        }
+      }
+    }
+    const float inv0 = 1.0f / sum0, inv1 = 1.0f / sum1;
+    const int t0 = mt * 16 + g, t1 = t0 + 8;
+    if (t0 < q_frames) {
+      __nv_bfloat16* orow = out + (static_cast<long long>(b * q_frames + t0) * OASIS_TOKENS + p) * OASIS_HIDDEN + h * 64;
+#pragma unroll
+      for (int jd = 0; jd < 8; ++jd)
+        *reinterpret_cast<uint32_t*>(orow + jd * 8 + 2 * c) = pack_bf16x2(o[jd][0] * inv0, o[jd][1] * inv0);
+    }
+    if (t1 < q_frames) {
+      __nv_bfloat16* orow = out + (static_cast<long long>(b * q_frames + t1) * OASIS_TOKENS + p) * OASIS_HIDDEN + h * 64;
+#pragma unroll
+      for (int jd = 0; jd < 8; ++jd)
+        *reinterpret_cast<uint32_t*>(orow + jd * 8 + 2 * c) = pack_bf16x2(o[jd][2] * inv1, o[jd][3] * inv1);
+    }
+  }
+}
+
+// ----------------------------------------------------------------------------------
+// host launchers
+// ----------------------------------------------------------------------------------
+constexpr float kScaleLog2 = 0.125f * 1.4426950408889634f;  // (1/sqrt(64)) * log2(e)
+
+int launch_attn_spatial(const void* qkv, void* out, int frames, cudaStream_t stream) {
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(attn_spatial_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kSpSmem);
+    if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(attn_spatial)");
+    configured = true;
+  }
+  dim3 grid(frames, OASIS_HEADS);
+  attn_spatial_kernel<<<grid, kSpThreads, kSpSmem, stream>>>(
+      static_cast<const __nv_bfloat16*>(qkv), static_cast<__nv_bfloat16*>(out), kScaleLog2);
+  OASIS_CHECK_LAUNCH("attn_spatial_kernel");
+  return OASIS_OK;
+}
+
+int make_kv_view(const oasis_kv_cache_t* c, KvView* v) {
+  *v = KvView{};
+  if (!c) return OASIS_OK;
+  v->layers = c->layers;
+  v->n_bf16 = c->n_bf16;
+  v->n_fp8 = c->n_fp8;
+  v->n_int4 = c->n_int4;
+  for (int s = 0; s < OASIS_MAX_FRAMES; ++s) {
+    v->kind[s] = c->slot_kind[s];
+    v->index[s] = c->slot_index[s];
+  }
+  for (int s = 0; s < c->n_slots && s < OASIS_MAX_FRAMES; ++s) {
+    const int kind = c->slot_kind[s], idx = c->slot_index[s];
+    const bool ok = (kind == OASIS_KV_BF16 && idx < c->n_bf16 && c->k_bf16 && c->v_bf16) ||
+                    (kind == OASIS_KV_FP8 && idx < c->n_fp8 && c->k_fp8 && c->v_fp8 &&
+                     c->k_fp8_scale && c->v_fp8_scale) ||
+                    (kind == OASIS_KV_INT4 && idx < c->n_int4 && c->k_int4 && c->v_int4 &&
+                     c->k_i4_scale && c->k_i4_zero && c->v_i4_scale && c->v_i4_zero);
+    if (!ok) return fail(OASIS_ERR_INVALID_ARG, "KV cache slot " + std::to_string(s) +
+                                                    " has an invalid kind/index or missing pool");
+  }
+  v->k_bf16 = static_cast<const __nv_bfloat16*>(c->k_bf16);
+  v->v_bf16 = static_cast<const __nv_bfloat16*>(c->v_bf16);
+  v->k_fp8 = c->k_fp8;
+  v->v_fp8 = c->v_fp8;
+  v->k_fp8_scale = static_cast<const __nv_bfloat16*>(c->k_fp8_scale);
+  v->v_fp8_scale = static_cast<const __nv_bfloat16*>(c->v_fp8_scale);
+  v->k_int4 = c->k_int4;
+  v->v_int4 = c->v_int4;
+  v->k_i4_scale = static_cast<const __half*>(c->k_i4_scale);
+  v->k_i4_zero = static_cast<const __half*>(c->k_i4_zero);
+  v->v_i4_scale = static_cast<const __half*>(c->v_i4_scale);
+  v->v_i4_zero = static_cast<const __half*>(c->v_i4_zero);
+  return OASIS_OK;
+}
+
+int launch_attn_temporal(const void* qkv, const KvView& kv, int layer, void* out, int batch,
+                         int q_frames, int q_pos0, int n_past, int n_kv, cudaStream_t stream) {
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(attn_temporal_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kTpSmem);
+    if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(attn_temporal)");
+    configured = true;
+  }
+  dim3 grid(OASIS_TOKENS, OASIS_HEADS / kTpWarps, batch);
+  attn_temporal_kernel<<<grid, kTpWarps * 32, kTpSmem, stream>>>(
+      static_cast<const __nv_bfloat16*>(qkv), static_cast<__nv_bfloat16*>(out), kv, layer, q_frames,
+      q_pos0, n_past, n_kv, kScaleLog2);
+  OASIS_CHECK_LAUNCH("attn_temporal_kernel");
+  return OASIS_OK;
+}
+
+}  // namespace oasis
+
+extern "C" int oasis_attn_spatial(const void* qkv, void* out, int frames, cudaStream_t stream) {
+  using namespace oasis;
+  if (!qkv || !out || frames <= 0) return fail(OASIS_ERR_INVALID_ARG, "oasis_attn_spatial: bad args");
+  if (!aligned16(qkv) || !aligned16(out)) return fail(OASIS_ERR_ALIGNMENT, "oasis_attn_spatial: alignment");
+  if (frames > 65535 * 16) return fail(OASIS_ERR_UNSUPPORTED, "oasis_attn_spatial: too many frames");
+  return launch_attn_spatial(qkv, out, frames, stream);
+}
+
+extern "C" int oasis_attn_temporal(const void* qkv, const oasis_kv_cache_t* cache, int layer,
+                                   void* out, int batch, int q_frames, int q_pos0, int n_past,
+                                   int n_kv, cudaStream_t stream) {
+  using namespace oasis;
+  if (!qkv || !out || batch <= 0 || q_frames <= 0)
+    return fail(OASIS_ERR_INVALID_ARG, "oasis_attn_temporal: bad args");
+  if (n_kv < 1 || n_kv > OASIS_MAX_FRAMES || q_frames > OASIS_MAX_FRAMES || n_past < 0 ||
+      n_past > n_kv || n_kv - n_past > q_frames || q_pos0 < 0)
+    return fail(OASIS_ERR_INVALID_ARG, "oasis_attn_temporal: inconsistent frame counts");
+  if (n_past > 0 && (!cache || n_past > cache->n_slots || layer < 0 || layer >= cache->layers ||
+                     batch > cache->batch))
+    return fail(OASIS_ERR_INVALID_ARG, "oasis_attn_temporal: cache does not cover n_past/layer/batch");
+  if (!aligned16(qkv) || !aligned16(out)) return fail(OASIS_ERR_ALIGNMENT, "oasis_attn_temporal: alignment");
+  KvView v;
+  if (int s = make_kv_view(n_past > 0 ? cache : nullptr, &v)) return s;
+  return launch_attn_temporal(qkv, v, layer, out, batch, q_frames, q_pos0, n_past, n_kv, stream);
+}

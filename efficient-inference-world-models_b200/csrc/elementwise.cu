@@ -1,0 +1,259 @@
+// Memory-bound kernels around the GEMMs: LayerNorm + adaLN modulate, timestep /
+// action / patch embeddings (small fp32 SIMT GEMMs), and the sampler updates.
+#include "launch.cuh"
+
+namespace oasis {
+
+// ----------------------------------------------------------------------------------
+// LayerNorm (eps 1e-6, no affine) + modulate: out = bf16(LN(x) * (1 + scale[f]) + shift[f])
+// x fp32 [M][1024]; frame f = row / rows_per_frame; shift/scale rows of the adaLN table.
+// One warp per row: lane holds 8 float4 (columns lane*4 + i*128).
+// ----------------------------------------------------------------------------------
+__global__ void __launch_bounds__(256)
+    ln_modulate_kernel(const float* __restrict__ x, const float* __restrict__ shift,
+                       const float* __restrict__ scale, long long mod_ld,
+                       __nv_bfloat16* __restrict__ out, int M, int rows_per_frame) {
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= M) return;
+  const float4* xr = reinterpret_cast<const float4*>(x + static_cast<long long>(row) * OASIS_HIDDEN);
+  float4 v[8];
+  float sum = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    v[i] = xr[lane + 32 * i];
+    sum += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  const float mean = sum * (1.0f / OASIS_HIDDEN);
+  float sq = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float a = v[i].x - mean, b = v[i].y - mean, c = v[i].z - mean, d = v[i].w - mean;
+    sq += (a * a + b * b) + (c * c + d * d);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+  const float rstd = rsqrtf(sq * (1.0f / OASIS_HIDDEN) + 1e-6f);
+  const long long f = row / rows_per_frame;
+  const float4* sh = reinterpret_cast<const float4*>(shift + f * mod_ld);
+  const float4* sc = reinterpret_cast<const float4*>(scale + f * mod_ld);
+  uint2* o2 = reinterpret_cast<uint2*>(out + static_cast<long long>(row) * OASIS_HIDDEN);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float4 a = sh[lane + 32 * i];
+    const float4 s = sc[lane + 32 * i];
+    const float y0 = (v[i].x - mean) * rstd * (1.0f + s.x) + a.x;
+    const float y1 = (v[i].y - mean) * rstd * (1.0f + s.y) + a.y;
+    const float y2 = (v[i].z - mean) * rstd * (1.0f + s.z) + a.z;
+    const float y3 = (v[i].w - mean) * rstd * (1.0f + s.w) + a.w;
+    o2[lane + 32 * i] = make_uint2(pack_bf16x2(y0, y1), pack_bf16x2(y2, y3));
+  }
+}
+
+int launch_ln_modulate(const float* x, const float* shift, const float* scale, long long mod_ld,
+                       void* out, int M, int rows_per_frame, cudaStream_t stream) {
+  ln_modulate_kernel<<<(M + 7) / 8, 256, 0, stream>>>(x, shift, scale, mod_ld,
+                                                      static_cast<__nv_bfloat16*>(out), M,
+                                                      rows_per_frame);
+  OASIS_CHECK_LAUNCH("ln_modulate_kernel");
+  return OASIS_OK;
+}
+
+// ----------------------------------------------------------------------------------
+// small fp32 GEMM: out[m][n] (+)= act(sum_k in[m][k] * W[n][k] + b[n]); 64x64 tiles,
+// 256 threads x (4 x 4) outputs, K staged 32 at a time.  act: 0 none, 1 SiLU.
+// ----------------------------------------------------------------------------------
+template <int ACT, bool ACCUM>
+__global__ void __launch_bounds__(256)
+    linear_f32_kernel(const float* __restrict__ in, int ldi, const float* __restrict__ W,
+                      const float* __restrict__ bias, float* __restrict__ out, int ldo, int M,
+                      int N, int K) {
+  __shared__ float As[32][65];
+  __shared__ float Ws[32][65];
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  const int m0 = blockIdx.y * 64, n0 = blockIdx.x * 64;
+  float acc[4][4] = {};
+  for (int k0 = 0; k0 < K; k0 += 32) {
+    for (int i = threadIdx.x; i < 64 * 32; i += 256) {
+      const int r = i >> 5, k = i & 31;
+      const int gm = m0 + r, gn = n0 + r, gk = k0 + k;
+      As[k][r] = (gm < M && gk < K) ? in[static_cast<long long>(gm) * ldi + gk] : 0.0f;
+      Ws[k][r] = (gn < N && gk < K) ? W[static_cast<long long>(gn) * K + gk] : 0.0f;
+    }
+    __syncthreads();
+#pragma unroll 8
+    for (int k = 0; k < 32; ++k) {
+      float a[4], w[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        a[i] = As[k][ty * 4 + i];
+        w[i] = Ws[k][tx * 4 + i];
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], w[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int gm = m0 + ty * 4 + i;
+    if (gm >= M) continue;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int gn = n0 + tx * 4 + j;
+      if (gn >= N) continue;
+      float y = acc[i][j] + (bias ? bias[gn] : 0.0f);
+      if (ACT == 1) y = y / (1.0f + expf(-y));
+      float* o = out + static_cast<long long>(gm) * ldo + gn;
+      *o = ACCUM ? *o + y : y;
+    }
+  }
+}
+
+int launch_linear_f32(const float* in, int ldi, const float* W, const float* b, float* out, int ldo,
+                      int M, int N, int K, int act, bool accum, cudaStream_t stream) {
+  dim3 grid((N + 63) / 64, (M + 63) / 64);
+  if (act == 1 && !accum)
+    linear_f32_kernel<1, false><<<grid, 256, 0, stream>>>(in, ldi, W, b, out, ldo, M, N, K);
+  else if (act == 0 && !accum)
+    linear_f32_kernel<0, false><<<grid, 256, 0, stream>>>(in, ldi, W, b, out, ldo, M, N, K);
+  else
+    linear_f32_kernel<0, true><<<grid, 256, 0, stream>>>(in, ldi, W, b, out, ldo, M, N, K);
+  OASIS_CHECK_LAUNCH("linear_f32_kernel");
+  return OASIS_OK;
+}
+
+// Sinusoidal timestep embedding (256): [cos(t * f_i) | sin(t * f_i)],
+// f_i = exp(-ln(10000) * i / 128), i < 128, computed in fp32.
+__global__ void temb_sinusoid_kernel(const int64_t* __restrict__ t, float* __restrict__ emb, int F) {
+  const int f = blockIdx.x;
+  const int i = threadIdx.x;  // 128 threads
+  if (f >= F) return;
+  const float freq = expf(-9.210340371976184f * static_cast<float>(i) / 128.0f);
+  const float arg = static_cast<float>(t[f]) * freq;
+  emb[f * 256 + i] = cosf(arg);
+  emb[f * 256 + 128 + i] = sinf(arg);
+}
+
+int launch_temb_sinusoid(const int64_t* t, float* emb, int F, cudaStream_t stream) {
+  temb_sinusoid_kernel<<<F, 128, 0, stream>>>(t, emb, F);
+  OASIS_CHECK_LAUNCH("temb_sinusoid_kernel");
+  return OASIS_OK;
+}
+
+// bf16(silu(c)): the shared input of every adaLN modulation linear.
+__global__ void silu_bf16_kernel(const float* __restrict__ c, __nv_bfloat16* __restrict__ out, int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) {
+    const float y = c[i];
+    out[i] = __float2bfloat16_rn(y / (1.0f + expf(-y)));
+  }
+}
+
+int launch_silu_bf16(const float* c, void* out, int n, cudaStream_t stream) {
+  silu_bf16_kernel<<<(n + 255) / 256, 256, 0, stream>>>(c, static_cast<__nv_bfloat16*>(out), n);
+  OASIS_CHECK_LAUNCH("silu_bf16_kernel");
+  return OASIS_OK;
+}
+
+// im2col of the 2x2 patch embedding: x fp32 [F][16][18][32] -> cols [F*144][64], column
+// index c*4 + pi*2 + qi (Conv2d weight order [out][c][pi][qi]).
+__global__ void patch_im2col_kernel(const float* __restrict__ x, float* __restrict__ cols, int F) {
+  const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const long long total = static_cast<long long>(F) * OASIS_TOKENS * 64;
+  if (i >= total) return;
+  const int k = static_cast<int>(i & 63);
+  const long long m = i >> 6;
+  const int f = static_cast<int>(m / OASIS_TOKENS);
+  const int pp = static_cast<int>(m % OASIS_TOKENS);
+  const int hp = pp / 16, wp = pp % 16;
+  const int c = k >> 2, pi = (k >> 1) & 1, qi = k & 1;
+  cols[i] = x[((static_cast<long long>(f) * 16 + c) * 18 + hp * 2 + pi) * 32 + wp * 2 + qi];
+}
+
+int launch_patch_im2col(const float* x, float* cols, int F, cudaStream_t stream) {
+  const long long total = static_cast<long long>(F) * OASIS_TOKENS * 64;
+  patch_im2col_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, stream>>>(x, cols, F);
+  OASIS_CHECK_LAUNCH("patch_im2col_kernel");
+  return OASIS_OK;
+}
+
+// ----------------------------------------------------------------------------------
+// samplers
+// ----------------------------------------------------------------------------------
+// DPM-Solver++ 2M (v-prediction) on `n` elements per session; with first != 0 it is the
+// DDIM v-step.  a = sqrt(ab_t), b = sqrt(1 - ab_t), c = sqrt(ab_next), d = sqrt(1 - ab_next).
+__global__ void dpmpp2m_kernel(float* __restrict__ x, const float* __restrict__ v,
+                               float* __restrict__ eps_prev, int n, long long xs, long long vs,
+                               float a, float b, float c, float d, int first) {
+  const int sess = blockIdx.y;
+  const int i = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
+  if (i >= n) return;
+  float4 xv = *reinterpret_cast<float4*>(x + sess * xs + i);
+  const float4 vv = *reinterpret_cast<const float4*>(v + sess * vs + i);
+  float* ep = eps_prev ? eps_prev + static_cast<long long>(sess) * n + i : nullptr;
+  float4 pv = make_float4(0, 0, 0, 0);
+  if (!first && ep) pv = *reinterpret_cast<float4*>(ep);
+  float xs4[4] = {xv.x, xv.y, xv.z, xv.w};
+  const float vs4[4] = {vv.x, vv.y, vv.z, vv.w};
+  const float ps4[4] = {pv.x, pv.y, pv.z, pv.w};
+  float es4[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const float x0 = a * xs4[k] - b * vs4[k];
+    const float eps = b * xs4[k] + a * vs4[k];
+    const float D = first ? eps : (3.0f * eps - ps4[k]) / 2.0f;
+    es4[k] = eps;
+    xs4[k] = c * x0 + d * D;
+  }
+  *reinterpret_cast<float4*>(x + sess * xs + i) = make_float4(xs4[0], xs4[1], xs4[2], xs4[3]);
+  if (ep) *reinterpret_cast<float4*>(ep) = make_float4(es4[0], es4[1], es4[2], es4[3]);
+}
+
+__global__ void ab_update_kernel(const float* __restrict__ x, const float* __restrict__ d0,
+                                 const float* __restrict__ d1, const float* __restrict__ d2,
+                                 float* __restrict__ out, long long n, float h, float c0, float c1,
+                                 float c2) {
+  const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  float acc = c0 * d0[i];
+  if (d1) acc += c1 * d1[i];
+  if (d2) acc += c2 * d2[i];
+  out[i] = x[i] + h * acc;
+}
+
+}  // namespace oasis
+
+extern "C" int oasis_dpmpp2m_update(float* x, const float* v, float* eps_prev, int batch, int n,
+                                    long long x_stride, long long v_stride, float ab_t,
+                                    float ab_next, int first, cudaStream_t stream) {
+  using namespace oasis;
+  if (!x || !v || batch <= 0 || n <= 0) return fail(OASIS_ERR_INVALID_ARG, "oasis_dpmpp2m_update: bad args");
+  if (!first && !eps_prev) return fail(OASIS_ERR_INVALID_ARG, "oasis_dpmpp2m_update: multistep needs eps_prev");
+  if ((n % 4) || (x_stride % 4) || (v_stride % 4) || !aligned16(x) || !aligned16(v) ||
+      (eps_prev && !aligned16(eps_prev)))
+    return fail(OASIS_ERR_ALIGNMENT, "oasis_dpmpp2m_update: n/strides must be multiples of 4, 16-byte aligned");
+  if (batch > 65535) return fail(OASIS_ERR_UNSUPPORTED, "oasis_dpmpp2m_update: batch too large");
+  const float a = sqrtf(ab_t), b = sqrtf(1.0f - ab_t), c = sqrtf(ab_next), d = sqrtf(1.0f - ab_next);
+  dim3 grid((n / 4 + 255) / 256, batch);
+  dpmpp2m_kernel<<<grid, 256, 0, stream>>>(x, v, eps_prev, n, x_stride, v_stride, a, b, c, d, first);
+  OASIS_CHECK_LAUNCH("dpmpp2m_kernel");
+  return OASIS_OK;
+}
+
+extern "C" int oasis_ab_update(const float* x, const float* d0, const float* d1, const float* d2,
+                               float* out, long long n, float h, float c0, float c1, float c2,
+                               cudaStream_t stream) {
+  using namespace oasis;
+  if (!x || !d0 || !out || n <= 0) return fail(OASIS_ERR_INVALID_ARG, "oasis_ab_update: bad args");
+  if ((c1 != 0.0f && !d1) || (c2 != 0.0f && !d2))
+    return fail(OASIS_ERR_INVALID_ARG, "oasis_ab_update: missing history for a non-zero coefficient");
+  ab_update_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, stream>>>(
+      x, d0, c1 != 0.0f ? d1 : nullptr, c2 != 0.0f ? d2 : nullptr, out, n, h, c0, c1, c2);
+  OASIS_CHECK_LAUNCH("ab_update_kernel");
+  return OASIS_OK;
+}

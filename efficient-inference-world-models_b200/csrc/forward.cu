@@ -1,0 +1,432 @@
+// Forward plan: the native runtime that drives one Oasis DiT denoising forward.
+//
+// Per call (frames F = batch * frames_per_session, tokens M = F * 144):
+//   patch im2col + fp32 linear -> residual x (fp32, [M][1024])
+//   timestep sinusoid -> MLP (SiLU) + action linear -> c; bf16(SiLU(c))
+//   ONE swap-AB tcgen05 GEMM for all 33 adaLN modulations -> mod [F][2*depth*6144 + 2048]
+//   per sub-block (spatial, then temporal, x depth):
+//     LN+modulate -> QKV GEMM (+RoPE epilogue) -> attention [-> KV store] ->
+//     out GEMM (gate*(.+b) + residual epilogue) -> LN+modulate -> fc1 GEMM (+b, GELU) ->
+//     fc2 GEMM (gate*(.+b) + residual epilogue)
+//   final LN+modulate -> 1024->64 GEMM with the unpatchify store into v.
+// All launches go to the caller's stream; nothing allocates or synchronises, so a
+// forward can be captured into a CUDA graph.
+#include <cstring>
+#include <vector>
+
+#include "gemm.cuh"
+#include "launch.cuh"
+
+namespace oasis {
+
+namespace {
+
+constexpr int kFamilies = 7;
+enum Family { kFamGemm = 0, kFamAda, kFamSpatial, kFamTemporal, kFamLn, kFamEmbed, kFamKv };
+
+size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+struct Layout {
+  size_t resid, hbuf, qkv, attn, mlp, cols, emb, h1, c, silu, mod, total;
+};
+
+Layout layout_for(int F, int depth) {
+  const size_t M = static_cast<size_t>(F) * OASIS_TOKENS;
+  const size_t mod_ld = static_cast<size_t>(2 * depth) * OASIS_ADA_PER_SUB + 2 * OASIS_HIDDEN;
+  Layout L{};
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off = align256(off + bytes);
+    return o;
+  };
+  L.resid = take(M * OASIS_HIDDEN * 4);
+  L.hbuf = take(M * OASIS_HIDDEN * 2);
+  L.qkv = take(M * 3 * OASIS_HIDDEN * 2);
+  L.attn = take(M * OASIS_HIDDEN * 2);
+  L.mlp = take(M * OASIS_MLP_HIDDEN * 2);
+  L.cols = take(M * 64 * 4);
+  L.emb = take(static_cast<size_t>(F) * 256 * 4);
+  L.h1 = take(static_cast<size_t>(F) * OASIS_HIDDEN * 4);
+  L.c = take(static_cast<size_t>(F) * OASIS_HIDDEN * 4);
+  L.silu = take(static_cast<size_t>(F) * OASIS_HIDDEN * 2);
+  L.mod = take(static_cast<size_t>(F) * mod_ld * 4);
+  L.total = off;
+  return L;
+}
+
+}  // namespace
+}  // namespace oasis
+
+struct oasis_plan {
+  oasis_dit_weights_t w;
+  int batch = 0, frames = 0, F = 0, M = 0, depth = 0;
+  long long mod_ld = 0;
+  uint8_t* ws = nullptr;
+  oasis::Layout L{};
+  // GEMM operand descriptors
+  oasis::GemmOperands ada;
+  oasis::GemmOperands fin;
+  std::vector<oasis::GemmOperands> qkv, out, fc1, fc2;  // per sub-block
+  // timing
+  bool timing = false;
+  std::vector<cudaEvent_t> ev;
+  std::vector<int> ev_family;
+  int ev_used = 0;
+  float fam_ms[oasis::kFamilies] = {};
+  int fam_launches[oasis::kFamilies] = {};
+};
+
+namespace oasis {
+namespace {
+
+struct Timer {
+  oasis_plan* p;
+  cudaStream_t s;
+  int fam;
+  int idx = -1;
+  Timer(oasis_plan* p_, cudaStream_t s_, int fam_) : p(p_), s(s_), fam(fam_) {
+    if (p->timing && p->ev_used + 2 <= static_cast<int>(p->ev.size())) {
+      idx = p->ev_used;
+      p->ev_used += 2;
+      p->ev_family[idx] = fam;
+      cudaEventRecord(p->ev[idx], s);
+    }
+  }
+  ~Timer() {
+    if (idx >= 0) cudaEventRecord(p->ev[idx + 1], s);
+  }
+};
+
+template <typename T>
+T* at(oasis_plan* p, size_t off) {
+  return reinterpret_cast<T*>(p->ws + off);
+}
+
+int pick_bn(int N, int M) {
+  // 128-row tiles along M; choose the widest N tile that still gives >= ~1 wave
+  const int sms = num_sms();
+  const int mt = (M + kGemmBM - 1) / kGemmBM;
+  for (int bn : {256, 128, 64}) {
+    if (N % bn) continue;
+    if (static_cast<long long>(mt) * (N / bn) >= sms || bn == 64) return bn;
+  }
+  return 64;
+}
+
+int run_forward(oasis_plan* p, const float* x, const int64_t* t, const float* act, float* v,
+                const oasis_kv_cache_t* cache, int n_past, bool cached, cudaStream_t s) {
+  const int F = p->F, M = p->M;
+  const oasis_dit_weights_t& w = p->w;
+  float* resid = at<float>(p, p->L.resid);
+  void* hbuf = at<void>(p, p->L.hbuf);
+  void* qkv = at<void>(p, p->L.qkv);
+  void* attn = at<void>(p, p->L.attn);
+  void* mlp = at<void>(p, p->L.mlp);
+  float* mod = at<float>(p, p->L.mod);
+  const long long mld = p->mod_ld;
+
+  // ---- embeddings ----
+  {
+    Timer tm(p, s, kFamEmbed);
+    if (int e = launch_patch_im2col(x, at<float>(p, p->L.cols), F, s)) return e;
+    if (int e = launch_linear_f32(at<float>(p, p->L.cols), 64, w.patch_w, w.patch_b, resid,
+                                  OASIS_HIDDEN, M, OASIS_HIDDEN, 64, 0, false, s))
+      return e;
+    if (int e = launch_temb_sinusoid(t, at<float>(p, p->L.emb), F, s)) return e;
+    if (int e = launch_linear_f32(at<float>(p, p->L.emb), 256, w.t_fc1_w, w.t_fc1_b,
+                                  at<float>(p, p->L.h1), OASIS_HIDDEN, F, OASIS_HIDDEN, 256, 1,
+                                  false, s))
+      return e;
+    if (int e = launch_linear_f32(at<float>(p, p->L.h1), OASIS_HIDDEN, w.t_fc2_w, w.t_fc2_b,
+                                  at<float>(p, p->L.c), OASIS_HIDDEN, F, OASIS_HIDDEN, OASIS_HIDDEN,
+                                  0, false, s))
+      return e;
+    if (act) {
+      if (int e = launch_linear_f32(act, OASIS_ACTION_DIM, w.act_w, w.act_b, at<float>(p, p->L.c),
+                                    OASIS_HIDDEN, F, OASIS_HIDDEN, OASIS_ACTION_DIM, 0, true, s))
+        return e;
+    }
+    if (int e = launch_silu_bf16(at<float>(p, p->L.c), at<void>(p, p->L.silu), F * OASIS_HIDDEN, s))
+      return e;
+  }
+  // ---- all adaLN modulations in one swap-AB GEMM ----
+  {
+    Timer tm(p, s, kFamAda);
+    EpiParams ep{};
+    ep.out = mod;
+    ep.ldd = mld;
+    ep.bias = w.ada_b;
+    ep.n_valid = F;
+    if (int e = launch_gemm(p->ada, kEpiAdaT, ep, s)) return e;
+  }
+
+  KvView kvv;
+  if (int e = make_kv_view(cached ? cache : nullptr, &kvv)) return e;
+
+  const int T = p->frames;
+  const int pos0 = cached ? n_past : 0;
+  for (int j = 0; j < 2 * p->depth; ++j) {
+    const bool spatial = (j % 2) == 0;
+    const int blk = j / 2;
+    const oasis_sub_weights_t& sw = w.sub[j];
+    const float* modj = mod + static_cast<long long>(j) * OASIS_ADA_PER_SUB;
+    {
+      Timer tm(p, s, kFamLn);
+      if (int e = launch_ln_modulate(resid, modj + 0 * OASIS_HIDDEN, modj + 1 * OASIS_HIDDEN, mld,
+                                     hbuf, M, OASIS_TOKENS, s))
+        return e;
+    }
+    {
+      Timer tm(p, s, kFamGemm);
+      EpiParams ep{};
+      ep.out = qkv;
+      ep.ldd = 3 * OASIS_HIDDEN;
+      ep.rope_cols = 2 * OASIS_HIDDEN;
+      if (spatial) {
+        ep.rope = w.rope_spatial;
+        ep.rope_div = 1;
+        ep.rope_mod = OASIS_TOKENS;
+        ep.rope_add = 0;
+      } else {
+        ep.rope = w.rope_temporal;
+        ep.rope_div = OASIS_TOKENS;
+        ep.rope_mod = T;
+        ep.rope_add = pos0;
+      }
+      if (int e = launch_gemm(p->qkv[j], kEpiQkvRope, ep, s)) return e;
+    }
+    if (spatial) {
+      Timer tm(p, s, kFamSpatial);
+      if (int e = launch_attn_spatial(qkv, attn, F, s)) return e;
+    } else {
+      if (cache && !cached && T > 1) {
+        // post-RoPE K/V of window frames 0..T-2 -> cache slots 0..T-2
+        Timer tm(p, s, kFamKv);
+        if (int e = launch_kv_store(qkv, 3 * OASIS_HIDDEN, OASIS_HIDDEN, 2 * OASIS_HIDDEN, cache,
+                                    blk, p->batch, T - 1, T, 0, s))
+          return e;
+      }
+      Timer tm(p, s, kFamTemporal);
+      if (cached) {
+        // newest frame at window position n_past: cached slots 0..n_past-1 + its own K/V
+        if (int e = launch_attn_temporal(qkv, kvv, blk, attn, p->batch, 1, n_past, n_past,
+                                         n_past + 1, s))
+          return e;
+      } else {
+        if (int e = launch_attn_temporal(qkv, kvv, blk, attn, p->batch, T, 0, 0, T, s)) return e;
+      }
+    }
+    {
+      Timer tm(p, s, kFamGemm);
+      EpiParams ep{};
+      ep.out = resid;
+      ep.ldd = OASIS_HIDDEN;
+      ep.bias = sw.out_b;
+      ep.gate = modj + 2 * OASIS_HIDDEN;
+      ep.gate_ld = mld;
+      if (int e = launch_gemm(p->out[j], kEpiGateResid, ep, s)) return e;
+    }
+    {
+      Timer tm(p, s, kFamLn);
+      if (int e = launch_ln_modulate(resid, modj + 3 * OASIS_HIDDEN, modj + 4 * OASIS_HIDDEN, mld,
+                                     hbuf, M, OASIS_TOKENS, s))
+        return e;
+    }
+    {
+      Timer tm(p, s, kFamGemm);
+      EpiParams ep{};
+      ep.out = mlp;
+      ep.ldd = OASIS_MLP_HIDDEN;
+      ep.bias = sw.fc1_b;
+      if (int e = launch_gemm(p->fc1[j], kEpiBiasGelu, ep, s)) return e;
+    }
+    {
+      Timer tm(p, s, kFamGemm);
+      EpiParams ep{};
+      ep.out = resid;
+      ep.ldd = OASIS_HIDDEN;
+      ep.bias = sw.fc2_b;
+      ep.gate = modj + 5 * OASIS_HIDDEN;
+      ep.gate_ld = mld;
+      if (int e = launch_gemm(p->fc2[j], kEpiGateResid, ep, s)) return e;
+    }
+  }
+  // ---- final layer ----
+  {
+    Timer tm(p, s, kFamEmbed);
+    const float* fmod = mod + static_cast<long long>(2 * p->depth) * OASIS_ADA_PER_SUB;
+    if (int e = launch_ln_modulate(resid, fmod, fmod + OASIS_HIDDEN, mld, hbuf, M, OASIS_TOKENS, s))
+      return e;
+    EpiParams ep{};
+    ep.out = v;
+    ep.bias = w.final_b;
+    if (int e = launch_gemm(p->fin, kEpiFinal, ep, s)) return e;
+  }
+  return OASIS_OK;
+}
+
+}  // namespace
+}  // namespace oasis
+
+// ------------------------------------------------------------------ C ABI
+using namespace oasis;
+
+extern "C" size_t oasis_plan_workspace_size(int batch, int frames, int depth) {
+  if (batch <= 0 || frames <= 0 || depth <= 0) return 0;
+  return layout_for(batch * frames, depth).total;
+}
+
+extern "C" int oasis_plan_create(const oasis_dit_weights_t* w, int batch, int frames,
+                                 void* workspace, size_t workspace_bytes, oasis_plan_t** out) {
+  if (!w || !out) return fail(OASIS_ERR_INVALID_ARG, "oasis_plan_create: null argument");
+  *out = nullptr;
+  if (batch <= 0 || frames <= 0 || frames > OASIS_MAX_FRAMES)
+    return fail(OASIS_ERR_INVALID_ARG, "oasis_plan_create: need batch > 0 and 1 <= frames <= 32");
+  if (w->depth <= 0 || w->depth > OASIS_MAX_DEPTH)
+    return fail(OASIS_ERR_INVALID_ARG, "oasis_plan_create: depth must be 1..16");
+  const int F = batch * frames;
+  if (static_cast<long long>(F) * OASIS_TOKENS > (1LL << 30))
+    return fail(OASIS_ERR_UNSUPPORTED, "oasis_plan_create: too many tokens");
+  Layout L = layout_for(F, w->depth);
+  if (!workspace || workspace_bytes < L.total)
+    return fail(OASIS_ERR_WORKSPACE, "oasis_plan_create: workspace missing or smaller than "
+                                     "oasis_plan_workspace_size()");
+  if (reinterpret_cast<uintptr_t>(workspace) & 255)
+    return fail(OASIS_ERR_ALIGNMENT, "oasis_plan_create: workspace must be 256-byte aligned");
+  const void* req[] = {w->patch_w, w->patch_b, w->t_fc1_w, w->t_fc1_b, w->t_fc2_w, w->t_fc2_b,
+                       w->act_w,   w->act_b,   w->ada_w,   w->ada_b,   w->final_w, w->final_b,
+                       w->rope_spatial, w->rope_temporal};
+  for (const void* q : req)
+    if (!q) return fail(OASIS_ERR_INVALID_ARG, "oasis_plan_create: a weight pointer is NULL");
+  for (int j = 0; j < 2 * w->depth; ++j) {
+    const oasis_sub_weights_t& s = w->sub[j];
+    if (!s.qkv_w || !s.out_w || !s.out_b || !s.fc1_w || !s.fc1_b || !s.fc2_w || !s.fc2_b)
+      return fail(OASIS_ERR_INVALID_ARG, "oasis_plan_create: a sub-block weight pointer is NULL");
+  }
+
+  oasis_plan* p = new oasis_plan();
+  p->w = *w;
+  p->batch = batch;
+  p->frames = frames;
+  p->F = F;
+  p->M = F * OASIS_TOKENS;
+  p->depth = w->depth;
+  p->mod_ld = static_cast<long long>(2 * w->depth) * OASIS_ADA_PER_SUB + 2 * OASIS_HIDDEN;
+  p->ws = static_cast<uint8_t*>(workspace);
+  p->L = L;
+  const int M = p->M;
+  int st = OASIS_OK;
+  // adaLN: A = stacked weights (rows = mod_ld), B = bf16 SiLU(c) (rows = F)
+  {
+    int bn = 32;
+    while (bn < 256 && bn < F) bn <<= 1;
+    st = make_gemm_operands(&p->ada, w->ada_w, OASIS_HIDDEN, p->ws + L.silu, OASIS_HIDDEN,
+                            static_cast<int>(p->mod_ld), F, OASIS_HIDDEN, bn);
+  }
+  if (!st)
+    st = make_gemm_operands(&p->fin, p->ws + L.hbuf, OASIS_HIDDEN, w->final_w, OASIS_HIDDEN, M, 64,
+                            OASIS_HIDDEN, 64);
+  p->qkv.resize(2 * w->depth);
+  p->out.resize(2 * w->depth);
+  p->fc1.resize(2 * w->depth);
+  p->fc2.resize(2 * w->depth);
+  for (int j = 0; j < 2 * w->depth && !st; ++j) {
+    const oasis_sub_weights_t& s = w->sub[j];
+    st = make_gemm_operands(&p->qkv[j], p->ws + L.hbuf, OASIS_HIDDEN, s.qkv_w, OASIS_HIDDEN, M,
+                            3 * OASIS_HIDDEN, OASIS_HIDDEN, pick_bn(3 * OASIS_HIDDEN, M));
+    if (!st)
+      st = make_gemm_operands(&p->out[j], p->ws + L.attn, OASIS_HIDDEN, s.out_w, OASIS_HIDDEN, M,
+                              OASIS_HIDDEN, OASIS_HIDDEN, pick_bn(OASIS_HIDDEN, M));
+    if (!st)
+      st = make_gemm_operands(&p->fc1[j], p->ws + L.hbuf, OASIS_HIDDEN, s.fc1_w, OASIS_HIDDEN, M,
+                              OASIS_MLP_HIDDEN, OASIS_HIDDEN, pick_bn(OASIS_MLP_HIDDEN, M));
+    if (!st)
+      st = make_gemm_operands(&p->fc2[j], p->ws + L.mlp, OASIS_MLP_HIDDEN, s.fc2_w,
+                              OASIS_MLP_HIDDEN, M, OASIS_HIDDEN, OASIS_MLP_HIDDEN,
+                              pick_bn(OASIS_HIDDEN, M));
+  }
+  if (st) {
+    delete p;
+    return st;
+  }
+  *out = p;
+  return OASIS_OK;
+}
+
+extern "C" void oasis_plan_destroy(oasis_plan_t* plan) {
+  if (!plan) return;
+  for (cudaEvent_t e : plan->ev) cudaEventDestroy(e);
+  delete plan;
+}
+
+static int check_cache_for_plan(const oasis_plan* p, const oasis_kv_cache_t* c, int n_slots_needed) {
+  if (c->batch < p->batch || c->layers < p->depth)
+    return fail(OASIS_ERR_INVALID_ARG, "KV cache batch/layers smaller than the plan's");
+  return validate_slots(c, 0, n_slots_needed);
+}
+
+extern "C" int oasis_dit_forward(oasis_plan_t* plan, const float* x, const int64_t* t,
+                                 const float* act, float* v, const oasis_kv_cache_t* cache,
+                                 cudaStream_t stream) {
+  if (!plan || !x || !t || !v) return fail(OASIS_ERR_INVALID_ARG, "oasis_dit_forward: null argument");
+  if (!aligned16(x) || !aligned16(v)) return fail(OASIS_ERR_ALIGNMENT, "oasis_dit_forward: x/v alignment");
+  if (cache && plan->frames > 1)
+    if (int s = check_cache_for_plan(plan, cache, plan->frames - 1)) return s;
+  return run_forward(plan, x, t, act, v, cache, 0, false, stream);
+}
+
+extern "C" int oasis_dit_forward_cached(oasis_plan_t* plan, const float* x, const int64_t* t,
+                                        const float* act, float* v, const oasis_kv_cache_t* cache,
+                                        int n_past, cudaStream_t stream) {
+  if (!plan || !x || !t || !v || !cache)
+    return fail(OASIS_ERR_INVALID_ARG, "oasis_dit_forward_cached: null argument");
+  if (plan->frames != 1)
+    return fail(OASIS_ERR_INVALID_ARG, "oasis_dit_forward_cached: plan must be built with frames == 1");
+  if (n_past < 1 || n_past >= OASIS_MAX_FRAMES)
+    return fail(OASIS_ERR_INVALID_ARG, "oasis_dit_forward_cached: need 1 <= n_past <= 31");
+  if (!aligned16(x) || !aligned16(v)) return fail(OASIS_ERR_ALIGNMENT, "oasis_dit_forward_cached: alignment");
+  if (int s = check_cache_for_plan(plan, cache, n_past)) return s;
+  return run_forward(plan, x, t, act, v, cache, n_past, true, stream);
+}
+
+extern "C" int oasis_plan_set_timing(oasis_plan_t* plan, int enable) {
+  if (!plan) return fail(OASIS_ERR_INVALID_ARG, "oasis_plan_set_timing: null plan");
+  if (enable && plan->ev.empty()) {
+    const int n = 2 * (16 * plan->depth + 16);
+    plan->ev.resize(n);
+    plan->ev_family.assign(n, 0);
+    for (auto& e : plan->ev)
+      if (cudaEventCreate(&e) != cudaSuccess) return fail(OASIS_ERR_CUDA, "cudaEventCreate");
+  }
+  plan->timing = enable != 0;
+  plan->ev_used = 0;
+  for (int i = 0; i < kFamilies; ++i) {
+    plan->fam_ms[i] = 0.0f;
+    plan->fam_launches[i] = 0;
+  }
+  return OASIS_OK;
+}
+
+static void harvest_timing(oasis_plan* p) {
+  if (p->ev_used == 0) return;
+  cudaEventSynchronize(p->ev[p->ev_used - 1]);
+  for (int i = 0; i < p->ev_used; i += 2) {
+    float ms = 0.0f;
+    if (cudaEventElapsedTime(&ms, p->ev[i], p->ev[i + 1]) == cudaSuccess) {
+      p->fam_ms[p->ev_family[i]] += ms;
+      p->fam_launches[p->ev_family[i]] += 1;
+    }
+  }
+  p->ev_used = 0;
+}
+
+extern "C" int oasis_plan_get_timing(oasis_plan_t* plan, float* ms, int* launches, int n) {
+  if (!plan || !ms || !launches) return fail(OASIS_ERR_INVALID_ARG, "oasis_plan_get_timing: null");
+  harvest_timing(plan);
+  for (int i = 0; i < n && i < kFamilies; ++i) {
+    ms[i] = plan->fam_ms[i];
+    launches[i] = plan->fam_launches[i];
+  }
+  return OASIS_OK;
+}

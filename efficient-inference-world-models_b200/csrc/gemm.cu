@@ -1,0 +1,142 @@
+// Host side of the tcgen05 GEMM: tensor maps, instantiation table, launches.
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "gemm.cuh"
+#include "launch.cuh"
+
+namespace oasis {
+
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+
+int get_encoder() {
+  std::call_once(g_encode_once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  });
+  if (!g_encode) return fail(OASIS_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+  return OASIS_OK;
+}
+
+// 2-D bf16 K-major operand [rows][ld], box = 64 (K) x box_rows, 128-byte swizzle.
+int encode_kmajor(CUtensorMap* map, const void* base, long long rows, long long cols, long long ld,
+                  int box_rows) {
+  if (int s = get_encoder()) return s;
+  if (!aligned16(base)) return fail(OASIS_ERR_ALIGNMENT, "GEMM operand base not 16-byte aligned");
+  if ((ld * 2) % 16 != 0) return fail(OASIS_ERR_ALIGNMENT, "GEMM leading dim not a multiple of 8");
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * 2)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(kGemmBK), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims,
+                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(OASIS_ERR_CUDA, "cuTensorMapEncodeTiled failed");
+  return OASIS_OK;
+}
+
+template <int BN, int EPI>
+int launch_one(const GemmOperands& g, const EpiParams& ep, cudaStream_t stream, int max_ctas) {
+  using S = GemmShape<BN>;
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_tcgen05_kernel<BN, EPI>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, S::kSmemBytes);
+    if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(gemm)");
+    configured = true;
+  }
+  const int tiles = ((g.M + kGemmBM - 1) / kGemmBM) * ((g.N + BN - 1) / BN);
+  int grid = num_sms();
+  if (max_ctas > 0 && max_ctas < grid) grid = max_ctas;
+  if (tiles < grid) grid = tiles;
+  gemm_tcgen05_kernel<BN, EPI><<<grid, kGemmThreads, S::kSmemBytes, stream>>>(g.a, g.b, g.M, g.N,
+                                                                              g.K, ep);
+  OASIS_CHECK_LAUNCH("gemm_tcgen05_kernel");
+  return OASIS_OK;
+}
+
+template <int BN>
+int dispatch_epi(const GemmOperands& g, int epi, const EpiParams& ep, cudaStream_t s, int mc) {
+  switch (epi) {
+    case kEpiStoreBF16: return launch_one<BN, kEpiStoreBF16>(g, ep, s, mc);
+    case kEpiStoreF32Bias: return launch_one<BN, kEpiStoreF32Bias>(g, ep, s, mc);
+    case kEpiQkvRope: return launch_one<BN, kEpiQkvRope>(g, ep, s, mc);
+    case kEpiBiasGelu: return launch_one<BN, kEpiBiasGelu>(g, ep, s, mc);
+    case kEpiGateResid: return launch_one<BN, kEpiGateResid>(g, ep, s, mc);
+    case kEpiAdaT: return launch_one<BN, kEpiAdaT>(g, ep, s, mc);
+    case kEpiFinal: return launch_one<BN, kEpiFinal>(g, ep, s, mc);
+  }
+  return fail(OASIS_ERR_INVALID_ARG, "unknown GEMM epilogue");
+}
+
+}  // namespace
+
+int num_sms() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
+
+int make_gemm_operands(GemmOperands* g, const void* A, long long lda, const void* B, long long ldb,
+                       int M, int N, int K, int bn) {
+  if (M <= 0 || N <= 0 || K <= 0) return fail(OASIS_ERR_INVALID_ARG, "GEMM sizes must be positive");
+  if (K % kGemmBK) return fail(OASIS_ERR_UNSUPPORTED, "GEMM K must be a multiple of 64");
+  if (bn != 32 && bn != 64 && bn != 128 && bn != 256)
+    return fail(OASIS_ERR_UNSUPPORTED, "GEMM tile N must be 32, 64, 128 or 256");
+  if (int s = encode_kmajor(&g->a, A, M, K, lda, kGemmBM)) return s;
+  if (int s = encode_kmajor(&g->b, B, N, K, ldb, bn)) return s;
+  g->M = M;
+  g->N = N;
+  g->K = K;
+  g->bn = bn;
+  return OASIS_OK;
+}
+
+int launch_gemm(const GemmOperands& g, int epi, const EpiParams& ep, cudaStream_t stream,
+                int max_ctas) {
+  switch (g.bn) {
+    case 32: return dispatch_epi<32>(g, epi, ep, stream, max_ctas);
+    case 64: return dispatch_epi<64>(g, epi, ep, stream, max_ctas);
+    case 128: return dispatch_epi<128>(g, epi, ep, stream, max_ctas);
+    case 256: return dispatch_epi<256>(g, epi, ep, stream, max_ctas);
+  }
+  return fail(OASIS_ERR_UNSUPPORTED, "GEMM tile N");
+}
+
+}  // namespace oasis
+
+// ------------------------------------------------------------------ C ABI
+extern "C" int oasis_gemm_bf16(const void* A, const void* B, void* D, const float* bias, int M,
+                               int N, int K, int lda, int ldb, int ldd, int epilogue,
+                               cudaStream_t stream) {
+  using namespace oasis;
+  if (!A || !B || !D) return fail(OASIS_ERR_INVALID_ARG, "oasis_gemm_bf16: null pointer");
+  if (epilogue != 0 && epilogue != 1)
+    return fail(OASIS_ERR_INVALID_ARG, "oasis_gemm_bf16: epilogue must be 0 or 1");
+  if (N % 32) return fail(OASIS_ERR_UNSUPPORTED, "oasis_gemm_bf16: N must be a multiple of 32");
+  if (!aligned16(D) || (epilogue == 0 ? (ldd % 8) : (ldd % 4)))
+    return fail(OASIS_ERR_ALIGNMENT, "oasis_gemm_bf16: D must be 16-byte aligned rows");
+  int bn = 256;
+  while (bn > 32 && (N % bn)) bn >>= 1;
+  GemmOperands g;
+  if (int s = make_gemm_operands(&g, A, lda, B, ldb, M, N, K, bn)) return s;
+  EpiParams ep{};
+  ep.out = D;
+  ep.ldd = ldd;
+  ep.bias = bias;
+  return launch_gemm(g, epilogue == 0 ? kEpiStoreBF16 : kEpiStoreF32Bias, ep, stream);
+}

@@ -1,0 +1,41 @@
+// Internal launcher interface shared by the translation units of the library.
+#pragma once
+
+#include "common.cuh"
+
+namespace oasis {
+
+// By-value view of a KV cache handed to the temporal attention kernel.
+struct KvView {
+  int layers, n_bf16, n_fp8, n_int4;
+  uint8_t kind[OASIS_MAX_FRAMES];
+  uint8_t index[OASIS_MAX_FRAMES];
+  const __nv_bfloat16* k_bf16; const __nv_bfloat16* v_bf16;
+  const uint8_t* k_fp8; const uint8_t* v_fp8;
+  const __nv_bfloat16* k_fp8_scale; const __nv_bfloat16* v_fp8_scale;
+  const uint8_t* k_int4; const uint8_t* v_int4;
+  const __half* k_i4_scale; const __half* k_i4_zero;
+  const __half* v_i4_scale; const __half* v_i4_zero;
+};
+
+int make_kv_view(const oasis_kv_cache_t* c, KvView* v);
+int validate_slots(const oasis_kv_cache_t* c, int slot0, int frames);
+
+int launch_attn_spatial(const void* qkv, void* out, int frames, cudaStream_t stream);
+int launch_attn_temporal(const void* qkv, const KvView& kv, int layer, void* out, int batch,
+                         int q_frames, int q_pos0, int n_past, int n_kv, cudaStream_t stream);
+// Store frames [0, frames) of each session (session rows strided by src_frames frames)
+// into cache slots slot0.. of one layer.
+int launch_kv_store(const void* kv, long long ld, int k_col, int v_col, const oasis_kv_cache_t* c,
+                    int layer, int batch, int frames, int src_frames, int slot0,
+                    cudaStream_t stream);
+
+int launch_ln_modulate(const float* x, const float* shift, const float* scale, long long mod_ld,
+                       void* out, int M, int rows_per_frame, cudaStream_t stream);
+int launch_linear_f32(const float* in, int ldi, const float* W, const float* b, float* out, int ldo,
+                      int M, int N, int K, int act, bool accum, cudaStream_t stream);
+int launch_temb_sinusoid(const int64_t* t, float* emb, int F, cudaStream_t stream);
+int launch_silu_bf16(const float* c, void* out, int n, cudaStream_t stream);
+int launch_patch_im2col(const float* x, float* cols, int F, cudaStream_t stream);
+
+}  // namespace oasis

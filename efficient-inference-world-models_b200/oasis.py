@@ -1,0 +1,158 @@
+"""Oasis autoregressive samplers on the B200 DiT (mirrors ``worldserve/models/oasis.py``
+and the DPM-Solver++ 2M loop of ``benchmarks/optimised/oasis_dpmpp_modal.py``).
+
+Semantics kept from the reference:
+* sigmoid beta schedule over 1000 steps; ``noise_range = linspace(-1, 999, steps+1)``
+  (``models/oasis.py:88-110``);
+* DDIM-v update of the new frame only, past frames at t=0 (``models/oasis.py:174-235``);
+* DPM++ 2M: context frames at ``stabilization_level - 1``, sliding window of
+  ``max_frames`` (32), new chunk ~ N(0, 1) clamped to +-20, eps_prev reset per frame,
+  only ``x[:, -1:]`` written back (``oasis_dpmpp_modal.py:118-164``).
+
+``rollout_dpmpp(..., use_cache=True)`` runs the first solver step of each frame as a
+full-window forward that also stores the window's temporal K/V, and the remaining steps
+as incremental forwards of the new frame against that cache (the reference's
+persistent past-frame reuse, ``kv_cache/oasis_temporal_persistent_wrapper.py``).
+The VAE decode (``models/oasis.py:237-245``) is outside this library.
+"""
+
+from __future__ import annotations
+
+from typing import Any, Dict, Optional
+
+import torch
+
+from .kv_cache import KVCacheB200
+from . import _native as N
+from .samplers import FRAME_ELEMS, _stream_ptr, ddim_update
+
+LATENT_C, LATENT_H, LATENT_W = 16, 18, 32
+ACTION_DIM = 25
+DDPM_T = 1000
+DEFAULT_DDIM_STEPS = 10
+N_PROMPT = 1
+VAE_SCALE = 0.07843137255
+
+
+def sigmoid_beta_schedule(timesteps: int = DDPM_T, start: float = -3.0, end: float = 3.0,
+                          tau: float = 1.0) -> torch.Tensor:
+    """Sigmoid schedule (Jabri et al. 2022, arXiv:2212.11972), float64, clipped to [0, 0.999]."""
+    t = torch.linspace(0, timesteps, timesteps + 1, dtype=torch.float64) / timesteps
+    v_start = torch.tensor(start / tau, dtype=torch.float64).sigmoid()
+    v_end = torch.tensor(end / tau, dtype=torch.float64).sigmoid()
+    ac = (-((t * (end - start) + start) / tau).sigmoid() + v_end) / (v_end - v_start)
+    ac = ac / ac[0]
+    return torch.clip(1 - ac[1:] / ac[:-1], 0, 0.999)
+
+
+def alphas_cumprod(timesteps: int = DDPM_T) -> torch.Tensor:
+    betas = sigmoid_beta_schedule(timesteps).float()
+    return torch.cumprod(1.0 - betas, dim=0)
+
+
+def _build_schedule(ddim_steps: int, alpha_bar_override: Optional[torch.Tensor] = None):
+    ab = alpha_bar_override.float().cpu() if alpha_bar_override is not None else alphas_cumprod()
+    noise_range = torch.linspace(-1, DDPM_T - 1, ddim_steps + 1)
+    return ab, noise_range
+
+
+@torch.no_grad()
+def generate(model: Dict[str, Any], num_frames: int = 16, num_steps: int = DEFAULT_DDIM_STEPS,
+             n_prompt: int = N_PROMPT, seed: int = 42, optimizations: Any = None) -> Dict[str, Any]:
+    """DDIM-v autoregressive generation with ``model["dit"]`` (an ``OasisDiTB200``).
+
+    Returns the latents (B, n_prompt + num_frames, 16, 18, 32); frames are decoded only
+    if ``model`` carries a ``vae`` with ``decode``."""
+    dit = model["dit"]
+    device = model.get("device", "cuda")
+    gen = torch.Generator(device=device).manual_seed(seed)
+    B = 1
+    total = n_prompt + num_frames
+    ab, nr = _build_schedule(num_steps, model.get("alpha_bar_override"))
+    x = torch.randn(B, n_prompt, LATENT_C, LATENT_H, LATENT_W, device=device, generator=gen)
+    actions = torch.zeros(B, total, ACTION_DIM, device=device)
+    step = 0
+    for frame_i in range(n_prompt, total):
+        chunk = torch.randn(B, 1, LATENT_C, LATENT_H, LATENT_W, device=device, generator=gen)
+        x = torch.cat([x, chunk], dim=1)
+        for noise_idx in reversed(range(1, num_steps + 1)):
+            t_val = int(nr[noise_idx].long().clamp(0, DDPM_T - 1))
+            t_in = torch.zeros(B, frame_i + 1, dtype=torch.long, device=device)
+            t_in[:, -1] = t_val
+            if optimizations is not None and optimizations.pre_step(step, num_frames * num_steps, x[:, -1:]):
+                step += 1
+                continue
+            v = dit(x[:, -dit.max_frames:] if x.shape[1] > dit.max_frames else x,
+                    t_in[:, -dit.max_frames:], actions[:, max(0, frame_i + 1 - dit.max_frames): frame_i + 1])
+            t_prev = max(int(nr[noise_idx - 1]), 0)
+            ddim_update(x, v, float(ab[t_val]), float(ab[t_prev]))
+            if optimizations is not None:
+                optimizations.post_step(step, num_frames * num_steps, x[:, -1:])
+            step += 1
+    out = {"latents": x, "num_frames": num_frames, "num_steps": num_steps, "n_prompt": n_prompt,
+           "total_dit_fwd_passes": num_frames * num_steps}
+    vae = model.get("vae")
+    if vae is not None and hasattr(vae, "decode"):
+        Bx, Tx = x.shape[:2]
+        z = (x / VAE_SCALE).reshape(Bx * Tx, LATENT_C, LATENT_H * LATENT_W).permute(0, 2, 1)
+        out["frames"] = vae.decode(z)
+    return out
+
+
+@torch.no_grad()
+def rollout_dpmpp(dit, prompt_latent: torch.Tensor, actions: torch.Tensor, num_frames: int,
+                  solver_steps: int = 5, stabilization_level: int = 15, noise_abs_max: float = 20.0,
+                  seed: int = 42, use_cache: bool = False, kv_kinds=None,
+                  alpha_bar: Optional[torch.Tensor] = None, step_callback=None) -> torch.Tensor:
+    """DPM-Solver++ 2M rollout of ``num_frames`` new frames for B sessions.
+
+    prompt_latent (B, n_prompt, 16, 18, 32) on the device; actions (B, n_prompt +
+    num_frames, 25).  Returns all latents (B, n_prompt + num_frames, 16, 18, 32)."""
+    device = prompt_latent.device
+    ab = (alpha_bar if alpha_bar is not None else alphas_cumprod()).float().cpu()
+    nr = torch.linspace(-1, DDPM_T - 1, solver_steps + 1)
+    max_frames = dit.max_frames
+    B, n_prompt = prompt_latent.shape[:2]
+    total = n_prompt + num_frames
+    gen = torch.Generator(device=device).manual_seed(seed)
+    x = torch.empty(B, total, LATENT_C, LATENT_H, LATENT_W, device=device)
+    x[:, :n_prompt] = prompt_latent
+    eps_prev = torch.empty(B, LATENT_C * LATENT_H * LATENT_W, device=device)
+    cache = None
+    for i in range(n_prompt, total):
+        chunk = torch.randn((B, LATENT_C, LATENT_H, LATENT_W), device=device, generator=gen)
+        x[:, i] = chunk.clamp(-noise_abs_max, noise_abs_max)
+        start = max(0, i + 1 - max_frames)
+        T = i + 1 - start
+        window = x[:, start: i + 1]
+        act = actions[:, start: i + 1].contiguous()
+        t_win = torch.full((B, T), stabilization_level - 1, dtype=torch.long, device=device)
+        if use_cache and T > 1 and (cache is None or cache.n_slots != T - 1):
+            kinds = kv_kinds(T - 1) if kv_kinds is not None else ["bf16"] * (T - 1)
+            cache = KVCacheB200(B, dit.depth, kinds, device=device)
+        for k, noise_idx in enumerate(reversed(range(1, solver_steps + 1))):
+            t = int(nr[noise_idx])
+            tn = int(nr[noise_idx - 1])
+            tn = t if tn < 0 else tn
+            ab_t = float(ab[t])
+            ab_next = 1.0 if noise_idx == 1 else float(ab[tn])
+            t_win[:, -1] = t
+            if use_cache and T > 1 and k > 0:
+                v = dit.forward_cached(x[:, i], t_win[:, -1], act[:, -1], cache, n_past=T - 1)
+            else:
+                v = dit(window.contiguous(), t_win, act,
+                        kv_cache=cache if (use_cache and T > 1) else None)
+            _update_newest(x, i, v, eps_prev, ab_t, ab_next, k == 0)
+            if step_callback is not None:
+                step_callback(i, k)
+    return x
+
+
+def _update_newest(x, i, v, eps_prev, ab_t, ab_next, first):
+    """DPM++ 2M update of frame ``i`` of x in place (v: newest-frame prediction)."""
+    B, total = x.shape[:2]
+    vl = v[:, -1] if v.dim() == 5 else v
+    v_stride = (v.shape[1] if v.dim() == 5 else 1) * FRAME_ELEMS
+    N.call("oasis_dpmpp2m_update", x[:, i].data_ptr(), vl.data_ptr(), eps_prev.data_ptr(), B,
+           FRAME_ELEMS, total * FRAME_ELEMS, v_stride, float(ab_t), float(ab_next), int(first),
+           _stream_ptr())

@@ -32,10 +32,12 @@ def sigmoid_beta_schedule(timesteps: int = 1000, start: float = -3.0, end: float
 
 
 def alphas_cumprod(timesteps: int = 1000) -> np.ndarray:
-    """fp32 cumulative product of (1 - beta) as the reference computes it
-    (``betas.float()`` then ``torch.cumprod`` in fp32)."""
+    """Cumulative product of (1 - beta) as the reference computes it: ``betas.float()``,
+    ``1 - betas`` in fp32, then ``torch.cumprod`` (whose CPU kernel accumulates in
+    float64 and rounds each output to fp32)."""
     betas = sigmoid_beta_schedule(timesteps).astype(np.float32)
-    return np.cumprod(np.float32(1.0) - betas, dtype=np.float32)
+    alphas = (np.float32(1.0) - betas).astype(np.float32)
+    return np.cumprod(alphas.astype(np.float64)).astype(np.float32)
 
 
 def ddim_vpred_step(x, v, ab_t, ab_prev):

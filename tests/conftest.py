@@ -1,10 +1,29 @@
+import importlib
 import os
 import sys
+
+import pytest
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
+PKG_NAME = "efficient-inference-world-models_b200"
+
 
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA device (B200, sm_100a)")
+
+
+@pytest.fixture(scope="session")
+def pkg():
+    return importlib.import_module(PKG_NAME)
+
+
+@pytest.fixture(scope="session")
+def cuda(pkg):
+    import torch
+    if not torch.cuda.is_available():
+        pytest.fail("GPU test collected on a machine without CUDA")
+    pkg.lib()
+    return torch.device("cuda:0")

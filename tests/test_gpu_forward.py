@@ -1,0 +1,164 @@
+"""GPU parity of the whole Oasis DiT forward (through the C ABI) against the CPU oracle.
+
+Bar: rel-L2 <= 1e-2 on the predicted v for bf16 (fp32 oracle on the same seeded
+random-init weights and inputs).  The cached incremental forward must equal the
+newest frame of the full forward when the cache is bf16, and stay within the same
+bar against the oracle's quantise->dequantise round trip when it is FP8/INT4."""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import quant_ref
+from oracle.dit_ref import build_oracle
+
+pytestmark = pytest.mark.gpu
+
+_SD_CACHE = {}
+
+
+def state(pkg, depth, seed=0):
+    key = (depth, seed)
+    if key not in _SD_CACHE:
+        _SD_CACHE[key] = pkg.random_state_dict(seed=seed, depth=depth)
+    return _SD_CACHE[key]
+
+
+def inputs(B, T, seed=0):
+    """Config-0 style inputs: N(0,1) latents, t ~ U{0..999}, 23 Bernoulli(0.1) keys + 2
+    camera floats N(0, 0.3)."""
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(B, T, 16, 18, 32, generator=g)
+    t = torch.randint(0, 1000, (B, T), generator=g)
+    a = torch.zeros(B, T, 25)
+    a[..., :23] = (torch.rand(B, T, 23, generator=g) < 0.1).float()
+    a[..., 23:] = torch.randn(B, T, 2, generator=g) * 0.3
+    return x, t, a
+
+
+def rel_l2(a, b):
+    a, b = a.double().cpu(), b.double().cpu()
+    return ((a - b).norm() / b.norm()).item()
+
+
+@pytest.mark.parametrize("depth,B,T", [(16, 1, 4), (2, 2, 3), (2, 1, 32), (1, 3, 1)])
+def test_forward_matches_oracle(pkg, cuda, depth, B, T):
+    sd = state(pkg, depth)
+    model = pkg.OasisDiTB200.from_state_dict(sd, device=cuda, depth=depth)
+    x, t, a = inputs(B, T, seed=depth * 10 + T)
+    v = model(x.to(cuda), t.to(cuda), a.to(cuda))
+    ref = build_oracle(sd, depth=depth)
+    with torch.no_grad():
+        v_ref = ref(x, t, a)
+    err = rel_l2(v, v_ref)
+    assert torch.isfinite(v).all()
+    assert err <= 1e-2, err
+
+
+def test_forward_host_tensors_and_no_actions(pkg, cuda):
+    depth = 1
+    sd = state(pkg, depth)
+    model = pkg.OasisDiTB200.from_state_dict(sd, device=cuda, depth=depth)
+    x, t, _ = inputs(1, 2, seed=3)
+    v = model(x, t)  # host in, host out, external_cond None
+    assert v.device.type == "cpu"
+    with torch.no_grad():
+        v_ref = build_oracle(sd, depth=depth)(x, t, None)
+    assert rel_l2(v, v_ref) <= 1e-2
+
+
+def test_forward_is_deterministic(pkg, cuda):
+    model = pkg.OasisDiTB200.from_state_dict(state(pkg, 2), device=cuda, depth=2)
+    x, t, a = (z.to(cuda) for z in inputs(2, 5, seed=9))
+    v1 = model(x, t, a).clone()
+    v2 = model(x, t, a)
+    assert torch.equal(v1, v2)
+
+
+def test_cached_forward_equals_full_forward_bf16(pkg, cuda):
+    """Persistent past-frame reuse is exact (oasis_persistent_kv_theory.py:24-112)."""
+    depth, B, T = 2, 2, 6
+    model = pkg.OasisDiTB200.from_state_dict(state(pkg, depth), device=cuda, depth=depth)
+    x, t, a = (z.to(cuda) for z in inputs(B, T, seed=21))
+    cache = pkg.KVCacheB200.uniform(B, depth, T - 1, "bf16", device=cuda)
+    model(x, t, a, kv_cache=cache)  # prefill writes frames 0..T-2
+    # a later solver step: only the newest frame's latent and timestep change
+    x2, t2 = x.clone(), t.clone()
+    x2[:, -1] = torch.randn(B, 16, 18, 32, device=cuda)
+    t2[:, -1] = 123
+    v_full = model(x2, t2, a)[:, -1]
+    v_inc = model.forward_cached(x2[:, -1], t2[:, -1], a[:, -1], cache, n_past=T - 1)
+    torch.cuda.synchronize()
+    assert rel_l2(v_inc, v_full) < 1e-5
+
+
+def _oracle_incremental(sd, depth, x, t, a, kinds, x_new, t_new):
+    """Oracle: prefill on the window, round-trip past K/V through the reference
+    quantiser at the cache granularity, then the newest frame's forward."""
+    ref = build_oracle(sd, depth=depth)
+    B, T = x.shape[:2]
+    P = T - 1
+    with torch.no_grad():
+        _, kvs = ref.forward_capture_kv(x, t, a)
+        past = []
+        for k, v in kvs:  # (B*144, 16, T, 64) post-RoPE, fp32
+            kv = []
+            for z in (k, v):
+                z = z[:, :, :P].reshape(B, 144, 16, P, 64).permute(0, 3, 1, 2, 4)  # (B,P,144,16,64)
+                zb = quant_ref.bf16_round(z.numpy().astype(np.float32))
+                out = zb.copy()
+                for s, kind in enumerate(kinds):
+                    for b in range(B):
+                        for h in range(16):
+                            sl = zb[b, s, :, h]  # (144, 64)
+                            if kind == "fp8":
+                                c, sc = quant_ref.quantize_to_fp8_bf16(sl)
+                                out[b, s, :, h] = quant_ref.dequantize_fp8_bf16(c, sc)
+                            elif kind == "int4":
+                                p, s16, z16, _, _ = quant_ref.quantize_int4_rows(sl)
+                                q = quant_ref.unpack_int4(p.reshape(-1)).reshape(144, 64).astype(np.float32)
+                                out[b, s, :, h] = q * s16.astype(np.float32)[:, None] + z16.astype(np.float32)[:, None]
+                kv.append(torch.from_numpy(out).permute(0, 2, 3, 1, 4).reshape(B * 144, 16, P, 64))
+            past.append(tuple(kv))
+        return ref.forward_incremental(x_new[:, None], t_new[:, None], a[:, -1:], past, pos=P)[:, 0]
+
+
+@pytest.mark.parametrize("kinds", [["fp8"] * 5, ["int4"] * 3 + ["bf16"] * 2])
+def test_cached_forward_quantized_matches_oracle(pkg, cuda, kinds):
+    depth, B, T = 2, 2, 6
+    sd = state(pkg, depth)
+    model = pkg.OasisDiTB200.from_state_dict(sd, device=cuda, depth=depth)
+    x, t, a = inputs(B, T, seed=31)
+    cache = pkg.KVCacheB200(B, depth, kinds, device=cuda)
+    model(x.to(cuda), t.to(cuda), a.to(cuda), kv_cache=cache)
+    g = torch.Generator().manual_seed(5)
+    x_new = torch.randn(B, 16, 18, 32, generator=g)
+    t_new = torch.full((B,), 399)
+    v_inc = model.forward_cached(x_new.to(cuda), t_new.to(cuda), a[:, -1].to(cuda), cache, n_past=T - 1)
+    x_o = x.clone()
+    x_o[:, -1] = x_new
+    t_o = t.clone()
+    t_o[:, -1] = t_new
+    want = _oracle_incremental(sd, depth, x_o, t_o, a, kinds, x_new, t_new)
+    assert rel_l2(v_inc, want) <= 1e-2
+
+
+def test_dpmpp_rollout_cached_matches_uncached(pkg, cuda):
+    depth, B = 2, 1
+    model = pkg.OasisDiTB200.from_state_dict(state(pkg, depth), device=cuda, depth=depth)
+    g = torch.Generator().manual_seed(2)
+    prompt = torch.randn(B, 1, 16, 18, 32, generator=g).to(cuda)
+    acts = torch.zeros(B, 5, 25, device=cuda)
+    xa = pkg.rollout_dpmpp(model, prompt, acts, num_frames=4, solver_steps=3, use_cache=False, seed=1)
+    xb = pkg.rollout_dpmpp(model, prompt, acts, num_frames=4, solver_steps=3, use_cache=True, seed=1)
+    torch.cuda.synchronize()
+    assert torch.isfinite(xa).all()
+    assert rel_l2(xb, xa) < 1e-4
+
+
+def test_generate_ddim_runs(pkg, cuda):
+    model = pkg.OasisDiTB200.from_state_dict(state(pkg, 1), device=cuda, depth=1)
+    out = pkg.generate({"dit": model, "device": cuda}, num_frames=2, num_steps=3)
+    assert out["latents"].shape == (1, 3, 16, 18, 32)
+    assert torch.isfinite(out["latents"]).all()
+    pkg._native.check(pkg.lib().oasis_check_device_error())

@@ -1,0 +1,108 @@
+"""CPU-only checks of the host side: the C ABI library loads and exports every symbol
+the header declares, argument validation fails cleanly, and the host-computed
+constants (RoPE tables, schedule, parameter layout) agree with the oracle."""
+
+import ctypes
+import math
+import os
+import re
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import sampler_ref
+from oracle.dit_ref import DiT, RotaryEmbedding
+
+HEADER = os.path.join(os.path.dirname(os.path.dirname(__file__)), "include", "oasis_b200.h")
+
+
+def header_functions():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(oasis_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_library_exports_every_header_symbol(pkg):
+    L = pkg.lib()
+    names = header_functions()
+    assert len(names) >= 15
+    for n in names:
+        assert hasattr(L, n), f"{n} declared in oasis_b200.h but not exported"
+    # the ctypes signature table covers the same set
+    assert sorted(pkg._native.SIGNATURES) == names
+
+
+def test_version_and_no_error(pkg):
+    assert "sm_100a" in pkg.version()
+    assert pkg.lib().oasis_last_error() == b""
+
+
+def test_invalid_arguments_are_reported_not_fatal(pkg):
+    L = pkg.lib()
+    h = ctypes.c_void_p()
+    st = L.oasis_plan_create(None, 1, 4, None, 0, ctypes.byref(h))
+    assert st == 1 and b"null" in L.oasis_last_error()
+    w = pkg._native.DiTWeights()
+    w.depth = 16
+    st = L.oasis_plan_create(ctypes.byref(w), 1, 33, None, 0, ctypes.byref(h))
+    assert st == 1 and b"frames" in L.oasis_last_error()
+    st = L.oasis_plan_create(ctypes.byref(w), 1, 4, None, 0, ctypes.byref(h))
+    assert st == 3  # workspace missing
+    with pytest.raises(pkg.OasisError):
+        pkg._native.check(st)
+    st = L.oasis_attn_temporal(ctypes.c_void_p(16), None, 0, ctypes.c_void_p(16), 1, 4, 0, 2, 6, None)
+    assert st == 1  # n_past > 0 without a cache
+    st = L.oasis_dpmpp2m_update(ctypes.c_void_p(16), ctypes.c_void_p(16), None, 1, 8, 8, 8,
+                                0.5, 0.5, 0, None)
+    assert st == 1  # multistep without eps_prev
+
+
+def test_workspace_size_formula(pkg):
+    L = pkg.lib()
+    ws = L.oasis_plan_workspace_size(1, 32, 16)
+    M = 32 * 144
+    act = M * 1024 * 4 + M * 1024 * 2 + M * 3072 * 2 + M * 1024 * 2 + M * 4096 * 2 + M * 64 * 4
+    mod = 32 * (32 * 6144 + 2048) * 4
+    assert act + mod <= ws <= act + mod + 2 * 1024 * 1024
+    assert L.oasis_plan_workspace_size(0, 32, 16) == 0
+
+
+def test_rope_tables_match_oracle_rotary(pkg):
+    sp, tp = pkg.rope_tables()
+    # spatial: oracle axial frequencies (9, 16, 64) interleaved -> pairs
+    rot = RotaryEmbedding(32, freqs_for="pixel", max_freq=256)
+    ang = rot.get_axial_freqs(9, 16).reshape(144, 64)[:, 0::2]
+    np.testing.assert_array_equal(sp[..., 0].numpy(), ang.cos().numpy())
+    np.testing.assert_array_equal(sp[..., 1].numpy(), ang.sin().numpy())
+    rt = RotaryEmbedding(64)
+    pos = torch.arange(32).float()
+    ang_t = RotaryEmbedding._angles(pos, rt.freqs)[:, 0::2]
+    np.testing.assert_array_equal(tp[..., 0].numpy(), ang_t.cos().numpy())
+    np.testing.assert_array_equal(tp[..., 1].numpy(), ang_t.sin().numpy())
+
+
+def test_state_dict_loads_into_oracle(pkg):
+    sd = pkg.random_state_dict(seed=1, depth=2)
+    m = DiT(depth=2)
+    missing, unexpected = m.load_state_dict(sd, strict=False)
+    assert not unexpected
+    assert all(k.endswith("rotary_emb.freqs") for k in missing)
+    full = sum(math.prod(s) for s in pkg.param_shapes(16).values())
+    assert 600e6 < full < 615e6  # Oasis-500M: ~608M parameters
+
+
+def test_schedule_matches_oracle(pkg):
+    # float64 schedule: the two restatements differ only in how sigmoid is evaluated
+    np.testing.assert_allclose(pkg.sigmoid_beta_schedule(1000).numpy(),
+                               sampler_ref.sigmoid_beta_schedule(1000), rtol=1e-12, atol=0)
+    np.testing.assert_array_equal(pkg.alphas_cumprod().numpy(), sampler_ref.alphas_cumprod(1000))
+
+
+def test_progressive_policy_matches_reference_thresholds(pkg):
+    q = pkg.ProgressiveKVQuantizerB200(fp8_age_threshold=3, int4_age_threshold=10,
+                                       key_value_asymmetry=True)
+    assert (q.v_fp8_age, q.v_int4_age) == (2, 7)  # int(0.7 * threshold), progressive_quant.py:93-95
+    kinds = q.slot_kinds(12)  # slot s holds a frame of age 12 - s
+    assert kinds[-1] == "bf16" and kinds[-2] == "fp8" and kinds[0] == "int4"
+    assert kinds.count("int4") == 6  # ages 12..7 (V reaches INT4 at 7)
