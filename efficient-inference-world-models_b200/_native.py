@@ -44,7 +44,6 @@ class DiTWeights(Structure):
                 ("patch_w", c_void_p), ("patch_b", c_void_p),
                 ("t_fc1_w", c_void_p), ("t_fc1_b", c_void_p),
                 ("t_fc2_w", c_void_p), ("t_fc2_b", c_void_p),
-                ("act_w", c_void_p), ("act_b", c_void_p),
                 ("ada_w", c_void_p), ("ada_b", c_void_p),
                 ("final_w", c_void_p), ("final_b", c_void_p),
                 ("sub", SubWeights * (2 * MAX_DEPTH)),

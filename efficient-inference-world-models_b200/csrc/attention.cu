@@ -19,7 +19,7 @@ constexpr int kSmemStride = 72;           // bf16 per staged row (64 + 8 pad: co
 constexpr int kSpThreads = 288;
 constexpr int kSpSmem = 3 * OASIS_TOKENS * kSmemStride * 2;  // 62,208 B
 
-__global__ void __launch_bounds__(kSpThreads)
+__global__ void __launch_bounds__(kSpThreads, 2)
     attn_spatial_kernel(const __nv_bfloat16* __restrict__ qkv, __nv_bfloat16* __restrict__ out,
                         float scale_log2) {
   extern __shared__ __align__(16) uint8_t sm_sp[];
@@ -50,70 +50,85 @@ __global__ void __launch_bounds__(kSpThreads)
     ldsm_x4(smem_u32(sQ + (r0 + (lane & 15)) * kSmemStride + kk * 16 + (lane >> 4) * 8), qa[kk][0],
             qa[kk][1], qa[kk][2], qa[kk][3]);
 
-  float s[18][4];
-#pragma unroll
-  for (int j = 0; j < 18; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.0f;
-#pragma unroll
-  for (int jp = 0; jp < 9; ++jp) {
-#pragma unroll
-    for (int kk = 0; kk < 4; ++kk) {
-      uint32_t b0, b1, b2, b3;
-      const int key = jp * 16 + (lane & 7) + ((lane >> 4) << 3);
-      const int col = kk * 16 + ((lane >> 3) & 1) * 8;
-      ldsm_x4(smem_u32(sK + key * kSmemStride + col), b0, b1, b2, b3);
-      mma_bf16_16816(s[2 * jp], qa[kk], b0, b1);
-      mma_bf16_16816(s[2 * jp + 1], qa[kk], b2, b3);
-    }
-  }
-
-  float mx0 = -INFINITY, mx1 = -INFINITY;
-#pragma unroll
-  for (int j = 0; j < 18; ++j) {
-    mx0 = fmaxf(mx0, fmaxf(s[j][0], s[j][1]));
-    mx1 = fmaxf(mx1, fmaxf(s[j][2], s[j][3]));
-  }
-  mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
-  mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
-  mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
-  mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
-  const float o0 = mx0 * scale_log2, o1 = mx1 * scale_log2;
-  float sum0 = 0.0f, sum1 = 0.0f;
-#pragma unroll
-  for (int j = 0; j < 18; ++j) {
-    s[j][0] = exp2f(s[j][0] * scale_log2 - o0);
-    s[j][1] = exp2f(s[j][1] * scale_log2 - o0);
-    s[j][2] = exp2f(s[j][2] * scale_log2 - o1);
-    s[j][3] = exp2f(s[j][3] * scale_log2 - o1);
-    sum0 += s[j][0] + s[j][1];
-    sum1 += s[j][2] + s[j][3];
-  }
-  sum0 += __shfl_xor_sync(0xffffffffu, sum0, 1);
-  sum0 += __shfl_xor_sync(0xffffffffu, sum0, 2);
-  sum1 += __shfl_xor_sync(0xffffffffu, sum1, 1);
-  sum1 += __shfl_xor_sync(0xffffffffu, sum1, 2);
-
+  // online softmax over 3 key blocks of 48 (keeps ~100 registers -> 2 CTAs per SM)
   float o[8][4];
 #pragma unroll
   for (int j = 0; j < 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.0f;
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
+#pragma unroll 1
+  for (int kb = 0; kb < 3; ++kb) {
+    float s[6][4];
 #pragma unroll
-  for (int kk = 0; kk < 9; ++kk) {
-    uint32_t pa[4];
-    pa[0] = pack_bf16x2(s[2 * kk][0], s[2 * kk][1]);
-    pa[1] = pack_bf16x2(s[2 * kk][2], s[2 * kk][3]);
-    pa[2] = pack_bf16x2(s[2 * kk + 1][0], s[2 * kk + 1][1]);
-    pa[3] = pack_bf16x2(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+    for (int j = 0; j < 6; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.0f;
 #pragma unroll
-    for (int jd = 0; jd < 8; jd += 2) {
-      uint32_t b0, b1, b2, b3;
-      const int key = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
-      const int col = jd * 8 + (lane >> 4) * 8;
-      ldsm_x4_t(smem_u32(sV + key * kSmemStride + col), b0, b1, b2, b3);
-      mma_bf16_16816(o[jd], pa, b0, b1);
-      mma_bf16_16816(o[jd + 1], pa, b2, b3);
+    for (int jp = 0; jp < 3; ++jp) {
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        uint32_t b0, b1, b2, b3;
+        const int key = kb * 48 + jp * 16 + (lane & 7) + ((lane >> 4) << 3);
+        const int col = kk * 16 + ((lane >> 3) & 1) * 8;
+        ldsm_x4(smem_u32(sK + key * kSmemStride + col), b0, b1, b2, b3);
+        mma_bf16_16816(s[2 * jp], qa[kk], b0, b1);
+        mma_bf16_16816(s[2 * jp + 1], qa[kk], b2, b3);
+      }
+    }
+    float bm0 = m0, bm1 = m1;
+#pragma unroll
+    for (int j = 0; j < 6; ++j) {
+      bm0 = fmaxf(bm0, fmaxf(s[j][0], s[j][1]));
+      bm1 = fmaxf(bm1, fmaxf(s[j][2], s[j][3]));
+    }
+    bm0 = fmaxf(bm0, __shfl_xor_sync(0xffffffffu, bm0, 1));
+    bm0 = fmaxf(bm0, __shfl_xor_sync(0xffffffffu, bm0, 2));
+    bm1 = fmaxf(bm1, __shfl_xor_sync(0xffffffffu, bm1, 1));
+    bm1 = fmaxf(bm1, __shfl_xor_sync(0xffffffffu, bm1, 2));
+    const float alpha0 = exp2f((m0 - bm0) * scale_log2), alpha1 = exp2f((m1 - bm1) * scale_log2);
+    m0 = bm0;
+    m1 = bm1;
+    const float o0 = m0 * scale_log2, o1 = m1 * scale_log2;
+    float sum0 = 0.0f, sum1 = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 6; ++j) {
+      s[j][0] = exp2f(s[j][0] * scale_log2 - o0);
+      s[j][1] = exp2f(s[j][1] * scale_log2 - o0);
+      s[j][2] = exp2f(s[j][2] * scale_log2 - o1);
+      s[j][3] = exp2f(s[j][3] * scale_log2 - o1);
+      sum0 += s[j][0] + s[j][1];
+      sum1 += s[j][2] + s[j][3];
+    }
+    l0 = l0 * alpha0 + sum0;
+    l1 = l1 * alpha1 + sum1;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      o[j][0] *= alpha0;
+      o[j][1] *= alpha0;
+      o[j][2] *= alpha1;
+      o[j][3] *= alpha1;
+    }
+#pragma unroll
+    for (int kk = 0; kk < 3; ++kk) {
+      uint32_t pa[4];
+      pa[0] = pack_bf16x2(s[2 * kk][0], s[2 * kk][1]);
+      pa[1] = pack_bf16x2(s[2 * kk][2], s[2 * kk][3]);
+      pa[2] = pack_bf16x2(s[2 * kk + 1][0], s[2 * kk + 1][1]);
+      pa[3] = pack_bf16x2(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+#pragma unroll
+      for (int jd = 0; jd < 8; jd += 2) {
+        uint32_t b0, b1, b2, b3;
+        const int key = kb * 48 + kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+        const int col = jd * 8 + (lane >> 4) * 8;
+        ldsm_x4_t(smem_u32(sV + key * kSmemStride + col), b0, b1, b2, b3);
+        mma_bf16_16816(o[jd], pa, b0, b1);
+        mma_bf16_16816(o[jd + 1], pa, b2, b3);
+      }
     }
   }
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
 
-  const float inv0 = 1.0f / sum0, inv1 = 1.0f / sum1;
+  const float inv0 = 1.0f / l0, inv1 = 1.0f / l1;
   const int g = lane >> 2, c = lane & 3;
   __nv_bfloat16* orow0 = out + (static_cast<long long>(f) * OASIS_TOKENS + r0 + g) * OASIS_HIDDEN + h * 64;
   __nv_bfloat16* orow1 = orow0 + 8 * OASIS_HIDDEN;
@@ -134,61 +149,24 @@ constexpr int kTpRowsPerMat = 32;
 constexpr int kTpWarpSmem = 3 * kTpRowsPerMat * kSmemStride;  // bf16 elements
 constexpr int kTpSmem = kTpWarps * kTpWarpSmem * 2;             // 55,296 B
 
-// Stage one 64-wide K or V row of cache slot `s` into shared memory as bf16.
-__device__ __forceinline__ void stage_cache_row(const KvView& kv, bool is_v, int b, int layer,
-                                                int s, int p, int h, __nv_bfloat16* dst) {
-  const int kind = kv.kind[s];
-  const int idx = kv.index[s];
-  if (kind == OASIS_KV_BF16) {
-    const long long slot = (static_cast<long long>(b) * kv.layers + layer) * kv.n_bf16 + idx;
-    const uint4* src = reinterpret_cast<const uint4*>(
-        (is_v ? kv.v_bf16 : kv.k_bf16) + (slot * OASIS_TOKENS + p) * OASIS_HIDDEN + h * 64);
-    uint4* d = reinterpret_cast<uint4*>(dst);
+__device__ __forceinline__ uint4 dequant_fp8x8(uint32_t lo, uint32_t hi, float scale) {
+  // dequantise exactly as q.to(bf16) * scale in bf16 (one rounding)
+  return make_uint4(pack_bf16x2(e4m3_to_float(lo & 0xFF) * scale, e4m3_to_float((lo >> 8) & 0xFF) * scale),
+                    pack_bf16x2(e4m3_to_float((lo >> 16) & 0xFF) * scale, e4m3_to_float(lo >> 24) * scale),
+                    pack_bf16x2(e4m3_to_float(hi & 0xFF) * scale, e4m3_to_float((hi >> 8) & 0xFF) * scale),
+                    pack_bf16x2(e4m3_to_float((hi >> 16) & 0xFF) * scale, e4m3_to_float(hi >> 24) * scale));
+}
+
+__device__ __forceinline__ uint4 dequant_int4x8(uint32_t w, float scale, float zero) {
+  // 4 bytes = 8 codes; element 2i in the high nibble
+  uint32_t r[4];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) d[i] = src[i];
-  } else if (kind == OASIS_KV_FP8) {
-    const long long slot = (static_cast<long long>(b) * kv.layers + layer) * kv.n_fp8 + idx;
-    const uint4* src = reinterpret_cast<const uint4*>(
-        (is_v ? kv.v_fp8 : kv.k_fp8) + (slot * OASIS_TOKENS + p) * OASIS_HIDDEN + h * 64);
-    const float scale = __bfloat162float((is_v ? kv.v_fp8_scale : kv.k_fp8_scale)[slot * OASIS_HEADS + h]);
-    uint32_t* d = reinterpret_cast<uint32_t*>(dst);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const uint4 w = src[i];
-      const uint32_t words[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const uint32_t x = words[j];
-        // dequantise exactly as q.to(bf16) * scale in bf16 (one rounding)
-        d[i * 8 + j * 2 + 0] = pack_bf16x2(e4m3_to_float(x & 0xFF) * scale,
-                                           e4m3_to_float((x >> 8) & 0xFF) * scale);
-        d[i * 8 + j * 2 + 1] = pack_bf16x2(e4m3_to_float((x >> 16) & 0xFF) * scale,
-                                           e4m3_to_float(x >> 24) * scale);
-      }
-    }
-  } else {
-    const long long slot = (static_cast<long long>(b) * kv.layers + layer) * kv.n_int4 + idx;
-    const long long grp = (slot * OASIS_TOKENS + p) * OASIS_HEADS + h;
-    const uint4* src = reinterpret_cast<const uint4*>((is_v ? kv.v_int4 : kv.k_int4) + grp * 32);
-    const float scale = __half2float((is_v ? kv.v_i4_scale : kv.k_i4_scale)[grp]);
-    const float zero = __half2float((is_v ? kv.v_i4_zero : kv.k_i4_zero)[grp]);
-    uint32_t* d = reinterpret_cast<uint32_t*>(dst);
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      const uint4 w = src[i];
-      const uint32_t words[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-#pragma unroll
-        for (int bt = 0; bt < 4; ++bt) {
-          const uint32_t byte = (words[j] >> (8 * bt)) & 0xFFu;  // element 2i high, 2i+1 low
-          const float hi = static_cast<float>(byte >> 4) * scale + zero;
-          const float lo = static_cast<float>(byte & 0xFu) * scale + zero;
-          d[i * 16 + j * 4 + bt] = pack_bf16x2(hi, lo);
-        }
-      }
-    }
+  for (int b = 0; b < 4; ++b) {
+    const uint32_t byte = (w >> (8 * b)) & 0xFFu;
+    r[b] = pack_bf16x2(static_cast<float>(byte >> 4) * scale + zero,
+                       static_cast<float>(byte & 0xFu) * scale + zero);
   }
+  return make_uint4(r[0], r[1], r[2], r[3]);
 }
 
 __global__ void __launch_bounds__(kTpWarps * 32)
@@ -199,51 +177,79 @@ __global__ void __launch_bounds__(kTpWarps * 32)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int p = blockIdx.x;                 // token within frame
-  const int h = blockIdx.y * kTpWarps + warp;
+  const int hg = blockIdx.y;                // group of 4 heads
+  const int h = hg * kTpWarps + warp;
   const int b = blockIdx.z;                 // session
-  __nv_bfloat16* sQ = reinterpret_cast<__nv_bfloat16*>(sm_tp) + warp * kTpWarpSmem;
-  __nv_bfloat16* sK = sQ + kTpRowsPerMat * kSmemStride;
-  __nv_bfloat16* sV = sK + kTpRowsPerMat * kSmemStride;
-
-  // lane r stages row r of Q, K and V
-  {
-    const int r = lane;
-    uint4* dq = reinterpret_cast<uint4*>(sQ + r * kSmemStride);
-    if (r < q_frames) {
-      const uint4* src = reinterpret_cast<const uint4*>(
-          qkv + (static_cast<long long>(b * q_frames + r) * OASIS_TOKENS + p) * kQkvLd + h * 64);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) dq[i] = src[i];
-    } else {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) dq[i] = make_uint4(0, 0, 0, 0);
-    }
-    __nv_bfloat16* dk = sK + r * kSmemStride;
-    __nv_bfloat16* dv = sV + r * kSmemStride;
-    if (r < n_past) {
-      stage_cache_row(kv, false, b, layer, r, p, h, dk);
-      stage_cache_row(kv, true, b, layer, r, p, h, dv);
-    } else if (r < n_kv) {
-      const long long row = static_cast<long long>(b * q_frames + (r - n_past)) * OASIS_TOKENS + p;
-      const uint4* srck = reinterpret_cast<const uint4*>(qkv + row * kQkvLd + OASIS_HIDDEN + h * 64);
-      const uint4* srcv = reinterpret_cast<const uint4*>(qkv + row * kQkvLd + 2 * OASIS_HIDDEN + h * 64);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        reinterpret_cast<uint4*>(dk)[i] = srck[i];
-        reinterpret_cast<uint4*>(dv)[i] = srcv[i];
-      }
-    } else {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        reinterpret_cast<uint4*>(dk)[i] = make_uint4(0, 0, 0, 0);
-        reinterpret_cast<uint4*>(dv)[i] = make_uint4(0, 0, 0, 0);
-      }
-    }
-  }
-  __syncwarp();
+  __nv_bfloat16* smem_all = reinterpret_cast<__nv_bfloat16*>(sm_tp);
+  // per head hh: Q, K, V blocks of 32 rows x kSmemStride
+  auto mat = [&](int hh, int which) { return smem_all + hh * kTpWarpSmem + which * kTpRowsPerMat * kSmemStride; };
 
   const int m_tiles = (q_frames + 15) >> 4;  // 1 or 2
   const int n_pairs = (n_kv + 15) >> 4;      // key tiles of 16 (1 or 2)
+  const int tid = threadIdx.x;
+  const int n_live = n_kv - n_past;
+
+  // ---- cooperative staging: the 4 heads of one (session, token) are contiguous ----
+  // Q rows and live K/V rows: 3 x 512 B per frame (cp.async, 16-byte chunks)
+  for (int i = tid; i < q_frames * 32; i += kTpWarps * 32) {
+    const int t = i >> 5, c = i & 31;
+    const __nv_bfloat16* src = qkv + (static_cast<long long>(b * q_frames + t) * OASIS_TOKENS + p) * kQkvLd + hg * 256 + c * 8;
+    cp_async16(mat(c >> 3, 0) + t * kSmemStride + (c & 7) * 8, src);
+  }
+  for (int i = tid; i < n_live * 64; i += kTpWarps * 32) {
+    const int j = i >> 6, which = 1 + ((i >> 5) & 1), c = i & 31;
+    const __nv_bfloat16* src = qkv + (static_cast<long long>(b * q_frames + j) * OASIS_TOKENS + p) * kQkvLd +
+                               which * OASIS_HIDDEN + hg * 256 + c * 8;
+    cp_async16(mat(c >> 3, which) + (n_past + j) * kSmemStride + (c & 7) * 8, src);
+  }
+  // cached rows: bf16 by cp.async, FP8 / INT4 dequantised through registers
+  for (int i = tid; i < n_past * 64; i += kTpWarps * 32) {
+    const int s = i >> 6, which = 1 + ((i >> 5) & 1), u = i & 31;
+    const bool is_v = which == 2;
+    const int kind = kv.kind[s], idx = kv.index[s];
+    if (kind == OASIS_KV_BF16) {
+      const long long slot = (static_cast<long long>(b) * kv.layers + layer) * kv.n_bf16 + idx;
+      const __nv_bfloat16* src = (is_v ? kv.v_bf16 : kv.k_bf16) + (slot * OASIS_TOKENS + p) * OASIS_HIDDEN + hg * 256 + u * 8;
+      cp_async16(mat(u >> 3, which) + s * kSmemStride + (u & 7) * 8, src);
+    } else if (kind == OASIS_KV_FP8) {
+      if (u < 16) {  // 16 chunks of 16 codes cover the 4 heads
+        const long long slot = (static_cast<long long>(b) * kv.layers + layer) * kv.n_fp8 + idx;
+        const uint4 w = *reinterpret_cast<const uint4*>((is_v ? kv.v_fp8 : kv.k_fp8) +
+                                                        (slot * OASIS_TOKENS + p) * OASIS_HIDDEN + hg * 256 + u * 16);
+        const int hh = u >> 2;
+        const float scale = __bfloat162float((is_v ? kv.v_fp8_scale : kv.k_fp8_scale)[slot * OASIS_HEADS + hg * 4 + hh]);
+        __nv_bfloat16* d = mat(hh, which) + s * kSmemStride + (u & 3) * 16;
+        reinterpret_cast<uint4*>(d)[0] = dequant_fp8x8(w.x, w.y, scale);
+        reinterpret_cast<uint4*>(d)[1] = dequant_fp8x8(w.z, w.w, scale);
+      }
+    } else {
+      if (u < 8) {  // 8 chunks of 32 codes cover the 4 heads
+        const long long slot = (static_cast<long long>(b) * kv.layers + layer) * kv.n_int4 + idx;
+        const int hh = u >> 1;
+        const long long grp = (slot * OASIS_TOKENS + p) * OASIS_HEADS + hg * 4 + hh;
+        const uint4 w = *reinterpret_cast<const uint4*>((is_v ? kv.v_int4 : kv.k_int4) + grp * 32 + (u & 1) * 16);
+        const float scale = __half2float((is_v ? kv.v_i4_scale : kv.k_i4_scale)[grp]);
+        const float zero = __half2float((is_v ? kv.v_i4_zero : kv.k_i4_zero)[grp]);
+        uint4* d = reinterpret_cast<uint4*>(mat(hh, which) + s * kSmemStride + (u & 1) * 32);
+        d[0] = dequant_int4x8(w.x, scale, zero);
+        d[1] = dequant_int4x8(w.y, scale, zero);
+        d[2] = dequant_int4x8(w.z, scale, zero);
+        d[3] = dequant_int4x8(w.w, scale, zero);
+      }
+    }
+  }
+  // zero the padding rows the MMAs read (keeps masked products finite)
+  for (int i = tid; i < kTpWarps * 3 * 32 * 8; i += kTpWarps * 32) {
+    const int hh = i / (3 * 32 * 8), which = (i / (32 * 8)) % 3, r = (i >> 3) & 31, c = i & 7;
+    const bool pad = which == 0 ? (r >= q_frames && r < m_tiles * 16) : (r >= n_kv && r < n_pairs * 16);
+    if (pad) *reinterpret_cast<uint4*>(mat(hh, which) + r * kSmemStride + c * 8) = make_uint4(0, 0, 0, 0);
+  }
+  cp_async_wait_all();
+  __syncthreads();
+
+  __nv_bfloat16* sQ = mat(warp, 0);
+  __nv_bfloat16* sK = mat(warp, 1);
+  __nv_bfloat16* sV = mat(warp, 2);
   const int g = lane >> 2, c = lane & 3;
 
   for (int mt = 0; mt < m_tiles; ++mt) {

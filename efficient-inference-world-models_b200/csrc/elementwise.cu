@@ -1,5 +1,6 @@
-// Memory-bound kernels around the GEMMs: LayerNorm + adaLN modulate, timestep /
-// action / patch embeddings (small fp32 SIMT GEMMs), and the sampler updates.
+// Memory-bound kernels around the GEMMs: LayerNorm + adaLN modulate, the inputs of the
+// embedding GEMMs (timestep sinusoid, action columns, patch im2col), and the sampler
+// updates.
 #include "launch.cuh"
 
 namespace oasis {
@@ -17,13 +18,20 @@ __global__ void __launch_bounds__(256)
   const int lane = threadIdx.x & 31;
   if (row >= M) return;
   const float4* xr = reinterpret_cast<const float4*>(x + static_cast<long long>(row) * OASIS_HIDDEN);
-  float4 v[8];
+  const long long f = row / rows_per_frame;
+  const float4* sh = reinterpret_cast<const float4*>(shift + f * mod_ld);
+  const float4* sc = reinterpret_cast<const float4*>(scale + f * mod_ld);
+  float4 v[8], a4[8], s4[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = xr[lane + 32 * i];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {  // modulation rows issued before the reductions
+    a4[i] = sh[lane + 32 * i];
+    s4[i] = sc[lane + 32 * i];
+  }
   float sum = 0.0f;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    v[i] = xr[lane + 32 * i];
-    sum += (v[i].x + v[i].y) + (v[i].z + v[i].w);
-  }
+  for (int i = 0; i < 8; ++i) sum += (v[i].x + v[i].y) + (v[i].z + v[i].w);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
   const float mean = sum * (1.0f / OASIS_HIDDEN);
@@ -36,14 +44,11 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
   const float rstd = rsqrtf(sq * (1.0f / OASIS_HIDDEN) + 1e-6f);
-  const long long f = row / rows_per_frame;
-  const float4* sh = reinterpret_cast<const float4*>(shift + f * mod_ld);
-  const float4* sc = reinterpret_cast<const float4*>(scale + f * mod_ld);
   uint2* o2 = reinterpret_cast<uint2*>(out + static_cast<long long>(row) * OASIS_HIDDEN);
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
-    const float4 a = sh[lane + 32 * i];
-    const float4 s = sc[lane + 32 * i];
+    const float4 a = a4[i];
+    const float4 s = s4[i];
     const float y0 = (v[i].x - mean) * rstd * (1.0f + s.x) + a.x;
     const float y1 = (v[i].y - mean) * rstd * (1.0f + s.y) + a.y;
     const float y2 = (v[i].z - mean) * rstd * (1.0f + s.z) + a.z;
@@ -62,122 +67,66 @@ int launch_ln_modulate(const float* x, const float* shift, const float* scale, l
 }
 
 // ----------------------------------------------------------------------------------
-// small fp32 GEMM: out[m][n] (+)= act(sum_k in[m][k] * W[n][k] + b[n]); 64x64 tiles,
-// 256 threads x (4 x 4) outputs, K staged 32 at a time.  act: 0 none, 1 SiLU.
+// conditioning inputs of the two timestep-MLP GEMMs
+//   emb [F][256] bf16: sinusoidal timestep embedding [cos(t f_i) | sin(t f_i)],
+//                      f_i = exp(-ln(10000) i / 128), computed in fp32
+//   h1a [F][1088] bf16: columns 1024..1087 <- the 25 action values, a 1 for the action
+//                      bias column (0 without actions), zeros (the first-linear GEMM
+//                      writes columns 0..1023)
 // ----------------------------------------------------------------------------------
-template <int ACT, bool ACCUM>
-__global__ void __launch_bounds__(256)
-    linear_f32_kernel(const float* __restrict__ in, int ldi, const float* __restrict__ W,
-                      const float* __restrict__ bias, float* __restrict__ out, int ldo, int M,
-                      int N, int K) {
-  __shared__ float As[32][65];
-  __shared__ float Ws[32][65];
-  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
-  const int m0 = blockIdx.y * 64, n0 = blockIdx.x * 64;
-  float acc[4][4] = {};
-  for (int k0 = 0; k0 < K; k0 += 32) {
-    for (int i = threadIdx.x; i < 64 * 32; i += 256) {
-      const int r = i >> 5, k = i & 31;
-      const int gm = m0 + r, gn = n0 + r, gk = k0 + k;
-      As[k][r] = (gm < M && gk < K) ? in[static_cast<long long>(gm) * ldi + gk] : 0.0f;
-      Ws[k][r] = (gn < N && gk < K) ? W[static_cast<long long>(gn) * K + gk] : 0.0f;
-    }
-    __syncthreads();
-#pragma unroll 8
-    for (int k = 0; k < 32; ++k) {
-      float a[4], w[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        a[i] = As[k][ty * 4 + i];
-        w[i] = Ws[k][tx * 4 + i];
-      }
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], w[j], acc[i][j]);
-    }
-    __syncthreads();
-  }
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int gm = m0 + ty * 4 + i;
-    if (gm >= M) continue;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int gn = n0 + tx * 4 + j;
-      if (gn >= N) continue;
-      float y = acc[i][j] + (bias ? bias[gn] : 0.0f);
-      if (ACT == 1) y = y / (1.0f + expf(-y));
-      float* o = out + static_cast<long long>(gm) * ldo + gn;
-      *o = ACCUM ? *o + y : y;
-    }
-  }
-}
-
-int launch_linear_f32(const float* in, int ldi, const float* W, const float* b, float* out, int ldo,
-                      int M, int N, int K, int act, bool accum, cudaStream_t stream) {
-  dim3 grid((N + 63) / 64, (M + 63) / 64);
-  if (act == 1 && !accum)
-    linear_f32_kernel<1, false><<<grid, 256, 0, stream>>>(in, ldi, W, b, out, ldo, M, N, K);
-  else if (act == 0 && !accum)
-    linear_f32_kernel<0, false><<<grid, 256, 0, stream>>>(in, ldi, W, b, out, ldo, M, N, K);
-  else
-    linear_f32_kernel<0, true><<<grid, 256, 0, stream>>>(in, ldi, W, b, out, ldo, M, N, K);
-  OASIS_CHECK_LAUNCH("linear_f32_kernel");
-  return OASIS_OK;
-}
-
-// Sinusoidal timestep embedding (256): [cos(t * f_i) | sin(t * f_i)],
-// f_i = exp(-ln(10000) * i / 128), i < 128, computed in fp32.
-__global__ void temb_sinusoid_kernel(const int64_t* __restrict__ t, float* __restrict__ emb, int F) {
+__global__ void temb_prep_kernel(const int64_t* __restrict__ t, const float* __restrict__ act,
+                                 __nv_bfloat16* __restrict__ emb, __nv_bfloat16* __restrict__ h1a,
+                                 int F) {
   const int f = blockIdx.x;
   const int i = threadIdx.x;  // 128 threads
   if (f >= F) return;
   const float freq = expf(-9.210340371976184f * static_cast<float>(i) / 128.0f);
   const float arg = static_cast<float>(t[f]) * freq;
-  emb[f * 256 + i] = cosf(arg);
-  emb[f * 256 + 128 + i] = sinf(arg);
-}
-
-int launch_temb_sinusoid(const int64_t* t, float* emb, int F, cudaStream_t stream) {
-  temb_sinusoid_kernel<<<F, 128, 0, stream>>>(t, emb, F);
-  OASIS_CHECK_LAUNCH("temb_sinusoid_kernel");
-  return OASIS_OK;
-}
-
-// bf16(silu(c)): the shared input of every adaLN modulation linear.
-__global__ void silu_bf16_kernel(const float* __restrict__ c, __nv_bfloat16* __restrict__ out, int n) {
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i < n) {
-    const float y = c[i];
-    out[i] = __float2bfloat16_rn(y / (1.0f + expf(-y)));
+  emb[f * 256 + i] = __float2bfloat16_rn(cosf(arg));
+  emb[f * 256 + 128 + i] = __float2bfloat16_rn(sinf(arg));
+  if (i < 64) {
+    // 25 action values, then the constant input of the action bias column
+    float a = 0.0f;
+    if (act && i < OASIS_ACTION_DIM) a = act[f * OASIS_ACTION_DIM + i];
+    if (act && i == OASIS_ACTION_DIM) a = 1.0f;
+    h1a[static_cast<long long>(f) * (OASIS_HIDDEN + 64) + OASIS_HIDDEN + i] = __float2bfloat16_rn(a);
   }
 }
 
-int launch_silu_bf16(const float* c, void* out, int n, cudaStream_t stream) {
-  silu_bf16_kernel<<<(n + 255) / 256, 256, 0, stream>>>(c, static_cast<__nv_bfloat16*>(out), n);
-  OASIS_CHECK_LAUNCH("silu_bf16_kernel");
+int launch_temb_prep(const int64_t* t, const float* act, void* emb, void* h1a, int F,
+                     cudaStream_t stream) {
+  temb_prep_kernel<<<F, 128, 0, stream>>>(t, act, static_cast<__nv_bfloat16*>(emb),
+                                          static_cast<__nv_bfloat16*>(h1a), F);
+  OASIS_CHECK_LAUNCH("temb_prep_kernel");
   return OASIS_OK;
 }
 
-// im2col of the 2x2 patch embedding: x fp32 [F][16][18][32] -> cols [F*144][64], column
-// index c*4 + pi*2 + qi (Conv2d weight order [out][c][pi][qi]).
-__global__ void patch_im2col_kernel(const float* __restrict__ x, float* __restrict__ cols, int F) {
+// im2col of the 2x2 patch embedding: x fp32 [F][16][18][32] -> cols bf16 [F*144][64],
+// column c*4 + pi*2 + qi (Conv2d weight order [out][c][pi][qi]).  One thread per
+// (token, channel) writes its 4 patch values.
+__global__ void patch_im2col_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ cols,
+                                    int F) {
   const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
-  const long long total = static_cast<long long>(F) * OASIS_TOKENS * 64;
+  const long long total = static_cast<long long>(F) * OASIS_TOKENS * 16;
   if (i >= total) return;
-  const int k = static_cast<int>(i & 63);
-  const long long m = i >> 6;
+  const int c = static_cast<int>(i & 15);
+  const long long m = i >> 4;
   const int f = static_cast<int>(m / OASIS_TOKENS);
   const int pp = static_cast<int>(m % OASIS_TOKENS);
   const int hp = pp / 16, wp = pp % 16;
-  const int c = k >> 2, pi = (k >> 1) & 1, qi = k & 1;
-  cols[i] = x[((static_cast<long long>(f) * 16 + c) * 18 + hp * 2 + pi) * 32 + wp * 2 + qi];
+  const float* src = x + ((static_cast<long long>(f) * 16 + c) * 18 + hp * 2) * 32 + wp * 2;
+  const float2 r0 = *reinterpret_cast<const float2*>(src);
+  const float2 r1 = *reinterpret_cast<const float2*>(src + 32);
+  uint2 w;
+  w.x = pack_bf16x2(r0.x, r0.y);
+  w.y = pack_bf16x2(r1.x, r1.y);
+  *reinterpret_cast<uint2*>(cols + m * 64 + c * 4) = w;
 }
 
-int launch_patch_im2col(const float* x, float* cols, int F, cudaStream_t stream) {
-  const long long total = static_cast<long long>(F) * OASIS_TOKENS * 64;
-  patch_im2col_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, stream>>>(x, cols, F);
+int launch_patch_im2col(const float* x, void* cols, int F, cudaStream_t stream) {
+  const long long total = static_cast<long long>(F) * OASIS_TOKENS * 16;
+  patch_im2col_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, stream>>>(
+      x, static_cast<__nv_bfloat16*>(cols), F);
   OASIS_CHECK_LAUNCH("patch_im2col_kernel");
   return OASIS_OK;
 }

@@ -27,8 +27,10 @@ enum Family { kFamGemm = 0, kFamAda, kFamSpatial, kFamTemporal, kFamLn, kFamEmbe
 size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 
 struct Layout {
-  size_t resid, hbuf, qkv, attn, mlp, cols, emb, h1, c, silu, mod, total;
+  size_t resid, hbuf, qkv, attn, mlp, cols, emb, h1a, silu, mod, total;
 };
+
+constexpr int kH1aLd = OASIS_HIDDEN + 64;  // [first-linear output | actions | zero pad]
 
 Layout layout_for(int F, int depth) {
   const size_t M = static_cast<size_t>(F) * OASIS_TOKENS;
@@ -45,10 +47,9 @@ Layout layout_for(int F, int depth) {
   L.qkv = take(M * 3 * OASIS_HIDDEN * 2);
   L.attn = take(M * OASIS_HIDDEN * 2);
   L.mlp = take(M * OASIS_MLP_HIDDEN * 2);
-  L.cols = take(M * 64 * 4);
-  L.emb = take(static_cast<size_t>(F) * 256 * 4);
-  L.h1 = take(static_cast<size_t>(F) * OASIS_HIDDEN * 4);
-  L.c = take(static_cast<size_t>(F) * OASIS_HIDDEN * 4);
+  L.cols = take(M * 64 * 2);
+  L.emb = take(static_cast<size_t>(F) * 256 * 2);
+  L.h1a = take(static_cast<size_t>(F) * kH1aLd * 2);
   L.silu = take(static_cast<size_t>(F) * OASIS_HIDDEN * 2);
   L.mod = take(static_cast<size_t>(F) * mod_ld * 4);
   L.total = off;
@@ -65,6 +66,7 @@ struct oasis_plan {
   uint8_t* ws = nullptr;
   oasis::Layout L{};
   // GEMM operand descriptors
+  oasis::GemmOperands patch, temb1, temb2;  // embeddings
   oasis::GemmOperands ada;
   oasis::GemmOperands fin;
   std::vector<oasis::GemmOperands> qkv, out, fc1, fc2;  // per sub-block
@@ -104,12 +106,14 @@ T* at(oasis_plan* p, size_t off) {
 }
 
 int pick_bn(int N, int M) {
-  // 128-row tiles along M; choose the widest N tile that still gives >= ~1 wave
+  // 128-row tiles along M.  N=256 tiles keep the tensor core under the shared-memory
+  // bandwidth limit (N=128 tiles need the full 128 B/clk), so take the widest tile
+  // that still fills ~3/4 of the SMs; narrower tiles only for small M.
   const int sms = num_sms();
   const int mt = (M + kGemmBM - 1) / kGemmBM;
   for (int bn : {256, 128, 64}) {
     if (N % bn) continue;
-    if (static_cast<long long>(mt) * (N / bn) >= sms || bn == 64) return bn;
+    if (4LL * mt * (N / bn) >= 3LL * sms || bn == 64) return bn;
   }
   return 64;
 }
@@ -126,29 +130,29 @@ int run_forward(oasis_plan* p, const float* x, const int64_t* t, const float* ac
   float* mod = at<float>(p, p->L.mod);
   const long long mld = p->mod_ld;
 
-  // ---- embeddings ----
+  // ---- embeddings (three small tcgen05 GEMMs) ----
   {
     Timer tm(p, s, kFamEmbed);
-    if (int e = launch_patch_im2col(x, at<float>(p, p->L.cols), F, s)) return e;
-    if (int e = launch_linear_f32(at<float>(p, p->L.cols), 64, w.patch_w, w.patch_b, resid,
-                                  OASIS_HIDDEN, M, OASIS_HIDDEN, 64, 0, false, s))
+    if (int e = launch_patch_im2col(x, at<void>(p, p->L.cols), F, s)) return e;
+    EpiParams pe{};
+    pe.out = resid;
+    pe.ldd = OASIS_HIDDEN;
+    pe.bias = w.patch_b;
+    if (int e = launch_gemm(p->patch, kEpiStoreF32Bias, pe, s)) return e;
+    if (int e = launch_temb_prep(t, act, at<void>(p, p->L.emb), at<void>(p, p->L.h1a), F, s))
       return e;
-    if (int e = launch_temb_sinusoid(t, at<float>(p, p->L.emb), F, s)) return e;
-    if (int e = launch_linear_f32(at<float>(p, p->L.emb), 256, w.t_fc1_w, w.t_fc1_b,
-                                  at<float>(p, p->L.h1), OASIS_HIDDEN, F, OASIS_HIDDEN, 256, 1,
-                                  false, s))
-      return e;
-    if (int e = launch_linear_f32(at<float>(p, p->L.h1), OASIS_HIDDEN, w.t_fc2_w, w.t_fc2_b,
-                                  at<float>(p, p->L.c), OASIS_HIDDEN, F, OASIS_HIDDEN, OASIS_HIDDEN,
-                                  0, false, s))
-      return e;
-    if (act) {
-      if (int e = launch_linear_f32(act, OASIS_ACTION_DIM, w.act_w, w.act_b, at<float>(p, p->L.c),
-                                    OASIS_HIDDEN, F, OASIS_HIDDEN, OASIS_ACTION_DIM, 0, true, s))
-        return e;
-    }
-    if (int e = launch_silu_bf16(at<float>(p, p->L.c), at<void>(p, p->L.silu), F * OASIS_HIDDEN, s))
-      return e;
+    EpiParams e1{};  // h1 = SiLU(W1 emb + b1) -> h1a[:, 0:1024]
+    e1.out = at<void>(p, p->L.h1a);
+    e1.ldd = kH1aLd;
+    e1.bias = w.t_fc1_b;
+    e1.n_valid = F;
+    if (int e = launch_gemm(p->temb1, kEpiAdaTSilu, e1, s)) return e;
+    EpiParams e2{};  // SiLU(c), c = W2 h1 + Wa a + b2 + ba: the input of every adaLN linear
+    e2.out = at<void>(p, p->L.silu);
+    e2.ldd = OASIS_HIDDEN;
+    e2.bias = w.t_fc2_b;
+    e2.n_valid = F;
+    if (int e = launch_gemm(p->temb2, kEpiAdaTSilu, e2, s)) return e;
   }
   // ---- all adaLN modulations in one swap-AB GEMM ----
   {
@@ -295,8 +299,8 @@ extern "C" int oasis_plan_create(const oasis_dit_weights_t* w, int batch, int fr
   if (reinterpret_cast<uintptr_t>(workspace) & 255)
     return fail(OASIS_ERR_ALIGNMENT, "oasis_plan_create: workspace must be 256-byte aligned");
   const void* req[] = {w->patch_w, w->patch_b, w->t_fc1_w, w->t_fc1_b, w->t_fc2_w, w->t_fc2_b,
-                       w->act_w,   w->act_b,   w->ada_w,   w->ada_b,   w->final_w, w->final_b,
-                       w->rope_spatial, w->rope_temporal};
+                       w->ada_w,   w->ada_b,   w->final_w, w->final_b, w->rope_spatial,
+                       w->rope_temporal};
   for (const void* q : req)
     if (!q) return fail(OASIS_ERR_INVALID_ARG, "oasis_plan_create: a weight pointer is NULL");
   for (int j = 0; j < 2 * w->depth; ++j) {
@@ -317,13 +321,21 @@ extern "C" int oasis_plan_create(const oasis_dit_weights_t* w, int batch, int fr
   p->L = L;
   const int M = p->M;
   int st = OASIS_OK;
-  // adaLN: A = stacked weights (rows = mod_ld), B = bf16 SiLU(c) (rows = F)
-  {
-    int bn = 32;
-    while (bn < 256 && bn < F) bn <<= 1;
-    st = make_gemm_operands(&p->ada, w->ada_w, OASIS_HIDDEN, p->ws + L.silu, OASIS_HIDDEN,
-                            static_cast<int>(p->mod_ld), F, OASIS_HIDDEN, bn);
-  }
+  // swap-AB GEMMs over the F conditioning rows: A = weights, B = per-frame vectors
+  int bnf = 32;
+  while (bnf < 256 && bnf < F) bnf <<= 1;
+  st = make_gemm_operands(&p->ada, w->ada_w, OASIS_HIDDEN, p->ws + L.silu, OASIS_HIDDEN,
+                          static_cast<int>(p->mod_ld), F, OASIS_HIDDEN, bnf);
+  if (!st)
+    st = make_gemm_operands(&p->temb1, w->t_fc1_w, 256, p->ws + L.emb, 256, OASIS_HIDDEN, F, 256,
+                            bnf);
+  if (!st)
+    st = make_gemm_operands(&p->temb2, w->t_fc2_w, kH1aLd, p->ws + L.h1a, kH1aLd, OASIS_HIDDEN, F,
+                            kH1aLd, bnf);
+  if (!st)
+    st = make_gemm_operands(&p->patch, p->ws + L.cols, 64, w->patch_w, 64, M, OASIS_HIDDEN, 64,
+                            pick_bn(OASIS_HIDDEN, M));
+  if (!st) st = set_gemm_output(&p->patch, p->ws + L.resid, OASIS_HIDDEN, true);
   if (!st)
     st = make_gemm_operands(&p->fin, p->ws + L.hbuf, OASIS_HIDDEN, w->final_w, OASIS_HIDDEN, M, 64,
                             OASIS_HIDDEN, 64);
@@ -335,16 +347,20 @@ extern "C" int oasis_plan_create(const oasis_dit_weights_t* w, int batch, int fr
     const oasis_sub_weights_t& s = w->sub[j];
     st = make_gemm_operands(&p->qkv[j], p->ws + L.hbuf, OASIS_HIDDEN, s.qkv_w, OASIS_HIDDEN, M,
                             3 * OASIS_HIDDEN, OASIS_HIDDEN, pick_bn(3 * OASIS_HIDDEN, M));
+    if (!st) st = set_gemm_output(&p->qkv[j], p->ws + L.qkv, 3 * OASIS_HIDDEN, false);
     if (!st)
       st = make_gemm_operands(&p->out[j], p->ws + L.attn, OASIS_HIDDEN, s.out_w, OASIS_HIDDEN, M,
                               OASIS_HIDDEN, OASIS_HIDDEN, pick_bn(OASIS_HIDDEN, M));
+    if (!st) st = set_gemm_output(&p->out[j], p->ws + L.resid, OASIS_HIDDEN, true);
     if (!st)
       st = make_gemm_operands(&p->fc1[j], p->ws + L.hbuf, OASIS_HIDDEN, s.fc1_w, OASIS_HIDDEN, M,
                               OASIS_MLP_HIDDEN, OASIS_HIDDEN, pick_bn(OASIS_MLP_HIDDEN, M));
+    if (!st) st = set_gemm_output(&p->fc1[j], p->ws + L.mlp, OASIS_MLP_HIDDEN, false);
     if (!st)
       st = make_gemm_operands(&p->fc2[j], p->ws + L.mlp, OASIS_MLP_HIDDEN, s.fc2_w,
                               OASIS_MLP_HIDDEN, M, OASIS_HIDDEN, OASIS_MLP_HIDDEN,
                               pick_bn(OASIS_HIDDEN, M));
+    if (!st) st = set_gemm_output(&p->fc2[j], p->ws + L.resid, OASIS_HIDDEN, true);
   }
   if (st) {
     delete p;
@@ -393,7 +409,7 @@ extern "C" int oasis_dit_forward_cached(oasis_plan_t* plan, const float* x, cons
 extern "C" int oasis_plan_set_timing(oasis_plan_t* plan, int enable) {
   if (!plan) return fail(OASIS_ERR_INVALID_ARG, "oasis_plan_set_timing: null plan");
   if (enable && plan->ev.empty()) {
-    const int n = 2 * (16 * plan->depth + 16);
+    const int n = 2 * 8 * (8 * 2 * plan->depth + 8);  // 8 forwards of timed launch groups
     plan->ev.resize(n);
     plan->ev_family.assign(n, 0);
     for (auto& e : plan->ev)

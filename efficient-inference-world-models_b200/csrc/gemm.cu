@@ -26,20 +26,21 @@ int get_encoder() {
   return OASIS_OK;
 }
 
-// 2-D bf16 K-major operand [rows][ld], box = 64 (K) x box_rows, 128-byte swizzle.
-int encode_kmajor(CUtensorMap* map, const void* base, long long rows, long long cols, long long ld,
-                  int box_rows) {
+// 2-D row-major tensor [rows][ld] of `esize`-byte elements, box = box_cols x box_rows
+// with 128-byte swizzle (box_cols * esize == 128).
+int encode_2d(CUtensorMap* map, const void* base, long long rows, long long cols, long long ld,
+              int box_cols, int box_rows, int esize) {
   if (int s = get_encoder()) return s;
   if (!aligned16(base)) return fail(OASIS_ERR_ALIGNMENT, "GEMM operand base not 16-byte aligned");
-  if ((ld * 2) % 16 != 0) return fail(OASIS_ERR_ALIGNMENT, "GEMM leading dim not a multiple of 8");
+  if ((ld * esize) % 16 != 0) return fail(OASIS_ERR_ALIGNMENT, "GEMM leading dim not 16-byte aligned");
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
-  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * 2)};
-  cuuint32_t box[2] = {static_cast<cuuint32_t>(kGemmBK), static_cast<cuuint32_t>(box_rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * esize)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims,
-                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r = g_encode(map, esize == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+                        2, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(OASIS_ERR_CUDA, "cuTensorMapEncodeTiled failed");
   return OASIS_OK;
 }
@@ -58,8 +59,10 @@ int launch_one(const GemmOperands& g, const EpiParams& ep, cudaStream_t stream, 
   int grid = num_sms();
   if (max_ctas > 0 && max_ctas < grid) grid = max_ctas;
   if (tiles < grid) grid = tiles;
-  gemm_tcgen05_kernel<BN, EPI><<<grid, kGemmThreads, S::kSmemBytes, stream>>>(g.a, g.b, g.M, g.N,
-                                                                              g.K, ep);
+  if (epi_uses_tma(EPI) && !g.has_d)
+    return fail(OASIS_ERR_INVALID_ARG, "GEMM epilogue needs an output tensor map");
+  gemm_tcgen05_kernel<BN, EPI><<<grid, kGemmThreads, S::kSmemBytes, stream>>>(g.a, g.b, g.d, g.M,
+                                                                              g.N, g.K, ep);
   OASIS_CHECK_LAUNCH("gemm_tcgen05_kernel");
   return OASIS_OK;
 }
@@ -74,6 +77,7 @@ int dispatch_epi(const GemmOperands& g, int epi, const EpiParams& ep, cudaStream
     case kEpiGateResid: return launch_one<BN, kEpiGateResid>(g, ep, s, mc);
     case kEpiAdaT: return launch_one<BN, kEpiAdaT>(g, ep, s, mc);
     case kEpiFinal: return launch_one<BN, kEpiFinal>(g, ep, s, mc);
+    case kEpiAdaTSilu: return launch_one<BN, kEpiAdaTSilu>(g, ep, s, mc);
   }
   return fail(OASIS_ERR_INVALID_ARG, "unknown GEMM epilogue");
 }
@@ -97,12 +101,23 @@ int make_gemm_operands(GemmOperands* g, const void* A, long long lda, const void
   if (K % kGemmBK) return fail(OASIS_ERR_UNSUPPORTED, "GEMM K must be a multiple of 64");
   if (bn != 32 && bn != 64 && bn != 128 && bn != 256)
     return fail(OASIS_ERR_UNSUPPORTED, "GEMM tile N must be 32, 64, 128 or 256");
-  if (int s = encode_kmajor(&g->a, A, M, K, lda, kGemmBM)) return s;
-  if (int s = encode_kmajor(&g->b, B, N, K, ldb, bn)) return s;
+  *g = GemmOperands{};
+  if (int s = encode_2d(&g->a, A, M, K, lda, kGemmBK, kGemmBM, 2)) return s;
+  if (int s = encode_2d(&g->b, B, N, K, ldb, kGemmBK, bn, 2)) return s;
   g->M = M;
   g->N = N;
   g->K = K;
   g->bn = bn;
+  g->has_d = false;
+  return OASIS_OK;
+}
+
+int set_gemm_output(GemmOperands* g, void* D, long long ldd, bool f32) {
+  const int esize = f32 ? 4 : 2;
+  if (g->N % (f32 ? 32 : 64))
+    return fail(OASIS_ERR_UNSUPPORTED, "TMA-store GEMM epilogue needs N % 64 == 0 (bf16) / 32 (fp32)");
+  if (int s = encode_2d(&g->d, D, g->M, g->N, ldd, 128 / esize, 32, esize)) return s;
+  g->has_d = true;
   return OASIS_OK;
 }
 
@@ -127,13 +142,15 @@ extern "C" int oasis_gemm_bf16(const void* A, const void* B, void* D, const floa
   if (!A || !B || !D) return fail(OASIS_ERR_INVALID_ARG, "oasis_gemm_bf16: null pointer");
   if (epilogue != 0 && epilogue != 1)
     return fail(OASIS_ERR_INVALID_ARG, "oasis_gemm_bf16: epilogue must be 0 or 1");
-  if (N % 32) return fail(OASIS_ERR_UNSUPPORTED, "oasis_gemm_bf16: N must be a multiple of 32");
+  if (N % (epilogue == 0 ? 64 : 32))
+    return fail(OASIS_ERR_UNSUPPORTED, "oasis_gemm_bf16: N must be a multiple of 64 (bf16) / 32 (fp32)");
   if (!aligned16(D) || (epilogue == 0 ? (ldd % 8) : (ldd % 4)))
     return fail(OASIS_ERR_ALIGNMENT, "oasis_gemm_bf16: D must be 16-byte aligned rows");
   int bn = 256;
-  while (bn > 32 && (N % bn)) bn >>= 1;
+  while (bn > (epilogue == 0 ? 64 : 32) && (N % bn)) bn >>= 1;
   GemmOperands g;
   if (int s = make_gemm_operands(&g, A, lda, B, ldb, M, N, K, bn)) return s;
+  if (int s = set_gemm_output(&g, D, ldd, epilogue == 1)) return s;
   EpiParams ep{};
   ep.out = D;
   ep.ldd = ldd;

@@ -5,9 +5,13 @@
 // One persistent CTA per SM, 6 warps:
 //   warp 0      TMA producer: A tile 128x64 and B tile BNx64 per stage (128-byte swizzle)
 //   warp 1      TMEM allocator + single-thread tcgen05.mma issuer (M=128, N=BN, K=16)
-//   warps 2..5  epilogue: tcgen05.ld of the fp32 accumulator, fused math, global stores
+//   warps 2..5  epilogue: tcgen05.ld of the fp32 accumulator (one TMEM lane quarter
+//               each), fused math in registers, then a 128B-swizzled shared-memory
+//               tile and a TMA tensor store (bf16 outputs) or TMA reduce-add (the fp32
+//               residual update), so global traffic leaves in full lines asynchronously.
 // The accumulator is double-buffered in TMEM (2 x BN columns) so the epilogue of one
-// tile overlaps the main loop of the next.
+// tile overlaps the main loop of the next; TMEM is released as soon as a tile's last
+// tcgen05.ld has completed.
 #pragma once
 
 #include "common.cuh"
@@ -15,30 +19,40 @@
 namespace oasis {
 
 enum EpiKind : int {
-  kEpiStoreBF16 = 0,     // D bf16
-  kEpiStoreF32Bias = 1,  // D fp32 (+ bias[n])
-  kEpiQkvRope = 2,       // D bf16, RoPE on columns < rope_cols (q and k), pairs (2i, 2i+1)
-  kEpiBiasGelu = 3,      // D bf16 = gelu_tanh(acc + bias[n])
-  kEpiGateResid = 4,     // resid fp32 [m][n] += gate[m / 144][n] * (acc + bias[n])
+  kEpiStoreBF16 = 0,     // D bf16                                         (TMA store)
+  kEpiStoreF32Bias = 1,  // D fp32 = acc + bias[n]                         (TMA store)
+  kEpiQkvRope = 2,       // D bf16, RoPE on columns < rope_cols (q and k)  (TMA store)
+  kEpiBiasGelu = 3,      // D bf16 = gelu_tanh(acc + bias[n])              (TMA store)
+  kEpiGateResid = 4,     // resid fp32 += gate[m / 144][n] * (acc + bias[n]) (TMA reduce-add)
   kEpiAdaT = 5,          // swap-AB: out fp32 [n][m] = acc + bias[m]   (n < n_valid)
   kEpiFinal = 6,         // v fp32 unpatchified: token m, column (pi*2+qi)*16 + c
+  kEpiAdaTSilu = 7,      // swap-AB: out bf16 [n][m] = silu(acc + bias[m])   (n < n_valid)
 };
 
+__host__ __device__ constexpr bool epi_uses_tma(int e) {
+  return e == kEpiStoreBF16 || e == kEpiStoreF32Bias || e == kEpiQkvRope || e == kEpiBiasGelu ||
+         e == kEpiGateResid;
+}
+__host__ __device__ constexpr bool epi_out_f32(int e) {
+  return e == kEpiStoreF32Bias || e == kEpiGateResid;
+}
+
 struct EpiParams {
-  void* out;            // output base
+  void* out;            // output base (row-per-thread epilogues)
   long long ldd;        // output leading dim (elements)
-  const float* bias;    // per-column bias (kEpiAdaT: per-row)
+  const float* bias;    // per-column bias (swap-AB epilogues: per-row)
   const float* gate;    // kEpiGateResid: gate rows, row stride gate_ld
   long long gate_ld;
   const float* rope;    // kEpiQkvRope: table [positions][32][2] (cos, sin)
   int rope_cols;        // columns < rope_cols are rotated (2048: q and k)
   int rope_div, rope_mod, rope_add;  // position(m) = (m / div) % mod + add
-  int n_valid;          // kEpiAdaT: number of valid B rows
+  int n_valid;          // swap-AB epilogues: number of valid B rows
 };
 
 constexpr int kGemmBM = 128;
 constexpr int kGemmBK = 64;
 constexpr int kGemmThreads = 192;
+constexpr int kEpiBufBytes = 32 * 128;  // 32 rows x 128 B: one TMA store box
 
 template <int BN>
 struct GemmShape {
@@ -48,22 +62,64 @@ struct GemmShape {
   static constexpr int kStages = (192 * 1024) / kStageBytes > 8 ? 8 : (192 * 1024) / kStageBytes;
   static constexpr int kTmemCols = 2 * BN;  // power of two >= 64 for BN in {32..256}
   static constexpr int kBarBytes = 1024;
-  static constexpr int kSmemBytes = kStages * kStageBytes + kBarBytes + 1024;  // +1 KB align slack
+  static constexpr int kEpiBytes = 4 * 2 * kEpiBufBytes;  // 4 warps x double buffer
+  static constexpr int kSmemBytes =
+      kStages * kStageBytes + kEpiBytes + kBarBytes + 1024;  // +1 KB alignment slack
 };
 
+// GELU, tanh approximation (nn.GELU(approximate="tanh")); tanh from the SFU
+// (tanh.approx.f32, ~2^-11 relative error, below the bf16 rounding of the output).
+__device__ __forceinline__ float tanh_sfu(float x) {
+  float y;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 __device__ __forceinline__ float gelu_tanh(float x) {
   const float k0 = 0.7978845608028654f;  // sqrt(2/pi)
   const float k1 = 0.044715f;
-  return 0.5f * x * (1.0f + tanhf(k0 * (x + k1 * x * x * x)));
+  return 0.5f * x * (1.0f + tanh_sfu(k0 * (x + k1 * x * x * x)));
 }
 
-// Epilogue for one thread: row m (global), 32 consecutive columns starting at n0.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int c0, int c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(src)), "r"(c0), "r"(c1)
+               : "memory");
+}
+__device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* map, const void* src, int c0,
+                                                  int c1) {
+  asm volatile(
+      "cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(smem_u32(src)), "r"(c0), "r"(c1)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+template <int N>
+__device__ __forceinline__ void bulk_wait() {
+  asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void fence_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Write 16-byte chunk `c` (0..7) of row `r` (0..31) of a 128B-swizzled 32 x 128 B box.
+__device__ __forceinline__ void st_swizzled(uint8_t* buf, int r, int c, uint4 v) {
+  *reinterpret_cast<uint4*>(buf + r * 128 + ((c ^ (r & 7)) << 4)) = v;
+}
+
+// Row-per-thread epilogues (lane = row m, 32 consecutive columns from n0): used where
+// that layout is already the coalesced one (swap-AB writes out[n][m]: lanes hold
+// consecutive m) or the output is tiny and scattered (kEpiFinal).
 template <int EPI>
-__device__ __forceinline__ void epilogue_chunk(const EpiParams& p, int M, int N, int m, int n0,
-                                               float (&v)[32]) {
+__device__ __forceinline__ void epilogue_rows(const EpiParams& p, int M, int m, int n0,
+                                              const float (&v)[32]) {
+  if (m >= M) return;
   if (EPI == kEpiAdaT) {
-    // out[n][m]: lanes hold consecutive m -> coalesced across the warp for each n
-    if (m >= M) return;
     const float b = p.bias ? p.bias[m] : 0.0f;
     float* out = static_cast<float*>(p.out);
 #pragma unroll
@@ -71,78 +127,16 @@ __device__ __forceinline__ void epilogue_chunk(const EpiParams& p, int M, int N,
       const int n = n0 + i;
       if (n < p.n_valid) out[static_cast<long long>(n) * p.ldd + m] = v[i] + b;
     }
-    return;
-  }
-  if (m >= M) return;
-  if (EPI == kEpiStoreBF16 || EPI == kEpiBiasGelu || EPI == kEpiQkvRope) {
-    if (EPI == kEpiBiasGelu) {
+  } else if (EPI == kEpiAdaTSilu) {
+    const float b = p.bias[m];
+    __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.out);
 #pragma unroll
-      for (int i = 0; i < 32; ++i) v[i] = gelu_tanh(v[i] + p.bias[n0 + i]);
+    for (int i = 0; i < 32; ++i) {
+      const int n = n0 + i;
+      const float y = v[i] + b;
+      if (n < p.n_valid) out[static_cast<long long>(n) * p.ldd + m] = __float2bfloat16_rn(y / (1.0f + expf(-y)));
     }
-    if (EPI == kEpiQkvRope) {
-      if (n0 < p.rope_cols) {
-        const int pos = (m / p.rope_div) % p.rope_mod + p.rope_add;
-        const int pair0 = (n0 & 63) >> 1;  // 0 or 16
-        const float2* tab = reinterpret_cast<const float2*>(p.rope) + pos * 32 + pair0;
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          // round the projection to bf16 first (the reference rotates the bf16 tensor)
-          const float x0 = bf16_round(v[2 * i]);
-          const float x1 = bf16_round(v[2 * i + 1]);
-          const float2 cs = tab[i];
-          v[2 * i] = x0 * cs.x - x1 * cs.y;
-          v[2 * i + 1] = x1 * cs.x + x0 * cs.y;
-        }
-      }
-    }
-    __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.out) + static_cast<long long>(m) * p.ldd + n0;
-    uint4* o4 = reinterpret_cast<uint4*>(out);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      uint4 w;
-      w.x = pack_bf16x2(v[8 * j + 0], v[8 * j + 1]);
-      w.y = pack_bf16x2(v[8 * j + 2], v[8 * j + 3]);
-      w.z = pack_bf16x2(v[8 * j + 4], v[8 * j + 5]);
-      w.w = pack_bf16x2(v[8 * j + 6], v[8 * j + 7]);
-      o4[j] = w;
-    }
-    return;
-  }
-  if (EPI == kEpiStoreF32Bias) {
-    float* out = static_cast<float*>(p.out) + static_cast<long long>(m) * p.ldd + n0;
-    float4* o4 = reinterpret_cast<float4*>(out);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      float4 w;
-      w.x = v[4 * j + 0] + (p.bias ? p.bias[n0 + 4 * j + 0] : 0.0f);
-      w.y = v[4 * j + 1] + (p.bias ? p.bias[n0 + 4 * j + 1] : 0.0f);
-      w.z = v[4 * j + 2] + (p.bias ? p.bias[n0 + 4 * j + 2] : 0.0f);
-      w.w = v[4 * j + 3] + (p.bias ? p.bias[n0 + 4 * j + 3] : 0.0f);
-      o4[j] = w;
-    }
-    return;
-  }
-  if (EPI == kEpiGateResid) {
-    const float* g = p.gate + static_cast<long long>(m / OASIS_TOKENS) * p.gate_ld + n0;
-    const float* b = p.bias + n0;
-    float4* r4 = reinterpret_cast<float4*>(static_cast<float*>(p.out) +
-                                           static_cast<long long>(m) * p.ldd + n0);
-    const float4* g4 = reinterpret_cast<const float4*>(g);
-    const float4* b4 = reinterpret_cast<const float4*>(b);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      float4 r = r4[j];
-      const float4 gg = g4[j];
-      const float4 bb = b4[j];
-      r.x += gg.x * (v[4 * j + 0] + bb.x);
-      r.y += gg.y * (v[4 * j + 1] + bb.y);
-      r.z += gg.z * (v[4 * j + 2] + bb.z);
-      r.w += gg.w * (v[4 * j + 3] + bb.w);
-      r4[j] = r;
-    }
-    return;
-  }
-  if (EPI == kEpiFinal) {
+  } else if (EPI == kEpiFinal) {
     // token m = (frame, hp, wp); column j = (pi*2 + qi)*16 + c
     const int f = m / OASIS_TOKENS;
     const int pp = m % OASIS_TOKENS;
@@ -156,21 +150,73 @@ __device__ __forceinline__ void epilogue_chunk(const EpiParams& p, int M, int N,
       const int pi = pq >> 1, qi = pq & 1;
       out[(c * 18 + hp * 2 + pi) * 32 + wp * 2 + qi] = v[i] + p.bias[j];
     }
-    return;
+  }
+}
+
+// Elementwise math of the TMA epilogues on one thread's row segment (row m, columns
+// n0..n0+31), in registers.
+template <int EPI>
+__device__ __forceinline__ void epilogue_math(const EpiParams& p, int m, int n0, float (&v)[32]) {
+  if (EPI == kEpiBiasGelu || EPI == kEpiStoreF32Bias) {
+    if (EPI == kEpiStoreF32Bias && !p.bias) return;
+    const float4* b4 = reinterpret_cast<const float4*>(p.bias + n0);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float4 b = b4[j];
+      v[4 * j + 0] += b.x;
+      v[4 * j + 1] += b.y;
+      v[4 * j + 2] += b.z;
+      v[4 * j + 3] += b.w;
+    }
+    if (EPI == kEpiBiasGelu) {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = gelu_tanh(v[i]);
+    }
+  } else if (EPI == kEpiQkvRope) {
+    if (n0 < p.rope_cols) {
+      const int pos = (m / p.rope_div) % p.rope_mod + p.rope_add;
+      const float4* tab = reinterpret_cast<const float4*>(p.rope) + pos * 16 + ((n0 & 63) >> 2);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float4 cs = tab[i];  // (cos, sin) of two consecutive pairs
+        const float a0 = bf16_round(v[4 * i + 0]), a1 = bf16_round(v[4 * i + 1]);
+        const float b0 = bf16_round(v[4 * i + 2]), b1 = bf16_round(v[4 * i + 3]);
+        // the reference rotates the bf16-rounded projection: (x0, x1) -> (x0 c - x1 s, x1 c + x0 s)
+        v[4 * i + 0] = a0 * cs.x - a1 * cs.y;
+        v[4 * i + 1] = a1 * cs.x + a0 * cs.y;
+        v[4 * i + 2] = b0 * cs.z - b1 * cs.w;
+        v[4 * i + 3] = b1 * cs.z + b0 * cs.w;
+      }
+    }
+  } else if (EPI == kEpiGateResid) {
+    const float4* g4 = reinterpret_cast<const float4*>(
+        p.gate + static_cast<long long>(m / OASIS_TOKENS) * p.gate_ld + n0);
+    const float4* b4 = reinterpret_cast<const float4*>(p.bias + n0);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float4 g = g4[j];
+      const float4 b = b4[j];
+      v[4 * j + 0] = g.x * (v[4 * j + 0] + b.x);
+      v[4 * j + 1] = g.y * (v[4 * j + 1] + b.y);
+      v[4 * j + 2] = g.z * (v[4 * j + 2] + b.z);
+      v[4 * j + 3] = g.w * (v[4 * j + 3] + b.w);
+    }
   }
 }
 
 template <int BN, int EPI>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA,
-                        const __grid_constant__ CUtensorMap tmB, int M, int N, int K,
+                        const __grid_constant__ CUtensorMap tmB,
+                        const __grid_constant__ CUtensorMap tmD, int M, int N, int K,
                         EpiParams ep) {
   using S = GemmShape<BN>;
   constexpr int STAGES = S::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + STAGES * S::kStageBytes);
+  uint8_t* epi_smem = smem + STAGES * S::kStageBytes;  // 1024-aligned
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(epi_smem + S::kEpiBytes);
   uint64_t* empty_bar = full_bar + STAGES;
   uint64_t* tfull_bar = empty_bar + STAGES;   // [2]
   uint64_t* tempty_bar = tfull_bar + 2;       // [2]
@@ -199,6 +245,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     mbar_fence_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    if (epi_uses_tma(EPI)) tma_prefetch_desc(&tmD);
   }
   if (warp == 1) tmem_alloc<S::kTmemCols>(tmem_holder);
   tc_fence_before();
@@ -269,7 +316,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else {
     // ---------------- epilogue warps 2..5 ----------------
     const int quarter = warp & 3;  // TMEM lanes this warp may access
-    const int row_in_tile = quarter * 32 + lane;
+    uint8_t* bufs = epi_smem + quarter * 2 * kEpiBufBytes;
+    int nbuf = 0;  // TMA stores issued by this warp (round-robin over 2 buffers)
     int it = 0;
     for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x, ++it) {
       const int m0 = (tile % num_m) * kGemmBM;
@@ -280,16 +328,74 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       tc_fence_after();
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                              static_cast<uint32_t>(acc * BN);
+      const int m_row = m0 + quarter * 32 + lane;  // this thread's row
+      const bool rows_live = m0 + quarter * 32 < M;
+      if (epi_uses_tma(EPI)) {
+        // bf16: 64 columns per box (2 TMEM loads); fp32: 32 columns per box
+        constexpr int COLS = epi_out_f32(EPI) ? 32 : 64;
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        float v[32];
-        tmem_ld32(taddr + c * 32, v);
-        const int n_chunk = n0 + c * 32;
-        if (EPI == kEpiAdaT || n_chunk < N) epilogue_chunk<EPI>(ep, M, N, m0 + row_in_tile, n_chunk, v);
+        for (int blk = 0; blk < BN / COLS; ++blk) {
+          const int nb = n0 + blk * COLS;
+          float v[32], w[32];
+          tmem_ld32(taddr + blk * COLS, v);
+          if (COLS == 64) tmem_ld32(taddr + blk * COLS + 32, w);
+          if (blk == BN / COLS - 1) {  // accumulator fully read: hand TMEM back to the MMA
+            tc_fence_before();
+            mbar_arrive(&tempty_bar[acc]);
+          }
+          if (!rows_live || nb >= N) continue;
+          uint8_t* buf = bufs + (nbuf & 1) * kEpiBufBytes;
+          if (nbuf >= 2) {  // the store issued from this buffer two boxes ago must have read it
+            if (lane == 0) bulk_wait_read<1>();
+            __syncwarp();
+          }
+          epilogue_math<EPI>(ep, m_row, nb, v);
+          if (COLS == 64) {
+            epilogue_math<EPI>(ep, m_row, nb + 32, w);
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              st_swizzled(buf, lane, c, make_uint4(pack_bf16x2(v[8 * c + 0], v[8 * c + 1]),
+                                                   pack_bf16x2(v[8 * c + 2], v[8 * c + 3]),
+                                                   pack_bf16x2(v[8 * c + 4], v[8 * c + 5]),
+                                                   pack_bf16x2(v[8 * c + 6], v[8 * c + 7])));
+              st_swizzled(buf, lane, 4 + c, make_uint4(pack_bf16x2(w[8 * c + 0], w[8 * c + 1]),
+                                                       pack_bf16x2(w[8 * c + 2], w[8 * c + 3]),
+                                                       pack_bf16x2(w[8 * c + 4], w[8 * c + 5]),
+                                                       pack_bf16x2(w[8 * c + 6], w[8 * c + 7])));
+            }
+          } else {
+#pragma unroll
+            for (int c = 0; c < 8; ++c)
+              st_swizzled(buf, lane, c, make_uint4(__float_as_uint(v[4 * c + 0]), __float_as_uint(v[4 * c + 1]),
+                                                   __float_as_uint(v[4 * c + 2]), __float_as_uint(v[4 * c + 3])));
+          }
+          fence_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            if (EPI == kEpiGateResid)
+              tma_reduce_add_2d(&tmD, buf, nb, m0 + quarter * 32);
+            else
+              tma_store_2d(&tmD, buf, nb, m0 + quarter * 32);
+            bulk_commit();
+          }
+          ++nbuf;
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          float v[32];
+          tmem_ld32(taddr + c * 32, v);
+          if (c == BN / 32 - 1) {
+            tc_fence_before();
+            mbar_arrive(&tempty_bar[acc]);
+          }
+          const int n_chunk = n0 + c * 32;
+          if (EPI != kEpiFinal || n_chunk < N) epilogue_rows<EPI>(ep, M, m_row, n_chunk, v);
+        }
       }
-      tc_fence_before();
-      mbar_arrive(&tempty_bar[acc]);
     }
+    if (epi_uses_tma(EPI) && lane == 0) bulk_wait<0>();  // all stores complete before exit
+    __syncwarp();
   }
 
   tc_fence_before();
@@ -298,13 +404,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (warp == 1) tmem_dealloc<S::kTmemCols>(tmem_base);
 }
 
-// Host launcher (gemm.cu).  A: [M][lda] bf16, B: [N][ldb] bf16.
+// Host side (gemm.cu).  A: [M][lda] bf16, B: [N][ldb] bf16; D described by its own
+// tensor map for the TMA epilogues.
 struct GemmOperands {
-  CUtensorMap a, b;
+  CUtensorMap a, b, d;
   int M, N, K, bn;
+  bool has_d;
 };
 int make_gemm_operands(GemmOperands* g, const void* A, long long lda, const void* B, long long ldb,
                        int M, int N, int K, int bn);
+// Output tensor map for the TMA epilogues: D [M][N] with leading dim ldd, bf16 or fp32.
+int set_gemm_output(GemmOperands* g, void* D, long long ldd, bool f32);
 int launch_gemm(const GemmOperands& g, int epi, const EpiParams& ep, cudaStream_t stream,
                 int max_ctas = 0);
 int num_sms();

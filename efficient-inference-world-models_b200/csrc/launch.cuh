@@ -32,10 +32,8 @@ int launch_kv_store(const void* kv, long long ld, int k_col, int v_col, const oa
 
 int launch_ln_modulate(const float* x, const float* shift, const float* scale, long long mod_ld,
                        void* out, int M, int rows_per_frame, cudaStream_t stream);
-int launch_linear_f32(const float* in, int ldi, const float* W, const float* b, float* out, int ldo,
-                      int M, int N, int K, int act, bool accum, cudaStream_t stream);
-int launch_temb_sinusoid(const int64_t* t, float* emb, int F, cudaStream_t stream);
-int launch_silu_bf16(const float* c, void* out, int n, cudaStream_t stream);
-int launch_patch_im2col(const float* x, float* cols, int F, cudaStream_t stream);
+int launch_temb_prep(const int64_t* t, const float* act, void* emb, void* h1a, int F,
+                     cudaStream_t stream);
+int launch_patch_im2col(const float* x, void* cols, int F, cudaStream_t stream);
 
 }  // namespace oasis

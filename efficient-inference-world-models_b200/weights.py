@@ -130,14 +130,18 @@ def pack_weights(sd: Dict[str, torch.Tensor], device="cuda", depth: int = None) 
 
     w = N.DiTWeights()
     w.depth = depth
-    w.patch_w = f32("x_embedder.proj.weight", (HIDDEN, IN_CH * PATCH * PATCH))
+    w.patch_w = bf16(sd["x_embedder.proj.weight"].reshape(HIDDEN, IN_CH * PATCH * PATCH))
     w.patch_b = f32("x_embedder.proj.bias")
-    w.t_fc1_w = f32("t_embedder.mlp.0.weight")
+    w.t_fc1_w = bf16(sd["t_embedder.mlp.0.weight"])
     w.t_fc1_b = f32("t_embedder.mlp.0.bias")
-    w.t_fc2_w = f32("t_embedder.mlp.2.weight")
+    # second timestep linear and the action linear share one GEMM along K; the action
+    # bias rides in column 1049 against an input that is 1 only when actions are given
+    w2 = torch.zeros(HIDDEN, HIDDEN + 64)
+    w2[:, :HIDDEN] = sd["t_embedder.mlp.2.weight"].float()
+    w2[:, HIDDEN:HIDDEN + ACTION_DIM] = sd["external_cond.weight"].float()
+    w2[:, HIDDEN + ACTION_DIM] = sd["external_cond.bias"].float()
+    w.t_fc2_w = bf16(w2)
     w.t_fc2_b = f32("t_embedder.mlp.2.bias")
-    w.act_w = f32("external_cond.weight")
-    w.act_b = f32("external_cond.bias")
     ada_w, ada_b = [], []
     for i in range(depth):
         for a in ("s", "t"):

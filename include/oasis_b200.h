@@ -73,14 +73,17 @@ typedef struct {
 
 typedef struct {
   int depth;                 /* number of SpatioTemporal blocks (16)            */
-  const float* patch_w;      /* fp32 [1024][16*2*2]: Conv2d(16,1024,2,2) weight */
+  const void*  patch_w;      /* bf16 [1024][64]: Conv2d(16,1024,2,2) weight as
+                                [out][c*4 + pi*2 + qi]                          */
   const float* patch_b;      /* fp32 [1024]                                     */
-  const float* t_fc1_w;      /* fp32 [1024][256] timestep MLP                   */
+  const void*  t_fc1_w;      /* bf16 [1024][256] timestep MLP first linear      */
   const float* t_fc1_b;      /* fp32 [1024]                                     */
-  const float* t_fc2_w;      /* fp32 [1024][1024]                               */
+  /* timestep MLP second linear with the external_cond (action) linear appended
+   * along K: columns 0..1023 = t_embedder.mlp.2.weight, 1024..1048 =
+   * external_cond.weight, 1049 = external_cond.bias (multiplied by an input of 1
+   * when actions are given, 0 otherwise), 1050..1087 = 0; bias = mlp.2.bias     */
+  const void*  t_fc2_w;      /* bf16 [1024][1088]                               */
   const float* t_fc2_b;      /* fp32 [1024]                                     */
-  const float* act_w;        /* fp32 [1024][25] external_cond                   */
-  const float* act_b;        /* fp32 [1024]                                     */
   /* All adaLN modulation linears stacked row-wise: sub-block j = 2*i (spatial)
    * or 2*i+1 (temporal) owns rows [j*6144, (j+1)*6144) in chunk order
    * shift_msa, scale_msa, gate_msa, shift_mlp, scale_mlp, gate_mlp; the final

@@ -25,7 +25,7 @@ def rel_l2(a, b):
 # ----------------------------------------------------------------- GEMM (tcgen05)
 
 @pytest.mark.parametrize("M,N,K", [(128, 256, 64), (200, 512, 1024), (576, 3072, 1024),
-                                   (1000, 64, 4096), (4608, 1024, 1024), (130, 96, 128)])
+                                   (1000, 64, 4096), (4608, 1024, 1024), (130, 192, 128)])
 def test_gemm_bf16_store(pkg, cuda, M, N, K):
     g = torch.Generator(device=cuda).manual_seed(M + N + K)
     A = torch.randn(M, K, device=cuda, generator=g).bfloat16()

@@ -62,7 +62,7 @@ def test_workspace_size_formula(pkg):
     L = pkg.lib()
     ws = L.oasis_plan_workspace_size(1, 32, 16)
     M = 32 * 144
-    act = M * 1024 * 4 + M * 1024 * 2 + M * 3072 * 2 + M * 1024 * 2 + M * 4096 * 2 + M * 64 * 4
+    act = M * 1024 * 4 + M * 1024 * 2 + M * 3072 * 2 + M * 1024 * 2 + M * 4096 * 2 + M * 64 * 2
     mod = 32 * (32 * 6144 + 2048) * 4
     assert act + mod <= ws <= act + mod + 2 * 1024 * 1024
     assert L.oasis_plan_workspace_size(0, 32, 16) == 0
