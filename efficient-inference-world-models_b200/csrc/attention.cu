@@ -22,6 +22,8 @@ constexpr int kSpSmem = 3 * OASIS_TOKENS * kSmemStride * 2;  // 62,208 B
 __global__ void __launch_bounds__(kSpThreads, 2)
     attn_spatial_kernel(const __nv_bfloat16* __restrict__ qkv, __nv_bfloat16* __restrict__ out,
                         float scale_log2) {
+  pdl_trigger();
+  pdl_wait();
   extern __shared__ __align__(16) uint8_t sm_sp[];
   __nv_bfloat16* sQ = reinterpret_cast<__nv_bfloat16*>(sm_sp);
   const int f = blockIdx.x;
@@ -149,12 +151,20 @@ constexpr int kTpRowsPerMat = 32;
 constexpr int kTpWarpSmem = 3 * kTpRowsPerMat * kSmemStride;  // bf16 elements
 constexpr int kTpSmem = kTpWarps * kTpWarpSmem * 2;             // 55,296 B
 
+// two e4m3fn codes -> floats (hardware conversion to f16 is exact, NaN codes stay NaN)
+__device__ __forceinline__ float2 e4m3x2_to_float2(uint32_t two_codes) {
+  uint32_t h;
+  const uint16_t v = static_cast<uint16_t>(two_codes);
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h) : "h"(v));
+  return __half22float2(*reinterpret_cast<const __half2*>(&h));
+}
+
+// 8 codes -> 8 bf16, dequantised exactly as q.to(bf16) * scale in bf16 (one rounding)
 __device__ __forceinline__ uint4 dequant_fp8x8(uint32_t lo, uint32_t hi, float scale) {
-  // dequantise exactly as q.to(bf16) * scale in bf16 (one rounding)
-  return make_uint4(pack_bf16x2(e4m3_to_float(lo & 0xFF) * scale, e4m3_to_float((lo >> 8) & 0xFF) * scale),
-                    pack_bf16x2(e4m3_to_float((lo >> 16) & 0xFF) * scale, e4m3_to_float(lo >> 24) * scale),
-                    pack_bf16x2(e4m3_to_float(hi & 0xFF) * scale, e4m3_to_float((hi >> 8) & 0xFF) * scale),
-                    pack_bf16x2(e4m3_to_float((hi >> 16) & 0xFF) * scale, e4m3_to_float(hi >> 24) * scale));
+  const float2 a = e4m3x2_to_float2(lo), b = e4m3x2_to_float2(lo >> 16);
+  const float2 c = e4m3x2_to_float2(hi), d = e4m3x2_to_float2(hi >> 16);
+  return make_uint4(pack_bf16x2(a.x * scale, a.y * scale), pack_bf16x2(b.x * scale, b.y * scale),
+                    pack_bf16x2(c.x * scale, c.y * scale), pack_bf16x2(d.x * scale, d.y * scale));
 }
 
 __device__ __forceinline__ uint4 dequant_int4x8(uint32_t w, float scale, float zero) {
@@ -173,6 +183,8 @@ __global__ void __launch_bounds__(kTpWarps * 32)
     attn_temporal_kernel(const __nv_bfloat16* __restrict__ qkv, __nv_bfloat16* __restrict__ out,
                          KvView kv, int layer, int q_frames, int q_pos0, int n_past, int n_kv,
                          float scale_log2) {
+  pdl_trigger();
+  pdl_wait();
   extern __shared__ __align__(16) uint8_t sm_tp[];
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -202,41 +214,45 @@ __global__ void __launch_bounds__(kTpWarps * 32)
                                which * OASIS_HIDDEN + hg * 256 + c * 8;
     cp_async16(mat(c >> 3, which) + (n_past + j) * kSmemStride + (c & 7) * 8, src);
   }
-  // cached rows: bf16 by cp.async, FP8 / INT4 dequantised through registers
+  // cached rows, one loop per storage kind so every thread has a unit of work:
+  //   bf16: 32 x 16-byte chunks per (slot, K|V) row of 4 heads (cp.async)
+  //   FP8 : 16 x 16-byte chunks of codes, dequantised through registers
+  //   INT4:  8 x 16-byte chunks of packed codes, dequantised through registers
   for (int i = tid; i < n_past * 64; i += kTpWarps * 32) {
     const int s = i >> 6, which = 1 + ((i >> 5) & 1), u = i & 31;
+    if (kv.kind[s] != OASIS_KV_BF16) continue;
+    const long long slot = (static_cast<long long>(b) * kv.layers + layer) * kv.n_bf16 + kv.index[s];
+    const __nv_bfloat16* src = (which == 2 ? kv.v_bf16 : kv.k_bf16) + (slot * OASIS_TOKENS + p) * OASIS_HIDDEN + hg * 256 + u * 8;
+    cp_async16(mat(u >> 3, which) + s * kSmemStride + (u & 7) * 8, src);
+  }
+  for (int i = tid; i < n_past * 32; i += kTpWarps * 32) {
+    const int s = i >> 5, which = 1 + ((i >> 4) & 1), u = i & 15;
+    if (kv.kind[s] != OASIS_KV_FP8) continue;
     const bool is_v = which == 2;
-    const int kind = kv.kind[s], idx = kv.index[s];
-    if (kind == OASIS_KV_BF16) {
-      const long long slot = (static_cast<long long>(b) * kv.layers + layer) * kv.n_bf16 + idx;
-      const __nv_bfloat16* src = (is_v ? kv.v_bf16 : kv.k_bf16) + (slot * OASIS_TOKENS + p) * OASIS_HIDDEN + hg * 256 + u * 8;
-      cp_async16(mat(u >> 3, which) + s * kSmemStride + (u & 7) * 8, src);
-    } else if (kind == OASIS_KV_FP8) {
-      if (u < 16) {  // 16 chunks of 16 codes cover the 4 heads
-        const long long slot = (static_cast<long long>(b) * kv.layers + layer) * kv.n_fp8 + idx;
-        const uint4 w = *reinterpret_cast<const uint4*>((is_v ? kv.v_fp8 : kv.k_fp8) +
-                                                        (slot * OASIS_TOKENS + p) * OASIS_HIDDEN + hg * 256 + u * 16);
-        const int hh = u >> 2;
-        const float scale = __bfloat162float((is_v ? kv.v_fp8_scale : kv.k_fp8_scale)[slot * OASIS_HEADS + hg * 4 + hh]);
-        __nv_bfloat16* d = mat(hh, which) + s * kSmemStride + (u & 3) * 16;
-        reinterpret_cast<uint4*>(d)[0] = dequant_fp8x8(w.x, w.y, scale);
-        reinterpret_cast<uint4*>(d)[1] = dequant_fp8x8(w.z, w.w, scale);
-      }
-    } else {
-      if (u < 8) {  // 8 chunks of 32 codes cover the 4 heads
-        const long long slot = (static_cast<long long>(b) * kv.layers + layer) * kv.n_int4 + idx;
-        const int hh = u >> 1;
-        const long long grp = (slot * OASIS_TOKENS + p) * OASIS_HEADS + hg * 4 + hh;
-        const uint4 w = *reinterpret_cast<const uint4*>((is_v ? kv.v_int4 : kv.k_int4) + grp * 32 + (u & 1) * 16);
-        const float scale = __half2float((is_v ? kv.v_i4_scale : kv.k_i4_scale)[grp]);
-        const float zero = __half2float((is_v ? kv.v_i4_zero : kv.k_i4_zero)[grp]);
-        uint4* d = reinterpret_cast<uint4*>(mat(hh, which) + s * kSmemStride + (u & 1) * 32);
-        d[0] = dequant_int4x8(w.x, scale, zero);
-        d[1] = dequant_int4x8(w.y, scale, zero);
-        d[2] = dequant_int4x8(w.z, scale, zero);
-        d[3] = dequant_int4x8(w.w, scale, zero);
-      }
-    }
+    const long long slot = (static_cast<long long>(b) * kv.layers + layer) * kv.n_fp8 + kv.index[s];
+    const uint4 w = *reinterpret_cast<const uint4*>((is_v ? kv.v_fp8 : kv.k_fp8) +
+                                                    (slot * OASIS_TOKENS + p) * OASIS_HIDDEN + hg * 256 + u * 16);
+    const int hh = u >> 2;
+    const float scale = __bfloat162float((is_v ? kv.v_fp8_scale : kv.k_fp8_scale)[slot * OASIS_HEADS + hg * 4 + hh]);
+    uint4* d = reinterpret_cast<uint4*>(mat(hh, which) + s * kSmemStride + (u & 3) * 16);
+    d[0] = dequant_fp8x8(w.x, w.y, scale);
+    d[1] = dequant_fp8x8(w.z, w.w, scale);
+  }
+  for (int i = tid; i < n_past * 16; i += kTpWarps * 32) {
+    const int s = i >> 4, which = 1 + ((i >> 3) & 1), u = i & 7;
+    if (kv.kind[s] != OASIS_KV_INT4) continue;
+    const bool is_v = which == 2;
+    const long long slot = (static_cast<long long>(b) * kv.layers + layer) * kv.n_int4 + kv.index[s];
+    const int hh = u >> 1;
+    const long long grp = (slot * OASIS_TOKENS + p) * OASIS_HEADS + hg * 4 + hh;
+    const uint4 w = *reinterpret_cast<const uint4*>((is_v ? kv.v_int4 : kv.k_int4) + grp * 32 + (u & 1) * 16);
+    const float scale = __half2float((is_v ? kv.v_i4_scale : kv.k_i4_scale)[grp]);
+    const float zero = __half2float((is_v ? kv.v_i4_zero : kv.k_i4_zero)[grp]);
+    uint4* d = reinterpret_cast<uint4*>(mat(hh, which) + s * kSmemStride + (u & 1) * 32);
+    d[0] = dequant_int4x8(w.x, scale, zero);
+    d[1] = dequant_int4x8(w.y, scale, zero);
+    d[2] = dequant_int4x8(w.z, scale, zero);
+    d[3] = dequant_int4x8(w.w, scale, zero);
   }
   // zero the padding rows the MMAs read (keeps masked products finite)
   for (int i = tid; i < kTpWarps * 3 * 32 * 8; i += kTpWarps * 32) {
@@ -364,9 +380,10 @@ int launch_attn_spatial(const void* qkv, void* out, int frames, cudaStream_t str
     configured = true;
   }
   dim3 grid(frames, OASIS_HEADS);
-  attn_spatial_kernel<<<grid, kSpThreads, kSpSmem, stream>>>(
-      static_cast<const __nv_bfloat16*>(qkv), static_cast<__nv_bfloat16*>(out), kScaleLog2);
-  OASIS_CHECK_LAUNCH("attn_spatial_kernel");
+  cudaError_t e = launch_pdl(attn_spatial_kernel, grid, dim3(kSpThreads), kSpSmem, stream,
+                             static_cast<const __nv_bfloat16*>(qkv), static_cast<__nv_bfloat16*>(out),
+                             kScaleLog2);
+  if (e != cudaSuccess) return cuda_status(e, "attn_spatial_kernel");
   return OASIS_OK;
 }
 
@@ -416,10 +433,10 @@ int launch_attn_temporal(const void* qkv, const KvView& kv, int layer, void* out
     configured = true;
   }
   dim3 grid(OASIS_TOKENS, OASIS_HEADS / kTpWarps, batch);
-  attn_temporal_kernel<<<grid, kTpWarps * 32, kTpSmem, stream>>>(
-      static_cast<const __nv_bfloat16*>(qkv), static_cast<__nv_bfloat16*>(out), kv, layer, q_frames,
-      q_pos0, n_past, n_kv, kScaleLog2);
-  OASIS_CHECK_LAUNCH("attn_temporal_kernel");
+  cudaError_t e = launch_pdl(attn_temporal_kernel, grid, dim3(kTpWarps * 32), kTpSmem, stream,
+                             static_cast<const __nv_bfloat16*>(qkv), static_cast<__nv_bfloat16*>(out),
+                             kv, layer, q_frames, q_pos0, n_past, n_kv, kScaleLog2);
+  if (e != cudaSuccess) return cuda_status(e, "attn_temporal_kernel");
   return OASIS_OK;
 }
 

@@ -8,61 +8,84 @@ namespace oasis {
 // ----------------------------------------------------------------------------------
 // LayerNorm (eps 1e-6, no affine) + modulate: out = bf16(LN(x) * (1 + scale[f]) + shift[f])
 // x fp32 [M][1024]; frame f = row / rows_per_frame; shift/scale rows of the adaLN table.
-// One warp per row: lane holds 8 float4 (columns lane*4 + i*128).
+// A CTA takes 16 rows of one frame (4 warps x 4 rows): each warp loads its frame's
+// shift/scale once into registers and reuses them for its rows; lane holds columns
+// lane*4 + i*128.
 // ----------------------------------------------------------------------------------
-__global__ void __launch_bounds__(256)
+constexpr int kLnRowsPerWarp = 4;
+constexpr int kLnWarps = 4;
+constexpr int kLnRowsPerCta = kLnRowsPerWarp * kLnWarps;
+
+__global__ void __launch_bounds__(kLnWarps * 32)
     ln_modulate_kernel(const float* __restrict__ x, const float* __restrict__ shift,
                        const float* __restrict__ scale, long long mod_ld,
                        __nv_bfloat16* __restrict__ out, int M, int rows_per_frame) {
-  const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+  pdl_trigger();
+  pdl_wait();
+  const int chunks = (rows_per_frame + kLnRowsPerCta - 1) / kLnRowsPerCta;
+  const long long f = blockIdx.x / chunks;
+  const int row0 = static_cast<int>(f * rows_per_frame) + (blockIdx.x % chunks) * kLnRowsPerCta +
+                   (threadIdx.x >> 5) * kLnRowsPerWarp;
+  const int row_end = min(static_cast<int>((f + 1) * rows_per_frame), M);
   const int lane = threadIdx.x & 31;
-  if (row >= M) return;
-  const float4* xr = reinterpret_cast<const float4*>(x + static_cast<long long>(row) * OASIS_HIDDEN);
-  const long long f = row / rows_per_frame;
+  if (row0 >= row_end) return;
   const float4* sh = reinterpret_cast<const float4*>(shift + f * mod_ld);
   const float4* sc = reinterpret_cast<const float4*>(scale + f * mod_ld);
-  float4 v[8], a4[8], s4[8];
+  float4 v[kLnRowsPerWarp][8];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) v[i] = xr[lane + 32 * i];
+  for (int r = 0; r < kLnRowsPerWarp; ++r) {
+    if (row0 + r < row_end) {
+      const float4* xr = reinterpret_cast<const float4*>(x + static_cast<long long>(row0 + r) * OASIS_HIDDEN);
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {  // modulation rows issued before the reductions
+      for (int i = 0; i < 8; ++i) v[r][i] = xr[lane + 32 * i];
+    }
+  }
+  float4 a4[8], s4[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
     a4[i] = sh[lane + 32 * i];
     s4[i] = sc[lane + 32 * i];
   }
-  float sum = 0.0f;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) sum += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+  for (int r = 0; r < kLnRowsPerWarp; ++r) {
+    if (row0 + r >= row_end) break;
+    float sum = 0.0f;
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-  const float mean = sum * (1.0f / OASIS_HIDDEN);
-  float sq = 0.0f;
+    for (int i = 0; i < 8; ++i) sum += (v[r][i].x + v[r][i].y) + (v[r][i].z + v[r][i].w);
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const float a = v[i].x - mean, b = v[i].y - mean, c = v[i].z - mean, d = v[i].w - mean;
-    sq += (a * a + b * b) + (c * c + d * d);
-  }
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    const float mean = sum * (1.0f / OASIS_HIDDEN);
+    float sq = 0.0f;
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
-  const float rstd = rsqrtf(sq * (1.0f / OASIS_HIDDEN) + 1e-6f);
-  uint2* o2 = reinterpret_cast<uint2*>(out + static_cast<long long>(row) * OASIS_HIDDEN);
+    for (int i = 0; i < 8; ++i) {
+      const float a = v[r][i].x - mean, b = v[r][i].y - mean, c = v[r][i].z - mean, d = v[r][i].w - mean;
+      sq += (a * a + b * b) + (c * c + d * d);
+    }
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const float4 a = a4[i];
-    const float4 s = s4[i];
-    const float y0 = (v[i].x - mean) * rstd * (1.0f + s.x) + a.x;
-    const float y1 = (v[i].y - mean) * rstd * (1.0f + s.y) + a.y;
-    const float y2 = (v[i].z - mean) * rstd * (1.0f + s.z) + a.z;
-    const float y3 = (v[i].w - mean) * rstd * (1.0f + s.w) + a.w;
-    o2[lane + 32 * i] = make_uint2(pack_bf16x2(y0, y1), pack_bf16x2(y2, y3));
+    for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+    const float rstd = rsqrtf(sq * (1.0f / OASIS_HIDDEN) + 1e-6f);
+    uint2* o2 = reinterpret_cast<uint2*>(out + static_cast<long long>(row0 + r) * OASIS_HIDDEN);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float4 a = a4[i];
+      const float4 s = s4[i];
+      const float y0 = (v[r][i].x - mean) * rstd * (1.0f + s.x) + a.x;
+      const float y1 = (v[r][i].y - mean) * rstd * (1.0f + s.y) + a.y;
+      const float y2 = (v[r][i].z - mean) * rstd * (1.0f + s.z) + a.z;
+      const float y3 = (v[r][i].w - mean) * rstd * (1.0f + s.w) + a.w;
+      o2[lane + 32 * i] = make_uint2(pack_bf16x2(y0, y1), pack_bf16x2(y2, y3));
+    }
   }
 }
 
 int launch_ln_modulate(const float* x, const float* shift, const float* scale, long long mod_ld,
                        void* out, int M, int rows_per_frame, cudaStream_t stream) {
-  ln_modulate_kernel<<<(M + 7) / 8, 256, 0, stream>>>(x, shift, scale, mod_ld,
-                                                      static_cast<__nv_bfloat16*>(out), M,
-                                                      rows_per_frame);
-  OASIS_CHECK_LAUNCH("ln_modulate_kernel");
+  const int frames = (M + rows_per_frame - 1) / rows_per_frame;
+  const int chunks = (rows_per_frame + kLnRowsPerCta - 1) / kLnRowsPerCta;
+  cudaError_t e = launch_pdl(ln_modulate_kernel, dim3(frames * chunks), dim3(kLnWarps * 32), 0, stream,
+                             x, shift, scale, mod_ld, static_cast<__nv_bfloat16*>(out), M,
+                             rows_per_frame);
+  if (e != cudaSuccess) return cuda_status(e, "ln_modulate_kernel");
   return OASIS_OK;
 }
 
@@ -77,6 +100,8 @@ int launch_ln_modulate(const float* x, const float* shift, const float* scale, l
 __global__ void temb_prep_kernel(const int64_t* __restrict__ t, const float* __restrict__ act,
                                  __nv_bfloat16* __restrict__ emb, __nv_bfloat16* __restrict__ h1a,
                                  int F) {
+  pdl_trigger();
+  pdl_wait();
   const int f = blockIdx.x;
   const int i = threadIdx.x;  // 128 threads
   if (f >= F) return;
@@ -95,9 +120,9 @@ __global__ void temb_prep_kernel(const int64_t* __restrict__ t, const float* __r
 
 int launch_temb_prep(const int64_t* t, const float* act, void* emb, void* h1a, int F,
                      cudaStream_t stream) {
-  temb_prep_kernel<<<F, 128, 0, stream>>>(t, act, static_cast<__nv_bfloat16*>(emb),
-                                          static_cast<__nv_bfloat16*>(h1a), F);
-  OASIS_CHECK_LAUNCH("temb_prep_kernel");
+  cudaError_t e = launch_pdl(temb_prep_kernel, dim3(F), dim3(128), 0, stream, t, act,
+                             static_cast<__nv_bfloat16*>(emb), static_cast<__nv_bfloat16*>(h1a), F);
+  if (e != cudaSuccess) return cuda_status(e, "temb_prep_kernel");
   return OASIS_OK;
 }
 
@@ -106,6 +131,8 @@ int launch_temb_prep(const int64_t* t, const float* act, void* emb, void* h1a, i
 // (token, channel) writes its 4 patch values.
 __global__ void patch_im2col_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ cols,
                                     int F) {
+  pdl_trigger();
+  pdl_wait();
   const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   const long long total = static_cast<long long>(F) * OASIS_TOKENS * 16;
   if (i >= total) return;
@@ -125,9 +152,9 @@ __global__ void patch_im2col_kernel(const float* __restrict__ x, __nv_bfloat16* 
 
 int launch_patch_im2col(const float* x, void* cols, int F, cudaStream_t stream) {
   const long long total = static_cast<long long>(F) * OASIS_TOKENS * 16;
-  patch_im2col_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, stream>>>(
-      x, static_cast<__nv_bfloat16*>(cols), F);
-  OASIS_CHECK_LAUNCH("patch_im2col_kernel");
+  cudaError_t e = launch_pdl(patch_im2col_kernel, dim3(static_cast<unsigned>((total + 255) / 256)),
+                             dim3(256), 0, stream, x, static_cast<__nv_bfloat16*>(cols), F);
+  if (e != cudaSuccess) return cuda_status(e, "patch_im2col_kernel");
   return OASIS_OK;
 }
 
@@ -139,6 +166,8 @@ int launch_patch_im2col(const float* x, void* cols, int F, cudaStream_t stream) 
 __global__ void dpmpp2m_kernel(float* __restrict__ x, const float* __restrict__ v,
                                float* __restrict__ eps_prev, int n, long long xs, long long vs,
                                float a, float b, float c, float d, int first) {
+  pdl_trigger();
+  pdl_wait();
   const int sess = blockIdx.y;
   const int i = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
   if (i >= n) return;
@@ -167,6 +196,8 @@ __global__ void ab_update_kernel(const float* __restrict__ x, const float* __res
                                  const float* __restrict__ d1, const float* __restrict__ d2,
                                  float* __restrict__ out, long long n, float h, float c0, float c1,
                                  float c2) {
+  pdl_trigger();
+  pdl_wait();
   const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= n) return;
   float acc = c0 * d0[i];
@@ -189,8 +220,9 @@ extern "C" int oasis_dpmpp2m_update(float* x, const float* v, float* eps_prev, i
   if (batch > 65535) return fail(OASIS_ERR_UNSUPPORTED, "oasis_dpmpp2m_update: batch too large");
   const float a = sqrtf(ab_t), b = sqrtf(1.0f - ab_t), c = sqrtf(ab_next), d = sqrtf(1.0f - ab_next);
   dim3 grid((n / 4 + 255) / 256, batch);
-  dpmpp2m_kernel<<<grid, 256, 0, stream>>>(x, v, eps_prev, n, x_stride, v_stride, a, b, c, d, first);
-  OASIS_CHECK_LAUNCH("dpmpp2m_kernel");
+  cudaError_t e = launch_pdl(dpmpp2m_kernel, grid, dim3(256), 0, stream, x, v, eps_prev, n, x_stride,
+                             v_stride, a, b, c, d, first);
+  if (e != cudaSuccess) return cuda_status(e, "dpmpp2m_kernel");
   return OASIS_OK;
 }
 
@@ -201,8 +233,9 @@ extern "C" int oasis_ab_update(const float* x, const float* d0, const float* d1,
   if (!x || !d0 || !out || n <= 0) return fail(OASIS_ERR_INVALID_ARG, "oasis_ab_update: bad args");
   if ((c1 != 0.0f && !d1) || (c2 != 0.0f && !d2))
     return fail(OASIS_ERR_INVALID_ARG, "oasis_ab_update: missing history for a non-zero coefficient");
-  ab_update_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, stream>>>(
-      x, d0, c1 != 0.0f ? d1 : nullptr, c2 != 0.0f ? d2 : nullptr, out, n, h, c0, c1, c2);
-  OASIS_CHECK_LAUNCH("ab_update_kernel");
+  cudaError_t e = launch_pdl(ab_update_kernel, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256),
+                             0, stream, x, d0, c1 != 0.0f ? d1 : nullptr, c2 != 0.0f ? d2 : nullptr,
+                             out, n, h, c0, c1, c2);
+  if (e != cudaSuccess) return cuda_status(e, "ab_update_kernel");
   return OASIS_OK;
 }

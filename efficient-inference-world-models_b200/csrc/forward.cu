@@ -366,6 +366,11 @@ extern "C" int oasis_plan_create(const oasis_dit_weights_t* w, int batch, int fr
     delete p;
     return st;
   }
+  // weights are the B operand of these GEMMs (swap-AB GEMMs read activations as B)
+  p->patch.b_is_weight = true;
+  p->fin.b_is_weight = true;
+  for (int j = 0; j < 2 * w->depth; ++j)
+    p->qkv[j].b_is_weight = p->out[j].b_is_weight = p->fc1[j].b_is_weight = p->fc2[j].b_is_weight = true;
   *out = p;
   return OASIS_OK;
 }

@@ -61,9 +61,10 @@ int launch_one(const GemmOperands& g, const EpiParams& ep, cudaStream_t stream, 
   if (tiles < grid) grid = tiles;
   if (epi_uses_tma(EPI) && !g.has_d)
     return fail(OASIS_ERR_INVALID_ARG, "GEMM epilogue needs an output tensor map");
-  gemm_tcgen05_kernel<BN, EPI><<<grid, kGemmThreads, S::kSmemBytes, stream>>>(g.a, g.b, g.d, g.M,
-                                                                              g.N, g.K, ep);
-  OASIS_CHECK_LAUNCH("gemm_tcgen05_kernel");
+  cudaError_t e = launch_pdl(gemm_tcgen05_kernel<BN, EPI>, dim3(grid), dim3(kGemmThreads),
+                             S::kSmemBytes, stream, g.a, g.b, g.d, g.M, g.N, g.K,
+                             g.b_is_weight ? 1 : 0, ep);
+  if (e != cudaSuccess) return cuda_status(e, "gemm_tcgen05_kernel");
   return OASIS_OK;
 }
 
@@ -109,6 +110,7 @@ int make_gemm_operands(GemmOperands* g, const void* A, long long lda, const void
   g->K = K;
   g->bn = bn;
   g->has_d = false;
+  g->b_is_weight = false;
   return OASIS_OK;
 }
 

@@ -5,10 +5,11 @@
 // One persistent CTA per SM, 6 warps:
 //   warp 0      TMA producer: A tile 128x64 and B tile BNx64 per stage (128-byte swizzle)
 //   warp 1      TMEM allocator + single-thread tcgen05.mma issuer (M=128, N=BN, K=16)
-//   warps 2..5  epilogue: tcgen05.ld of the fp32 accumulator (one TMEM lane quarter
-//               each), fused math in registers, then a 128B-swizzled shared-memory
-//               tile and a TMA tensor store (bf16 outputs) or TMA reduce-add (the fp32
-//               residual update), so global traffic leaves in full lines asynchronously.
+//   warps 2..9  epilogue, two warps per TMEM lane quarter splitting the columns:
+//               tcgen05.ld of the fp32 accumulator, fused math in registers, then a
+//               128B-swizzled shared-memory tile and a TMA tensor store (bf16 outputs) or
+//               TMA reduce-add (the fp32 residual update), so global traffic leaves in
+//               full lines asynchronously.
 // The accumulator is double-buffered in TMEM (2 x BN columns) so the epilogue of one
 // tile overlaps the main loop of the next; TMEM is released as soon as a tile's last
 // tcgen05.ld has completed.
@@ -51,7 +52,8 @@ struct EpiParams {
 
 constexpr int kGemmBM = 128;
 constexpr int kGemmBK = 64;
-constexpr int kGemmThreads = 192;
+constexpr int kGemmThreads = 320;
+constexpr int kEpiWarps = 8;
 constexpr int kEpiBufBytes = 32 * 128;  // 32 rows x 128 B: one TMA store box
 
 template <int BN>
@@ -62,7 +64,7 @@ struct GemmShape {
   static constexpr int kStages = (192 * 1024) / kStageBytes > 8 ? 8 : (192 * 1024) / kStageBytes;
   static constexpr int kTmemCols = 2 * BN;  // power of two >= 64 for BN in {32..256}
   static constexpr int kBarBytes = 1024;
-  static constexpr int kEpiBytes = 4 * 2 * kEpiBufBytes;  // 4 warps x double buffer
+  static constexpr int kEpiBytes = kEpiWarps * kEpiBufBytes;  // one TMA box per epilogue warp
   static constexpr int kSmemBytes =
       kStages * kStageBytes + kEpiBytes + kBarBytes + 1024;  // +1 KB alignment slack
 };
@@ -209,7 +211,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA,
                         const __grid_constant__ CUtensorMap tmB,
                         const __grid_constant__ CUtensorMap tmD, int M, int N, int K,
-                        EpiParams ep) {
+                        int prefetch_b, EpiParams ep) {
   using S = GemmShape<BN>;
   constexpr int STAGES = S::kStages;
   extern __shared__ uint8_t smem_raw[];
@@ -224,6 +226,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
+  pdl_trigger();
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int num_m = (M + kGemmBM - 1) / kGemmBM;
@@ -238,7 +241,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull_bar[a], 1);
-      mbar_init(&tempty_bar[a], 128);
+      mbar_init(&tempty_bar[a], kEpiWarps * 32);
     }
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
@@ -261,16 +264,33 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       int last_phase[8];
 #pragma unroll
       for (int s = 0; s < 8; ++s) last_phase[s] = -1;
+      // When B is a weight (never written by an earlier kernel) the B tiles of the first
+      // stages are fetched before waiting on the previous kernel, the A tiles after.
+      int pre = 0;
+      if (prefetch_b && static_cast<int>(blockIdx.x) < num_tiles) {
+        const int n0 = (static_cast<int>(blockIdx.x) / num_m) * BN;
+        pre = num_kb < STAGES ? num_kb : STAGES;
+        for (int kb = 0; kb < pre; ++kb) {
+          mbar_arrive_expect_tx(&full_bar[kb], S::kStageBytes);
+          tma_load_2d(smem + kb * S::kStageBytes + S::kABytes, &tmB, &full_bar[kb], kb * kGemmBK, n0);
+        }
+      }
+      pdl_wait();
       for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
         const int m0 = (tile % num_m) * kGemmBM;
         const int n0 = (tile / num_m) * BN;
         for (int kb = 0; kb < num_kb; ++kb) {
-          if (!mbar_wait(&empty_bar[stage], phase ^ 1)) { *abort_flag = 1; break; }
           uint8_t* sa = smem + stage * S::kStageBytes;
           uint8_t* sb = sa + S::kABytes;
-          mbar_arrive_expect_tx(&full_bar[stage], S::kStageBytes);
-          tma_load_2d(sa, &tmA, &full_bar[stage], kb * kGemmBK, m0);
-          tma_load_2d(sb, &tmB, &full_bar[stage], kb * kGemmBK, n0);
+          if (pre > 0) {  // stage already armed and its B tile in flight
+            --pre;
+            tma_load_2d(sa, &tmA, &full_bar[stage], kb * kGemmBK, m0);
+          } else {
+            if (!mbar_wait(&empty_bar[stage], phase ^ 1)) { *abort_flag = 1; break; }
+            mbar_arrive_expect_tx(&full_bar[stage], S::kStageBytes);
+            tma_load_2d(sa, &tmA, &full_bar[stage], kb * kGemmBK, m0);
+            tma_load_2d(sb, &tmB, &full_bar[stage], kb * kGemmBK, n0);
+          }
           last_phase[stage] = static_cast<int>(phase);
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
@@ -281,7 +301,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      // ---------------- MMA issuer ----------------
+      // ---------------- MMA issuer (reads only shared memory and TMEM) ----------------
       constexpr uint32_t idesc = umma_idesc_bf16(kGemmBM, BN);
       int stage = 0;
       uint32_t phase = 0;
@@ -314,10 +334,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_wait(drain_bar, 0);
     }
   } else {
-    // ---------------- epilogue warps 2..5 ----------------
-    const int quarter = warp & 3;  // TMEM lanes this warp may access
-    uint8_t* bufs = epi_smem + quarter * 2 * kEpiBufBytes;
-    int nbuf = 0;  // TMA stores issued by this warp (round-robin over 2 buffers)
+    // ---------------- epilogue warps 2..9 ----------------
+    pdl_wait();  // bias/gate/rope tables and the output buffers belong to earlier kernels
+    const int quarter = warp & 3;        // TMEM lanes this warp may access
+    const int half = (warp - 2) >> 2;    // which interleaved column blocks it owns
+    uint8_t* buf = epi_smem + (warp - 2) * kEpiBufBytes;
+    int nbuf = 0;  // TMA stores issued by this warp
     int it = 0;
     for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x, ++it) {
       const int m0 = (tile % num_m) * kGemmBM;
@@ -330,68 +352,64 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                              static_cast<uint32_t>(acc * BN);
       const int m_row = m0 + quarter * 32 + lane;  // this thread's row
       const bool rows_live = m0 + quarter * 32 < M;
-      if (epi_uses_tma(EPI)) {
-        // bf16: 64 columns per box (2 TMEM loads); fp32: 32 columns per box
-        constexpr int COLS = epi_out_f32(EPI) ? 32 : 64;
+      // bf16 TMA boxes: 64 columns (2 TMEM loads); fp32 boxes and row epilogues: 32
+      constexpr int COLS = (epi_uses_tma(EPI) && !epi_out_f32(EPI)) ? 64 : 32;
+      constexpr int NBLK = BN / COLS;
+      const int last_blk = (NBLK - 1 - half) >= 0 ? ((NBLK - 1 - half) / 2) * 2 + half : -1;
+      if (last_blk < 0) {  // owns no columns of this tile
+        tc_fence_before();
+        mbar_arrive(&tempty_bar[acc]);
+        continue;
+      }
 #pragma unroll 1
-        for (int blk = 0; blk < BN / COLS; ++blk) {
-          const int nb = n0 + blk * COLS;
-          float v[32], w[32];
-          tmem_ld32(taddr + blk * COLS, v);
-          if (COLS == 64) tmem_ld32(taddr + blk * COLS + 32, w);
-          if (blk == BN / COLS - 1) {  // accumulator fully read: hand TMEM back to the MMA
-            tc_fence_before();
-            mbar_arrive(&tempty_bar[acc]);
-          }
-          if (!rows_live || nb >= N) continue;
-          uint8_t* buf = bufs + (nbuf & 1) * kEpiBufBytes;
-          if (nbuf >= 2) {  // the store issued from this buffer two boxes ago must have read it
-            if (lane == 0) bulk_wait_read<1>();
-            __syncwarp();
-          }
-          epilogue_math<EPI>(ep, m_row, nb, v);
-          if (COLS == 64) {
-            epilogue_math<EPI>(ep, m_row, nb + 32, w);
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-              st_swizzled(buf, lane, c, make_uint4(pack_bf16x2(v[8 * c + 0], v[8 * c + 1]),
-                                                   pack_bf16x2(v[8 * c + 2], v[8 * c + 3]),
-                                                   pack_bf16x2(v[8 * c + 4], v[8 * c + 5]),
-                                                   pack_bf16x2(v[8 * c + 6], v[8 * c + 7])));
-              st_swizzled(buf, lane, 4 + c, make_uint4(pack_bf16x2(w[8 * c + 0], w[8 * c + 1]),
-                                                       pack_bf16x2(w[8 * c + 2], w[8 * c + 3]),
-                                                       pack_bf16x2(w[8 * c + 4], w[8 * c + 5]),
-                                                       pack_bf16x2(w[8 * c + 6], w[8 * c + 7])));
-            }
-          } else {
-#pragma unroll
-            for (int c = 0; c < 8; ++c)
-              st_swizzled(buf, lane, c, make_uint4(__float_as_uint(v[4 * c + 0]), __float_as_uint(v[4 * c + 1]),
-                                                   __float_as_uint(v[4 * c + 2]), __float_as_uint(v[4 * c + 3])));
-          }
-          fence_async_smem();
+      for (int blk = half; blk < NBLK; blk += 2) {
+        const int nb = n0 + blk * COLS;
+        float v[32], w[32];
+        tmem_ld32(taddr + blk * COLS, v);
+        if (COLS == 64) tmem_ld32(taddr + blk * COLS + 32, w);
+        if (blk == last_blk) {  // this warp's share of the accumulator is read
+          tc_fence_before();
+          mbar_arrive(&tempty_bar[acc]);
+        }
+        if (!epi_uses_tma(EPI)) {
+          if (EPI != kEpiFinal || nb < N) epilogue_rows<EPI>(ep, M, m_row, nb, v);
+          continue;
+        }
+        if (!rows_live || nb >= N) continue;
+        if (nbuf > 0) {  // the previous store from this buffer must have read it
+          if (lane == 0) bulk_wait_read<0>();
           __syncwarp();
-          if (lane == 0) {
-            if (EPI == kEpiGateResid)
-              tma_reduce_add_2d(&tmD, buf, nb, m0 + quarter * 32);
-            else
-              tma_store_2d(&tmD, buf, nb, m0 + quarter * 32);
-            bulk_commit();
-          }
-          ++nbuf;
         }
-      } else {
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          float v[32];
-          tmem_ld32(taddr + c * 32, v);
-          if (c == BN / 32 - 1) {
-            tc_fence_before();
-            mbar_arrive(&tempty_bar[acc]);
+        epilogue_math<EPI>(ep, m_row, nb, v);
+        if (COLS == 64) {
+          epilogue_math<EPI>(ep, m_row, nb + 32, w);
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            st_swizzled(buf, lane, c, make_uint4(pack_bf16x2(v[8 * c + 0], v[8 * c + 1]),
+                                                 pack_bf16x2(v[8 * c + 2], v[8 * c + 3]),
+                                                 pack_bf16x2(v[8 * c + 4], v[8 * c + 5]),
+                                                 pack_bf16x2(v[8 * c + 6], v[8 * c + 7])));
+            st_swizzled(buf, lane, 4 + c, make_uint4(pack_bf16x2(w[8 * c + 0], w[8 * c + 1]),
+                                                     pack_bf16x2(w[8 * c + 2], w[8 * c + 3]),
+                                                     pack_bf16x2(w[8 * c + 4], w[8 * c + 5]),
+                                                     pack_bf16x2(w[8 * c + 6], w[8 * c + 7])));
           }
-          const int n_chunk = n0 + c * 32;
-          if (EPI != kEpiFinal || n_chunk < N) epilogue_rows<EPI>(ep, M, m_row, n_chunk, v);
+        } else {
+#pragma unroll
+          for (int c = 0; c < 8; ++c)
+            st_swizzled(buf, lane, c, make_uint4(__float_as_uint(v[4 * c + 0]), __float_as_uint(v[4 * c + 1]),
+                                                 __float_as_uint(v[4 * c + 2]), __float_as_uint(v[4 * c + 3])));
         }
+        fence_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          if (EPI == kEpiGateResid)
+            tma_reduce_add_2d(&tmD, buf, nb, m0 + quarter * 32);
+          else
+            tma_store_2d(&tmD, buf, nb, m0 + quarter * 32);
+          bulk_commit();
+        }
+        ++nbuf;
       }
     }
     if (epi_uses_tma(EPI) && lane == 0) bulk_wait<0>();  // all stores complete before exit
@@ -410,6 +428,7 @@ struct GemmOperands {
   CUtensorMap a, b, d;
   int M, N, K, bn;
   bool has_d;
+  bool b_is_weight;  // B is never written by another kernel: may be prefetched early
 };
 int make_gemm_operands(GemmOperands* g, const void* A, long long lda, const void* B, long long ldb,
                        int M, int N, int K, int bn);

@@ -33,6 +33,8 @@ constexpr int kStoreThreads = 256;
 
 // grid: (frames*batch, 2 [K,V], 16 heads); one CTA quantises one 144 x 64 slice.
 __global__ void __launch_bounds__(kStoreThreads) kv_store_kernel(KvStoreParams p) {
+  pdl_trigger();
+  pdl_wait();
   const int fb = blockIdx.x;
   const int j = fb % p.frames;
   const int b = fb / p.frames;
@@ -135,6 +137,8 @@ __global__ void __launch_bounds__(kStoreThreads) kv_store_kernel(KvStoreParams p
 // Dequantise slots [slot0, slot0+frames) of one layer to bf16 [batch][frames][144][1024].
 // grid: (frames*batch, 2 [K,V]); 256 threads stride over the 144*1024 elements.
 __global__ void __launch_bounds__(256) kv_load_kernel(KvStoreParams p) {
+  pdl_trigger();
+  pdl_wait();
   const int fb = blockIdx.x;
   const int j = fb % p.frames, b = fb / p.frames;
   const bool is_v = blockIdx.y == 1;
@@ -221,8 +225,8 @@ int launch_kv_store(const void* kv, long long ld, int k_col, int v_col, const oa
   p.src_frames = src_frames;
   p.slot0 = slot0;
   dim3 grid(frames * batch, 2, OASIS_HEADS);
-  kv_store_kernel<<<grid, kStoreThreads, 0, stream>>>(p);
-  OASIS_CHECK_LAUNCH("kv_store_kernel");
+  cudaError_t e = launch_pdl(kv_store_kernel, grid, dim3(kStoreThreads), 0, stream, p);
+  if (e != cudaSuccess) return cuda_status(e, "kv_store_kernel");
   return OASIS_OK;
 }
 
@@ -281,7 +285,7 @@ extern "C" int oasis_kv_load(const oasis_kv_cache_t* cache, int layer, int slot0
   for (int j = 0; j < frames; ++j)
     if (cache->slot_kind[slot0 + j] == OASIS_KV_BF16) p.kind[slot0 + j] = 0xFF;
   dim3 grid(frames * cache->batch, 2);
-  kv_load_kernel<<<grid, 256, 0, stream>>>(p);
-  OASIS_CHECK_LAUNCH("kv_load_kernel");
+  cudaError_t e = launch_pdl(kv_load_kernel, grid, dim3(256), 0, stream, p);
+  if (e != cudaSuccess) return cuda_status(e, "kv_load_kernel");
   return OASIS_OK;
 }
