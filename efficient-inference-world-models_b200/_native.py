@@ -75,6 +75,8 @@ SIGNATURES = {
                                   POINTER(KvCache), c_void_p]),
     "oasis_dit_forward_cached": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                          POINTER(KvCache), c_int, c_void_p]),
+    "oasis_dit_forward_noalloc": (c_int, [POINTER(DiTWeights), c_int, c_int, c_void_p, c_void_p,
+                                          c_void_p, c_void_p, c_void_p]),
     "oasis_plan_set_timing": (c_int, [c_void_p, c_int]),
     "oasis_plan_get_timing": (c_int, [c_void_p, POINTER(c_float), POINTER(c_int), c_int]),
     "oasis_gemm_bf16": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,

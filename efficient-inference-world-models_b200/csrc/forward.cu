@@ -69,7 +69,8 @@ struct oasis_plan {
   oasis::GemmOperands patch, temb1, temb2;  // embeddings
   oasis::GemmOperands ada;
   oasis::GemmOperands fin;
-  std::vector<oasis::GemmOperands> qkv, out, fc1, fc2;  // per sub-block
+  oasis::GemmOperands qkv[2 * OASIS_MAX_DEPTH], out[2 * OASIS_MAX_DEPTH];  // per sub-block
+  oasis::GemmOperands fc1[2 * OASIS_MAX_DEPTH], fc2[2 * OASIS_MAX_DEPTH];
   // timing
   bool timing = false;
   std::vector<cudaEvent_t> ev;
@@ -281,10 +282,13 @@ extern "C" size_t oasis_plan_workspace_size(int batch, int frames, int depth) {
   return layout_for(batch * frames, depth).total;
 }
 
-extern "C" int oasis_plan_create(const oasis_dit_weights_t* w, int batch, int frames,
-                                 void* workspace, size_t workspace_bytes, oasis_plan_t** out) {
-  if (!w || !out) return fail(OASIS_ERR_INVALID_ARG, "oasis_plan_create: null argument");
-  *out = nullptr;
+namespace oasis {
+
+// Validates the arguments and fills `p` (which may live in static storage): no device
+// memory is allocated, only tensor maps are encoded on the host.
+int plan_init(oasis_plan* p, const oasis_dit_weights_t* w, int batch, int frames, void* workspace,
+              size_t workspace_bytes) {
+  if (!w) return fail(OASIS_ERR_INVALID_ARG, "oasis_plan_create: null argument");
   if (batch <= 0 || frames <= 0 || frames > OASIS_MAX_FRAMES)
     return fail(OASIS_ERR_INVALID_ARG, "oasis_plan_create: need batch > 0 and 1 <= frames <= 32");
   if (w->depth <= 0 || w->depth > OASIS_MAX_DEPTH)
@@ -308,8 +312,6 @@ extern "C" int oasis_plan_create(const oasis_dit_weights_t* w, int batch, int fr
     if (!s.qkv_w || !s.out_w || !s.out_b || !s.fc1_w || !s.fc1_b || !s.fc2_w || !s.fc2_b)
       return fail(OASIS_ERR_INVALID_ARG, "oasis_plan_create: a sub-block weight pointer is NULL");
   }
-
-  oasis_plan* p = new oasis_plan();
   p->w = *w;
   p->batch = batch;
   p->frames = frames;
@@ -339,10 +341,6 @@ extern "C" int oasis_plan_create(const oasis_dit_weights_t* w, int batch, int fr
   if (!st)
     st = make_gemm_operands(&p->fin, p->ws + L.hbuf, OASIS_HIDDEN, w->final_w, OASIS_HIDDEN, M, 64,
                             OASIS_HIDDEN, 64);
-  p->qkv.resize(2 * w->depth);
-  p->out.resize(2 * w->depth);
-  p->fc1.resize(2 * w->depth);
-  p->fc2.resize(2 * w->depth);
   for (int j = 0; j < 2 * w->depth && !st; ++j) {
     const oasis_sub_weights_t& s = w->sub[j];
     st = make_gemm_operands(&p->qkv[j], p->ws + L.hbuf, OASIS_HIDDEN, s.qkv_w, OASIS_HIDDEN, M,
@@ -362,15 +360,31 @@ extern "C" int oasis_plan_create(const oasis_dit_weights_t* w, int batch, int fr
                               pick_bn(OASIS_HIDDEN, M));
     if (!st) st = set_gemm_output(&p->fc2[j], p->ws + L.resid, OASIS_HIDDEN, true);
   }
-  if (st) {
-    delete p;
-    return st;
-  }
+  if (st) return st;
   // weights are the B operand of these GEMMs (swap-AB GEMMs read activations as B)
   p->patch.b_is_weight = true;
   p->fin.b_is_weight = true;
   for (int j = 0; j < 2 * w->depth; ++j)
     p->qkv[j].b_is_weight = p->out[j].b_is_weight = p->fc1[j].b_is_weight = p->fc2[j].b_is_weight = true;
+  return OASIS_OK;
+}
+
+int plan_run(oasis_plan* p, const float* x, const int64_t* t, const float* act, float* v,
+             const oasis_kv_cache_t* cache, int n_past, bool cached, cudaStream_t s) {
+  return run_forward(p, x, t, act, v, cache, n_past, cached, s);
+}
+
+}  // namespace oasis
+
+extern "C" int oasis_plan_create(const oasis_dit_weights_t* w, int batch, int frames,
+                                 void* workspace, size_t workspace_bytes, oasis_plan_t** out) {
+  if (!w || !out) return fail(OASIS_ERR_INVALID_ARG, "oasis_plan_create: null argument");
+  *out = nullptr;
+  oasis_plan* p = new oasis_plan();
+  if (int st = plan_init(p, w, batch, frames, workspace, workspace_bytes)) {
+    delete p;
+    return st;
+  }
   *out = p;
   return OASIS_OK;
 }

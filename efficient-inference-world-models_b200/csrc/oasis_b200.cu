@@ -6,3 +6,4 @@
 #include "kv.cu"
 #include "elementwise.cu"
 #include "forward.cu"
+#include "noalloc.cu"

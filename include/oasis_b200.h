@@ -172,6 +172,22 @@ int oasis_plan_set_timing(oasis_plan_t* plan, int enable);
 int oasis_plan_get_timing(oasis_plan_t* plan, float* ms_per_family, int* launches_per_family,
                           int n_families);
 
+/* Full-window forward (same arguments and results as oasis_dit_forward without a
+ * cache) for callers that cannot allocate device memory: it takes only the weights,
+ * inputs and outputs, and uses as scratch a fixed 17 MiB file-scope device array of
+ * this library, which every GPU that loads the library holds until the process exits.
+ * Limit: batch * frames <= OASIS_NOALLOC_MAX_FRAMES; larger shapes are rejected with
+ * OASIS_ERR_UNSUPPORTED.  The first call on a device looks up that array's device
+ * address (cudaGetSymbolAddress), so make that first call before any stream capture.
+ * Calls share the one array: calls that overlap on the GPU (other streams, other host
+ * threads) race.  No scratch byte has to start at zero: every byte the forward reads
+ * is written earlier in the same call.  No counterpart in the reference (it has no
+ * C ABI and allocates through PyTorch). */
+#define OASIS_NOALLOC_MAX_FRAMES 4
+int oasis_dit_forward_noalloc(const oasis_dit_weights_t* w, int batch, int frames,
+                              const float* x, const int64_t* t, const float* act, float* v,
+                              cudaStream_t stream);
+
 /* ------------------------------------------------------------------ operators */
 /* D[m][n] = sum_k A[m][k] * B[n][k] on tcgen05 tensor cores (bf16 in, fp32
  * accumulate).  epilogue: 0 store bf16 D; 1 store fp32 D + bias[n] (bias may be
