@@ -68,6 +68,20 @@ def load_traffic():
         return None
 
 
+def max_over_ranks(x: float, dist=None, device="cpu") -> float:
+    """Max of a per-rank scalar (device time of the timed region) over all ranks."""
+    t = torch.tensor([float(x)], device=device, dtype=torch.float64)
+    if dist is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def whole_job_rate(units_per_rank: int, world: int, ms_max: float) -> float:
+    """Whole-job throughput: every rank processed units_per_rank units; the job took
+    the slowest rank's time."""
+    return world * units_per_rank / (ms_max / 1000.0)
+
+
 def synthetic_actions(g, B, T):
     a = torch.zeros(B, T, 25)
     a[..., :23] = (torch.rand(B, T, 23, generator=g) < 0.1).float()
@@ -305,13 +319,8 @@ def run_ours(args, rank, world, local_rank):
     e1.record()
     barrier()
     clk = clocks.stop()
-    ms = e0.elapsed_time(e1)
-    ms_t = torch.tensor([ms], device=dev)
-    if dist is not None:
-        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
-    ms_max = float(ms_t.item())
-    total_fwd = world * B * args.steps
-    value = total_fwd / (ms_max / 1000.0)
+    ms_max = max_over_ranks(e0.elapsed_time(e1), dist, dev)
+    value = whole_job_rate(B * args.steps, world, ms_max)
 
     # ---- e2e: public API, pinned host buffers, copies inside the timed region ----
     hx = torch.randn(B, T, *FRAME, generator=g).pin_memory()
@@ -346,10 +355,7 @@ def run_ours(args, rank, world, local_rank):
         e2e_step(s)
     f1.record()
     barrier()
-    ms_e2e = torch.tensor([f0.elapsed_time(f1)], device=dev)
-    if dist is not None:
-        dist.all_reduce(ms_e2e, op=dist.ReduceOp.MAX)
-    e2e_value = world * B * e2e_steps / (float(ms_e2e.item()) / 1000.0)
+    e2e_value = whole_job_rate(B * e2e_steps, world, max_over_ranks(f0.elapsed_time(f1), dist, dev))
     h2d = hx.numel() * 4 + hts[0].numel() * 8 + ha.numel() * 4
     d2h = hout.numel() * 4
 

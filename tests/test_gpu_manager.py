@@ -10,11 +10,12 @@ def test_manager_prefill_retrieve_update_snapshot(pkg, cuda):
     depth, B, T = 2, 2, 5
     model = pkg.OasisDiTB200.random(seed=4, depth=depth, device=cuda)
     mgr = pkg.KVCacheManagerB200({"num_layers": depth, "batch": B,
-                                  "progressive_quant": {"fp8_age_threshold": 2,
-                                                        "int4_age_threshold": 3}})
+                                  "progressive_quant": {"fp8_age_threshold": 3,
+                                                        "int4_age_threshold": 4}})
     assert mgr.wire_to_model(model) == depth
     cache = mgr.cache_for_window(T - 1)
-    assert cache.slot_kinds == ["int4", "int4", "fp8", "bf16"]  # ages 4, 3, 2, 1 (V at 0.7x)
+    # ages 4, 3, 2, 1; V thresholds are int(0.7x) = 2 (fp8) and 2 (int4): the coarser tier wins
+    assert cache.slot_kinds == ["int4", "int4", "int4", "bf16"]
     g = torch.Generator().manual_seed(0)
     x = torch.randn(B, T, 16, 18, 32, generator=g).to(cuda)
     t = torch.randint(0, 1000, (B, T), generator=g).to(cuda)
