@@ -106,17 +106,12 @@ T* at(oasis_plan* p, size_t off) {
   return reinterpret_cast<T*>(p->ws + off);
 }
 
-int pick_bn(int N, int M) {
-  // 128-row tiles along M.  N=256 tiles keep the tensor core under the shared-memory
-  // bandwidth limit (N=128 tiles need the full 128 B/clk), so take the widest tile
-  // that still fills ~3/4 of the SMs; narrower tiles only for small M.
-  const int sms = num_sms();
-  const int mt = (M + kGemmBM - 1) / kGemmBM;
-  for (int bn : {256, 128, 64}) {
-    if (N % bn) continue;
-    if (4LL * mt * (N / bn) >= 3LL * sms || bn == 64) return bn;
-  }
-  return 64;
+// A projection GEMM over the M token rows: tile shape from choose_tiles.
+int make_proj(GemmOperands* g, const void* A, long long lda, const void* B, long long ldb, int M,
+              int N, int K) {
+  int bn = 256, ctas = 1;
+  choose_tiles(M, N, &bn, &ctas);
+  return make_gemm_operands(g, A, lda, B, ldb, M, N, K, bn, ctas);
 }
 
 int run_forward(oasis_plan* p, const float* x, const int64_t* t, const float* act, float* v,
@@ -335,29 +330,27 @@ int plan_init(oasis_plan* p, const oasis_dit_weights_t* w, int batch, int frames
     st = make_gemm_operands(&p->temb2, w->t_fc2_w, kH1aLd, p->ws + L.h1a, kH1aLd, OASIS_HIDDEN, F,
                             kH1aLd, bnf);
   if (!st)
-    st = make_gemm_operands(&p->patch, p->ws + L.cols, 64, w->patch_w, 64, M, OASIS_HIDDEN, 64,
-                            pick_bn(OASIS_HIDDEN, M));
+    st = make_proj(&p->patch, p->ws + L.cols, 64, w->patch_w, 64, M, OASIS_HIDDEN, 64);
   if (!st) st = set_gemm_output(&p->patch, p->ws + L.resid, OASIS_HIDDEN, true);
   if (!st)
     st = make_gemm_operands(&p->fin, p->ws + L.hbuf, OASIS_HIDDEN, w->final_w, OASIS_HIDDEN, M, 64,
                             OASIS_HIDDEN, 64);
   for (int j = 0; j < 2 * w->depth && !st; ++j) {
     const oasis_sub_weights_t& s = w->sub[j];
-    st = make_gemm_operands(&p->qkv[j], p->ws + L.hbuf, OASIS_HIDDEN, s.qkv_w, OASIS_HIDDEN, M,
-                            3 * OASIS_HIDDEN, OASIS_HIDDEN, pick_bn(3 * OASIS_HIDDEN, M));
+    st = make_proj(&p->qkv[j], p->ws + L.hbuf, OASIS_HIDDEN, s.qkv_w, OASIS_HIDDEN, M,
+                   3 * OASIS_HIDDEN, OASIS_HIDDEN);
     if (!st) st = set_gemm_output(&p->qkv[j], p->ws + L.qkv, 3 * OASIS_HIDDEN, false);
     if (!st)
-      st = make_gemm_operands(&p->out[j], p->ws + L.attn, OASIS_HIDDEN, s.out_w, OASIS_HIDDEN, M,
-                              OASIS_HIDDEN, OASIS_HIDDEN, pick_bn(OASIS_HIDDEN, M));
+      st = make_proj(&p->out[j], p->ws + L.attn, OASIS_HIDDEN, s.out_w, OASIS_HIDDEN, M, OASIS_HIDDEN,
+                     OASIS_HIDDEN);
     if (!st) st = set_gemm_output(&p->out[j], p->ws + L.resid, OASIS_HIDDEN, true);
     if (!st)
-      st = make_gemm_operands(&p->fc1[j], p->ws + L.hbuf, OASIS_HIDDEN, s.fc1_w, OASIS_HIDDEN, M,
-                              OASIS_MLP_HIDDEN, OASIS_HIDDEN, pick_bn(OASIS_MLP_HIDDEN, M));
+      st = make_proj(&p->fc1[j], p->ws + L.hbuf, OASIS_HIDDEN, s.fc1_w, OASIS_HIDDEN, M,
+                     OASIS_MLP_HIDDEN, OASIS_HIDDEN);
     if (!st) st = set_gemm_output(&p->fc1[j], p->ws + L.mlp, OASIS_MLP_HIDDEN, false);
     if (!st)
-      st = make_gemm_operands(&p->fc2[j], p->ws + L.mlp, OASIS_MLP_HIDDEN, s.fc2_w,
-                              OASIS_MLP_HIDDEN, M, OASIS_HIDDEN, OASIS_MLP_HIDDEN,
-                              pick_bn(OASIS_HIDDEN, M));
+      st = make_proj(&p->fc2[j], p->ws + L.mlp, OASIS_MLP_HIDDEN, s.fc2_w, OASIS_MLP_HIDDEN, M,
+                     OASIS_HIDDEN, OASIS_MLP_HIDDEN);
     if (!st) st = set_gemm_output(&p->fc2[j], p->ws + L.resid, OASIS_HIDDEN, true);
   }
   if (st) return st;

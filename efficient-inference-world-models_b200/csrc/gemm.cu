@@ -45,42 +45,80 @@ int encode_2d(CUtensorMap* map, const void* base, long long rows, long long cols
   return OASIS_OK;
 }
 
+// Most CTA pairs of this kernel that can be resident at once (clusters are placed
+// within a GPC, so this can be below num_sms() / 2).
 template <int BN, int EPI>
+int max_pairs() {
+  using S = GemmShape<BN, 2>;
+  static int pairs = 0;
+  if (pairs == 0) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * (num_sms() / 2));
+    cfg.blockDim = dim3(kGemmThreads);
+    cfg.dynamicSmemBytes = S::kSmemBytes;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, gemm_tcgen05_kernel<BN, EPI, 2>, &cfg) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = num_sms() / 2;
+    }
+    pairs = n;
+  }
+  return pairs;
+}
+
+template <int BN, int EPI, int CTAS>
 int launch_one(const GemmOperands& g, const EpiParams& ep, cudaStream_t stream, int max_ctas) {
-  using S = GemmShape<BN>;
+  using S = GemmShape<BN, CTAS>;
   static bool configured = false;
   if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_tcgen05_kernel<BN, EPI>,
+    cudaError_t e = cudaFuncSetAttribute(gemm_tcgen05_kernel<BN, EPI, CTAS>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, S::kSmemBytes);
     if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(gemm)");
     configured = true;
   }
-  const int tiles = ((g.M + kGemmBM - 1) / kGemmBM) * ((g.N + BN - 1) / BN);
-  int grid = num_sms();
-  if (max_ctas > 0 && max_ctas < grid) grid = max_ctas;
-  if (tiles < grid) grid = tiles;
+  const int tiles = ((g.M + kGemmBM * CTAS - 1) / (kGemmBM * CTAS)) * ((g.N + BN - 1) / BN);
+  int units = num_sms();
+  if constexpr (CTAS == 2) units = max_pairs<BN, EPI>();
+  if (max_ctas > 0 && max_ctas / CTAS < units) units = max_ctas / CTAS > 0 ? max_ctas / CTAS : 1;
+  if (tiles < units) units = tiles;
   if (epi_uses_tma(EPI) && !g.has_d)
     return fail(OASIS_ERR_INVALID_ARG, "GEMM epilogue needs an output tensor map");
-  cudaError_t e = launch_pdl(gemm_tcgen05_kernel<BN, EPI>, dim3(grid), dim3(kGemmThreads),
-                             S::kSmemBytes, stream, g.a, g.b, g.d, g.M, g.N, g.K,
-                             g.b_is_weight ? 1 : 0, ep);
+  cudaError_t e;
+  if constexpr (CTAS == 2)
+    e = launch_pdl_cluster(gemm_tcgen05_kernel<BN, EPI, CTAS>, dim3(units * CTAS), dim3(kGemmThreads),
+                           S::kSmemBytes, stream, CTAS, g.a, g.b, g.d, g.M, g.N, g.K,
+                           g.b_is_weight ? 1 : 0, ep);
+  else
+    e = launch_pdl(gemm_tcgen05_kernel<BN, EPI, CTAS>, dim3(units), dim3(kGemmThreads), S::kSmemBytes,
+                   stream, g.a, g.b, g.d, g.M, g.N, g.K, g.b_is_weight ? 1 : 0, ep);
   if (e != cudaSuccess) return cuda_status(e, "gemm_tcgen05_kernel");
   return OASIS_OK;
 }
 
-template <int BN>
+template <int BN, int CTAS>
 int dispatch_epi(const GemmOperands& g, int epi, const EpiParams& ep, cudaStream_t s, int mc) {
   switch (epi) {
-    case kEpiStoreBF16: return launch_one<BN, kEpiStoreBF16>(g, ep, s, mc);
-    case kEpiStoreF32Bias: return launch_one<BN, kEpiStoreF32Bias>(g, ep, s, mc);
-    case kEpiQkvRope: return launch_one<BN, kEpiQkvRope>(g, ep, s, mc);
-    case kEpiBiasGelu: return launch_one<BN, kEpiBiasGelu>(g, ep, s, mc);
-    case kEpiGateResid: return launch_one<BN, kEpiGateResid>(g, ep, s, mc);
-    case kEpiAdaT: return launch_one<BN, kEpiAdaT>(g, ep, s, mc);
-    case kEpiFinal: return launch_one<BN, kEpiFinal>(g, ep, s, mc);
-    case kEpiAdaTSilu: return launch_one<BN, kEpiAdaTSilu>(g, ep, s, mc);
+    case kEpiStoreBF16: return launch_one<BN, kEpiStoreBF16, CTAS>(g, ep, s, mc);
+    case kEpiStoreF32Bias: return launch_one<BN, kEpiStoreF32Bias, CTAS>(g, ep, s, mc);
+    case kEpiQkvRope: return launch_one<BN, kEpiQkvRope, CTAS>(g, ep, s, mc);
+    case kEpiBiasGelu: return launch_one<BN, kEpiBiasGelu, CTAS>(g, ep, s, mc);
+    case kEpiGateResid: return launch_one<BN, kEpiGateResid, CTAS>(g, ep, s, mc);
   }
-  return fail(OASIS_ERR_INVALID_ARG, "unknown GEMM epilogue");
+  if (CTAS == 1) {  // swap-AB and row epilogues: small shapes, single CTAs only
+    switch (epi) {
+      case kEpiAdaT: return launch_one<BN, kEpiAdaT, 1>(g, ep, s, mc);
+      case kEpiFinal: return launch_one<BN, kEpiFinal, 1>(g, ep, s, mc);
+      case kEpiAdaTSilu: return launch_one<BN, kEpiAdaTSilu, 1>(g, ep, s, mc);
+    }
+  }
+  return fail(OASIS_ERR_INVALID_ARG, "unknown GEMM epilogue (or not available on CTA pairs)");
 }
 
 }  // namespace
@@ -97,18 +135,22 @@ int num_sms() {
 }
 
 int make_gemm_operands(GemmOperands* g, const void* A, long long lda, const void* B, long long ldb,
-                       int M, int N, int K, int bn) {
+                       int M, int N, int K, int bn, int ctas) {
   if (M <= 0 || N <= 0 || K <= 0) return fail(OASIS_ERR_INVALID_ARG, "GEMM sizes must be positive");
   if (K % kGemmBK) return fail(OASIS_ERR_UNSUPPORTED, "GEMM K must be a multiple of 64");
   if (bn != 32 && bn != 64 && bn != 128 && bn != 256)
     return fail(OASIS_ERR_UNSUPPORTED, "GEMM tile N must be 32, 64, 128 or 256");
+  if (ctas != 1 && !(ctas == 2 && bn == 256))
+    return fail(OASIS_ERR_UNSUPPORTED, "GEMM CTA pairs need tile N 256");
   *g = GemmOperands{};
   if (int s = encode_2d(&g->a, A, M, K, lda, kGemmBK, kGemmBM, 2)) return s;
-  if (int s = encode_2d(&g->b, B, N, K, ldb, kGemmBK, bn, 2)) return s;
+  // each CTA of a pair loads half of the tile's B rows
+  if (int s = encode_2d(&g->b, B, N, K, ldb, kGemmBK, bn / ctas, 2)) return s;
   g->M = M;
   g->N = N;
   g->K = K;
   g->bn = bn;
+  g->ctas = ctas;
   g->has_d = false;
   g->b_is_weight = false;
   return OASIS_OK;
@@ -125,13 +167,38 @@ int set_gemm_output(GemmOperands* g, void* D, long long ldd, bool f32) {
 
 int launch_gemm(const GemmOperands& g, int epi, const EpiParams& ep, cudaStream_t stream,
                 int max_ctas) {
+  if (g.ctas == 2) {
+    if (g.bn == 256) return dispatch_epi<256, 2>(g, epi, ep, stream, max_ctas);
+    return fail(OASIS_ERR_UNSUPPORTED, "GEMM CTA-pair tile N");
+  }
   switch (g.bn) {
-    case 32: return dispatch_epi<32>(g, epi, ep, stream, max_ctas);
-    case 64: return dispatch_epi<64>(g, epi, ep, stream, max_ctas);
-    case 128: return dispatch_epi<128>(g, epi, ep, stream, max_ctas);
-    case 256: return dispatch_epi<256>(g, epi, ep, stream, max_ctas);
+    case 32: return dispatch_epi<32, 1>(g, epi, ep, stream, max_ctas);
+    case 64: return dispatch_epi<64, 1>(g, epi, ep, stream, max_ctas);
+    case 128: return dispatch_epi<128, 1>(g, epi, ep, stream, max_ctas);
+    case 256: return dispatch_epi<256, 1>(g, epi, ep, stream, max_ctas);
   }
   return fail(OASIS_ERR_UNSUPPORTED, "GEMM tile N");
+}
+
+// CTA pairs on 256 x 256 tiles when there are about as many tiles as SM pairs or more
+// (each SM then stages half the B bytes per MMA: the N = 256 main loop stays
+// tensor-bound); otherwise single CTAs with the widest tile N that still gives every
+// SM work (at least 3/4 of a wave).
+void choose_tiles(int M, int N, int* bn, int* ctas) {
+  const long long sms = num_sms();
+  const long long pair_m = (M + 2 * kGemmBM - 1) / (2 * kGemmBM);
+  if (N % 256 == 0 && 10 * pair_m * (N / 256) >= 9 * (sms / 2)) {
+    *bn = 256;
+    *ctas = 2;
+    return;
+  }
+  const long long mt = (M + kGemmBM - 1) / kGemmBM;
+  int b = 256;
+  for (; b > 64; b >>= 1)
+    if (N % b == 0 && 4 * mt * (N / b) >= 3 * sms) break;
+  while (b > 32 && N % b) b >>= 1;
+  *bn = b;
+  *ctas = 1;
 }
 
 }  // namespace oasis
@@ -148,10 +215,11 @@ extern "C" int oasis_gemm_bf16(const void* A, const void* B, void* D, const floa
     return fail(OASIS_ERR_UNSUPPORTED, "oasis_gemm_bf16: N must be a multiple of 64 (bf16) / 32 (fp32)");
   if (!aligned16(D) || (epilogue == 0 ? (ldd % 8) : (ldd % 4)))
     return fail(OASIS_ERR_ALIGNMENT, "oasis_gemm_bf16: D must be 16-byte aligned rows");
-  int bn = 256;
-  while (bn > (epilogue == 0 ? 64 : 32) && (N % bn)) bn >>= 1;
+  int bn = 256, ctas = 1;
+  choose_tiles(M, N, &bn, &ctas);
+  if (epilogue == 0 && bn < 64) bn = 64;  // the bf16 TMA-store box is 64 columns wide
   GemmOperands g;
-  if (int s = make_gemm_operands(&g, A, lda, B, ldb, M, N, K, bn)) return s;
+  if (int s = make_gemm_operands(&g, A, lda, B, ldb, M, N, K, bn, ctas)) return s;
   if (int s = set_gemm_output(&g, D, ldd, epilogue == 1)) return s;
   EpiParams ep{};
   ep.out = D;

@@ -2,7 +2,7 @@
 //
 //   D[m][n] = sum_k A[m][k] * B[n][k]        (A activations, B = nn.Linear weight)
 //
-// One persistent CTA per SM, 6 warps:
+// Persistent CTAs, one per SM, 10 warps:
 //   warp 0      TMA producer: A tile 128x64 and B tile BNx64 per stage (128-byte swizzle)
 //   warp 1      TMEM allocator + single-thread tcgen05.mma issuer (M=128, N=BN, K=16)
 //   warps 2..9  epilogue, two warps per TMEM lane quarter splitting the columns:
@@ -13,6 +13,12 @@
 // The accumulator is double-buffered in TMEM (2 x BN columns) so the epilogue of one
 // tile overlaps the main loop of the next; TMEM is released as soon as a tile's last
 // tcgen05.ld has completed.
+//
+// CTA pairs (clusters of 2, tcgen05 cta_group::2) run 256 x BN tiles: each CTA stages
+// its 128 rows of A and half of the BN rows of B, the leader issues M=256 MMAs that
+// read both CTAs' shared memory and write each CTA's 128 accumulator rows into its own
+// TMEM.  Per SM this halves the B bytes staged and read per MMA, which is what keeps
+// the tensor pipe fed at N=256.
 #pragma once
 
 #include "common.cuh"
@@ -56,10 +62,13 @@ constexpr int kGemmThreads = 320;
 constexpr int kEpiWarps = 8;
 constexpr int kEpiBufBytes = 32 * 128;  // 32 rows x 128 B: one TMA store box
 
-template <int BN>
+// Per-CTA shared-memory plan.  A CTA pair (CTAS = 2) computes a 256 x BN tile: each
+// CTA stages 128 rows of A and BN/2 rows of B per k-block and holds a 128 x BN
+// accumulator in its own TMEM.
+template <int BN, int CTAS = 1>
 struct GemmShape {
   static constexpr int kABytes = kGemmBM * kGemmBK * 2;
-  static constexpr int kBBytes = BN * kGemmBK * 2;
+  static constexpr int kBBytes = (BN / CTAS) * kGemmBK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kStages = (192 * 1024) / kStageBytes > 8 ? 8 : (192 * 1024) / kStageBytes;
   static constexpr int kTmemCols = 2 * BN;  // power of two >= 64 for BN in {32..256}
@@ -206,14 +215,16 @@ __device__ __forceinline__ void epilogue_math(const EpiParams& p, int m, int n0,
   }
 }
 
-template <int BN, int EPI>
+template <int BN, int EPI, int CTAS>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA,
                         const __grid_constant__ CUtensorMap tmB,
                         const __grid_constant__ CUtensorMap tmD, int M, int N, int K,
                         int prefetch_b, EpiParams ep) {
-  using S = GemmShape<BN>;
+  static_assert(CTAS == 1 || CTAS == 2, "one CTA or a CTA pair per tile");
+  using S = GemmShape<BN, CTAS>;
   constexpr int STAGES = S::kStages;
+  constexpr int TILE_M = kGemmBM * CTAS;  // rows of one tile (the pair's MMA M)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -229,10 +240,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   pdl_trigger();
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int num_m = (M + kGemmBM - 1) / kGemmBM;
+  // A pair shares one tile: rank 0 (the leader) issues the MMAs for both CTAs, rank r
+  // holds A rows [r*128, r*128+128) and B rows [r*BN/2, r*BN/2 + BN/2) of the tile.
+  const uint32_t rank = CTAS == 2 ? cluster_ctarank() : 0u;
+  const bool leader = rank == 0;
+  const int unit = static_cast<int>(blockIdx.x) / CTAS;
+  const int num_units = static_cast<int>(gridDim.x) / CTAS;
+  const int num_m = (M + TILE_M - 1) / TILE_M;
   const int num_n = (N + BN - 1) / BN;
   const int num_tiles = num_m * num_n;
   const int num_kb = K / kGemmBK;
+  const int a_row0 = static_cast<int>(rank) * kGemmBM;
+  const int b_row0 = static_cast<int>(rank) * (BN / CTAS);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -241,7 +260,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull_bar[a], 1);
-      mbar_init(&tempty_bar[a], kEpiWarps * 32);
+      mbar_init(&tempty_bar[a], CTAS * kEpiWarps);  // one arrival per epilogue warp of the pair
     }
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
@@ -250,63 +269,87 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     tma_prefetch_desc(&tmB);
     if (epi_uses_tma(EPI)) tma_prefetch_desc(&tmD);
   }
-  if (warp == 1) tmem_alloc<S::kTmemCols>(tmem_holder);
+  if (warp == 1) {
+    if (CTAS == 2)
+      tmem_alloc_pair<S::kTmemCols>(tmem_holder);
+    else
+      tmem_alloc<S::kTmemCols>(tmem_holder);
+  }
   tc_fence_before();
   __syncthreads();
+  if (CTAS == 2) cluster_sync_all();  // the peer's barriers are initialised before any use
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
+  // the leader's barriers as seen from either CTA of the pair
+  const uint32_t lead_full = CTAS == 2 ? mapa_shared(smem_u32(full_bar), 0) : smem_u32(full_bar);
+  const uint32_t lead_tempty =
+      CTAS == 2 ? mapa_shared(smem_u32(tempty_bar), 0) : smem_u32(tempty_bar);
 
   if (warp == 0) {
     if (lane == 0) {
-      // ---------------- TMA producer ----------------
+      // ---------------- TMA producer (both CTAs of a pair load their own halves) ----------
       int stage = 0;
       uint32_t phase = 0;
       int last_phase[8];
 #pragma unroll
       for (int s = 0; s < 8; ++s) last_phase[s] = -1;
+      auto load = [&](void* dst, const CUtensorMap* map, int s, int c0, int c1) {
+        if (CTAS == 2)
+          tma_load_2d_pair(dst, map, lead_full + s * 8, c0, c1);
+        else
+          tma_load_2d(dst, map, &full_bar[s], c0, c1);
+      };
       // When B is a weight (never written by an earlier kernel) the B tiles of the first
       // stages are fetched before waiting on the previous kernel, the A tiles after.
       int pre = 0;
-      if (prefetch_b && static_cast<int>(blockIdx.x) < num_tiles) {
-        const int n0 = (static_cast<int>(blockIdx.x) / num_m) * BN;
+      if (prefetch_b && unit < num_tiles) {
+        const int n0 = (unit / num_m) * BN;
         pre = num_kb < STAGES ? num_kb : STAGES;
         for (int kb = 0; kb < pre; ++kb) {
-          mbar_arrive_expect_tx(&full_bar[kb], S::kStageBytes);
-          tma_load_2d(smem + kb * S::kStageBytes + S::kABytes, &tmB, &full_bar[kb], kb * kGemmBK, n0);
+          if (leader) mbar_arrive_expect_tx(&full_bar[kb], CTAS * S::kStageBytes);
+          load(smem + kb * S::kStageBytes + S::kABytes, &tmB, kb, kb * kGemmBK, n0 + b_row0);
         }
       }
       pdl_wait();
-      for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
-        const int m0 = (tile % num_m) * kGemmBM;
+      for (int tile = unit; tile < num_tiles && !*abort_flag; tile += num_units) {
+        const int m0 = (tile % num_m) * TILE_M;
         const int n0 = (tile / num_m) * BN;
         for (int kb = 0; kb < num_kb; ++kb) {
           uint8_t* sa = smem + stage * S::kStageBytes;
           uint8_t* sb = sa + S::kABytes;
           if (pre > 0) {  // stage already armed and its B tile in flight
             --pre;
-            tma_load_2d(sa, &tmA, &full_bar[stage], kb * kGemmBK, m0);
+            load(sa, &tmA, stage, kb * kGemmBK, m0 + a_row0);
           } else {
+            // the stage is free once the MMAs that read it (in both CTAs) have completed
             if (!mbar_wait(&empty_bar[stage], phase ^ 1)) { *abort_flag = 1; break; }
-            mbar_arrive_expect_tx(&full_bar[stage], S::kStageBytes);
-            tma_load_2d(sa, &tmA, &full_bar[stage], kb * kGemmBK, m0);
-            tma_load_2d(sb, &tmB, &full_bar[stage], kb * kGemmBK, n0);
+            if (leader) mbar_arrive_expect_tx(&full_bar[stage], CTAS * S::kStageBytes);
+            load(sa, &tmA, stage, kb * kGemmBK, m0 + a_row0);
+            load(sb, &tmB, stage, kb * kGemmBK, n0 + b_row0);
           }
           last_phase[stage] = static_cast<int>(phase);
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
       }
-      // make sure no TMA write is still in flight when the CTA retires
+      // no TMA write may still be in flight when the CTA retires: the leader sees its
+      // full barriers complete; the peer's copies count on the leader's barrier, so it
+      // waits for the MMAs that consumed them to release its stages
       for (int s = 0; s < STAGES; ++s)
-        if (last_phase[s] >= 0) mbar_wait(&full_bar[s], static_cast<uint32_t>(last_phase[s]));
+        if (last_phase[s] >= 0) {
+          if (CTAS == 1 || leader)
+            mbar_wait(&full_bar[s], static_cast<uint32_t>(last_phase[s]));
+          else
+            mbar_wait(&empty_bar[s], static_cast<uint32_t>(last_phase[s]));
+        }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    if (lane == 0 && leader) {
       // ---------------- MMA issuer (reads only shared memory and TMEM) ----------------
-      constexpr uint32_t idesc = umma_idesc_bf16(kGemmBM, BN);
+      constexpr uint32_t idesc = umma_idesc_bf16(TILE_M, BN);
       int stage = 0;
       uint32_t phase = 0;
       int it = 0;
-      for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x, ++it) {
+      for (int tile = unit; tile < num_tiles && !*abort_flag; tile += num_units, ++it) {
         const int acc = it & 1;
         const uint32_t acc_phase = (it >> 1) & 1;
         if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1)) { *abort_flag = 1; break; }
@@ -320,17 +363,32 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           const uint32_t b_addr = a_addr + S::kABytes;
 #pragma unroll
           for (int k = 0; k < kGemmBK / 16; ++k) {
-            umma_bf16(d_tmem, umma_desc_sw128(a_addr + k * 32), umma_desc_sw128(b_addr + k * 32),
-                      idesc, (kb > 0 || k > 0) ? 1u : 0u);
+            const uint64_t ad = umma_desc_sw128(a_addr + k * 32), bd = umma_desc_sw128(b_addr + k * 32);
+            const uint32_t accum = (kb > 0 || k > 0) ? 1u : 0u;
+            if (CTAS == 2)
+              umma_bf16_pair(d_tmem, ad, bd, idesc, accum);
+            else
+              umma_bf16(d_tmem, ad, bd, idesc, accum);
           }
-          umma_commit(&empty_bar[stage]);  // frees the smem stage once these MMAs retire
+          // frees the smem stage (of both CTAs) once these MMAs retire
+          if (CTAS == 2)
+            umma_commit_pair(&empty_bar[stage]);
+          else
+            umma_commit(&empty_bar[stage]);
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
         if (!ok) { *abort_flag = 1; break; }
-        umma_commit(&tfull_bar[acc]);  // accumulator ready for the epilogue
+        // accumulator ready for the epilogue (of both CTAs)
+        if (CTAS == 2)
+          umma_commit_pair(&tfull_bar[acc]);
+        else
+          umma_commit(&tfull_bar[acc]);
       }
       // all issued MMAs must retire before TMEM is released
-      umma_commit(drain_bar);
+      if (CTAS == 2)
+        umma_commit_pair_local(drain_bar);
+      else
+        umma_commit(drain_bar);
       mbar_wait(drain_bar, 0);
     }
   } else {
@@ -341,8 +399,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     uint8_t* buf = epi_smem + (warp - 2) * kEpiBufBytes;
     int nbuf = 0;  // TMA stores issued by this warp
     int it = 0;
-    for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x, ++it) {
-      const int m0 = (tile % num_m) * kGemmBM;
+    // one arrival per warp on the leader's tempty barrier once all its lanes have read
+    auto release = [&](int acc) {
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        if (CTAS == 2)
+          mbar_arrive_cluster(lead_tempty + acc * 8);
+        else
+          mbar_arrive(&tempty_bar[acc]);
+      }
+    };
+    for (int tile = unit; tile < num_tiles && !*abort_flag; tile += num_units, ++it) {
+      const int m0 = (tile % num_m) * TILE_M + a_row0;  // this CTA's accumulator rows
       const int n0 = (tile / num_m) * BN;
       const int acc = it & 1;
       const uint32_t acc_phase = (it >> 1) & 1;
@@ -357,8 +426,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       constexpr int NBLK = BN / COLS;
       const int last_blk = (NBLK - 1 - half) >= 0 ? ((NBLK - 1 - half) / 2) * 2 + half : -1;
       if (last_blk < 0) {  // owns no columns of this tile
-        tc_fence_before();
-        mbar_arrive(&tempty_bar[acc]);
+        release(acc);
         continue;
       }
 #pragma unroll 1
@@ -367,10 +435,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         float v[32], w[32];
         tmem_ld32(taddr + blk * COLS, v);
         if (COLS == 64) tmem_ld32(taddr + blk * COLS + 32, w);
-        if (blk == last_blk) {  // this warp's share of the accumulator is read
-          tc_fence_before();
-          mbar_arrive(&tempty_bar[acc]);
-        }
+        if (blk == last_blk) release(acc);  // this warp's share of the accumulator is read
         if (!epi_uses_tma(EPI)) {
           if (EPI != kEpiFinal || nb < N) epilogue_rows<EPI>(ep, M, m_row, nb, v);
           continue;
@@ -418,8 +483,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
   tc_fence_before();
   __syncthreads();
+  // a pair frees its TMEM together, after both CTAs are done with it (and with each
+  // other's barriers)
+  if (CTAS == 2) cluster_sync_all();
   tc_fence_after();
-  if (warp == 1) tmem_dealloc<S::kTmemCols>(tmem_base);
+  if (warp == 1) {
+    if (CTAS == 2)
+      tmem_dealloc_pair<S::kTmemCols>(tmem_base);
+    else
+      tmem_dealloc<S::kTmemCols>(tmem_base);
+  }
 }
 
 // Host side (gemm.cu).  A: [M][lda] bf16, B: [N][ldb] bf16; D described by its own
@@ -427,11 +500,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 struct GemmOperands {
   CUtensorMap a, b, d;
   int M, N, K, bn;
+  int ctas;  // 1: one CTA per 128 x bn tile; 2: CTA pairs on 256 x 256 tiles
   bool has_d;
   bool b_is_weight;  // B is never written by another kernel: may be prefetched early
 };
 int make_gemm_operands(GemmOperands* g, const void* A, long long lda, const void* B, long long ldb,
-                       int M, int N, int K, int bn);
+                       int M, int N, int K, int bn, int ctas = 1);
+// Tile shape for an M x N x K projection on this GPU: CTA pairs where the tile count
+// fills the SM pairs, single CTAs otherwise.
+void choose_tiles(int M, int N, int* bn, int* ctas);
 // Output tensor map for the TMA epilogues: D [M][N] with leading dim ldd, bf16 or fp32.
 int set_gemm_output(GemmOperands* g, void* D, long long ldd, bool f32);
 int launch_gemm(const GemmOperands& g, int epi, const EpiParams& ep, cudaStream_t stream,
