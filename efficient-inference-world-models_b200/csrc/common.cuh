@@ -279,9 +279,16 @@ __device__ __forceinline__ void cluster_sync_all() {
 }
 
 // Arrive on an mbarrier given by its shared::cluster address (possibly another CTA's).
+// Default (CTA-scope release) semantics: the arrivals that use it hand over tensor
+// memory, which the tcgen05 fences around the barrier order; a cluster-scope release
+// would also wait for this thread's outstanding memory writes.
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
-               : "memory");
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+// Hint: bring the 128-byte line holding p into L1.
+__device__ __forceinline__ void prefetch_l1(const void* p) {
+  asm volatile("prefetch.global.L1 [%0];" ::"l"(p));
 }
 
 // TMA tile load into this CTA's shared memory whose completion bytes are counted on

@@ -215,6 +215,32 @@ __device__ __forceinline__ void epilogue_math(const EpiParams& p, int m, int n0,
   }
 }
 
+// L1 prefetch of the operands epilogue_math reads for this thread's row m and blocks
+// half, half+2, ... of the tile at n0 (issued before the accumulator is ready, so the
+// loads in the epilogue hit L1 instead of waiting on L2 after each TMEM load).
+template <int EPI, int COLS, int NBLK>
+__device__ __forceinline__ void epilogue_prefetch(const EpiParams& p, int M, int N, int m, int n0,
+                                                  int half) {
+  if (m >= M) return;
+#pragma unroll
+  for (int blk = half; blk < NBLK; blk += 2) {
+    const int nb = n0 + blk * COLS;
+    if (nb >= N) break;
+    if (EPI == kEpiGateResid) {
+      prefetch_l1(p.gate + static_cast<long long>(m / OASIS_TOKENS) * p.gate_ld + nb);
+      prefetch_l1(p.bias + nb);
+    } else if (EPI == kEpiBiasGelu || EPI == kEpiStoreF32Bias) {
+      if (p.bias)
+        for (int c = 0; c < COLS; c += 32) prefetch_l1(p.bias + nb + c);
+    } else if (EPI == kEpiQkvRope) {
+      if (nb < p.rope_cols) {
+        const int pos = (m / p.rope_div) % p.rope_mod + p.rope_add;
+        for (int c = 0; c < COLS; c += 32) prefetch_l1(p.rope + pos * 64 + ((nb + c) & 63));
+      }
+    }
+  }
+}
+
 template <int BN, int EPI, int CTAS>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA,
@@ -397,8 +423,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int quarter = warp & 3;        // TMEM lanes this warp may access
     const int half = (warp - 2) >> 2;    // which interleaved column blocks it owns
     uint8_t* buf = epi_smem + (warp - 2) * kEpiBufBytes;
-    int nbuf = 0;  // TMA stores issued by this warp
+    int nbuf = 0;  // TMA stores issued by this warp from buf
     int it = 0;
+    // bf16 TMA boxes: 64 columns (2 TMEM loads); fp32 boxes and row epilogues: 32
+    constexpr int COLS = (epi_uses_tma(EPI) && !epi_out_f32(EPI)) ? 64 : 32;
+    constexpr int NBLK = BN / COLS;
+    // The last tile of a CTA has the operand stages to itself once its accumulator is
+    // complete (no load is issued after its k-blocks and its MMAs have retired): each
+    // warp stages all of its boxes there and issues their TMA stores back to back
+    // instead of cycling one 4 KB buffer.
+    constexpr int kLastWarpBytes = ((NBLK + 1) / 2) * kEpiBufBytes;
+    static_assert(kEpiWarps * kLastWarpBytes <= STAGES * S::kStageBytes, "last-tile staging");
     // one arrival per warp on the leader's tempty barrier once all its lanes have read
     auto release = [&](int acc) {
       tc_fence_before();
@@ -415,15 +450,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int n0 = (tile / num_m) * BN;
       const int acc = it & 1;
       const uint32_t acc_phase = (it >> 1) & 1;
+      const int m_row = m0 + quarter * 32 + lane;  // this thread's row
+      if (epi_uses_tma(EPI)) epilogue_prefetch<EPI, COLS, NBLK>(ep, M, N, m_row, n0, half);
       if (!mbar_wait(&tfull_bar[acc], acc_phase)) { *abort_flag = 1; break; }
       tc_fence_after();
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                              static_cast<uint32_t>(acc * BN);
-      const int m_row = m0 + quarter * 32 + lane;  // this thread's row
       const bool rows_live = m0 + quarter * 32 < M;
-      // bf16 TMA boxes: 64 columns (2 TMEM loads); fp32 boxes and row epilogues: 32
-      constexpr int COLS = (epi_uses_tma(EPI) && !epi_out_f32(EPI)) ? 64 : 32;
-      constexpr int NBLK = BN / COLS;
+      const bool last_tile = tile + num_units >= num_tiles;
       const int last_blk = (NBLK - 1 - half) >= 0 ? ((NBLK - 1 - half) / 2) * 2 + half : -1;
       if (last_blk < 0) {  // owns no columns of this tile
         release(acc);
@@ -441,7 +475,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           continue;
         }
         if (!rows_live || nb >= N) continue;
-        if (nbuf > 0) {  // the previous store from this buffer must have read it
+        uint8_t* box = buf;
+        if (last_tile) {
+          box = smem + (warp - 2) * kLastWarpBytes + (blk >> 1) * kEpiBufBytes;
+        } else if (nbuf > 0) {  // the previous store from buf must have read it
           if (lane == 0) bulk_wait_read<0>();
           __syncwarp();
         }
@@ -450,11 +487,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           epilogue_math<EPI>(ep, m_row, nb + 32, w);
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
-            st_swizzled(buf, lane, c, make_uint4(pack_bf16x2(v[8 * c + 0], v[8 * c + 1]),
+            st_swizzled(box, lane, c, make_uint4(pack_bf16x2(v[8 * c + 0], v[8 * c + 1]),
                                                  pack_bf16x2(v[8 * c + 2], v[8 * c + 3]),
                                                  pack_bf16x2(v[8 * c + 4], v[8 * c + 5]),
                                                  pack_bf16x2(v[8 * c + 6], v[8 * c + 7])));
-            st_swizzled(buf, lane, 4 + c, make_uint4(pack_bf16x2(w[8 * c + 0], w[8 * c + 1]),
+            st_swizzled(box, lane, 4 + c, make_uint4(pack_bf16x2(w[8 * c + 0], w[8 * c + 1]),
                                                      pack_bf16x2(w[8 * c + 2], w[8 * c + 3]),
                                                      pack_bf16x2(w[8 * c + 4], w[8 * c + 5]),
                                                      pack_bf16x2(w[8 * c + 6], w[8 * c + 7])));
@@ -462,19 +499,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         } else {
 #pragma unroll
           for (int c = 0; c < 8; ++c)
-            st_swizzled(buf, lane, c, make_uint4(__float_as_uint(v[4 * c + 0]), __float_as_uint(v[4 * c + 1]),
+            st_swizzled(box, lane, c, make_uint4(__float_as_uint(v[4 * c + 0]), __float_as_uint(v[4 * c + 1]),
                                                  __float_as_uint(v[4 * c + 2]), __float_as_uint(v[4 * c + 3])));
         }
         fence_async_smem();
         __syncwarp();
         if (lane == 0) {
           if (EPI == kEpiGateResid)
-            tma_reduce_add_2d(&tmD, buf, nb, m0 + quarter * 32);
+            tma_reduce_add_2d(&tmD, box, nb, m0 + quarter * 32);
           else
-            tma_store_2d(&tmD, buf, nb, m0 + quarter * 32);
+            tma_store_2d(&tmD, box, nb, m0 + quarter * 32);
           bulk_commit();
         }
-        ++nbuf;
+        if (!last_tile) ++nbuf;
       }
     }
     if (epi_uses_tma(EPI) && lane == 0) bulk_wait<0>();  // all stores complete before exit
