@@ -2,17 +2,17 @@
 // embedding GEMMs (timestep sinusoid, action columns, patch im2col), and the sampler
 // updates.
 #include "launch.cuh"
+#include "ln.cuh"
 
 namespace oasis {
 
 // ----------------------------------------------------------------------------------
 // LayerNorm (eps 1e-6, no affine) + modulate: out = bf16(LN(x) * (1 + scale[f]) + shift[f])
 // x fp32 [M][1024]; frame f = row / rows_per_frame; shift/scale rows of the adaLN table.
-// A CTA takes 16 rows of one frame (4 warps x 4 rows): each warp loads its frame's
-// shift/scale once into registers and reuses them for its rows; lane holds columns
-// lane*4 + i*128.
+// A CTA takes 16 rows of one frame (4 warps x 4 rows, ln_modulate_rows).  The forward
+// runs this kernel only for the first LayerNorm; the others are the tail of the
+// residual GEMM that produces their input.
 // ----------------------------------------------------------------------------------
-constexpr int kLnRowsPerWarp = 4;
 constexpr int kLnWarps = 4;
 constexpr int kLnRowsPerCta = kLnRowsPerWarp * kLnWarps;
 
@@ -27,54 +27,24 @@ __global__ void __launch_bounds__(kLnWarps * 32)
   const int row0 = static_cast<int>(f * rows_per_frame) + (blockIdx.x % chunks) * kLnRowsPerCta +
                    (threadIdx.x >> 5) * kLnRowsPerWarp;
   const int row_end = min(static_cast<int>((f + 1) * rows_per_frame), M);
-  const int lane = threadIdx.x & 31;
   if (row0 >= row_end) return;
-  const float4* sh = reinterpret_cast<const float4*>(shift + f * mod_ld);
-  const float4* sc = reinterpret_cast<const float4*>(scale + f * mod_ld);
-  float4 v[kLnRowsPerWarp][8];
+  const int lane = threadIdx.x & 31;
+  const int nrows = min(kLnRowsPerWarp, row_end - row0);
+  float4 v[kLnRowsPerWarp][8];  // all rows in flight before any is reduced
 #pragma unroll
   for (int r = 0; r < kLnRowsPerWarp; ++r) {
-    if (row0 + r < row_end) {
+    if (r < nrows) {
       const float4* xr = reinterpret_cast<const float4*>(x + static_cast<long long>(row0 + r) * OASIS_HIDDEN);
 #pragma unroll
       for (int i = 0; i < 8; ++i) v[r][i] = xr[lane + 32 * i];
     }
   }
   float4 a4[8], s4[8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    a4[i] = sh[lane + 32 * i];
-    s4[i] = sc[lane + 32 * i];
-  }
+  ln_load_modulation(shift + f * mod_ld, scale + f * mod_ld, lane, a4, s4);
 #pragma unroll
   for (int r = 0; r < kLnRowsPerWarp; ++r) {
-    if (row0 + r >= row_end) break;
-    float sum = 0.0f;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) sum += (v[r][i].x + v[r][i].y) + (v[r][i].z + v[r][i].w);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-    const float mean = sum * (1.0f / OASIS_HIDDEN);
-    float sq = 0.0f;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float a = v[r][i].x - mean, b = v[r][i].y - mean, c = v[r][i].z - mean, d = v[r][i].w - mean;
-      sq += (a * a + b * b) + (c * c + d * d);
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
-    const float rstd = rsqrtf(sq * (1.0f / OASIS_HIDDEN) + 1e-6f);
-    uint2* o2 = reinterpret_cast<uint2*>(out + static_cast<long long>(row0 + r) * OASIS_HIDDEN);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float4 a = a4[i];
-      const float4 s = s4[i];
-      const float y0 = (v[r][i].x - mean) * rstd * (1.0f + s.x) + a.x;
-      const float y1 = (v[r][i].y - mean) * rstd * (1.0f + s.y) + a.y;
-      const float y2 = (v[r][i].z - mean) * rstd * (1.0f + s.z) + a.z;
-      const float y3 = (v[r][i].w - mean) * rstd * (1.0f + s.w) + a.w;
-      o2[lane + 32 * i] = make_uint2(pack_bf16x2(y0, y1), pack_bf16x2(y2, y3));
-    }
+    if (r >= nrows) break;
+    ln_modulate_row(v[r], a4, s4, out + static_cast<long long>(row0 + r) * OASIS_HIDDEN, lane);
   }
 }
 

@@ -27,8 +27,13 @@ enum Family { kFamGemm = 0, kFamAda, kFamSpatial, kFamTemporal, kFamLn, kFamEmbe
 size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 
 struct Layout {
-  size_t resid, hbuf, qkv, attn, mlp, cols, emb, h1a, silu, mod, total;
+  size_t resid, hbuf, qkv, attn, mlp, cols, emb, h1a, silu, mod, cnt, total;
+  size_t cnt_bytes;  // row-block counters of the residual GEMMs' LayerNorm tails
 };
+
+// One counter per 128-row block for each residual GEMM (out-proj and fc2 of every
+// sub-block), zeroed at the start of every forward.
+inline size_t row_blocks(size_t M) { return (M + 127) / 128; }
 
 constexpr int kH1aLd = OASIS_HIDDEN + 64;  // [first-linear output | actions | zero pad]
 
@@ -52,6 +57,8 @@ Layout layout_for(int F, int depth) {
   L.h1a = take(static_cast<size_t>(F) * kH1aLd * 2);
   L.silu = take(static_cast<size_t>(F) * OASIS_HIDDEN * 2);
   L.mod = take(static_cast<size_t>(F) * mod_ld * 4);
+  L.cnt_bytes = static_cast<size_t>(4 * depth) * row_blocks(M) * 4;
+  L.cnt = take(L.cnt_bytes);
   L.total = off;
   return L;
 }
@@ -126,6 +133,22 @@ int run_forward(oasis_plan* p, const float* x, const int64_t* t, const float* ac
   float* mod = at<float>(p, p->L.mod);
   const long long mld = p->mod_ld;
 
+  unsigned int* counters = at<unsigned int>(p, p->L.cnt);
+  const size_t nblk = row_blocks(static_cast<size_t>(M));
+  {
+    cudaError_t ce = cudaMemsetAsync(counters, 0, p->L.cnt_bytes, s);
+    if (ce != cudaSuccess) return cuda_status(ce, "cudaMemsetAsync(row-block counters)");
+  }
+  // the residual GEMMs (out-proj, fc2) end with the LayerNorm + modulate that feeds the
+  // next GEMM: shift/scale rows and counter slice for launch k
+  auto ln_tail = [&](EpiParams& ep, const float* shift, int k) {
+    ep.ln_out = static_cast<__nv_bfloat16*>(hbuf);
+    ep.ln_shift = shift;
+    ep.ln_scale = shift + OASIS_HIDDEN;
+    ep.ln_mod_ld = mld;
+    ep.ln_count = counters + static_cast<size_t>(k) * nblk;
+  };
+
   // ---- embeddings (three small tcgen05 GEMMs) ----
   {
     Timer tm(p, s, kFamEmbed);
@@ -171,7 +194,7 @@ int run_forward(oasis_plan* p, const float* x, const int64_t* t, const float* ac
     const int blk = j / 2;
     const oasis_sub_weights_t& sw = w.sub[j];
     const float* modj = mod + static_cast<long long>(j) * OASIS_ADA_PER_SUB;
-    {
+    if (j == 0) {  // later LayerNorms are the tails of the residual GEMMs
       Timer tm(p, s, kFamLn);
       if (int e = launch_ln_modulate(resid, modj + 0 * OASIS_HIDDEN, modj + 1 * OASIS_HIDDEN, mld,
                                      hbuf, M, OASIS_TOKENS, s))
@@ -225,13 +248,8 @@ int run_forward(oasis_plan* p, const float* x, const int64_t* t, const float* ac
       ep.bias = sw.out_b;
       ep.gate = modj + 2 * OASIS_HIDDEN;
       ep.gate_ld = mld;
+      ln_tail(ep, modj + 3 * OASIS_HIDDEN, 2 * j);  // -> input of fc1
       if (int e = launch_gemm(p->out[j], kEpiGateResid, ep, s)) return e;
-    }
-    {
-      Timer tm(p, s, kFamLn);
-      if (int e = launch_ln_modulate(resid, modj + 3 * OASIS_HIDDEN, modj + 4 * OASIS_HIDDEN, mld,
-                                     hbuf, M, OASIS_TOKENS, s))
-        return e;
     }
     {
       Timer tm(p, s, kFamGemm);
@@ -249,15 +267,14 @@ int run_forward(oasis_plan* p, const float* x, const int64_t* t, const float* ac
       ep.bias = sw.fc2_b;
       ep.gate = modj + 5 * OASIS_HIDDEN;
       ep.gate_ld = mld;
+      // -> input of the next sub-block's QKV, or of the final layer (its shift, scale)
+      ln_tail(ep, modj + OASIS_ADA_PER_SUB, 2 * j + 1);
       if (int e = launch_gemm(p->fc2[j], kEpiGateResid, ep, s)) return e;
     }
   }
-  // ---- final layer ----
+  // ---- final layer (its LayerNorm + modulate was the last fc2's tail) ----
   {
     Timer tm(p, s, kFamEmbed);
-    const float* fmod = mod + static_cast<long long>(2 * p->depth) * OASIS_ADA_PER_SUB;
-    if (int e = launch_ln_modulate(resid, fmod, fmod + OASIS_HIDDEN, mld, hbuf, M, OASIS_TOKENS, s))
-      return e;
     EpiParams ep{};
     ep.out = v;
     ep.bias = w.final_b;

@@ -22,6 +22,7 @@
 #pragma once
 
 #include "common.cuh"
+#include "ln.cuh"
 
 namespace oasis {
 
@@ -54,6 +55,15 @@ struct EpiParams {
   int rope_cols;        // columns < rope_cols are rotated (2048: q and k)
   int rope_div, rope_mod, rope_add;  // position(m) = (m / div) % mod + add
   int n_valid;          // swap-AB epilogues: number of valid B rows
+  // kEpiGateResid with ln_out set: LayerNorm + modulate of the updated residual rows
+  // into ln_out (bf16 [M][1024]) as the kernel's tail.  ln_count holds one zeroed
+  // counter per 128-row block (ceil(M / 128)); the kernel leaves each at the number of
+  // N tiles.
+  __nv_bfloat16* ln_out;
+  const float* ln_shift;  // per-frame rows, stride ln_mod_ld
+  const float* ln_scale;
+  long long ln_mod_ld;
+  unsigned int* ln_count;
 };
 
 constexpr int kGemmBM = 128;
@@ -116,6 +126,35 @@ __device__ __forceinline__ void bulk_wait() {
 }
 __device__ __forceinline__ void fence_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void fence_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+// Named barrier 1 over the 8 epilogue warps (warps 2..9).
+__device__ __forceinline__ void epilogue_bar_sync() {
+  asm volatile("bar.sync 1, %0;" ::"n"(kEpiWarps * 32) : "memory");
+}
+__device__ __forceinline__ void red_release_add(unsigned int* p, unsigned int v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned int ld_acquire(const unsigned int* p) {
+  unsigned int v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+// Bounded wait until *p >= target (another CTA of this grid publishes it); records a
+// timeout in the device error word and returns false after kWaitTimeoutNs.
+__device__ __forceinline__ bool wait_count_geq(const unsigned int* p, unsigned int target) {
+  if (ld_acquire(p) >= target) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+    __nanosleep(64);
+    if (ld_acquire(p) >= target) return true;
+    if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+      atomicOr(&g_dev_error, kDevErrTimeout);
+      return false;
+    }
+  }
 }
 
 // Write 16-byte chunk `c` (0..7) of row `r` (0..31) of a 128B-swizzled 32 x 128 B box.
@@ -516,6 +555,49 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     if (epi_uses_tma(EPI) && lane == 0) bulk_wait<0>();  // all stores complete before exit
     __syncwarp();
+    if (EPI == kEpiGateResid && ep.ln_out) {
+      // ---- tail: LayerNorm + modulate of the finished residual rows ----
+      // publish: every 128-row block this CTA updated gets one count per tile, released
+      // after all eight warps' reduce-adds have completed
+      if (lane == 0) fence_async_global();
+      epilogue_bar_sync();
+      if (warp == 2 && lane == 0 && !*abort_flag) {
+        const int nblk = (M + kGemmBM - 1) / kGemmBM;
+        for (int tile = unit; tile < num_tiles; tile += num_units) {
+          const int q = ((tile % num_m) * TILE_M + a_row0) / kGemmBM;
+          if (q < nblk) red_release_add(ep.ln_count + q, 1u);
+        }
+      }
+      // consume: this CTA normalises rows [c*R, c*R + R) once the N tiles of their
+      // block are all in.  Warp w takes 4-row groups w, w+8, ... (a group never crosses
+      // a frame or a block: 144 and 128 are multiples of 4); a group's 16 KB are copied
+      // into the now idle operand stages in one round trip, then reduced row by row.
+      const int R = ((M + static_cast<int>(gridDim.x) - 1) / static_cast<int>(gridDim.x) + 3) & ~3;
+      const int r_begin = static_cast<int>(blockIdx.x) * R;
+      const int r_end = min(M, r_begin + R);
+      float4* stage_rows = reinterpret_cast<float4*>(smem + (warp - 2) * (kLnRowsPerWarp * OASIS_HIDDEN * 4));
+      static_assert(kEpiWarps * kLnRowsPerWarp * OASIS_HIDDEN * 4 <= STAGES * S::kStageBytes, "LN staging");
+      for (int row0 = r_begin + (warp - 2) * kLnRowsPerWarp; row0 < r_end;
+           row0 += kEpiWarps * kLnRowsPerWarp) {
+        int ok = 1;
+        if (lane == 0) ok = wait_count_geq(ep.ln_count + row0 / kGemmBM, static_cast<unsigned>(num_n));
+        if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+        __syncwarp();  // the acquire by lane 0 orders the whole warp's loads
+        const int nrows = min(kLnRowsPerWarp, r_end - row0);
+        const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(ep.out) +
+                                                            static_cast<long long>(row0) * OASIS_HIDDEN);
+        for (int r = 0; r < nrows; ++r)
+#pragma unroll
+          for (int i = 0; i < 8; ++i)  // each lane copies (and later reads) its own columns
+            cp_async16(stage_rows + r * 256 + lane + 32 * i, src + r * 256 + lane + 32 * i);
+        const long long f = row0 / OASIS_TOKENS;
+        float4 a4[8], s4[8];
+        ln_load_modulation(ep.ln_shift + f * ep.ln_mod_ld, ep.ln_scale + f * ep.ln_mod_ld, lane, a4, s4);
+        cp_async_wait_all();
+        ln_modulate_rows_smem(stage_rows, nrows, a4, s4,
+                              ep.ln_out + static_cast<long long>(row0) * OASIS_HIDDEN, lane);
+      }
+    }
   }
 
   tc_fence_before();

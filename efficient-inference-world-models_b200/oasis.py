@@ -9,6 +9,11 @@ Semantics kept from the reference:
   ``max_frames`` (32), new chunk ~ N(0, 1) clamped to +-20, eps_prev reset per frame,
   only ``x[:, -1:]`` written back (``oasis_dpmpp_modal.py:118-164``).
 
+``action_step_schedule`` is the action-magnitude difficulty schedule
+(``benchmarks/optimised/oasis_difficulty_dpmpp_modal.py:93-101``): a frame whose action
+L1 norm is below 0.5 gets 2 solver steps, below 1.5 gets 3, otherwise 5; rollout_dpmpp
+accepts the per-frame list as ``solver_steps``.
+
 ``rollout_dpmpp(..., use_cache=True)`` runs the first solver step of each frame as a
 full-window forward that also stores the window's temporal K/V, and the remaining steps
 as incremental forwards of the new frame against that cache (the reference's
@@ -18,7 +23,7 @@ The VAE decode (``models/oasis.py:237-245``) is outside this library.
 
 from __future__ import annotations
 
-from typing import Any, Dict, Optional
+from typing import Any, Dict, List, Optional, Sequence, Union
 
 import torch
 
@@ -99,18 +104,39 @@ def generate(model: Dict[str, Any], num_frames: int = 16, num_steps: int = DEFAU
     return out
 
 
+def steps_for_action_magnitude(mag: float, lo_threshold: float = 0.5, hi_threshold: float = 1.5,
+                                reduced_steps: int = 2, mid_steps: int = 3, full_steps: int = 5) -> int:
+    """Solver steps for one frame from its action L1 norm (the reference's bucket
+    function, ``oasis_difficulty_dpmpp_modal.py:95-101``)."""
+    if mag < lo_threshold:
+        return reduced_steps
+    if mag < hi_threshold:
+        return mid_steps
+    return full_steps
+
+
+def action_step_schedule(actions: torch.Tensor, **thresholds) -> List[int]:
+    """Per-frame solver steps for a rollout: the action magnitudes of the first session
+    (``actions[0].abs().sum(-1)``, as the reference computes them) through
+    ``steps_for_action_magnitude``.  actions (B, frames, 25)."""
+    mags = actions[0].abs().sum(dim=-1).float().cpu().tolist()
+    return [steps_for_action_magnitude(m, **thresholds) for m in mags]
+
+
 @torch.no_grad()
 def rollout_dpmpp(dit, prompt_latent: torch.Tensor, actions: torch.Tensor, num_frames: int,
-                  solver_steps: int = 5, stabilization_level: int = 15, noise_abs_max: float = 20.0,
+                  solver_steps: Union[int, Sequence[int]] = 5, stabilization_level: int = 15,
+                  noise_abs_max: float = 20.0,
                   seed: int = 42, use_cache: bool = False, kv_kinds=None,
                   alpha_bar: Optional[torch.Tensor] = None, step_callback=None) -> torch.Tensor:
     """DPM-Solver++ 2M rollout of ``num_frames`` new frames for B sessions.
 
     prompt_latent (B, n_prompt, 16, 18, 32) on the device; actions (B, n_prompt +
-    num_frames, 25).  Returns all latents (B, n_prompt + num_frames, 16, 18, 32)."""
+    num_frames, 25).  ``solver_steps`` is one count for every frame or a per-frame list
+    indexed by absolute frame (e.g. ``action_step_schedule(actions)``).  Returns all
+    latents (B, n_prompt + num_frames, 16, 18, 32)."""
     device = prompt_latent.device
     ab = (alpha_bar if alpha_bar is not None else alphas_cumprod()).float().cpu()
-    nr = torch.linspace(-1, DDPM_T - 1, solver_steps + 1)
     max_frames = dit.max_frames
     B, n_prompt = prompt_latent.shape[:2]
     total = n_prompt + num_frames
@@ -130,7 +156,9 @@ def rollout_dpmpp(dit, prompt_latent: torch.Tensor, actions: torch.Tensor, num_f
         if use_cache and T > 1 and (cache is None or cache.n_slots != T - 1):
             kinds = kv_kinds(T - 1) if kv_kinds is not None else ["bf16"] * (T - 1)
             cache = KVCacheB200(B, dit.depth, kinds, device=device)
-        for k, noise_idx in enumerate(reversed(range(1, solver_steps + 1))):
+        steps_i = int(solver_steps) if isinstance(solver_steps, int) else int(solver_steps[i])
+        nr = torch.linspace(-1, DDPM_T - 1, steps_i + 1)
+        for k, noise_idx in enumerate(reversed(range(1, steps_i + 1))):
             t = int(nr[noise_idx])
             tn = int(nr[noise_idx - 1])
             tn = t if tn < 0 else tn

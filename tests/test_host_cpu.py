@@ -106,3 +106,17 @@ def test_progressive_policy_matches_reference_thresholds(pkg):
     kinds = q.slot_kinds(12)  # slot s holds a frame of age 12 - s
     assert kinds[-1] == "bf16" and kinds[-2] == "fp8" and kinds[0] == "int4"
     assert kinds.count("int4") == 6  # ages 12..7 (V reaches INT4 at 7)
+
+
+def test_action_step_schedule_buckets(pkg):
+    """steps(i) = 2 if ||a_i||_1 < 0.5, 3 if < 1.5, else 5 (the reference's bucket
+    function, oasis_difficulty_dpmpp_modal.py:95-101; report eq. 'bucket')."""
+    f = pkg.steps_for_action_magnitude
+    assert [f(m) for m in (0.0, 0.49, 0.5, 1.49, 1.5, 7.0)] == [2, 2, 3, 3, 5, 5]
+    assert f(0.7, lo_threshold=1.0, reduced_steps=1) == 1
+    a = torch.zeros(2, 4, 25)
+    a[0, 1, 0] = 1.0           # moderate
+    a[0, 2, :3] = 1.0          # active (L1 = 3)
+    a[0, 3, 23:] = -0.2        # camera only, idle (L1 = 0.4)
+    a[1] = 9.0                 # other sessions do not change the schedule
+    assert pkg.action_step_schedule(a) == [2, 3, 5, 2]
