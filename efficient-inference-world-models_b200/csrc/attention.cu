@@ -13,50 +13,65 @@ namespace oasis {
 constexpr int kQkvLd = 3 * OASIS_HIDDEN;  // 3072
 constexpr int kSmemStride = 72;           // bf16 per staged row (64 + 8 pad: conflict-free ldmatrix)
 
+// Address of 16-byte chunk `chunk` (0..7) of row `row` in a tile of 128-byte rows
+// written by TMA with 128-byte swizzle (tile base 1024-byte aligned): the chunk index
+// is XORed with row mod 8, which also makes 8-row ldmatrix reads bank-conflict free.
+__device__ __forceinline__ uint32_t sw128(uint32_t tile, int row, int chunk) {
+  return tile + row * 128 + ((chunk ^ (row & 7)) << 4);
+}
+
 // ----------------------------------------------------------------------------------
-// spatial attention: one CTA per (frame, head), 9 warps x 16 query rows
+// spatial attention: one CTA per (frame, head), 9 warps x 16 query rows.  Q, K and V
+// (144 x 64 each) arrive by three TMA tensor loads into 128B-swizzled tiles; Q and K
+// complete on one barrier and V on another, so QK^T starts while V is in flight.
 // ----------------------------------------------------------------------------------
 constexpr int kSpThreads = 288;
-constexpr int kSpSmem = 3 * OASIS_TOKENS * kSmemStride * 2;  // 62,208 B
+constexpr int kSpTile = OASIS_TOKENS * 128;            // 18,432 B
+constexpr int kSpSmem = 3 * kSpTile + 1024 + 64;       // tiles + alignment slack + barriers
 
 __global__ void __launch_bounds__(kSpThreads, 2)
-    attn_spatial_kernel(const __nv_bfloat16* __restrict__ qkv, __nv_bfloat16* __restrict__ out,
+    attn_spatial_kernel(const __grid_constant__ CUtensorMap tm_qkv, __nv_bfloat16* __restrict__ out,
                         float scale_log2) {
   pdl_trigger();
-  pdl_wait();
-  extern __shared__ __align__(16) uint8_t sm_sp[];
-  __nv_bfloat16* sQ = reinterpret_cast<__nv_bfloat16*>(sm_sp);
+  extern __shared__ uint8_t sm_sp[];
+  uint8_t* tiles = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(sm_sp) + 1023) &
+                                              ~static_cast<uintptr_t>(1023));
+  uint64_t* bar = reinterpret_cast<uint64_t*>(tiles + 3 * kSpTile);
   const int f = blockIdx.x;
   const int h = blockIdx.y;
-  const __nv_bfloat16* base = qkv + static_cast<long long>(f) * OASIS_TOKENS * kQkvLd + h * 64;
-
-  for (int i = threadIdx.x; i < 3 * OASIS_TOKENS * 8; i += kSpThreads) {
-    const int which = i / (OASIS_TOKENS * 8);
-    const int r = (i >> 3) % OASIS_TOKENS;
-    const int c = i & 7;
-    cp_async16(sQ + (which * OASIS_TOKENS + r) * kSmemStride + c * 8,
-               base + static_cast<long long>(r) * kQkvLd + which * OASIS_HIDDEN + c * 8);
+  if (threadIdx.x == 0) {
+    mbar_init(&bar[0], 1);
+    mbar_init(&bar[1], 1);
+    mbar_fence_init();
+    tma_prefetch_desc(&tm_qkv);
   }
-  cp_async_wait_all();
   __syncthreads();
-
-  const __nv_bfloat16* sK = sQ + OASIS_TOKENS * kSmemStride;
-  const __nv_bfloat16* sV = sK + OASIS_TOKENS * kSmemStride;
+  pdl_wait();  // qkv comes from the previous kernel; out is read by earlier ones
+  if (threadIdx.x == 0) {
+    mbar_arrive_expect_tx(&bar[0], 2 * kSpTile);
+    tma_load_2d(tiles, &tm_qkv, &bar[0], h * 64, f * OASIS_TOKENS);
+    tma_load_2d(tiles + kSpTile, &tm_qkv, &bar[0], OASIS_HIDDEN + h * 64, f * OASIS_TOKENS);
+    mbar_arrive_expect_tx(&bar[1], kSpTile);
+    tma_load_2d(tiles + 2 * kSpTile, &tm_qkv, &bar[1], 2 * OASIS_HIDDEN + h * 64, f * OASIS_TOKENS);
+  }
+  const uint32_t sQ = smem_u32(tiles), sK = sQ + kSpTile, sV = sK + kSpTile;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int r0 = warp * 16;
+  if (!mbar_wait(&bar[0], 0)) return;  // timeout recorded in the device error word
 
   uint32_t qa[4][4];
 #pragma unroll
   for (int kk = 0; kk < 4; ++kk)
-    ldsm_x4(smem_u32(sQ + (r0 + (lane & 15)) * kSmemStride + kk * 16 + (lane >> 4) * 8), qa[kk][0],
-            qa[kk][1], qa[kk][2], qa[kk][3]);
+    ldsm_x4(sw128(sQ, r0 + (lane & 15), kk * 2 + (lane >> 4)), qa[kk][0], qa[kk][1], qa[kk][2],
+            qa[kk][3]);
 
   // online softmax over 3 key blocks of 48 (keeps ~100 registers -> 2 CTAs per SM)
   float o[8][4];
 #pragma unroll
   for (int j = 0; j < 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.0f;
   float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
+  bool v_ready = false;
 #pragma unroll 1
   for (int kb = 0; kb < 3; ++kb) {
     float s[6][4];
@@ -68,8 +83,7 @@ __global__ void __launch_bounds__(kSpThreads, 2)
       for (int kk = 0; kk < 4; ++kk) {
         uint32_t b0, b1, b2, b3;
         const int key = kb * 48 + jp * 16 + (lane & 7) + ((lane >> 4) << 3);
-        const int col = kk * 16 + ((lane >> 3) & 1) * 8;
-        ldsm_x4(smem_u32(sK + key * kSmemStride + col), b0, b1, b2, b3);
+        ldsm_x4(sw128(sK, key, kk * 2 + ((lane >> 3) & 1)), b0, b1, b2, b3);
         mma_bf16_16816(s[2 * jp], qa[kk], b0, b1);
         mma_bf16_16816(s[2 * jp + 1], qa[kk], b2, b3);
       }
@@ -107,6 +121,10 @@ __global__ void __launch_bounds__(kSpThreads, 2)
       o[j][2] *= alpha1;
       o[j][3] *= alpha1;
     }
+    if (!v_ready) {
+      if (!mbar_wait(&bar[1], 0)) return;
+      v_ready = true;
+    }
 #pragma unroll
     for (int kk = 0; kk < 3; ++kk) {
       uint32_t pa[4];
@@ -118,8 +136,7 @@ __global__ void __launch_bounds__(kSpThreads, 2)
       for (int jd = 0; jd < 8; jd += 2) {
         uint32_t b0, b1, b2, b3;
         const int key = kb * 48 + kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
-        const int col = jd * 8 + (lane >> 4) * 8;
-        ldsm_x4_t(smem_u32(sV + key * kSmemStride + col), b0, b1, b2, b3);
+        ldsm_x4_t(sw128(sV, key, jd + (lane >> 4)), b0, b1, b2, b3);
         mma_bf16_16816(o[jd], pa, b0, b1);
         mma_bf16_16816(o[jd + 1], pa, b2, b3);
       }
@@ -150,6 +167,9 @@ constexpr int kTpWarps = 4;
 constexpr int kTpRowsPerMat = 32;
 constexpr int kTpWarpSmem = 3 * kTpRowsPerMat * kSmemStride;  // bf16 elements
 constexpr int kTpSmem = kTpWarps * kTpWarpSmem * 2;             // 55,296 B
+constexpr int kTpTmaTile = kTpRowsPerMat * 128;                   // 4 KB: 32 frames x 64 bf16
+constexpr int kTpTmaTiles = kTpWarps * 3 * kTpTmaTile;            // 48 KB
+constexpr int kTpSmemTma = kTpTmaTiles + 1024 + 64;               // + alignment slack, barrier
 
 // two e4m3fn codes -> floats (hardware conversion to f16 is exact, NaN codes stay NaN)
 __device__ __forceinline__ float2 e4m3x2_to_float2(uint32_t two_codes) {
@@ -179,13 +199,28 @@ __device__ __forceinline__ uint4 dequant_int4x8(uint32_t w, float scale, float z
   return make_uint4(r[0], r[1], r[2], r[3]);
 }
 
+// TMA = true: full-window call (no cached past): Q, K, V of the 4 heads arrive by 12
+// TMA tensor loads (box = 32 frames x 64 columns of one token) into 128B-swizzled
+// 4 KB tiles.  TMA = false: cached past frames, staged (and dequantised) by the threads.
+template <bool TMA>
 __global__ void __launch_bounds__(kTpWarps * 32)
-    attn_temporal_kernel(const __nv_bfloat16* __restrict__ qkv, __nv_bfloat16* __restrict__ out,
+    attn_temporal_kernel(const __grid_constant__ CUtensorMap tm_qkv,
+                         const __nv_bfloat16* __restrict__ qkv, __nv_bfloat16* __restrict__ out,
                          KvView kv, int layer, int q_frames, int q_pos0, int n_past, int n_kv,
                          float scale_log2) {
   pdl_trigger();
+  extern __shared__ __align__(16) uint8_t sm_tp_raw[];
+  uint8_t* sm_tp = TMA ? reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(sm_tp_raw) + 1023) &
+                                                    ~static_cast<uintptr_t>(1023))
+                       : sm_tp_raw;
+  uint64_t* tbar = reinterpret_cast<uint64_t*>(sm_tp + kTpTmaTiles);
+  if (TMA && threadIdx.x == 0) {
+    mbar_init(tbar, 1);
+    mbar_fence_init();
+    tma_prefetch_desc(&tm_qkv);
+  }
+  if (TMA) __syncthreads();
   pdl_wait();
-  extern __shared__ __align__(16) uint8_t sm_tp[];
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int p = blockIdx.x;                 // token within frame
@@ -201,6 +236,16 @@ __global__ void __launch_bounds__(kTpWarps * 32)
   const int tid = threadIdx.x;
   const int n_live = n_kv - n_past;
 
+  if constexpr (TMA) {
+    if (threadIdx.x == 0) {
+      mbar_arrive_expect_tx(tbar, kTpTmaTiles);
+      for (int hh = 0; hh < kTpWarps; ++hh)
+        for (int which = 0; which < 3; ++which)
+          tma_load_3d(sm_tp + (hh * 3 + which) * kTpTmaTile, &tm_qkv, tbar,
+                      which * OASIS_HIDDEN + (hg * kTpWarps + hh) * 64, p, b * q_frames);
+    }
+    if (!mbar_wait(tbar, 0)) return;  // timeout recorded in the device error word
+  } else {
   // ---- cooperative staging: the 4 heads of one (session, token) are contiguous ----
   // Q rows and live K/V rows: 3 x 512 B per frame (cp.async, 16-byte chunks)
   for (int i = tid; i < q_frames * 32; i += kTpWarps * 32) {
@@ -262,18 +307,23 @@ __global__ void __launch_bounds__(kTpWarps * 32)
   }
   cp_async_wait_all();
   __syncthreads();
+  }
 
-  __nv_bfloat16* sQ = mat(warp, 0);
-  __nv_bfloat16* sK = mat(warp, 1);
-  __nv_bfloat16* sV = mat(warp, 2);
+  // 16-byte chunk `chunk` of row `row` of this warp's Q (0), K (1) or V (2) tile
+  auto at = [&](int which, int row, int chunk) -> uint32_t {
+    if constexpr (TMA)
+      return sw128(smem_u32(sm_tp + (warp * 3 + which) * kTpTmaTile), row, chunk);
+    else
+      return smem_u32(mat(warp, which) + row * kSmemStride + chunk * 8);
+  };
   const int g = lane >> 2, c = lane & 3;
 
   for (int mt = 0; mt < m_tiles; ++mt) {
     uint32_t qa[4][4];
 #pragma unroll
     for (int kk = 0; kk < 4; ++kk)
-      ldsm_x4(smem_u32(sQ + (mt * 16 + (lane & 15)) * kSmemStride + kk * 16 + (lane >> 4) * 8),
-              qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3]);
+      ldsm_x4(at(0, mt * 16 + (lane & 15), kk * 2 + (lane >> 4)), qa[kk][0], qa[kk][1], qa[kk][2],
+              qa[kk][3]);
     float s[4][4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.0f;
@@ -284,8 +334,7 @@ __global__ void __launch_bounds__(kTpWarps * 32)
         for (int kk = 0; kk < 4; ++kk) {
           uint32_t b0, b1, b2, b3;
           const int key = jp * 16 + (lane & 7) + ((lane >> 4) << 3);
-          const int col = kk * 16 + ((lane >> 3) & 1) * 8;
-          ldsm_x4(smem_u32(sK + key * kSmemStride + col), b0, b1, b2, b3);
+          ldsm_x4(at(1, key, kk * 2 + ((lane >> 3) & 1)), b0, b1, b2, b3);
           mma_bf16_16816(s[2 * jp], qa[kk], b0, b1);
           mma_bf16_16816(s[2 * jp + 1], qa[kk], b2, b3);
         }
@@ -342,8 +391,7 @@ __global__ void __launch_bounds__(kTpWarps * 32)
         for (int jd = 0; jd < 8; jd += 2) {
           uint32_t b0, b1, b2, b3;
           const int key = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
-          const int col = jd * 8 + (lane >> 4) * 8;
-          ldsm_x4_t(smem_u32(sV + key * kSmemStride + col), b0, b1, b2, b3);
+          ldsm_x4_t(at(2, key, jd + (lane >> 4)), b0, b1, b2, b3);
           mma_bf16_16816(o[jd], pa, b0, b1);
           mma_bf16_16816(o[jd + 1], pa, b2, b3);
         }
@@ -379,10 +427,15 @@ int launch_attn_spatial(const void* qkv, void* out, int frames, cudaStream_t str
     if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(attn_spatial)");
     configured = true;
   }
+  // qkv [frames * 144][3072] bf16; box = one head's 64 columns of one frame's 144 rows
+  CUtensorMap tm;
+  const long long dims[2] = {3 * OASIS_HIDDEN, static_cast<long long>(frames) * OASIS_TOKENS};
+  const long long strides[1] = {3 * OASIS_HIDDEN * 2};
+  const int box[2] = {64, OASIS_TOKENS};
+  if (int st = encode_bf16_sw128(&tm, qkv, 2, dims, strides, box)) return st;
   dim3 grid(frames, OASIS_HEADS);
-  cudaError_t e = launch_pdl(attn_spatial_kernel, grid, dim3(kSpThreads), kSpSmem, stream,
-                             static_cast<const __nv_bfloat16*>(qkv), static_cast<__nv_bfloat16*>(out),
-                             kScaleLog2);
+  cudaError_t e = launch_pdl(attn_spatial_kernel, grid, dim3(kSpThreads), kSpSmem, stream, tm,
+                             static_cast<__nv_bfloat16*>(out), kScaleLog2);
   if (e != cudaSuccess) return cuda_status(e, "attn_spatial_kernel");
   return OASIS_OK;
 }
@@ -427,15 +480,32 @@ int launch_attn_temporal(const void* qkv, const KvView& kv, int layer, void* out
                          int q_frames, int q_pos0, int n_past, int n_kv, cudaStream_t stream) {
   static bool configured = false;
   if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(attn_temporal_kernel,
+    cudaError_t e = cudaFuncSetAttribute(attn_temporal_kernel<false>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, kTpSmem);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(attn_temporal_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               kTpSmemTma);
     if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(attn_temporal)");
     configured = true;
   }
   dim3 grid(OASIS_TOKENS, OASIS_HEADS / kTpWarps, batch);
-  cudaError_t e = launch_pdl(attn_temporal_kernel, grid, dim3(kTpWarps * 32), kTpSmem, stream,
-                             static_cast<const __nv_bfloat16*>(qkv), static_cast<__nv_bfloat16*>(out),
-                             kv, layer, q_frames, q_pos0, n_past, n_kv, kScaleLog2);
+  CUtensorMap tm{};
+  const bool tma = n_past == 0;
+  if (tma) {
+    // qkv viewed as [frames][144 tokens][3072]: box = 64 columns x 1 token x 32 frames
+    const long long dims[3] = {3 * OASIS_HIDDEN, OASIS_TOKENS, static_cast<long long>(batch) * q_frames};
+    const long long strides[2] = {3 * OASIS_HIDDEN * 2, static_cast<long long>(OASIS_TOKENS) * 3 * OASIS_HIDDEN * 2};
+    const int box[3] = {64, 1, kTpRowsPerMat};
+    if (int st = encode_bf16_sw128(&tm, qkv, 3, dims, strides, box)) return st;
+  }
+  cudaError_t e = tma ? launch_pdl(attn_temporal_kernel<true>, grid, dim3(kTpWarps * 32), kTpSmemTma,
+                                   stream, tm, static_cast<const __nv_bfloat16*>(qkv),
+                                   static_cast<__nv_bfloat16*>(out), kv, layer, q_frames, q_pos0,
+                                   n_past, n_kv, kScaleLog2)
+                      : launch_pdl(attn_temporal_kernel<false>, grid, dim3(kTpWarps * 32), kTpSmem,
+                                   stream, tm, static_cast<const __nv_bfloat16*>(qkv),
+                                   static_cast<__nv_bfloat16*>(out), kv, layer, q_frames, q_pos0,
+                                   n_past, n_kv, kScaleLog2);
   if (e != cudaSuccess) return cuda_status(e, "attn_temporal_kernel");
   return OASIS_OK;
 }

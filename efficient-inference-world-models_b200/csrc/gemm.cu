@@ -47,6 +47,33 @@ int encode_2d(CUtensorMap* map, const void* base, long long rows, long long cols
 
 // Most CTA pairs of this kernel that can be resident at once (clusters are placed
 // within a GPC, so this can be below num_sms() / 2).
+}  // namespace
+
+// bf16 tensor of rank 2 or 3 (dims innermost first, byte strides of dims 1..rank-1),
+// 128-byte swizzled boxes (box[0] * 2 == 128).
+int encode_bf16_sw128(CUtensorMap* map, const void* base, int rank, const long long* dims,
+                      const long long* strides_bytes, const int* box) {
+  if (int s = get_encoder()) return s;
+  if (!aligned16(base)) return fail(OASIS_ERR_ALIGNMENT, "tensor map base not 16-byte aligned");
+  cuuint64_t d[3], st[2];
+  cuuint32_t b[3], e[3] = {1, 1, 1};
+  for (int i = 0; i < rank; ++i) {
+    d[i] = static_cast<cuuint64_t>(dims[i]);
+    b[i] = static_cast<cuuint32_t>(box[i]);
+    if (i > 0) {
+      if (strides_bytes[i - 1] % 16) return fail(OASIS_ERR_ALIGNMENT, "tensor map stride not 16-byte aligned");
+      st[i - 1] = static_cast<cuuint64_t>(strides_bytes[i - 1]);
+    }
+  }
+  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<void*>(base), d, st, b,
+                        e, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(OASIS_ERR_CUDA, "cuTensorMapEncodeTiled failed");
+  return OASIS_OK;
+}
+
+namespace {
+
 template <int BN, int EPI>
 int max_pairs() {
   using S = GemmShape<BN, 2>;

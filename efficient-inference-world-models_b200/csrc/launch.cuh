@@ -19,6 +19,10 @@ struct KvView {
 };
 
 int make_kv_view(const oasis_kv_cache_t* c, KvView* v);
+// bf16 tensor map of rank 2 or 3 (dims innermost first, byte strides of dims 1..),
+// 128-byte swizzled boxes.
+int encode_bf16_sw128(CUtensorMap* map, const void* base, int rank, const long long* dims,
+                      const long long* strides_bytes, const int* box);
 int validate_slots(const oasis_kv_cache_t* c, int slot0, int frames);
 
 int launch_attn_spatial(const void* qkv, void* out, int frames, cudaStream_t stream);
