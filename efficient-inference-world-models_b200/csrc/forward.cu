@@ -31,9 +31,11 @@ struct Layout {
   size_t cnt_bytes;  // row-block counters of the residual GEMMs' LayerNorm tails
 };
 
-// One counter per 128-row block for each residual GEMM (out-proj and fc2 of every
-// sub-block), zeroed at the start of every forward.
+// Row-block counters (one per 128-row block), zeroed at the start of every forward.
+// Per sub-block: 0 out-proj tiles, 1 rows normalised after it, 2 fc1 tiles, 3 fc2
+// tiles, 4 rows normalised after fc2 (the separate-launch path uses 0 and 3).
 inline size_t row_blocks(size_t M) { return (M + 127) / 128; }
+constexpr int kCountersPerSub = 5;
 
 constexpr int kH1aLd = OASIS_HIDDEN + 64;  // [first-linear output | actions | zero pad]
 
@@ -57,7 +59,7 @@ Layout layout_for(int F, int depth) {
   L.h1a = take(static_cast<size_t>(F) * kH1aLd * 2);
   L.silu = take(static_cast<size_t>(F) * OASIS_HIDDEN * 2);
   L.mod = take(static_cast<size_t>(F) * mod_ld * 4);
-  L.cnt_bytes = static_cast<size_t>(4 * depth) * row_blocks(M) * 4;
+  L.cnt_bytes = static_cast<size_t>(2 * depth) * kCountersPerSub * row_blocks(M) * 4;
   L.cnt = take(L.cnt_bytes);
   L.total = off;
   return L;
@@ -78,6 +80,9 @@ struct oasis_plan {
   oasis::GemmOperands fin;
   oasis::GemmOperands qkv[2 * OASIS_MAX_DEPTH], out[2 * OASIS_MAX_DEPTH];  // per sub-block
   oasis::GemmOperands fc1[2 * OASIS_MAX_DEPTH], fc2[2 * OASIS_MAX_DEPTH];
+  // out-proj, fc1, fc2 and the next QKV of a sub-block run as one chained launch
+  // (gemm_chain_kernel) when all of them use CTA-pair 256-wide tiles
+  bool chain = false;
   // timing
   bool timing = false;
   std::vector<cudaEvent_t> ev;
@@ -141,12 +146,35 @@ int run_forward(oasis_plan* p, const float* x, const int64_t* t, const float* ac
   }
   // the residual GEMMs (out-proj, fc2) end with the LayerNorm + modulate that feeds the
   // next GEMM: shift/scale rows and counter slice for launch k
-  auto ln_tail = [&](EpiParams& ep, const float* shift, int k) {
+  auto cnt = [&](int j, int c) { return counters + (static_cast<size_t>(j) * kCountersPerSub + c) * nblk; };
+  auto ln_tail = [&](EpiParams& ep, const float* shift, unsigned int* tiles_done) {
     ep.ln_out = static_cast<__nv_bfloat16*>(hbuf);
     ep.ln_shift = shift;
     ep.ln_scale = shift + OASIS_HIDDEN;
     ep.ln_mod_ld = mld;
-    ep.ln_count = counters + static_cast<size_t>(k) * nblk;
+    ep.ln_count = tiles_done;
+  };
+  const int T = p->frames;
+  const int pos0 = cached ? n_past : 0;
+  // QKV of sub-block j (RoPE on q and k: axial over the 144 tokens for spatial
+  // sub-blocks, over the window position for temporal ones)
+  auto qkv_params = [&](int j) {
+    EpiParams ep{};
+    ep.out = qkv;
+    ep.ldd = 3 * OASIS_HIDDEN;
+    ep.rope_cols = 2 * OASIS_HIDDEN;
+    if (j % 2 == 0) {
+      ep.rope = w.rope_spatial;
+      ep.rope_div = 1;
+      ep.rope_mod = OASIS_TOKENS;
+      ep.rope_add = 0;
+    } else {
+      ep.rope = w.rope_temporal;
+      ep.rope_div = OASIS_TOKENS;
+      ep.rope_mod = T;
+      ep.rope_add = pos0;
+    }
+    return ep;
   };
 
   // ---- embeddings (three small tcgen05 GEMMs) ----
@@ -187,11 +215,11 @@ int run_forward(oasis_plan* p, const float* x, const int64_t* t, const float* ac
   KvView kvv;
   if (int e = make_kv_view(cached ? cache : nullptr, &kvv)) return e;
 
-  const int T = p->frames;
-  const int pos0 = cached ? n_past : 0;
+  const bool chain = p->chain;
   for (int j = 0; j < 2 * p->depth; ++j) {
     const bool spatial = (j % 2) == 0;
     const int blk = j / 2;
+    const bool last = j == 2 * p->depth - 1;
     const oasis_sub_weights_t& sw = w.sub[j];
     const float* modj = mod + static_cast<long long>(j) * OASIS_ADA_PER_SUB;
     if (j == 0) {  // later LayerNorms are the tails of the residual GEMMs
@@ -200,24 +228,9 @@ int run_forward(oasis_plan* p, const float* x, const int64_t* t, const float* ac
                                      hbuf, M, OASIS_TOKENS, s))
         return e;
     }
-    {
+    if (j == 0 || !chain) {  // otherwise the previous sub-block's chain computed it
       Timer tm(p, s, kFamGemm);
-      EpiParams ep{};
-      ep.out = qkv;
-      ep.ldd = 3 * OASIS_HIDDEN;
-      ep.rope_cols = 2 * OASIS_HIDDEN;
-      if (spatial) {
-        ep.rope = w.rope_spatial;
-        ep.rope_div = 1;
-        ep.rope_mod = OASIS_TOKENS;
-        ep.rope_add = 0;
-      } else {
-        ep.rope = w.rope_temporal;
-        ep.rope_div = OASIS_TOKENS;
-        ep.rope_mod = T;
-        ep.rope_add = pos0;
-      }
-      if (int e = launch_gemm(p->qkv[j], kEpiQkvRope, ep, s)) return e;
+      if (int e = launch_gemm(p->qkv[j], kEpiQkvRope, qkv_params(j), s)) return e;
     }
     if (spatial) {
       Timer tm(p, s, kFamSpatial);
@@ -240,36 +253,39 @@ int run_forward(oasis_plan* p, const float* x, const int64_t* t, const float* ac
         if (int e = launch_attn_temporal(qkv, kvv, blk, attn, p->batch, T, 0, 0, T, s)) return e;
       }
     }
-    {
-      Timer tm(p, s, kFamGemm);
-      EpiParams ep{};
-      ep.out = resid;
-      ep.ldd = OASIS_HIDDEN;
-      ep.bias = sw.out_b;
-      ep.gate = modj + 2 * OASIS_HIDDEN;
-      ep.gate_ld = mld;
-      ln_tail(ep, modj + 3 * OASIS_HIDDEN, 2 * j);  // -> input of fc1
-      if (int e = launch_gemm(p->out[j], kEpiGateResid, ep, s)) return e;
-    }
-    {
-      Timer tm(p, s, kFamGemm);
-      EpiParams ep{};
-      ep.out = mlp;
-      ep.ldd = OASIS_MLP_HIDDEN;
-      ep.bias = sw.fc1_b;
-      if (int e = launch_gemm(p->fc1[j], kEpiBiasGelu, ep, s)) return e;
-    }
-    {
-      Timer tm(p, s, kFamGemm);
-      EpiParams ep{};
-      ep.out = resid;
-      ep.ldd = OASIS_HIDDEN;
-      ep.bias = sw.fc2_b;
-      ep.gate = modj + 5 * OASIS_HIDDEN;
-      ep.gate_ld = mld;
-      // -> input of the next sub-block's QKV, or of the final layer (its shift, scale)
-      ln_tail(ep, modj + OASIS_ADA_PER_SUB, 2 * j + 1);
-      if (int e = launch_gemm(p->fc2[j], kEpiGateResid, ep, s)) return e;
+    EpiParams eo{};  // resid += gate_msa * (attn W_out^T + b); then LayerNorm -> input of fc1
+    eo.out = resid;
+    eo.ldd = OASIS_HIDDEN;
+    eo.bias = sw.out_b;
+    eo.gate = modj + 2 * OASIS_HIDDEN;
+    eo.gate_ld = mld;
+    ln_tail(eo, modj + 3 * OASIS_HIDDEN, cnt(j, 0));
+    EpiParams e1{};  // mlp = GELU(h W_1^T + b_1)
+    e1.out = mlp;
+    e1.ldd = OASIS_MLP_HIDDEN;
+    e1.bias = sw.fc1_b;
+    EpiParams e2{};  // resid += gate_mlp * (mlp W_2^T + b_2); then LayerNorm -> next QKV / final
+    e2.out = resid;
+    e2.ldd = OASIS_HIDDEN;
+    e2.bias = sw.fc2_b;
+    e2.gate = modj + 5 * OASIS_HIDDEN;
+    e2.gate_ld = mld;
+    ln_tail(e2, modj + OASIS_ADA_PER_SUB, cnt(j, 3));
+    Timer tm(p, s, kFamGemm);
+    if (chain) {
+      ChainStep st[kMaxChainOps];
+      st[0] = ChainStep{&p->out[j], kEpiGateResid, eo, nullptr, 0, cnt(j, 0), cnt(j, 1)};
+      st[1] = ChainStep{&p->fc1[j], kEpiBiasGelu, e1, cnt(j, 1), 0, cnt(j, 2), nullptr};
+      st[2] = ChainStep{&p->fc2[j], kEpiGateResid, e2, cnt(j, 2),
+                        static_cast<unsigned>(OASIS_MLP_HIDDEN / 256), cnt(j, 3), cnt(j, 4)};
+      int n = 3;
+      if (!last) st[n++] = ChainStep{&p->qkv[j + 1], kEpiQkvRope, qkv_params(j + 1), cnt(j, 4), 0,
+                                     nullptr, nullptr};
+      if (int e = launch_chain(st, n, s)) return e;
+    } else {
+      if (int e = launch_gemm(p->out[j], kEpiGateResid, eo, s)) return e;
+      if (int e = launch_gemm(p->fc1[j], kEpiBiasGelu, e1, s)) return e;
+      if (int e = launch_gemm(p->fc2[j], kEpiGateResid, e2, s)) return e;
     }
   }
   // ---- final layer (its LayerNorm + modulate was the last fc2's tail) ----
@@ -371,6 +387,10 @@ int plan_init(oasis_plan* p, const oasis_dit_weights_t* w, int batch, int frames
     if (!st) st = set_gemm_output(&p->fc2[j], p->ws + L.resid, OASIS_HIDDEN, true);
   }
   if (st) return st;
+  p->chain = true;
+  for (int j = 0; j < 2 * w->depth; ++j)
+    for (const GemmOperands* g : {&p->qkv[j], &p->out[j], &p->fc1[j], &p->fc2[j]})
+      if (g->ctas != 2 || g->bn != 256) p->chain = false;
   // weights are the B operand of these GEMMs (swap-AB GEMMs read activations as B)
   p->patch.b_is_weight = true;
   p->fin.b_is_weight = true;

@@ -207,6 +207,55 @@ int launch_gemm(const GemmOperands& g, int epi, const EpiParams& ep, cudaStream_
   return fail(OASIS_ERR_UNSUPPORTED, "GEMM tile N");
 }
 
+int launch_chain(const ChainStep* steps, int n, cudaStream_t stream) {
+  using S = GemmShape<256, 2>;
+  if (n < 1 || n > kMaxChainOps) return fail(OASIS_ERR_INVALID_ARG, "chain: 1..4 steps");
+  static bool configured = false;
+  static int pairs = 0;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         S::kSmemBytes);
+    if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(gemm_chain)");
+    pairs = max_pairs<256, kEpiGateResid>();
+    configured = true;
+  }
+  ChainParams P{};
+  P.n_ops = n;
+  P.prefetch_b = steps[0].g->b_is_weight ? 1 : 0;
+  int max_tiles = 0;
+  for (int i = 0; i < n; ++i) {
+    const GemmOperands& g = *steps[i].g;
+    if (g.ctas != 2 || g.bn != 256 || !g.has_d || g.N % 256)
+      return fail(OASIS_ERR_UNSUPPORTED, "chain: every step needs CTA-pair 256-wide tiles");
+    if (steps[i].epi != kEpiGateResid && steps[i].epi != kEpiBiasGelu && steps[i].epi != kEpiQkvRope)
+      return fail(OASIS_ERR_UNSUPPORTED, "chain: epilogue kind");
+    if (steps[i].ep.ln_out && (steps[i].epi != kEpiGateResid || !steps[i].tiles_done))
+      return fail(OASIS_ERR_INVALID_ARG, "chain: LayerNorm phase needs a residual step with counters");
+    ChainOp& op = P.op[i];
+    op.a = g.a;
+    op.b = g.b;
+    op.d = g.d;
+    op.ep = steps[i].ep;
+    op.ep.ln_count = steps[i].tiles_done;
+    op.M = g.M;
+    op.N = g.N;
+    op.K = g.K;
+    op.epi = steps[i].epi;
+    op.wait = steps[i].wait;
+    op.wait_tiles = steps[i].wait_tiles;
+    op.tiles_done = steps[i].tiles_done;
+    op.rows_done = steps[i].rows_done;
+    const int tiles = ((g.M + 255) / 256) * (g.N / 256);
+    if (tiles > max_tiles) max_tiles = tiles;
+  }
+  int units = pairs;
+  if (max_tiles < units) units = max_tiles;
+  cudaError_t e = launch_pdl_cluster(gemm_chain_kernel, dim3(units * 2), dim3(kGemmThreads),
+                                     S::kSmemBytes, stream, 2, P);
+  if (e != cudaSuccess) return cuda_status(e, "gemm_chain_kernel");
+  return OASIS_OK;
+}
+
 // CTA pairs on 256 x 256 tiles when there are about as many tiles as SM pairs or more
 // (each SM then stages half the B bytes per MMA: the N = 256 main loop stays
 // tensor-bound); otherwise single CTAs with the widest tile N that still gives every

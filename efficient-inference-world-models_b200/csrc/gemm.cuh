@@ -280,6 +280,127 @@ __device__ __forceinline__ void epilogue_prefetch(const EpiParams& p, int M, int
   }
 }
 
+// Box geometry of an epilogue: bf16 TMA boxes are 64 columns (2 TMEM loads); fp32 boxes
+// and row epilogues 32.
+template <int BN, int EPI>
+struct EpiGeom {
+  static constexpr int COLS = (epi_uses_tma(EPI) && !epi_out_f32(EPI)) ? 64 : 32;
+  static constexpr int NBLK = BN / COLS;
+  // bytes one warp needs to stage all of its boxes of a tile at once
+  static constexpr int kWarpTileBytes = ((NBLK + 1) / 2) * kEpiBufBytes;
+};
+
+// The epilogue of one accumulator tile by one epilogue warp (TMEM lane quarter
+// `quarter`, column blocks half, half+2, ...).  taddr: the warp's TMEM lanes at the
+// tile's accumulator; m0: this CTA's first row of the tile.  Boxes go through `buf`
+// (one 4 KB box, reused after its TMA store has read it; nbuf counts its stores) or,
+// when `staging` is set, each to its own 4 KB slot there (all stores in flight at once).
+// `release()` is called once the warp's last TMEM load of the tile has completed.
+template <int BN, int EPI, typename Release>
+__device__ __forceinline__ void epilogue_tile(const EpiParams& ep, const CUtensorMap* tmD, int M,
+                                              int N, uint32_t taddr, int m0, int n0, int quarter,
+                                              int half, int lane, uint8_t* buf, int& nbuf,
+                                              uint8_t* staging, Release release) {
+  using G = EpiGeom<BN, EPI>;
+  constexpr int COLS = G::COLS, NBLK = G::NBLK;
+  const int m_row = m0 + quarter * 32 + lane;  // this thread's row
+  const bool rows_live = m0 + quarter * 32 < M;
+  const int last_blk = (NBLK - 1 - half) >= 0 ? ((NBLK - 1 - half) / 2) * 2 + half : -1;
+  if (last_blk < 0) {  // owns no columns of this tile
+    release();
+    return;
+  }
+#pragma unroll 1
+  for (int blk = half; blk < NBLK; blk += 2) {
+    const int nb = n0 + blk * COLS;
+    float v[32], w[32];
+    tmem_ld32(taddr + blk * COLS, v);
+    if (COLS == 64) tmem_ld32(taddr + blk * COLS + 32, w);
+    if (blk == last_blk) release();  // this warp's share of the accumulator is read
+    if (!epi_uses_tma(EPI)) {
+      if (EPI != kEpiFinal || nb < N) epilogue_rows<EPI>(ep, M, m_row, nb, v);
+      continue;
+    }
+    if (!rows_live || nb >= N) continue;
+    uint8_t* box = buf;
+    if (staging) {
+      box = staging + (blk >> 1) * kEpiBufBytes;
+    } else if (nbuf > 0) {  // the previous store from buf must have read it
+      if (lane == 0) bulk_wait_read<0>();
+      __syncwarp();
+    }
+    epilogue_math<EPI>(ep, m_row, nb, v);
+    if (COLS == 64) {
+      epilogue_math<EPI>(ep, m_row, nb + 32, w);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        st_swizzled(box, lane, c, make_uint4(pack_bf16x2(v[8 * c + 0], v[8 * c + 1]),
+                                             pack_bf16x2(v[8 * c + 2], v[8 * c + 3]),
+                                             pack_bf16x2(v[8 * c + 4], v[8 * c + 5]),
+                                             pack_bf16x2(v[8 * c + 6], v[8 * c + 7])));
+        st_swizzled(box, lane, 4 + c, make_uint4(pack_bf16x2(w[8 * c + 0], w[8 * c + 1]),
+                                                 pack_bf16x2(w[8 * c + 2], w[8 * c + 3]),
+                                                 pack_bf16x2(w[8 * c + 4], w[8 * c + 5]),
+                                                 pack_bf16x2(w[8 * c + 6], w[8 * c + 7])));
+      }
+    } else {
+#pragma unroll
+      for (int c = 0; c < 8; ++c)
+        st_swizzled(box, lane, c, make_uint4(__float_as_uint(v[4 * c + 0]), __float_as_uint(v[4 * c + 1]),
+                                             __float_as_uint(v[4 * c + 2]), __float_as_uint(v[4 * c + 3])));
+    }
+    fence_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      if (EPI == kEpiGateResid)
+        tma_reduce_add_2d(tmD, box, nb, m0 + quarter * 32);
+      else
+        tma_store_2d(tmD, box, nb, m0 + quarter * 32);
+      bulk_commit();
+    }
+    if (!staging) ++nbuf;
+  }
+}
+
+// LayerNorm + modulate of the residual rows [c*R, c*R + R) of this CTA (c = blockIdx.x,
+// R = ceil(M / gridDim.x) rounded to 4) into ep.ln_out, each 4-row group once the
+// `target` tiles of its 128-row block have been counted in ep.ln_count.  Warp w
+// (0..7) takes groups w, w+8, ...; a group never crosses a frame or a block (144 and
+// 128 are multiples of 4).  A group's 16 KB are copied into `stage` (16 KB per warp,
+// idle shared memory) in one round trip and reduced from there.  When `rows_done` is
+// set, each finished group adds its row count to rows_done[block] (release).
+// Returns false when a wait timed out.
+__device__ __forceinline__ bool ln_rows_phase(const EpiParams& ep, int M, unsigned target, int w,
+                                              int lane, float4* stage, unsigned int* rows_done) {
+  const int R = ((M + static_cast<int>(gridDim.x) - 1) / static_cast<int>(gridDim.x) + 3) & ~3;
+  const int r_begin = static_cast<int>(blockIdx.x) * R;
+  const int r_end = min(M, r_begin + R);
+  for (int row0 = r_begin + w * kLnRowsPerWarp; row0 < r_end; row0 += kEpiWarps * kLnRowsPerWarp) {
+    int ok = 1;
+    if (lane == 0) ok = wait_count_geq(ep.ln_count + row0 / kGemmBM, target);
+    if (!__shfl_sync(0xffffffffu, ok, 0)) return false;
+    __syncwarp();  // the acquire by lane 0 orders the whole warp's loads
+    const int nrows = min(kLnRowsPerWarp, r_end - row0);
+    const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(ep.out) +
+                                                        static_cast<long long>(row0) * OASIS_HIDDEN);
+    for (int r = 0; r < nrows; ++r)
+#pragma unroll
+      for (int i = 0; i < 8; ++i)  // each lane copies (and later reads) its own columns
+        cp_async16(stage + r * 256 + lane + 32 * i, src + r * 256 + lane + 32 * i);
+    const long long f = row0 / OASIS_TOKENS;
+    float4 a4[8], s4[8];
+    ln_load_modulation(ep.ln_shift + f * ep.ln_mod_ld, ep.ln_scale + f * ep.ln_mod_ld, lane, a4, s4);
+    cp_async_wait_all();
+    ln_modulate_rows_smem(stage, nrows, a4, s4, ep.ln_out + static_cast<long long>(row0) * OASIS_HIDDEN,
+                          lane);
+    if (rows_done) {
+      __syncwarp();
+      if (lane == 0) red_release_add(rows_done + row0 / kGemmBM, static_cast<unsigned>(nrows));
+    }
+  }
+  return true;
+}
+
 template <int BN, int EPI, int CTAS>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA,
@@ -464,94 +585,37 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     uint8_t* buf = epi_smem + (warp - 2) * kEpiBufBytes;
     int nbuf = 0;  // TMA stores issued by this warp from buf
     int it = 0;
-    // bf16 TMA boxes: 64 columns (2 TMEM loads); fp32 boxes and row epilogues: 32
-    constexpr int COLS = (epi_uses_tma(EPI) && !epi_out_f32(EPI)) ? 64 : 32;
-    constexpr int NBLK = BN / COLS;
+    using G = EpiGeom<BN, EPI>;
     // The last tile of a CTA has the operand stages to itself once its accumulator is
     // complete (no load is issued after its k-blocks and its MMAs have retired): each
     // warp stages all of its boxes there and issues their TMA stores back to back
     // instead of cycling one 4 KB buffer.
-    constexpr int kLastWarpBytes = ((NBLK + 1) / 2) * kEpiBufBytes;
-    static_assert(kEpiWarps * kLastWarpBytes <= STAGES * S::kStageBytes, "last-tile staging");
-    // one arrival per warp on the leader's tempty barrier once all its lanes have read
-    auto release = [&](int acc) {
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) {
-        if (CTAS == 2)
-          mbar_arrive_cluster(lead_tempty + acc * 8);
-        else
-          mbar_arrive(&tempty_bar[acc]);
-      }
-    };
+    static_assert(kEpiWarps * G::kWarpTileBytes <= STAGES * S::kStageBytes, "last-tile staging");
     for (int tile = unit; tile < num_tiles && !*abort_flag; tile += num_units, ++it) {
       const int m0 = (tile % num_m) * TILE_M + a_row0;  // this CTA's accumulator rows
       const int n0 = (tile / num_m) * BN;
       const int acc = it & 1;
       const uint32_t acc_phase = (it >> 1) & 1;
-      const int m_row = m0 + quarter * 32 + lane;  // this thread's row
-      if (epi_uses_tma(EPI)) epilogue_prefetch<EPI, COLS, NBLK>(ep, M, N, m_row, n0, half);
+      if (epi_uses_tma(EPI))
+        epilogue_prefetch<EPI, G::COLS, G::NBLK>(ep, M, N, m0 + quarter * 32 + lane, n0, half);
       if (!mbar_wait(&tfull_bar[acc], acc_phase)) { *abort_flag = 1; break; }
       tc_fence_after();
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                              static_cast<uint32_t>(acc * BN);
-      const bool rows_live = m0 + quarter * 32 < M;
       const bool last_tile = tile + num_units >= num_tiles;
-      const int last_blk = (NBLK - 1 - half) >= 0 ? ((NBLK - 1 - half) / 2) * 2 + half : -1;
-      if (last_blk < 0) {  // owns no columns of this tile
-        release(acc);
-        continue;
-      }
-#pragma unroll 1
-      for (int blk = half; blk < NBLK; blk += 2) {
-        const int nb = n0 + blk * COLS;
-        float v[32], w[32];
-        tmem_ld32(taddr + blk * COLS, v);
-        if (COLS == 64) tmem_ld32(taddr + blk * COLS + 32, w);
-        if (blk == last_blk) release(acc);  // this warp's share of the accumulator is read
-        if (!epi_uses_tma(EPI)) {
-          if (EPI != kEpiFinal || nb < N) epilogue_rows<EPI>(ep, M, m_row, nb, v);
-          continue;
-        }
-        if (!rows_live || nb >= N) continue;
-        uint8_t* box = buf;
-        if (last_tile) {
-          box = smem + (warp - 2) * kLastWarpBytes + (blk >> 1) * kEpiBufBytes;
-        } else if (nbuf > 0) {  // the previous store from buf must have read it
-          if (lane == 0) bulk_wait_read<0>();
-          __syncwarp();
-        }
-        epilogue_math<EPI>(ep, m_row, nb, v);
-        if (COLS == 64) {
-          epilogue_math<EPI>(ep, m_row, nb + 32, w);
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            st_swizzled(box, lane, c, make_uint4(pack_bf16x2(v[8 * c + 0], v[8 * c + 1]),
-                                                 pack_bf16x2(v[8 * c + 2], v[8 * c + 3]),
-                                                 pack_bf16x2(v[8 * c + 4], v[8 * c + 5]),
-                                                 pack_bf16x2(v[8 * c + 6], v[8 * c + 7])));
-            st_swizzled(box, lane, 4 + c, make_uint4(pack_bf16x2(w[8 * c + 0], w[8 * c + 1]),
-                                                     pack_bf16x2(w[8 * c + 2], w[8 * c + 3]),
-                                                     pack_bf16x2(w[8 * c + 4], w[8 * c + 5]),
-                                                     pack_bf16x2(w[8 * c + 6], w[8 * c + 7])));
-          }
-        } else {
-#pragma unroll
-          for (int c = 0; c < 8; ++c)
-            st_swizzled(box, lane, c, make_uint4(__float_as_uint(v[4 * c + 0]), __float_as_uint(v[4 * c + 1]),
-                                                 __float_as_uint(v[4 * c + 2]), __float_as_uint(v[4 * c + 3])));
-        }
-        fence_async_smem();
+      // one arrival per warp on the leader's tempty barrier once all its lanes have read
+      auto release = [&]() {
+        tc_fence_before();
         __syncwarp();
         if (lane == 0) {
-          if (EPI == kEpiGateResid)
-            tma_reduce_add_2d(&tmD, box, nb, m0 + quarter * 32);
+          if (CTAS == 2)
+            mbar_arrive_cluster(lead_tempty + acc * 8);
           else
-            tma_store_2d(&tmD, box, nb, m0 + quarter * 32);
-          bulk_commit();
+            mbar_arrive(&tempty_bar[acc]);
         }
-        if (!last_tile) ++nbuf;
-      }
+      };
+      epilogue_tile<BN, EPI>(ep, &tmD, M, N, taddr, m0, n0, quarter, half, lane, buf, nbuf,
+                             last_tile ? smem + (warp - 2) * G::kWarpTileBytes : nullptr, release);
     }
     if (epi_uses_tma(EPI) && lane == 0) bulk_wait<0>();  // all stores complete before exit
     __syncwarp();
@@ -568,35 +632,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           if (q < nblk) red_release_add(ep.ln_count + q, 1u);
         }
       }
-      // consume: this CTA normalises rows [c*R, c*R + R) once the N tiles of their
-      // block are all in.  Warp w takes 4-row groups w, w+8, ... (a group never crosses
-      // a frame or a block: 144 and 128 are multiples of 4); a group's 16 KB are copied
-      // into the now idle operand stages in one round trip, then reduced row by row.
-      const int R = ((M + static_cast<int>(gridDim.x) - 1) / static_cast<int>(gridDim.x) + 3) & ~3;
-      const int r_begin = static_cast<int>(blockIdx.x) * R;
-      const int r_end = min(M, r_begin + R);
-      float4* stage_rows = reinterpret_cast<float4*>(smem + (warp - 2) * (kLnRowsPerWarp * OASIS_HIDDEN * 4));
+      // consume, staging rows in the now idle operand stages (16 KB per warp)
       static_assert(kEpiWarps * kLnRowsPerWarp * OASIS_HIDDEN * 4 <= STAGES * S::kStageBytes, "LN staging");
-      for (int row0 = r_begin + (warp - 2) * kLnRowsPerWarp; row0 < r_end;
-           row0 += kEpiWarps * kLnRowsPerWarp) {
-        int ok = 1;
-        if (lane == 0) ok = wait_count_geq(ep.ln_count + row0 / kGemmBM, static_cast<unsigned>(num_n));
-        if (!__shfl_sync(0xffffffffu, ok, 0)) break;
-        __syncwarp();  // the acquire by lane 0 orders the whole warp's loads
-        const int nrows = min(kLnRowsPerWarp, r_end - row0);
-        const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(ep.out) +
-                                                            static_cast<long long>(row0) * OASIS_HIDDEN);
-        for (int r = 0; r < nrows; ++r)
-#pragma unroll
-          for (int i = 0; i < 8; ++i)  // each lane copies (and later reads) its own columns
-            cp_async16(stage_rows + r * 256 + lane + 32 * i, src + r * 256 + lane + 32 * i);
-        const long long f = row0 / OASIS_TOKENS;
-        float4 a4[8], s4[8];
-        ln_load_modulation(ep.ln_shift + f * ep.ln_mod_ld, ep.ln_scale + f * ep.ln_mod_ld, lane, a4, s4);
-        cp_async_wait_all();
-        ln_modulate_rows_smem(stage_rows, nrows, a4, s4,
-                              ep.ln_out + static_cast<long long>(row0) * OASIS_HIDDEN, lane);
-      }
+      ln_rows_phase(ep, M, static_cast<unsigned>(num_n), warp - 2, lane,
+                    reinterpret_cast<float4*>(smem + (warp - 2) * (kLnRowsPerWarp * OASIS_HIDDEN * 4)),
+                    nullptr);
     }
   }
 
@@ -612,6 +652,318 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     else
       tmem_dealloc<S::kTmemCols>(tmem_base);
   }
+}
+
+// ----------------------------------------------------------------------------------
+// Chained projections in one persistent launch: the out-projection (+ LayerNorm tail),
+// fc1, fc2 (+ LayerNorm tail) and the next sub-block's QKV of one token window run as
+// successive ops of one grid of CTA pairs (256 x 256 tiles).  An op's A rows are
+// loaded as soon as the 128-row block they come from is complete (row-block counters
+// published with release / read with acquire), so one op's tail overlaps the next
+// op's first tiles instead of a kernel boundary.  Dependencies only point to earlier
+// ops and every CTA of the grid is resident, so every wait ends (each is also bounded).
+// ----------------------------------------------------------------------------------
+constexpr int kMaxChainOps = 4;
+
+struct alignas(64) ChainOp {
+  CUtensorMap a, b, d;
+  EpiParams ep;                // ep.ln_out set (kEpiGateResid): LayerNorm phase after the op
+  int M, N, K, epi;            // epi: kEpiGateResid, kEpiBiasGelu or kEpiQkvRope
+  const unsigned int* wait;    // per 128-row block counters the A rows wait on, or null
+  unsigned int wait_tiles;     // target: this many tiles, or (0) the block's row count
+  unsigned int* tiles_done;    // +1 per finished tile and 128-row block (also ep.ln_count)
+  unsigned int* rows_done;     // LayerNorm phase: + rows per finished group, or null
+};
+
+struct ChainParams {
+  ChainOp op[kMaxChainOps];
+  int n_ops;
+  int prefetch_b;  // op 0's B (weights) may be fetched before the previous kernel ends
+};
+
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_chain_kernel(const __grid_constant__ ChainParams P) {
+  constexpr int BN = 256, CTAS = 2;
+  using S = GemmShape<BN, CTAS>;
+  constexpr int STAGES = S::kStages;
+  constexpr int TILE_M = kGemmBM * CTAS;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* epi_smem = smem + STAGES * S::kStageBytes;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(epi_smem + S::kEpiBytes);
+  uint64_t* empty_bar = full_bar + STAGES;
+  uint64_t* tfull_bar = empty_bar + STAGES;   // [2]
+  uint64_t* tempty_bar = tfull_bar + 2;       // [2]
+  uint64_t* drain_bar = tempty_bar + 2;       // [1]
+  uint64_t* ln_free_bar = drain_bar + 1;      // [1] epilogue warps -> producer: stages free again
+  uint64_t* stored_bar = ln_free_bar + 1;     // [1] epilogue warps -> publisher: a tile's stores done
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(stored_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+  static_assert(kEpiWarps * kLnRowsPerWarp * OASIS_HIDDEN * 4 <= STAGES * S::kStageBytes, "LN staging");
+
+  pdl_trigger();
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int unit = static_cast<int>(blockIdx.x) / CTAS;
+  const int num_units = static_cast<int>(gridDim.x) / CTAS;
+  const int a_row0 = static_cast<int>(rank) * kGemmBM;
+  const int b_row0 = static_cast<int>(rank) * (BN / CTAS);
+  const int n_ops = P.n_ops;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull_bar[a], 1);
+      mbar_init(&tempty_bar[a], CTAS * kEpiWarps);
+    }
+    mbar_init(drain_bar, 1);
+    mbar_init(ln_free_bar, kEpiWarps);
+    mbar_init(stored_bar, kEpiWarps);
+    *abort_flag = 0;
+    mbar_fence_init();
+    for (int o = 0; o < n_ops; ++o) {
+      tma_prefetch_desc(&P.op[o].a);
+      tma_prefetch_desc(&P.op[o].b);
+      tma_prefetch_desc(&P.op[o].d);
+    }
+  }
+  if (warp == 1) tmem_alloc_pair<S::kTmemCols>(tmem_holder);
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+  const uint32_t lead_full = mapa_shared(smem_u32(full_bar), 0);
+  const uint32_t lead_tempty = mapa_shared(smem_u32(tempty_bar), 0);
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer ----------------
+      int stage = 0;
+      uint32_t phase = 0;
+      int last_phase[8];
+#pragma unroll
+      for (int s = 0; s < 8; ++s) last_phase[s] = -1;
+      int pre = 0;
+      if (P.prefetch_b && n_ops > 0) {
+        const ChainOp& op = P.op[0];
+        const int num_m = (op.M + TILE_M - 1) / TILE_M;
+        if (unit < num_m * (op.N / BN)) {
+          const int n0 = (unit / num_m) * BN;
+          const int num_kb = op.K / kGemmBK;
+          pre = num_kb < STAGES ? num_kb : STAGES;
+          for (int kb = 0; kb < pre; ++kb) {
+            if (leader) mbar_arrive_expect_tx(&full_bar[kb], CTAS * S::kStageBytes);
+            tma_load_2d_pair(smem + kb * S::kStageBytes + S::kABytes, &op.b, lead_full + kb * 8,
+                             kb * kGemmBK, n0 + b_row0);
+          }
+        }
+      }
+      pdl_wait();
+      uint32_t ln_phase = 0;
+      for (int o = 0; o < n_ops && !*abort_flag; ++o) {
+        const ChainOp& op = P.op[o];
+        if (o > 0 && P.op[o - 1].ep.ln_out) {
+          // the stages were lent to the previous op's LayerNorm phase
+          if (!mbar_wait(ln_free_bar, ln_phase)) { *abort_flag = 1; break; }
+          ln_phase ^= 1;
+        }
+        const int num_m = (op.M + TILE_M - 1) / TILE_M;
+        const int num_tiles = num_m * (op.N / BN);
+        const int num_kb = op.K / kGemmBK;
+        for (int tile = unit; tile < num_tiles && !*abort_flag; tile += num_units) {
+          const int m0 = (tile % num_m) * TILE_M;
+          const int n0 = (tile / num_m) * BN;
+          if (op.wait) {  // this CTA's 128 A rows must be complete
+            const int q = (m0 + a_row0) / kGemmBM;
+            const unsigned target = op.wait_tiles ? op.wait_tiles
+                                                  : static_cast<unsigned>(min(kGemmBM, op.M - q * kGemmBM));
+            if (m0 + a_row0 < op.M && !wait_count_geq(op.wait + q, target)) { *abort_flag = 1; break; }
+            fence_async_global();  // the acquired rows are read by TMA (async proxy)
+          }
+          for (int kb = 0; kb < num_kb; ++kb) {
+            uint8_t* sa = smem + stage * S::kStageBytes;
+            uint8_t* sb = sa + S::kABytes;
+            if (pre > 0) {
+              --pre;
+              tma_load_2d_pair(sa, &op.a, lead_full + stage * 8, kb * kGemmBK, m0 + a_row0);
+            } else {
+              if (!mbar_wait(&empty_bar[stage], phase ^ 1)) { *abort_flag = 1; break; }
+              if (leader) mbar_arrive_expect_tx(&full_bar[stage], CTAS * S::kStageBytes);
+              tma_load_2d_pair(sa, &op.a, lead_full + stage * 8, kb * kGemmBK, m0 + a_row0);
+              tma_load_2d_pair(sb, &op.b, lead_full + stage * 8, kb * kGemmBK, n0 + b_row0);
+            }
+            last_phase[stage] = static_cast<int>(phase);
+            if (++stage == STAGES) { stage = 0; phase ^= 1; }
+          }
+        }
+      }
+      for (int s = 0; s < STAGES; ++s)
+        if (last_phase[s] >= 0) {
+          if (leader)
+            mbar_wait(&full_bar[s], static_cast<uint32_t>(last_phase[s]));
+          else
+            mbar_wait(&empty_bar[s], static_cast<uint32_t>(last_phase[s]));
+        }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      // ---------------- MMA issuer ----------------
+      constexpr uint32_t idesc = umma_idesc_bf16(TILE_M, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int it = 0;
+      for (int o = 0; o < n_ops && !*abort_flag; ++o) {
+        const ChainOp& op = P.op[o];
+        const int num_tiles = ((op.M + TILE_M - 1) / TILE_M) * (op.N / BN);
+        const int num_kb = op.K / kGemmBK;
+        bool ok = true;
+        for (int tile = unit; tile < num_tiles && !*abort_flag; tile += num_units, ++it) {
+          const int acc = it & 1;
+          const uint32_t acc_phase = (it >> 1) & 1;
+          if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+          for (int kb = 0; kb < num_kb; ++kb) {
+            if (!mbar_wait(&full_bar[stage], phase)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t a_addr = smem_u32(smem + stage * S::kStageBytes);
+            const uint32_t b_addr = a_addr + S::kABytes;
+#pragma unroll
+            for (int k = 0; k < kGemmBK / 16; ++k)
+              umma_bf16_pair(d_tmem, umma_desc_sw128(a_addr + k * 32), umma_desc_sw128(b_addr + k * 32),
+                             idesc, (kb > 0 || k > 0) ? 1u : 0u);
+            umma_commit_pair(&empty_bar[stage]);
+            if (++stage == STAGES) { stage = 0; phase ^= 1; }
+          }
+          if (!ok) break;
+          umma_commit_pair(&tfull_bar[acc]);
+        }
+        if (!ok) { *abort_flag = 1; break; }
+      }
+      umma_commit_pair_local(drain_bar);
+      mbar_wait(drain_bar, 0);
+    }
+  } else {
+    // ---------------- epilogue warps 2..9 ----------------
+    pdl_wait();
+    const int w = warp - 2;
+    const int quarter = warp & 3;
+    const int half = w >> 2;
+    uint8_t* buf = epi_smem + w * kEpiBufBytes;
+    int nbuf = 0;
+    int it = 0;
+    uint32_t stored_phase = 0;
+    // (no bar.sync among the epilogue warps here: a warp that gives up on a timed-out
+    // wait must not leave the others blocked; they meet on bounded mbarrier waits)
+    for (int o = 0; o < n_ops && !*abort_flag; ++o) {
+      const ChainOp& op = P.op[o];
+      const int num_m = (op.M + TILE_M - 1) / TILE_M;
+      const int num_n = op.N / BN;
+      const int num_tiles = num_m * num_n;
+      const int nblk = (op.M + kGemmBM - 1) / kGemmBM;
+      // the stages are free for the last tile's boxes only if no later op is loading:
+      // after the last op, or before a LayerNorm phase (the producer waits for it)
+      const bool can_stage = o == n_ops - 1 || op.ep.ln_out != nullptr;
+      for (int tile = unit; tile < num_tiles && !*abort_flag; tile += num_units, ++it) {
+        const int m0 = (tile % num_m) * TILE_M + a_row0;
+        const int n0 = (tile / num_m) * BN;
+        const int acc = it & 1;
+        const uint32_t acc_phase = (it >> 1) & 1;
+        const int m_row = m0 + quarter * 32 + lane;
+        switch (op.epi) {
+          case kEpiGateResid:
+            epilogue_prefetch<kEpiGateResid, 32, 8>(op.ep, op.M, op.N, m_row, n0, half);
+            break;
+          case kEpiBiasGelu:
+            epilogue_prefetch<kEpiBiasGelu, 64, 4>(op.ep, op.M, op.N, m_row, n0, half);
+            break;
+          default:
+            epilogue_prefetch<kEpiQkvRope, 64, 4>(op.ep, op.M, op.N, m_row, n0, half);
+            break;
+        }
+        if (!mbar_wait(&tfull_bar[acc], acc_phase)) { *abort_flag = 1; break; }
+        tc_fence_after();
+        const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
+                               static_cast<uint32_t>(acc * BN);
+        const bool staged = can_stage && tile + num_units >= num_tiles;
+        auto release = [&]() {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(lead_tempty + acc * 8);
+        };
+        switch (op.epi) {
+          case kEpiGateResid:
+            epilogue_tile<BN, kEpiGateResid>(op.ep, &op.d, op.M, op.N, taddr, m0, n0, quarter, half,
+                                             lane, buf, nbuf,
+                                             staged ? smem + w * EpiGeom<BN, kEpiGateResid>::kWarpTileBytes
+                                                    : nullptr,
+                                             release);
+            break;
+          case kEpiBiasGelu:
+            epilogue_tile<BN, kEpiBiasGelu>(op.ep, &op.d, op.M, op.N, taddr, m0, n0, quarter, half,
+                                            lane, buf, nbuf,
+                                            staged ? smem + w * EpiGeom<BN, kEpiBiasGelu>::kWarpTileBytes
+                                                   : nullptr,
+                                            release);
+            break;
+          default:
+            epilogue_tile<BN, kEpiQkvRope>(op.ep, &op.d, op.M, op.N, taddr, m0, n0, quarter, half,
+                                           lane, buf, nbuf,
+                                           staged ? smem + w * EpiGeom<BN, kEpiQkvRope>::kWarpTileBytes
+                                                  : nullptr,
+                                           release);
+            break;
+        }
+        if (op.tiles_done) {
+          // publish the tile once all eight warps' stores to it have completed
+          if (lane == 0) {
+            bulk_wait<0>();
+            fence_async_global();
+            mbar_arrive(stored_bar);
+          }
+          nbuf = 0;  // buf is free again
+          // every warp waits for the phase, so no warp can arrive for the next tile first
+          if (lane == 0) {
+            if (!mbar_wait(stored_bar, stored_phase)) {
+              *abort_flag = 1;
+            } else if (w == 0) {
+              const int q = m0 / kGemmBM;
+              if (q < nblk) red_release_add(op.tiles_done + q, 1u);
+            }
+          }
+          stored_phase ^= 1;
+          __syncwarp();
+        }
+      }
+      if (*abort_flag) break;
+      if (op.ep.ln_out) {
+        // LayerNorm phase in the (lent) operand stages, then hand them back
+        if (!ln_rows_phase(op.ep, op.M, static_cast<unsigned>(num_n), w, lane,
+                           reinterpret_cast<float4*>(smem + w * (kLnRowsPerWarp * OASIS_HIDDEN * 4)),
+                           op.rows_done)) {
+          *abort_flag = 1;
+        }
+        fence_async_smem();  // these generic writes precede the producer's TMA writes
+        __syncwarp();
+        if (lane == 0) mbar_arrive(ln_free_bar);
+      }
+    }
+    if (lane == 0) bulk_wait<0>();
+    __syncwarp();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc_pair<S::kTmemCols>(tmem_base);
 }
 
 // Host side (gemm.cu).  A: [M][lda] bf16, B: [N][ldb] bf16; D described by its own
@@ -632,6 +984,18 @@ void choose_tiles(int M, int N, int* bn, int* ctas);
 int set_gemm_output(GemmOperands* g, void* D, long long ldd, bool f32);
 int launch_gemm(const GemmOperands& g, int epi, const EpiParams& ep, cudaStream_t stream,
                 int max_ctas = 0);
+// One step of a chained launch: operands from make_gemm_operands (CTA pairs, tile N
+// 256, output map set), epilogue, and the row-block counters it waits on / publishes.
+struct ChainStep {
+  const GemmOperands* g;
+  int epi;
+  EpiParams ep;
+  const unsigned int* wait;
+  unsigned int wait_tiles;
+  unsigned int* tiles_done;
+  unsigned int* rows_done;
+};
+int launch_chain(const ChainStep* steps, int n, cudaStream_t stream);
 int num_sms();
 
 }  // namespace oasis
