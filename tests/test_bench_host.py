@@ -52,7 +52,9 @@ def test_single_process_reduction_is_identity():
 
 def test_gpu_launch_count_per_step():
     # 7 embedding launches + 1 adaLN GEMM + 7 per sub-block x 32 + 2 final + 1 sampler
-    assert bench.gpu_launches_per_step(16) == 7 + 1 + 224 + 2 + 1
+    # 7 head kernels, first QKV, 32 x (attention + chained launch), final GEMM, sampler
+    assert bench.gpu_launches_per_step(16) == 7 + 1 + 64 + 1 + 1
+    assert bench.gpu_launches_per_step(2, chained=False, sampler=False) == 7 + 20 + 1
 
 
 def test_reference_arm_nonzero_rank_prints_nothing():
