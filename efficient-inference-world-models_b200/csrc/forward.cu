@@ -393,6 +393,7 @@ int plan_init(oasis_plan* p, const oasis_dit_weights_t* w, int batch, int frames
       if (g->ctas != 2 || g->bn != 256) p->chain = false;
   // weights are the B operand of these GEMMs (swap-AB GEMMs read activations as B)
   p->patch.b_is_weight = true;
+  p->ada.a_is_weight = p->temb1.a_is_weight = p->temb2.a_is_weight = true;
   p->fin.b_is_weight = true;
   for (int j = 0; j < 2 * w->depth; ++j)
     p->qkv[j].b_is_weight = p->out[j].b_is_weight = p->fc1[j].b_is_weight = p->fc2[j].b_is_weight = true;

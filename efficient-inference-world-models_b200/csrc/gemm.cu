@@ -100,6 +100,11 @@ int max_pairs() {
   return pairs;
 }
 
+// Which operand the kernel may fetch before the previous kernel ends (bit 0: B, bit 1: A).
+inline int prefetch_flags(const GemmOperands& g) {
+  return g.b_is_weight ? 1 : (g.a_is_weight ? 2 : 0);
+}
+
 template <int BN, int EPI, int CTAS>
 int launch_one(const GemmOperands& g, const EpiParams& ep, cudaStream_t stream, int max_ctas) {
   using S = GemmShape<BN, CTAS>;
@@ -121,10 +126,10 @@ int launch_one(const GemmOperands& g, const EpiParams& ep, cudaStream_t stream, 
   if constexpr (CTAS == 2)
     e = launch_pdl_cluster(gemm_tcgen05_kernel<BN, EPI, CTAS>, dim3(units * CTAS), dim3(kGemmThreads),
                            S::kSmemBytes, stream, CTAS, g.a, g.b, g.d, g.M, g.N, g.K,
-                           g.b_is_weight ? 1 : 0, ep);
+                           prefetch_flags(g), ep);
   else
     e = launch_pdl(gemm_tcgen05_kernel<BN, EPI, CTAS>, dim3(units), dim3(kGemmThreads), S::kSmemBytes,
-                   stream, g.a, g.b, g.d, g.M, g.N, g.K, g.b_is_weight ? 1 : 0, ep);
+                   stream, g.a, g.b, g.d, g.M, g.N, g.K, prefetch_flags(g), ep);
   if (e != cudaSuccess) return cuda_status(e, "gemm_tcgen05_kernel");
   return OASIS_OK;
 }

@@ -376,6 +376,10 @@ __device__ __forceinline__ bool ln_rows_phase(const EpiParams& ep, int M, unsign
   const int r_begin = static_cast<int>(blockIdx.x) * R;
   const int r_end = min(M, r_begin + R);
   for (int row0 = r_begin + w * kLnRowsPerWarp; row0 < r_end; row0 += kEpiWarps * kLnRowsPerWarp) {
+    // the frame's shift/scale (written by an earlier kernel) load while the rows finish
+    const long long f = row0 / OASIS_TOKENS;
+    float4 a4[8], s4[8];
+    ln_load_modulation(ep.ln_shift + f * ep.ln_mod_ld, ep.ln_scale + f * ep.ln_mod_ld, lane, a4, s4);
     int ok = 1;
     if (lane == 0) ok = wait_count_geq(ep.ln_count + row0 / kGemmBM, target);
     if (!__shfl_sync(0xffffffffu, ok, 0)) return false;
@@ -387,9 +391,6 @@ __device__ __forceinline__ bool ln_rows_phase(const EpiParams& ep, int M, unsign
 #pragma unroll
       for (int i = 0; i < 8; ++i)  // each lane copies (and later reads) its own columns
         cp_async16(stage + r * 256 + lane + 32 * i, src + r * 256 + lane + 32 * i);
-    const long long f = row0 / OASIS_TOKENS;
-    float4 a4[8], s4[8];
-    ln_load_modulation(ep.ln_shift + f * ep.ln_mod_ld, ep.ln_scale + f * ep.ln_mod_ld, lane, a4, s4);
     cp_async_wait_all();
     ln_modulate_rows_smem(stage, nrows, a4, s4, ep.ln_out + static_cast<long long>(row0) * OASIS_HIDDEN,
                           lane);
@@ -485,15 +486,22 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         else
           tma_load_2d(dst, map, &full_bar[s], c0, c1);
       };
-      // When B is a weight (never written by an earlier kernel) the B tiles of the first
-      // stages are fetched before waiting on the previous kernel, the A tiles after.
+      // The operand that is a weight (never written by an earlier kernel: B of the
+      // projections, A of the swap-AB GEMMs) is fetched for the first stages before
+      // waiting on the previous kernel, the other operand after.
+      // prefetch_b: bit 0 = B is a weight, bit 1 = A is a weight.
       int pre = 0;
+      const bool pre_a = (prefetch_b & 2) != 0;
       if (prefetch_b && unit < num_tiles) {
+        const int m0 = (unit % num_m) * TILE_M;
         const int n0 = (unit / num_m) * BN;
         pre = num_kb < STAGES ? num_kb : STAGES;
         for (int kb = 0; kb < pre; ++kb) {
           if (leader) mbar_arrive_expect_tx(&full_bar[kb], CTAS * S::kStageBytes);
-          load(smem + kb * S::kStageBytes + S::kABytes, &tmB, kb, kb * kGemmBK, n0 + b_row0);
+          if (pre_a)
+            load(smem + kb * S::kStageBytes, &tmA, kb, kb * kGemmBK, m0 + a_row0);
+          else
+            load(smem + kb * S::kStageBytes + S::kABytes, &tmB, kb, kb * kGemmBK, n0 + b_row0);
         }
       }
       pdl_wait();
@@ -503,9 +511,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         for (int kb = 0; kb < num_kb; ++kb) {
           uint8_t* sa = smem + stage * S::kStageBytes;
           uint8_t* sb = sa + S::kABytes;
-          if (pre > 0) {  // stage already armed and its B tile in flight
+          if (pre > 0) {  // stage already armed and its weight tile in flight
             --pre;
-            load(sa, &tmA, stage, kb * kGemmBK, m0 + a_row0);
+            if (pre_a)
+              load(sb, &tmB, stage, kb * kGemmBK, n0 + b_row0);
+            else
+              load(sa, &tmA, stage, kb * kGemmBK, m0 + a_row0);
           } else {
             // the stage is free once the MMAs that read it (in both CTAs) have completed
             if (!mbar_wait(&empty_bar[stage], phase ^ 1)) { *abort_flag = 1; break; }
@@ -974,6 +985,7 @@ struct GemmOperands {
   int ctas;  // 1: one CTA per 128 x bn tile; 2: CTA pairs on 256 x 256 tiles
   bool has_d;
   bool b_is_weight;  // B is never written by another kernel: may be prefetched early
+  bool a_is_weight;  // the same for A (swap-AB GEMMs)
 };
 int make_gemm_operands(GemmOperands* g, const void* A, long long lda, const void* B, long long ldb,
                        int M, int N, int K, int bn, int ctas = 1);
