@@ -21,57 +21,24 @@ __device__ __forceinline__ uint32_t sw128(uint32_t tile, int row, int chunk) {
 }
 
 // ----------------------------------------------------------------------------------
-// spatial attention: one CTA per (frame, head), 9 warps x 16 query rows.  Q, K and V
-// (144 x 64 each) arrive by three TMA tensor loads into 128B-swizzled tiles; Q and K
-// complete on one barrier and V on another, so QK^T starts while V is in flight.
+// spatial attention (144 tokens of one frame, non-causal)
 // ----------------------------------------------------------------------------------
-constexpr int kSpThreads = 288;
-constexpr int kSpTile = OASIS_TOKENS * 128;            // 18,432 B
-constexpr int kSpSmem = 3 * kSpTile + 1024 + 64;       // tiles + alignment slack + barriers
+constexpr int kSpTile = OASIS_TOKENS * 128;  // 18,432 B: 144 rows x 64 bf16, 128B-swizzled
 
-__global__ void __launch_bounds__(kSpThreads, 2)
-    attn_spatial_kernel(const __grid_constant__ CUtensorMap tm_qkv, __nv_bfloat16* __restrict__ out,
-                        float scale_log2) {
-  pdl_trigger();
-  extern __shared__ uint8_t sm_sp[];
-  uint8_t* tiles = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(sm_sp) + 1023) &
-                                              ~static_cast<uintptr_t>(1023));
-  uint64_t* bar = reinterpret_cast<uint64_t*>(tiles + 3 * kSpTile);
-  const int f = blockIdx.x;
-  const int h = blockIdx.y;
-  if (threadIdx.x == 0) {
-    mbar_init(&bar[0], 1);
-    mbar_init(&bar[1], 1);
-    mbar_fence_init();
-    tma_prefetch_desc(&tm_qkv);
-  }
-  __syncthreads();
-  pdl_wait();  // qkv comes from the previous kernel; out is read by earlier ones
-  if (threadIdx.x == 0) {
-    mbar_arrive_expect_tx(&bar[0], 2 * kSpTile);
-    tma_load_2d(tiles, &tm_qkv, &bar[0], h * 64, f * OASIS_TOKENS);
-    tma_load_2d(tiles + kSpTile, &tm_qkv, &bar[0], OASIS_HIDDEN + h * 64, f * OASIS_TOKENS);
-    mbar_arrive_expect_tx(&bar[1], kSpTile);
-    tma_load_2d(tiles + 2 * kSpTile, &tm_qkv, &bar[1], 2 * OASIS_HIDDEN + h * 64, f * OASIS_TOKENS);
-  }
-  const uint32_t sQ = smem_u32(tiles), sK = sQ + kSpTile, sV = sK + kSpTile;
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  const int r0 = warp * 16;
-  if (!mbar_wait(&bar[0], 0)) return;  // timeout recorded in the device error word
-
+// 16 query rows r0..r0+15 of one (frame, head) on the legacy tensor path (mma.sync
+// m16n8k16) by one warp, from swizzled Q/K/V tiles: online softmax over 3 key blocks
+// of 48; writes the 16 output rows (out points at the frame's row 0, head column 0).
+__device__ __forceinline__ void spatial_rows16(uint32_t sQ, uint32_t sK, uint32_t sV, int r0, int lane,
+                                               float scale_log2, __nv_bfloat16* out) {
   uint32_t qa[4][4];
 #pragma unroll
   for (int kk = 0; kk < 4; ++kk)
     ldsm_x4(sw128(sQ, r0 + (lane & 15), kk * 2 + (lane >> 4)), qa[kk][0], qa[kk][1], qa[kk][2],
             qa[kk][3]);
-
-  // online softmax over 3 key blocks of 48 (keeps ~100 registers -> 2 CTAs per SM)
   float o[8][4];
 #pragma unroll
   for (int j = 0; j < 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.0f;
   float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
-  bool v_ready = false;
 #pragma unroll 1
   for (int kb = 0; kb < 3; ++kb) {
     float s[6][4];
@@ -121,10 +88,6 @@ __global__ void __launch_bounds__(kSpThreads, 2)
       o[j][2] *= alpha1;
       o[j][3] *= alpha1;
     }
-    if (!v_ready) {
-      if (!mbar_wait(&bar[1], 0)) return;
-      v_ready = true;
-    }
 #pragma unroll
     for (int kk = 0; kk < 3; ++kk) {
       uint32_t pa[4];
@@ -146,16 +109,165 @@ __global__ void __launch_bounds__(kSpThreads, 2)
   l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
   l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
   l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
-
   const float inv0 = 1.0f / l0, inv1 = 1.0f / l1;
   const int g = lane >> 2, c = lane & 3;
-  __nv_bfloat16* orow0 = out + (static_cast<long long>(f) * OASIS_TOKENS + r0 + g) * OASIS_HIDDEN + h * 64;
+  __nv_bfloat16* orow0 = out + static_cast<long long>(r0 + g) * OASIS_HIDDEN;
   __nv_bfloat16* orow1 = orow0 + 8 * OASIS_HIDDEN;
 #pragma unroll
   for (int jd = 0; jd < 8; ++jd) {
     *reinterpret_cast<uint32_t*>(orow0 + jd * 8 + 2 * c) = pack_bf16x2(o[jd][0] * inv0, o[jd][1] * inv0);
     *reinterpret_cast<uint32_t*>(orow1 + jd * 8 + 2 * c) = pack_bf16x2(o[jd][2] * inv1, o[jd][3] * inv1);
   }
+}
+
+// One CTA per (frame, head), 6 warps.  Q, K, V (144 x 64 each) arrive by TMA into
+// 128B-swizzled tiles.  Query rows 0..127 run on tcgen05: warp 0 issues S = Q K^T
+// (M=128, N=144, K=64) into TMEM; warps 2..5 (one query row per TMEM lane) read their
+// row of S, take the exact softmax in registers and write P (bf16) as a K-major
+// swizzled tile; warp 0 issues O = P V (M=128, N=64, K=144, V as an MN-major operand)
+// into TMEM; warps 2..5 normalise and store O.  Rows 128..143 run concurrently on
+// warp 1 with mma.sync (spatial_rows16).
+constexpr int kSpThreads = 192;
+constexpr int kSpPAtom = 128 * 128;                          // 16 KB: 128 rows x 64 keys bf16
+constexpr int kSpSmem = 3 * kSpTile + 3 * kSpPAtom + 1024 + 64;  // 104,448 + slack + barriers
+constexpr int kSpTmemCols = 256;                             // S: columns 0..143, O: 192..255
+constexpr int kSpOCol = 192;
+
+__global__ void __launch_bounds__(kSpThreads, 2)
+    attn_spatial_kernel(const __grid_constant__ CUtensorMap tm_qkv, __nv_bfloat16* __restrict__ out,
+                        float scale_log2) {
+  pdl_trigger();
+  extern __shared__ uint8_t sm_sp[];
+  uint8_t* tiles = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(sm_sp) + 1023) &
+                                              ~static_cast<uintptr_t>(1023));
+  uint8_t* sP = tiles + 3 * kSpTile;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sP + 3 * kSpPAtom);  // qk, v, s, p, o
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bar + 5);
+  const int f = blockIdx.x;
+  const int h = blockIdx.y;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar[0], 1);
+    mbar_init(&bar[1], 1);
+    mbar_init(&bar[2], 1);
+    mbar_init(&bar[3], 4);  // one arrival per softmax warp
+    mbar_init(&bar[4], 1);
+    mbar_fence_init();
+    tma_prefetch_desc(&tm_qkv);
+  }
+  if (warp == 1) tmem_alloc<kSpTmemCols>(tmem_holder);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+  pdl_wait();  // qkv comes from the previous kernel; out is read by earlier ones
+  const uint32_t sQ = smem_u32(tiles), sK = sQ + kSpTile, sV = sK + kSpTile;
+  const uint32_t sPa = smem_u32(sP);
+  __nv_bfloat16* obase = out + static_cast<long long>(f) * OASIS_TOKENS * OASIS_HIDDEN + h * 64;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      mbar_arrive_expect_tx(&bar[0], 2 * kSpTile);
+      tma_load_2d(tiles, &tm_qkv, &bar[0], h * 64, f * OASIS_TOKENS);
+      tma_load_2d(tiles + kSpTile, &tm_qkv, &bar[0], OASIS_HIDDEN + h * 64, f * OASIS_TOKENS);
+      mbar_arrive_expect_tx(&bar[1], kSpTile);
+      tma_load_2d(tiles + 2 * kSpTile, &tm_qkv, &bar[1], 2 * OASIS_HIDDEN + h * 64, f * OASIS_TOKENS);
+      if (mbar_wait(&bar[0], 0)) {
+        tc_fence_after();
+        constexpr uint32_t idesc_s = umma_idesc_bf16(128, OASIS_TOKENS);
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          umma_bf16(tmem, umma_desc_sw128(sQ + k * 32), umma_desc_sw128(sK + k * 32), idesc_s, k > 0);
+        umma_commit(&bar[2]);
+        if (mbar_wait(&bar[1], 0) && mbar_wait(&bar[3], 0)) {
+          tc_fence_after();
+          constexpr uint32_t idesc_o = umma_idesc_bf16(128, 64, true);
+#pragma unroll
+          for (int k = 0; k < OASIS_TOKENS / 16; ++k)  // 9 steps of 16 keys
+            umma_bf16(tmem + kSpOCol,
+                      umma_desc_sw128(sPa + (k >> 2) * kSpPAtom + (k & 3) * 32),
+                      umma_desc_sw128_mn(sV + k * 2048), idesc_o, k > 0);
+          umma_commit(&bar[4]);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (mbar_wait(&bar[0], 0) && mbar_wait(&bar[1], 0))
+      spatial_rows16(sQ, sK, sV, 128, lane, scale_log2, obase);
+  } else {
+    const int quarter = warp & 3;       // TMEM lanes this warp may access
+    const int r = quarter * 32 + lane;  // this thread's query row
+    const uint32_t trow = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+    bool ok = mbar_wait(&bar[2], 0);
+    float inv = 0.0f;
+    if (ok) {
+      tc_fence_after();
+      float v[32], v16[16];
+      float m = -INFINITY;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        tmem_ld32(trow + c * 32, v);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) m = fmaxf(m, v[i]);
+      }
+      tmem_ld16(trow + 128, v16);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) m = fmaxf(m, v16[i]);
+      const float mo = m * scale_log2;
+      float sum = 0.0f;
+      // P row r, keys k: atom k / 64, 16-byte chunk (k % 64) / 8, swizzled by r mod 8
+      uint8_t* prow = sP + r * 128;
+      auto put8 = [&](int key0, const float* e) {
+        const uint4 q = make_uint4(pack_bf16x2(e[0], e[1]), pack_bf16x2(e[2], e[3]),
+                                   pack_bf16x2(e[4], e[5]), pack_bf16x2(e[6], e[7]));
+        *reinterpret_cast<uint4*>(prow + (key0 >> 6) * kSpPAtom + ((((key0 & 63) >> 3) ^ (r & 7)) << 4)) = q;
+      };
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        tmem_ld32(trow + c * 32, v);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          v[i] = exp2f(v[i] * scale_log2 - mo);
+          sum += v[i];
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) put8(c * 32 + j * 8, v + j * 8);
+      }
+      tmem_ld16(trow + 128, v16);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        v16[i] = exp2f(v16[i] * scale_log2 - mo);
+        sum += v16[i];
+      }
+      put8(128, v16);
+      put8(136, v16 + 8);
+      inv = 1.0f / sum;
+      fence_async_smem_cta();  // P (generic writes) is read by the tensor core next
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&bar[3]);
+    if (ok && mbar_wait(&bar[4], 0)) {
+      tc_fence_after();
+      __nv_bfloat16* orow = obase + static_cast<long long>(r) * OASIS_HIDDEN;
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        float o[32];
+        tmem_ld32(trow + kSpOCol + half * 32, o);
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          reinterpret_cast<uint4*>(orow + half * 32)[q] =
+              make_uint4(pack_bf16x2(o[8 * q + 0] * inv, o[8 * q + 1] * inv),
+                         pack_bf16x2(o[8 * q + 2] * inv, o[8 * q + 3] * inv),
+                         pack_bf16x2(o[8 * q + 4] * inv, o[8 * q + 5] * inv),
+                         pack_bf16x2(o[8 * q + 6] * inv, o[8 * q + 7] * inv));
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc<kSpTmemCols>(tmem);
 }
 
 // ----------------------------------------------------------------------------------

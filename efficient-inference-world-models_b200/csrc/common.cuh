@@ -222,6 +222,12 @@ __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
+// Orders this thread's generic shared-memory writes before later async-proxy reads
+// (TMA stores, tensor-core operand fetches) of the same bytes.
+__device__ __forceinline__ void fence_async_smem_cta() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 __device__ __forceinline__ void tc_fence_before() {
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
 }
@@ -375,6 +381,35 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// 32 lanes x 16 consecutive fp32 columns from TMEM.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// UMMA shared-memory descriptor, MN-major operand with 128-byte swizzle: rows of 128 B
+// hold 64 consecutive MN elements (one swizzle atom wide), consecutive K indices are
+// consecutive rows, 8-row groups 1024 B apart.  Used for B = V in O = P V, where V is
+// stored [key][dim] and N = 64 dims.
+__device__ __forceinline__ uint64_t umma_desc_sw128_mn(uint32_t smem_addr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu);  // start address
+  d |= static_cast<uint64_t>(1u) << 16;                    // leading byte offset: one atom wide in MN
+  d |= static_cast<uint64_t>(1024u >> 4) << 32;            // stride byte offset: next 8 K rows
+  d |= static_cast<uint64_t>(1u) << 46;                    // descriptor version (sm_100)
+  d |= static_cast<uint64_t>(2u) << 61;                    // SWIZZLE_128B
+  return d;
+}
+
 // UMMA shared-memory descriptor: K-major operand tile written by TMA with 128-byte
 // swizzle (rows of 64 bf16, 8-row atoms of 1024 B).  Start address must lie in a
 // 1024-byte aligned tile (+k*32 B to step along K inside the swizzle atom).
@@ -388,10 +423,11 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t smem_addr) {
   return d;
 }
 
-// Instruction descriptor for kind::f16: bf16 A/B, fp32 D, both K-major.
-__host__ __device__ constexpr uint32_t umma_idesc_bf16(int m, int n) {
-  return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
-         (static_cast<uint32_t>(m >> 4) << 24);
+// Instruction descriptor for kind::f16: bf16 A/B, fp32 D, both K-major (b_mn: B is
+// MN-major, bit 16).
+__host__ __device__ constexpr uint32_t umma_idesc_bf16(int m, int n, bool b_mn = false) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | (b_mn ? (1u << 16) : 0u) |
+         (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
 }
 
 // ----------------------------------------------------------------------------------
