@@ -203,13 +203,13 @@ __global__ void __launch_bounds__(kSpThreads, 2)
     float inv = 0.0f;
     if (ok) {
       tc_fence_after();
-      float v[32], v16[16];
+      float v[64], v16[16];
       float m = -INFINITY;
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        tmem_ld32(trow + c * 32, v);
+      for (int c = 0; c < 2; ++c) {
+        tmem_ld64(trow + c * 64, v);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) m = fmaxf(m, v[i]);
+        for (int i = 0; i < 64; ++i) m = fmaxf(m, v[i]);
       }
       tmem_ld16(trow + 128, v16);
 #pragma unroll
@@ -224,15 +224,15 @@ __global__ void __launch_bounds__(kSpThreads, 2)
         *reinterpret_cast<uint4*>(prow + (key0 >> 6) * kSpPAtom + ((((key0 & 63) >> 3) ^ (r & 7)) << 4)) = q;
       };
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        tmem_ld32(trow + c * 32, v);
+      for (int c = 0; c < 2; ++c) {
+        tmem_ld64(trow + c * 64, v);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
+        for (int i = 0; i < 64; ++i) {
           v[i] = exp2f(v[i] * scale_log2 - mo);
           sum += v[i];
         }
 #pragma unroll
-        for (int j = 0; j < 4; ++j) put8(c * 32 + j * 8, v + j * 8);
+        for (int j = 0; j < 8; ++j) put8(c * 64 + j * 8, v + j * 8);
       }
       tmem_ld16(trow + 128, v16);
 #pragma unroll
