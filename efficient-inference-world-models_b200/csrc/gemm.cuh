@@ -305,6 +305,9 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& ep, const CUtenso
   constexpr int COLS = G::COLS, NBLK = G::NBLK;
   const int m_row = m0 + quarter * 32 + lane;  // this thread's row
   const bool rows_live = m0 + quarter * 32 < M;
+  // operand row for the math: lanes past M (their stores are clipped) read row M - 1's
+  // gate, not a frame beyond the modulation rows
+  const int m_op = min(m_row, M - 1);
   const int last_blk = (NBLK - 1 - half) >= 0 ? ((NBLK - 1 - half) / 2) * 2 + half : -1;
   if (last_blk < 0) {  // owns no columns of this tile
     release();
@@ -329,9 +332,9 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& ep, const CUtenso
       if (lane == 0) bulk_wait_read<0>();
       __syncwarp();
     }
-    epilogue_math<EPI>(ep, m_row, nb, v);
+    epilogue_math<EPI>(ep, m_op, nb, v);
     if (COLS == 64) {
-      epilogue_math<EPI>(ep, m_row, nb + 32, w);
+      epilogue_math<EPI>(ep, m_op, nb + 32, w);
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         st_swizzled(box, lane, c, make_uint4(pack_bf16x2(v[8 * c + 0], v[8 * c + 1]),
