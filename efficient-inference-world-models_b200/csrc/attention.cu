@@ -317,6 +317,7 @@ __device__ __forceinline__ uint4 dequant_int4x8(uint32_t w, float scale, float z
 template <bool TMA>
 __global__ void __launch_bounds__(kTpWarps * 32)
     attn_temporal_kernel(const __grid_constant__ CUtensorMap tm_qkv,
+                         const __grid_constant__ CUtensorMap tm_out,
                          const __nv_bfloat16* __restrict__ qkv, __nv_bfloat16* __restrict__ out,
                          KvView kv, int layer, int q_frames, int q_pos0, int n_past, int n_kv,
                          float scale_log2) {
@@ -330,6 +331,7 @@ __global__ void __launch_bounds__(kTpWarps * 32)
     mbar_init(tbar, 1);
     mbar_fence_init();
     tma_prefetch_desc(&tm_qkv);
+    tma_prefetch_desc(&tm_out);
   }
   if (TMA) __syncthreads();
   pdl_wait();
@@ -511,6 +513,19 @@ __global__ void __launch_bounds__(kTpWarps * 32)
     }
     const float inv0 = 1.0f / sum0, inv1 = 1.0f / sum1;
     const int t0 = mt * 16 + g, t1 = t0 + 8;
+    if constexpr (TMA) {
+      // O rows t0, t1 into this warp's Q tile (rows mt*16.. were read into registers
+      // above and are not read again), same 128B swizzle; one TMA store per warp below
+      uint8_t* otile = sm_tp + (warp * 3) * kTpTmaTile;
+#pragma unroll
+      for (int jd = 0; jd < 8; ++jd) {
+        *reinterpret_cast<uint32_t*>(otile + t0 * 128 + ((jd ^ (t0 & 7)) << 4) + 4 * c) =
+            pack_bf16x2(o[jd][0] * inv0, o[jd][1] * inv0);
+        *reinterpret_cast<uint32_t*>(otile + t1 * 128 + ((jd ^ (t1 & 7)) << 4) + 4 * c) =
+            pack_bf16x2(o[jd][2] * inv1, o[jd][3] * inv1);
+      }
+      continue;
+    }
     if (t0 < q_frames) {
       __nv_bfloat16* orow = out + (static_cast<long long>(b * q_frames + t0) * OASIS_TOKENS + p) * OASIS_HIDDEN + h * 64;
 #pragma unroll
@@ -522,6 +537,16 @@ __global__ void __launch_bounds__(kTpWarps * 32)
 #pragma unroll
       for (int jd = 0; jd < 8; ++jd)
         *reinterpret_cast<uint32_t*>(orow + jd * 8 + 2 * c) = pack_bf16x2(o[jd][2] * inv1, o[jd][3] * inv1);
+    }
+  }
+  if constexpr (TMA) {
+    // the warp's head: q_frames rows x 128 B, strided by a frame in the output
+    fence_async_smem_cta();
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_3d(&tm_out, sm_tp + (warp * 3) * kTpTmaTile, h * 64, p, b * q_frames);
+      bulk_commit();
+      bulk_wait_read<0>();  // shared memory is read before the CTA exits
     }
   }
 }
@@ -601,7 +626,7 @@ int launch_attn_temporal(const void* qkv, const KvView& kv, int layer, void* out
     configured = true;
   }
   dim3 grid(OASIS_TOKENS, OASIS_HEADS / kTpWarps, batch);
-  CUtensorMap tm{};
+  CUtensorMap tm{}, tm_out{};
   const bool tma = n_past == 0;
   if (tma) {
     // qkv viewed as [frames][144 tokens][3072]: box = 64 columns x 1 token x 32 frames
@@ -609,13 +634,19 @@ int launch_attn_temporal(const void* qkv, const KvView& kv, int layer, void* out
     const long long strides[2] = {3 * OASIS_HIDDEN * 2, static_cast<long long>(OASIS_TOKENS) * 3 * OASIS_HIDDEN * 2};
     const int box[3] = {64, 1, kTpRowsPerMat};
     if (int st = encode_bf16_sw128(&tm, qkv, 3, dims, strides, box)) return st;
+    // out viewed as [frames][144 tokens][1024]: box = 64 columns x 1 token x q_frames frames
+    // (one session's window, so a store never reaches the next session's rows)
+    const long long odims[3] = {OASIS_HIDDEN, OASIS_TOKENS, static_cast<long long>(batch) * q_frames};
+    const long long ostrides[2] = {OASIS_HIDDEN * 2, static_cast<long long>(OASIS_TOKENS) * OASIS_HIDDEN * 2};
+    const int obox[3] = {64, 1, q_frames};
+    if (int st = encode_bf16_sw128(&tm_out, out, 3, odims, ostrides, obox)) return st;
   }
   cudaError_t e = tma ? launch_pdl(attn_temporal_kernel<true>, grid, dim3(kTpWarps * 32), kTpSmemTma,
-                                   stream, tm, static_cast<const __nv_bfloat16*>(qkv),
+                                   stream, tm, tm_out, static_cast<const __nv_bfloat16*>(qkv),
                                    static_cast<__nv_bfloat16*>(out), kv, layer, q_frames, q_pos0,
                                    n_past, n_kv, kScaleLog2)
                       : launch_pdl(attn_temporal_kernel<false>, grid, dim3(kTpWarps * 32), kTpSmem,
-                                   stream, tm, static_cast<const __nv_bfloat16*>(qkv),
+                                   stream, tm, tm_out, static_cast<const __nv_bfloat16*>(qkv),
                                    static_cast<__nv_bfloat16*>(out), kv, layer, q_frames, q_pos0,
                                    n_past, n_kv, kScaleLog2);
   if (e != cudaSuccess) return cuda_status(e, "attn_temporal_kernel");
