@@ -27,9 +27,10 @@ constexpr int kSpTile = OASIS_TOKENS * 128;  // 18,432 B: 144 rows x 64 bf16, 12
 
 // 16 query rows r0..r0+15 of one (frame, head) on the legacy tensor path (mma.sync
 // m16n8k16) by one warp, from swizzled Q/K/V tiles: online softmax over 3 key blocks
-// of 48; writes the 16 output rows (out points at the frame's row 0, head column 0).
+// of 48; writes the 16 output rows into the swizzled tile sO (the same rows of Q, read
+// into registers first).
 __device__ __forceinline__ void spatial_rows16(uint32_t sQ, uint32_t sK, uint32_t sV, int r0, int lane,
-                                               float scale_log2, __nv_bfloat16* out) {
+                                               float scale_log2, uint8_t* sO) {
   uint32_t qa[4][4];
 #pragma unroll
   for (int kk = 0; kk < 4; ++kk)
@@ -111,12 +112,13 @@ __device__ __forceinline__ void spatial_rows16(uint32_t sQ, uint32_t sK, uint32_
   l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
   const float inv0 = 1.0f / l0, inv1 = 1.0f / l1;
   const int g = lane >> 2, c = lane & 3;
-  __nv_bfloat16* orow0 = out + static_cast<long long>(r0 + g) * OASIS_HIDDEN;
-  __nv_bfloat16* orow1 = orow0 + 8 * OASIS_HIDDEN;
+  const int ra = r0 + g, rb = ra + 8;
 #pragma unroll
   for (int jd = 0; jd < 8; ++jd) {
-    *reinterpret_cast<uint32_t*>(orow0 + jd * 8 + 2 * c) = pack_bf16x2(o[jd][0] * inv0, o[jd][1] * inv0);
-    *reinterpret_cast<uint32_t*>(orow1 + jd * 8 + 2 * c) = pack_bf16x2(o[jd][2] * inv1, o[jd][3] * inv1);
+    *reinterpret_cast<uint32_t*>(sO + ra * 128 + ((jd ^ (ra & 7)) << 4) + 4 * c) =
+        pack_bf16x2(o[jd][0] * inv0, o[jd][1] * inv0);
+    *reinterpret_cast<uint32_t*>(sO + rb * 128 + ((jd ^ (rb & 7)) << 4) + 4 * c) =
+        pack_bf16x2(o[jd][2] * inv1, o[jd][3] * inv1);
   }
 }
 
@@ -125,8 +127,9 @@ __device__ __forceinline__ void spatial_rows16(uint32_t sQ, uint32_t sK, uint32_
 // (M=128, N=144, K=64) into TMEM; warps 2..5 (one query row per TMEM lane) read their
 // row of S, take the exact softmax in registers and write P (bf16) as a K-major
 // swizzled tile; warp 0 issues O = P V (M=128, N=64, K=144, V as an MN-major operand)
-// into TMEM; warps 2..5 normalise and store O.  Rows 128..143 run concurrently on
-// warp 1 with mma.sync (spatial_rows16).
+// into TMEM; warps 2..5 normalise O into the Q tile (free once S is computed).  Rows
+// 128..143 run concurrently on warp 1 with mma.sync (spatial_rows16).  The finished
+// 144 x 64 tile leaves by one TMA store.
 constexpr int kSpThreads = 192;
 constexpr int kSpPAtom = 128 * 128;                          // 16 KB: 128 rows x 64 keys bf16
 constexpr int kSpSmem = 3 * kSpTile + 3 * kSpPAtom + 1024 + 64;  // 104,448 + slack + barriers
@@ -134,8 +137,8 @@ constexpr int kSpTmemCols = 256;                             // S: columns 0..14
 constexpr int kSpOCol = 192;
 
 __global__ void __launch_bounds__(kSpThreads, 2)
-    attn_spatial_kernel(const __grid_constant__ CUtensorMap tm_qkv, __nv_bfloat16* __restrict__ out,
-                        float scale_log2) {
+    attn_spatial_kernel(const __grid_constant__ CUtensorMap tm_qkv,
+                        const __grid_constant__ CUtensorMap tm_out, float scale_log2) {
   pdl_trigger();
   extern __shared__ uint8_t sm_sp[];
   uint8_t* tiles = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(sm_sp) + 1023) &
@@ -155,6 +158,7 @@ __global__ void __launch_bounds__(kSpThreads, 2)
     mbar_init(&bar[4], 1);
     mbar_fence_init();
     tma_prefetch_desc(&tm_qkv);
+    tma_prefetch_desc(&tm_out);
   }
   if (warp == 1) tmem_alloc<kSpTmemCols>(tmem_holder);
   tc_fence_before();
@@ -164,7 +168,6 @@ __global__ void __launch_bounds__(kSpThreads, 2)
   pdl_wait();  // qkv comes from the previous kernel; out is read by earlier ones
   const uint32_t sQ = smem_u32(tiles), sK = sQ + kSpTile, sV = sK + kSpTile;
   const uint32_t sPa = smem_u32(sP);
-  __nv_bfloat16* obase = out + static_cast<long long>(f) * OASIS_TOKENS * OASIS_HIDDEN + h * 64;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -194,7 +197,7 @@ __global__ void __launch_bounds__(kSpThreads, 2)
     }
   } else if (warp == 1) {
     if (mbar_wait(&bar[0], 0) && mbar_wait(&bar[1], 0))
-      spatial_rows16(sQ, sK, sV, 128, lane, scale_log2, obase);
+      spatial_rows16(sQ, sK, sV, 128, lane, scale_log2, tiles);
   } else {
     const int quarter = warp & 3;       // TMEM lanes this warp may access
     const int r = quarter * 32 + lane;  // this thread's query row
@@ -249,14 +252,14 @@ __global__ void __launch_bounds__(kSpThreads, 2)
     if (lane == 0) mbar_arrive(&bar[3]);
     if (ok && mbar_wait(&bar[4], 0)) {
       tc_fence_after();
-      __nv_bfloat16* orow = obase + static_cast<long long>(r) * OASIS_HIDDEN;
+      // row r of O into row r of the Q tile (the S MMA that read it has completed)
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
         float o[32];
         tmem_ld32(trow + kSpOCol + half * 32, o);
 #pragma unroll
         for (int q = 0; q < 4; ++q)
-          reinterpret_cast<uint4*>(orow + half * 32)[q] =
+          *reinterpret_cast<uint4*>(tiles + r * 128 + (((half * 4 + q) ^ (r & 7)) << 4)) =
               make_uint4(pack_bf16x2(o[8 * q + 0] * inv, o[8 * q + 1] * inv),
                          pack_bf16x2(o[8 * q + 2] * inv, o[8 * q + 3] * inv),
                          pack_bf16x2(o[8 * q + 4] * inv, o[8 * q + 5] * inv),
@@ -264,10 +267,16 @@ __global__ void __launch_bounds__(kSpThreads, 2)
       }
     }
   }
+  fence_async_smem_cta();  // the O rows (generic writes) are read by the TMA store below
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   if (warp == 1) tmem_dealloc<kSpTmemCols>(tmem);
+  if (threadIdx.x == 0) {
+    tma_store_2d(&tm_out, tiles, h * 64, f * OASIS_TOKENS);
+    bulk_commit();
+    bulk_wait_read<0>();  // shared memory is read before the CTA exits
+  }
 }
 
 // ----------------------------------------------------------------------------------
@@ -570,9 +579,14 @@ int launch_attn_spatial(const void* qkv, void* out, int frames, cudaStream_t str
   const long long strides[1] = {3 * OASIS_HIDDEN * 2};
   const int box[2] = {64, OASIS_TOKENS};
   if (int st = encode_bf16_sw128(&tm, qkv, 2, dims, strides, box)) return st;
+  // out [frames * 144][1024] bf16; box = one head's 64 columns of one frame's 144 rows
+  CUtensorMap tm_out;
+  const long long odims[2] = {OASIS_HIDDEN, static_cast<long long>(frames) * OASIS_TOKENS};
+  const long long ostrides[1] = {OASIS_HIDDEN * 2};
+  if (int st = encode_bf16_sw128(&tm_out, out, 2, odims, ostrides, box)) return st;
   dim3 grid(frames, OASIS_HEADS);
   cudaError_t e = launch_pdl(attn_spatial_kernel, grid, dim3(kSpThreads), kSpSmem, stream, tm,
-                             static_cast<__nv_bfloat16*>(out), kScaleLog2);
+                             tm_out, kScaleLog2);
   if (e != cudaSuccess) return cuda_status(e, "attn_spatial_kernel");
   return OASIS_OK;
 }
