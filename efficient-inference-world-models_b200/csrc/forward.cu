@@ -32,8 +32,9 @@ struct Layout {
 };
 
 // Row-block counters (one per 128-row block), zeroed at the start of every forward.
-// Per sub-block: 0 out-proj tiles, 1 rows normalised after it, 2 fc1 tiles, 3 fc2
-// tiles, 4 rows normalised after fc2 (the separate-launch path uses 0 and 3).
+// Per sub-block: 0 out-proj tiles, 1 rows normalised after it, 2 fc1 tiles (a bitmask
+// of the finished N tiles), 3 fc2 tiles, 4 rows normalised after fc2 (the
+// separate-launch path uses 0 and 3).
 inline size_t row_blocks(size_t M) { return (M + 127) / 128; }
 constexpr int kCountersPerSub = 5;
 
@@ -274,13 +275,15 @@ int run_forward(oasis_plan* p, const float* x, const int64_t* t, const float* ac
     Timer tm(p, s, kFamGemm);
     if (chain) {
       ChainStep st[kMaxChainOps];
-      st[0] = ChainStep{&p->out[j], kEpiGateResid, eo, nullptr, 0, cnt(j, 0), cnt(j, 1)};
-      st[1] = ChainStep{&p->fc1[j], kEpiBiasGelu, e1, cnt(j, 1), 0, cnt(j, 2), nullptr};
-      st[2] = ChainStep{&p->fc2[j], kEpiGateResid, e2, cnt(j, 2),
-                        static_cast<unsigned>(OASIS_MLP_HIDDEN / 256), cnt(j, 3), cnt(j, 4)};
+      // fc1 publishes a bitmask of its finished N tiles per row block; each k-block of fc2
+      // waits only for the fc1 tile that produced its 64 columns, so fc2's main loop can
+      // start on the tiles of earlier waves while the last fc1 wave is still in flight
+      st[0] = ChainStep{&p->out[j], kEpiGateResid, eo, nullptr, 0, cnt(j, 0), cnt(j, 1), false, false};
+      st[1] = ChainStep{&p->fc1[j], kEpiBiasGelu, e1, cnt(j, 1), 0, cnt(j, 2), nullptr, true, false};
+      st[2] = ChainStep{&p->fc2[j], kEpiGateResid, e2, cnt(j, 2), 0, cnt(j, 3), cnt(j, 4), false, true};
       int n = 3;
       if (!last) st[n++] = ChainStep{&p->qkv[j + 1], kEpiQkvRope, qkv_params(j + 1), cnt(j, 4), 0,
-                                     nullptr, nullptr};
+                                     nullptr, nullptr, false, false};
       if (int e = launch_chain(st, n, s)) return e;
     } else {
       if (int e = launch_gemm(p->out[j], kEpiGateResid, eo, s)) return e;

@@ -250,6 +250,12 @@ int launch_chain(const ChainStep* steps, int n, cudaStream_t stream) {
     op.wait_tiles = steps[i].wait_tiles;
     op.tiles_done = steps[i].tiles_done;
     op.rows_done = steps[i].rows_done;
+    if (steps[i].publish_bits && (g.N / 256 > 32 || steps[i].ep.ln_out || !steps[i].tiles_done))
+      return fail(OASIS_ERR_INVALID_ARG, "chain: tile bitmasks need at most 32 N tiles, counters and no LayerNorm");
+    if (steps[i].wait_bits && (g.K / 256 > 32 || !steps[i].wait))
+      return fail(OASIS_ERR_INVALID_ARG, "chain: bitmask waits need at most 32 producer tiles along K");
+    op.publish_bits = steps[i].publish_bits ? 1 : 0;
+    op.wait_bits = steps[i].wait_bits ? 1 : 0;
     const int tiles = ((g.M + 255) / 256) * (g.N / 256);
     if (tiles > max_tiles) max_tiles = tiles;
   }

@@ -114,6 +114,9 @@ __device__ __forceinline__ void epilogue_bar_sync() {
 __device__ __forceinline__ void red_release_add(unsigned int* p, unsigned int v) {
   asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
+__device__ __forceinline__ void red_release_or(unsigned int* p, unsigned int v) {
+  asm volatile("red.release.gpu.global.or.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
 __device__ __forceinline__ unsigned int ld_acquire(const unsigned int* p) {
   unsigned int v;
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -127,6 +130,25 @@ __device__ __forceinline__ bool wait_count_geq(const unsigned int* p, unsigned i
   while (true) {
     __nanosleep(64);
     if (ld_acquire(p) >= target) return true;
+    if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+      atomicOr(&g_dev_error, kDevErrTimeout);
+      return false;
+    }
+  }
+}
+
+// Bounded wait until bit `bit` of *p is set (another CTA of this grid sets it); `have`
+// holds the last value read, so bits already seen cost no further round trip.  Records a
+// timeout in the device error word and returns false after kWaitTimeoutNs.
+__device__ __forceinline__ bool wait_bit(const unsigned int* p, int bit, unsigned int& have) {
+  if ((have >> bit) & 1u) return true;
+  have = ld_acquire(p);
+  if ((have >> bit) & 1u) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+    __nanosleep(64);
+    have = ld_acquire(p);
+    if ((have >> bit) & 1u) return true;
     if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
       atomicOr(&g_dev_error, kDevErrTimeout);
       return false;
@@ -664,6 +686,10 @@ struct alignas(64) ChainOp {
   unsigned int wait_tiles;     // target: this many tiles, or (0) the block's row count
   unsigned int* tiles_done;    // +1 per finished tile and 128-row block (also ep.ln_count)
   unsigned int* rows_done;     // LayerNorm phase: + rows per finished group, or null
+  int publish_bits;            // tiles_done[block] |= 1 << (n0 / 256) instead of += 1
+  int wait_bits;               // `wait` holds such bitmasks: k-block kb of a tile needs bit
+                               // kb * 64 / 256 of its block (the producing tile of those K
+                               // columns), polled as the k loop reaches it
 };
 
 struct ChainParams {
@@ -771,7 +797,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         for (int tile = unit; tile < num_tiles && !*abort_flag; tile += num_units) {
           const int m0 = (tile % num_m) * TILE_M;
           const int n0 = (tile / num_m) * BN;
-          if (op.wait) {  // this CTA's 128 A rows must be complete
+          const bool rows_in = m0 + a_row0 < op.M;
+          unsigned int have = 0;  // wait_bits: the block's tile bits seen so far
+          if (op.wait && !op.wait_bits) {  // this CTA's 128 A rows must be complete
             const int q = (m0 + a_row0) / kGemmBM;
             const unsigned target = op.wait_tiles ? op.wait_tiles
                                                   : static_cast<unsigned>(min(kGemmBM, op.M - q * kGemmBM));
@@ -781,6 +809,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           for (int kb = 0; kb < num_kb; ++kb) {
             uint8_t* sa = smem + stage * S::kStageBytes;
             uint8_t* sb = sa + S::kABytes;
+            if (op.wait_bits && rows_in && !((have >> ((kb * kGemmBK) / BN)) & 1u)) {
+              // the A columns of this k-block come from one producer tile of the block
+              if (!wait_bit(op.wait + (m0 + a_row0) / kGemmBM, (kb * kGemmBK) / BN, have)) {
+                *abort_flag = 1;
+                break;
+              }
+              fence_async_global();  // the acquired columns are read by TMA (async proxy)
+            }
             if (pre > 0) {
               --pre;
               tma_load_2d_pair(sa, &op.a, lead_full + stage * 8, kb * kGemmBK, m0 + a_row0);
@@ -926,7 +962,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               *abort_flag = 1;
             } else if (w == 0) {
               const int q = m0 / kGemmBM;
-              if (q < nblk) red_release_add(op.tiles_done + q, 1u);
+              if (q < nblk) {
+                if (op.publish_bits)
+                  red_release_or(op.tiles_done + q, 1u << (n0 / BN));
+                else
+                  red_release_add(op.tiles_done + q, 1u);
+              }
             }
           }
           stored_phase ^= 1;
@@ -986,6 +1027,8 @@ struct ChainStep {
   unsigned int wait_tiles;
   unsigned int* tiles_done;
   unsigned int* rows_done;
+  bool publish_bits;  // tiles_done as per-block bitmasks of finished N tiles (at most 32)
+  bool wait_bits;     // `wait` holds such bitmasks; each k-block waits for its producer tile
 };
 int launch_chain(const ChainStep* steps, int n, cudaStream_t stream);
 int num_sms();
