@@ -18,6 +18,9 @@ accepts the per-frame list as ``solver_steps``.
 full-window forward that also stores the window's temporal K/V, and the remaining steps
 as incremental forwards of the new frame against that cache (the reference's
 persistent past-frame reuse, ``kv_cache/oasis_temporal_persistent_wrapper.py``).
+``rollout_dpmpp(..., use_graph=True)`` captures each frame's whole solver loop (its
+forwards and latent updates) as one CUDA graph per (window length, step count) and
+replays it for every later frame of the same shape.
 The VAE decode (``models/oasis.py:237-245``) is outside this library.
 """
 
@@ -124,17 +127,92 @@ def action_step_schedule(actions: torch.Tensor, **thresholds) -> List[int]:
 
 
 @torch.no_grad()
+def _solver_levels(steps: int, ab: torch.Tensor):
+    """(t, alpha_bar(t), alpha_bar(next)) of each solver step of a frame, in order
+    (``noise_range = linspace(-1, 999, steps + 1)`` walked backwards; the last step
+    lands on alpha_bar = 1)."""
+    nr = torch.linspace(-1, DDPM_T - 1, steps + 1)
+    out = []
+    for noise_idx in reversed(range(1, steps + 1)):
+        t = int(nr[noise_idx])
+        tn = int(nr[noise_idx - 1])
+        tn = t if tn < 0 else tn
+        out.append((t, float(ab[t]), 1.0 if noise_idx == 1 else float(ab[tn])))
+    return out
+
+
+class _FrameGraph:
+    """One frame's solver loop for a window of T frames (B sessions, ``steps`` solver
+    steps) as a CUDA graph over static buffers: the window latents and actions are copied
+    in before a replay and the new frame is copied out after it.  The first call runs the
+    loop eagerly (creating the forward plans and KV cache outside any capture); the
+    second captures it, and every call from then on replays."""
+
+    def __init__(self, dit, B: int, T: int, steps: int, ab: torch.Tensor, stabilization_level: int,
+                 use_cache: bool, kv_kinds, device):
+        self.dit, self.T = dit, T
+        self.xw = torch.empty(B, T, LATENT_C, LATENT_H, LATENT_W, device=device)
+        self.aw = torch.zeros(B, T, ACTION_DIM, device=device)
+        self.eps = torch.empty(B, FRAME_ELEMS, device=device)
+        self.v = torch.empty(B, T, LATENT_C, LATENT_H, LATENT_W, device=device)
+        self.v1 = torch.empty(B, LATENT_C, LATENT_H, LATENT_W, device=device)
+        self.cache = None
+        if use_cache and T > 1:
+            kinds = kv_kinds(T - 1) if kv_kinds is not None else ["bf16"] * (T - 1)
+            self.cache = KVCacheB200(B, dit.depth, kinds, device=device)
+        self.levels = []
+        for t, ab_t, ab_next in _solver_levels(steps, ab):
+            tw = torch.full((B, T), stabilization_level - 1, dtype=torch.long, device=device)
+            tw[:, -1] = t
+            self.levels.append((tw, tw[:, -1].contiguous(), ab_t, ab_next))
+        self.graph = None
+        self.calls = 0
+
+    def _body(self) -> None:
+        T = self.T
+        for k, (tw, t_new, ab_t, ab_next) in enumerate(self.levels):
+            if self.cache is not None and k > 0:
+                v = self.dit.forward_cached(self.xw[:, -1], t_new, self.aw[:, -1], self.cache,
+                                            n_past=T - 1, out=self.v1)
+            else:
+                v = self.dit(self.xw, tw, self.aw, kv_cache=self.cache, out=self.v)
+            _update_newest(self.xw, T - 1, v, self.eps, ab_t, ab_next, k == 0)
+
+    def run(self, x: torch.Tensor, actions: torch.Tensor, start: int, i: int) -> None:
+        self.xw.copy_(x[:, start: i + 1])
+        self.aw.copy_(actions[:, start: i + 1])
+        if self.calls == 0:
+            self._body()
+        else:
+            if self.graph is None:
+                side = torch.cuda.Stream(device=self.xw.device)
+                side.wait_stream(torch.cuda.current_stream())
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.stream(side):
+                    with torch.cuda.graph(graph, stream=side):
+                        self._body()  # recorded, not run
+                torch.cuda.current_stream().wait_stream(side)
+                self.graph = graph
+            self.graph.replay()
+        self.calls += 1
+        x[:, i].copy_(self.xw[:, -1])
+
+
 def rollout_dpmpp(dit, prompt_latent: torch.Tensor, actions: torch.Tensor, num_frames: int,
                   solver_steps: Union[int, Sequence[int]] = 5, stabilization_level: int = 15,
                   noise_abs_max: float = 20.0,
                   seed: int = 42, use_cache: bool = False, kv_kinds=None,
-                  alpha_bar: Optional[torch.Tensor] = None, step_callback=None) -> torch.Tensor:
+                  alpha_bar: Optional[torch.Tensor] = None, step_callback=None,
+                  use_graph: bool = False) -> torch.Tensor:
     """DPM-Solver++ 2M rollout of ``num_frames`` new frames for B sessions.
 
     prompt_latent (B, n_prompt, 16, 18, 32) on the device; actions (B, n_prompt +
     num_frames, 25).  ``solver_steps`` is one count for every frame or a per-frame list
-    indexed by absolute frame (e.g. ``action_step_schedule(actions)``).  Returns all
-    latents (B, n_prompt + num_frames, 16, 18, 32)."""
+    indexed by absolute frame (e.g. ``action_step_schedule(actions)``).  With
+    ``use_graph`` each frame's solver loop is a replayed CUDA graph (no per-step
+    ``step_callback`` then).  Returns all latents (B, n_prompt + num_frames, 16, 18, 32)."""
+    if use_graph and step_callback is not None:
+        raise ValueError("step_callback runs between solver steps; it cannot be used with use_graph")
     device = prompt_latent.device
     ab = (alpha_bar if alpha_bar is not None else alphas_cumprod()).float().cpu()
     max_frames = dit.max_frames
@@ -145,25 +223,29 @@ def rollout_dpmpp(dit, prompt_latent: torch.Tensor, actions: torch.Tensor, num_f
     x[:, :n_prompt] = prompt_latent
     eps_prev = torch.empty(B, LATENT_C * LATENT_H * LATENT_W, device=device)
     cache = None
+    graphs: Dict[Any, _FrameGraph] = {}
     for i in range(n_prompt, total):
         chunk = torch.randn((B, LATENT_C, LATENT_H, LATENT_W), device=device, generator=gen)
         x[:, i] = chunk.clamp(-noise_abs_max, noise_abs_max)
         start = max(0, i + 1 - max_frames)
         T = i + 1 - start
+        steps_i = int(solver_steps) if isinstance(solver_steps, int) else int(solver_steps[i])
+        if use_graph:
+            if any(key[0] != T for key in graphs):  # the window grew: shorter shapes never recur
+                graphs = {key: g for key, g in graphs.items() if key[0] == T}
+            fg = graphs.get((T, steps_i))
+            if fg is None:
+                fg = graphs[(T, steps_i)] = _FrameGraph(dit, B, T, steps_i, ab, stabilization_level,
+                                                        use_cache, kv_kinds, device)
+            fg.run(x, actions, start, i)
+            continue
         window = x[:, start: i + 1]
         act = actions[:, start: i + 1].contiguous()
         t_win = torch.full((B, T), stabilization_level - 1, dtype=torch.long, device=device)
         if use_cache and T > 1 and (cache is None or cache.n_slots != T - 1):
             kinds = kv_kinds(T - 1) if kv_kinds is not None else ["bf16"] * (T - 1)
             cache = KVCacheB200(B, dit.depth, kinds, device=device)
-        steps_i = int(solver_steps) if isinstance(solver_steps, int) else int(solver_steps[i])
-        nr = torch.linspace(-1, DDPM_T - 1, steps_i + 1)
-        for k, noise_idx in enumerate(reversed(range(1, steps_i + 1))):
-            t = int(nr[noise_idx])
-            tn = int(nr[noise_idx - 1])
-            tn = t if tn < 0 else tn
-            ab_t = float(ab[t])
-            ab_next = 1.0 if noise_idx == 1 else float(ab[tn])
+        for k, (t, ab_t, ab_next) in enumerate(_solver_levels(steps_i, ab)):
             t_win[:, -1] = t
             if use_cache and T > 1 and k > 0:
                 v = dit.forward_cached(x[:, i], t_win[:, -1], act[:, -1], cache, n_past=T - 1)

@@ -187,6 +187,27 @@ def test_dpmpp_rollout_with_action_step_schedule(pkg, cuda):
     assert rel_l2(xb, xa) < 1e-4
 
 
+@pytest.mark.parametrize("use_cache", [False, True])
+def test_dpmpp_rollout_graph_equals_eager(pkg, cuda, use_cache):
+    """The frame loop replayed as a CUDA graph gives the same latents, bit for bit, as
+    the eager loop: 30 prompt frames and 5 new ones take the window to its 32-frame
+    maximum, so the last frames replay a captured graph."""
+    depth, B = 1, 1
+    model = pkg.OasisDiTB200.from_state_dict(state(pkg, depth), device=cuda, depth=depth)
+    g = torch.Generator().manual_seed(6)
+    prompt = torch.randn(B, 30, 16, 18, 32, generator=g).to(cuda)
+    acts = torch.zeros(B, 35, 25)
+    acts[:, :, :23] = (torch.rand(B, 35, 23, generator=g) < 0.1).float()
+    acts = acts.to(cuda)
+    xa = pkg.rollout_dpmpp(model, prompt, acts, num_frames=5, solver_steps=3, use_cache=use_cache,
+                           seed=7)
+    xb = pkg.rollout_dpmpp(model, prompt, acts, num_frames=5, solver_steps=3, use_cache=use_cache,
+                           seed=7, use_graph=True)
+    torch.cuda.synchronize()
+    assert torch.isfinite(xb).all()
+    assert torch.equal(xa, xb)
+
+
 def test_generate_ddim_runs(pkg, cuda):
     model = pkg.OasisDiTB200.from_state_dict(state(pkg, 1), device=cuda, depth=1)
     out = pkg.generate({"dit": model, "device": cuda}, num_frames=2, num_steps=3)
