@@ -123,7 +123,7 @@ class ClockSampler:
         except Exception:
             self.proc.kill()
         self.thread.join(timeout=2)
-        mhz, mx, reasons = [], None, set()
+        mhz, watts, mx, reasons = [], [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for ln in self.lines:
             parts = [p.strip() for p in ln.split(",")]
@@ -136,10 +136,15 @@ class ClockSampler:
                 mx = float(parts[3])
             except ValueError:
                 continue
+            try:
+                watts.append(float(parts[4]))
+            except ValueError:
+                pass
             for n, val in zip(names, parts[6:10]):
                 if val.lower() == "active":
                     reasons.add(n)
         return {"sm_mhz": statistics.median(mhz) if mhz else None, "sm_max_mhz": mx,
+                "power_w": statistics.median(watts) if watts else None,
                 "reasons": sorted(reasons), "samples": len(mhz)}
 
 
