@@ -450,9 +450,12 @@ __global__ void __launch_bounds__(kTpWarps * 32)
     float s[4][4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.0f;
+    // key tiles this query tile can see: a tile whose first key lies past the tile's last
+    // query position is fully masked (its products would be zeroed), so it is skipped
+    const int live_pairs = min(n_pairs, (q_pos0 + mt * 16 + 15) / 16 + 1);
 #pragma unroll
     for (int jp = 0; jp < 2; ++jp) {
-      if (jp < n_pairs) {
+      if (jp < live_pairs) {
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
           uint32_t b0, b1, b2, b3;
@@ -504,7 +507,7 @@ __global__ void __launch_bounds__(kTpWarps * 32)
     for (int j = 0; j < 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.0f;
 #pragma unroll
     for (int kk = 0; kk < 2; ++kk) {
-      if (kk < n_pairs) {
+      if (kk < live_pairs) {
         uint32_t pa[4];
         pa[0] = pack_bf16x2(s[2 * kk][0], s[2 * kk][1]);
         pa[1] = pack_bf16x2(s[2 * kk][2], s[2 * kk][3]);
