@@ -197,6 +197,18 @@ def cpu_oracle_rate(budget_s=12.0, threads=None):
                       f"{blk:.3f} s each); forward = embed+final + 16 blocks"}
 
 
+def workload_config(world, use_graph):
+    """The workload both arms report: one session per GPU, full 32-frame window, the DPM++
+    2M rollout of 16 frames x 5 solver steps."""
+    return {
+        "workload": "Oasis-500M DiT full-window forward + DPM-Solver++ 2M update, 1 session/GPU, "
+                    "T=32 sliding window, 5 solver steps/frame (80 steps = 16-frame rollout)",
+        "batch_per_gpu": 1, "frames": WINDOW, "tokens_per_forward": WINDOW * 144, "depth": DEPTH,
+        "parallelism": f"replicas x{world} (sessions sharded by GPU, no collective on the hot path)",
+        "l2": "inputs larger than L2: 1.21 GB of bf16 weights streamed per forward",
+        "cuda_graph": use_graph}
+
+
 def run_reference(args, rank, world):
     if rank != 0:
         return 0
@@ -216,8 +228,7 @@ def run_reference(args, rank, world):
         "value": value, "unit": "forwards/s", "n_gpus": world, "steps": steps, "warmup": warmup,
         "ms_per_step": 1000.0 / value, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "Oasis-500M DiT full-window forward, B=1, T=32 (CPU restatement)",
-                   "batch_per_gpu": 1, "frames": WINDOW, "depth": DEPTH},
+        "config": workload_config(world, not args.no_graph),
         "cpu_baseline": {"value": value, "unit": "forwards/s", "cores": o.cores, "kind": "port",
                          "sample": sample},
         "e2e": {"value": value, "unit": "forwards/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -407,13 +418,7 @@ def run_ours(args, rank, world, local_rank):
             "warmup": max(3, args.warmup), "ms_per_step": per_fwd_ms, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded N(0,1) latents, Bernoulli(0.1)+N(0,0.3) actions, random-init weights)",
-            "config": {
-                "workload": "Oasis-500M DiT full-window forward + DPM-Solver++ 2M update, 1 session/GPU, "
-                            "T=32 sliding window, 5 solver steps/frame (80 steps = 16-frame rollout)",
-                "batch_per_gpu": B, "frames": T, "tokens_per_forward": M, "depth": DEPTH,
-                "parallelism": f"replicas x{world} (sessions sharded by GPU, no collective on the hot path)",
-                "l2": "inputs larger than L2: 1.21 GB of bf16 weights streamed per forward",
-                "cuda_graph": use_graph},
+            "config": workload_config(world, use_graph),
             "e2e": {"value": e2e_value, "unit": "forwards/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "steps": e2e_steps},
             "gpu_launches": gpu_launches_per_step(DEPTH) * args.steps,
