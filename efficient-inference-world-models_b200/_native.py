@@ -67,6 +67,7 @@ SIGNATURES = {
     "oasis_last_error": (c_char_p, []),
     "oasis_version": (c_char_p, []),
     "oasis_check_device_error": (c_int, []),
+    "oasis_selftest_bounded_wait": (c_int, [c_void_p]),
     "oasis_plan_workspace_size": (c_size_t, [c_int, c_int, c_int]),
     "oasis_plan_create": (c_int, [POINTER(DiTWeights), c_int, c_int, c_void_p, c_size_t,
                                   POINTER(c_void_p)]),

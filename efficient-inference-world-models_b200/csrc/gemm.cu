@@ -290,6 +290,17 @@ void choose_tiles(int M, int N, int* bn, int* ctas) {
 
 }  // namespace oasis
 
+// ------------------------------------------------------------------ bounded-wait self-test
+namespace oasis {
+namespace {
+__device__ unsigned int g_never_set = 0;  // no kernel ever writes it
+
+__global__ void bounded_wait_selftest_kernel() {
+  if (threadIdx.x == 0) wait_count_geq(&g_never_set, 1u);  // gives up, records the timeout
+}
+}  // namespace
+}  // namespace oasis
+
 // ------------------------------------------------------------------ C ABI
 extern "C" int oasis_gemm_bf16(const void* A, const void* B, void* D, const float* bias, int M,
                                int N, int K, int lda, int ldb, int ldd, int epilogue,
@@ -313,4 +324,12 @@ extern "C" int oasis_gemm_bf16(const void* A, const void* B, void* D, const floa
   ep.ldd = ldd;
   ep.bias = bias;
   return launch_gemm(g, epilogue == 0 ? kEpiStoreBF16 : kEpiStoreF32Bias, ep, stream);
+}
+
+extern "C" int oasis_selftest_bounded_wait(cudaStream_t stream) {
+  using namespace oasis;
+  bounded_wait_selftest_kernel<<<1, 32, 0, stream>>>();
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_status(e, "bounded_wait_selftest_kernel");
+  return OASIS_OK;
 }

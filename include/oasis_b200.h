@@ -57,6 +57,13 @@ const char* oasis_version(void);
 /* Reads and clears the device-side error word set by bounded waits (synchronises
  * the device).  Returns OASIS_ERR_DEVICE_TIMEOUT if any kernel gave up a wait. */
 int oasis_check_device_error(void);
+/* Self-test of that failure path: launches one thread that waits, through the same
+ * bounded wait the chained GEMM and the LayerNorm tails use, for a device word that
+ * nothing ever sets.  After the 2 s limit the wait records a timeout in the device error
+ * word and the kernel returns normally, so oasis_check_device_error then reports
+ * OASIS_ERR_DEVICE_TIMEOUT (and clears it) while the context stays usable.  No
+ * counterpart in the reference, whose waits are all on the host. */
+int oasis_selftest_bounded_wait(cudaStream_t stream);
 
 /* ------------------------------------------------------------------ weights */
 /* One attention+MLP sub-block (spatial or temporal).  Linear weights are bf16

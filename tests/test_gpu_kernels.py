@@ -262,3 +262,21 @@ def test_ab_sampler_matches_reference_fixture(pkg, cuda, order):
 def test_no_device_timeouts_recorded(pkg, cuda):
     torch.cuda.synchronize()
     pkg._native.check(pkg.lib().oasis_check_device_error())
+
+
+def test_bounded_wait_gives_up_and_context_stays_usable(pkg, cuda):
+    """A device-side wait on a flag that nothing sets runs out after its 2 s limit: the
+    kernel records the timeout and returns, the host reads OASIS_ERR_DEVICE_TIMEOUT (5)
+    once, and the next kernels on the same context give correct results."""
+    L = pkg.lib()
+    pkg._native.check(L.oasis_check_device_error())  # start from a clear error word
+    assert L.oasis_selftest_bounded_wait(None) == 0
+    assert L.oasis_check_device_error() == 5
+    assert b"bounded wait" in L.oasis_last_error()
+    assert L.oasis_check_device_error() == 0  # reading it cleared it
+    qkv = _qkv(1 * 5, cuda, 77)
+    out = pkg.attn_temporal(qkv, batch=1, q_frames=5)
+    ref = _temporal_ref(qkv, 1, 5)
+    torch.cuda.synchronize()
+    assert rel_l2(out.float(), ref) < 1e-2
+    pkg._native.check(L.oasis_check_device_error())
