@@ -208,6 +208,30 @@ def test_dpmpp_rollout_graph_equals_eager(pkg, cuda, use_cache):
     assert torch.equal(xa, xb)
 
 
+def test_dpmpp_rollout_graph_two_sessions_step_schedule(pkg, cuda):
+    """Graph replay with two sessions (the newest-frame views are strided, so the copies
+    into contiguous buffers are part of the captured loop) and per-frame step counts from
+    the action schedule (several graph shapes for the same window length): equal, bit for
+    bit, to the eager loop, cached and uncached."""
+    depth, B = 1, 2
+    model = pkg.OasisDiTB200.from_state_dict(state(pkg, depth), device=cuda, depth=depth)
+    g = torch.Generator().manual_seed(8)
+    prompt = torch.randn(B, 30, 16, 18, 32, generator=g).to(cuda)
+    acts = torch.zeros(B, 36, 25)
+    acts[0, 31:33, 0] = 1.0    # frames 31, 32: 3 steps
+    acts[0, 34, :4] = 1.0      # frame 34: 5 steps
+    sched = pkg.action_step_schedule(acts)
+    acts = acts.to(cuda)
+    for use_cache in (False, True):
+        xa = pkg.rollout_dpmpp(model, prompt, acts, num_frames=6, solver_steps=sched,
+                               use_cache=use_cache, seed=9)
+        xb = pkg.rollout_dpmpp(model, prompt, acts, num_frames=6, solver_steps=sched,
+                               use_cache=use_cache, seed=9, use_graph=True)
+        torch.cuda.synchronize()
+        assert torch.isfinite(xb).all()
+        assert torch.equal(xa, xb), use_cache
+
+
 def test_generate_ddim_runs(pkg, cuda):
     model = pkg.OasisDiTB200.from_state_dict(state(pkg, 1), device=cuda, depth=1)
     out = pkg.generate({"dit": model, "device": cuda}, num_frames=2, num_steps=3)
