@@ -212,7 +212,7 @@ def test_dpmpp_rollout_graph_two_sessions_step_schedule(pkg, cuda):
     """Graph replay with two sessions (the newest-frame views are strided, so the copies
     into contiguous buffers are part of the captured loop) and per-frame step counts from
     the action schedule (several graph shapes for the same window length): equal, bit for
-    bit, to the eager loop, cached and uncached."""
+    bit, to the eager loop, uncached, with a bf16 cache and with an INT4 + bf16 cache."""
     depth, B = 1, 2
     model = pkg.OasisDiTB200.from_state_dict(state(pkg, depth), device=cuda, depth=depth)
     g = torch.Generator().manual_seed(8)
@@ -222,14 +222,17 @@ def test_dpmpp_rollout_graph_two_sessions_step_schedule(pkg, cuda):
     acts[0, 34, :4] = 1.0      # frame 34: 5 steps
     sched = pkg.action_step_schedule(acts)
     acts = acts.to(cuda)
-    for use_cache in (False, True):
+    def mixed(n):  # INT4 for frames older than the newest 8, bf16 for those
+        return ["int4"] * max(0, n - 8) + ["bf16"] * min(n, 8)
+
+    for use_cache, kinds in ((False, None), (True, None), (True, mixed)):
         xa = pkg.rollout_dpmpp(model, prompt, acts, num_frames=6, solver_steps=sched,
-                               use_cache=use_cache, seed=9)
+                               use_cache=use_cache, kv_kinds=kinds, seed=9)
         xb = pkg.rollout_dpmpp(model, prompt, acts, num_frames=6, solver_steps=sched,
-                               use_cache=use_cache, seed=9, use_graph=True)
+                               use_cache=use_cache, kv_kinds=kinds, seed=9, use_graph=True)
         torch.cuda.synchronize()
         assert torch.isfinite(xb).all()
-        assert torch.equal(xa, xb), use_cache
+        assert torch.equal(xa, xb), (use_cache, kinds)
 
 
 def test_generate_ddim_runs(pkg, cuda):
