@@ -156,3 +156,16 @@ def quantize_int4_rows(kv: np.ndarray):
     return (packed.reshape(*lead, kv.shape[-1] // 2),
             scale.astype(np.float16).reshape(lead), zero.astype(np.float16).reshape(lead),
             scale.reshape(lead), zero.reshape(lead))
+
+
+# ---------------------------------------------------------------- age promotions
+
+def promote_fp8_to_int4_rows(codes: np.ndarray, scale) -> tuple:
+    """``_promote_to_int4`` of an FP8 entry (progressive_quant.py:334-350): the codes are
+    dequantised with ``dequantize_fp8``'s default fp16 target, i.e. fp16(e4m3 x scale)
+    with the product exact in fp32 and rounded once (RNE), and those values are quantised
+    like ``quantize_int4_rows`` (one group per 64-element row)."""
+    x = (e4m3_decode(codes) * np.float32(scale)).astype(np.float32)
+    x16 = x.astype(np.float16).astype(np.float32)
+    return quantize_int4_rows(x16)
+

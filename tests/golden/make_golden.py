@@ -23,6 +23,11 @@ produced by calling the reference functions named below on seeded inputs:
   and in cached-prefix mode.
 * ``cached_past_golden.npz`` — ``attention_with_cached_past``
   (``kv_cache/oasis_persistent_kv_theory.py:97-124``).
+* ``promote_golden.npz`` — the age promotions of ``update_cache`` on the same bf16
+  slices (``progressive_quant.py:263-350``): ``_promote_to_fp8`` (``quantize_to_fp8``),
+  ``_promote_to_int4`` of an FP8 entry (``dequantize_fp8`` with its default fp16 target,
+  then ``quantize_to_int4``) and of a full-precision entry (``quantize_to_int4``), with
+  the cache's group of 64.
 """
 
 from __future__ import annotations
@@ -89,6 +94,34 @@ def make_quant():
         fp8_deq_bf16=np.stack(f8_deq), int4_packed=np.stack(i4_packed), int4_scale=np.stack(i4_scale),
         int4_zero=np.stack(i4_zero), int4_deq_f32=np.stack(i4_deq),
         flat_bf16=_bf16_bits(flat), flat_packed=p.numpy(), flat_scale=sc.numpy(), flat_zero=z.numpy(),
+    )
+
+
+def make_promote():
+    P = ProgressiveKVQuantizer
+    xs = quant_cases()
+    fp8_codes, fp8_scale, from_fp8, from_full, deq_dtype = [], [], [], [], []
+    for x in xs:
+        q, s = P.quantize_to_fp8(x)                       # _promote_to_fp8
+        fp8_codes.append(q.view(torch.uint8).numpy().copy())
+        fp8_scale.append(_bf16_bits(s.reshape(1))[0])
+        raw = P.dequantize_fp8(q, s)                      # _promote_to_int4, FP8 entry
+        deq_dtype.append(str(raw.dtype))
+        p, sc, z = P.quantize_to_int4(raw, group_size=64)
+        from_fp8.append((p.numpy().copy(), sc.numpy().copy(), z.numpy().copy()))
+        p, sc, z = P.quantize_to_int4(x, group_size=64)   # _promote_to_int4, full precision
+        from_full.append((p.numpy().copy(), sc.numpy().copy(), z.numpy().copy()))
+    assert len(set(deq_dtype)) == 1, deq_dtype
+    np.savez_compressed(
+        os.path.join(HERE, "promote_golden.npz"),
+        inp_bf16=np.stack([_bf16_bits(x) for x in xs]), fp8_codes=np.stack(fp8_codes),
+        fp8_scale_bf16=np.array(fp8_scale, np.uint16), dequant_dtype=np.array(deq_dtype[0]),
+        i4_from_fp8_packed=np.stack([a for a, _, _ in from_fp8]),
+        i4_from_fp8_scale=np.stack([b for _, b, _ in from_fp8]),
+        i4_from_fp8_zero=np.stack([c for _, _, c in from_fp8]),
+        i4_from_full_packed=np.stack([a for a, _, _ in from_full]),
+        i4_from_full_scale=np.stack([b for _, b, _ in from_full]),
+        i4_from_full_zero=np.stack([c for _, _, c in from_full]),
     )
 
 
@@ -201,4 +234,5 @@ if __name__ == "__main__":
     make_sampler()
     make_temporal_attn()
     make_cached_past()
+    make_promote()
     print("golden fixtures written to", HERE)

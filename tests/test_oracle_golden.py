@@ -54,6 +54,26 @@ def test_int4_default_group_ragged_bit_exact():
     np.testing.assert_array_equal(zero, g["flat_zero"])
 
 
+def test_age_promotions_bit_exact():
+    """bf16 -> FP8, FP8 -> INT4 (via the fp16 dequantisation) and bf16 -> INT4, as the
+    reference's update_cache promotes entries, on the cache's 64-element groups."""
+    g = _load("promote_golden.npz")
+    assert str(g["dequant_dtype"]) == "torch.float16"
+    xs = quant_ref.bf16_from_bits(g["inp_bf16"])
+    for i in range(xs.shape[0]):
+        codes, scale = quant_ref.quantize_to_fp8_bf16(xs[i])
+        np.testing.assert_array_equal(codes, g["fp8_codes"][i])
+        assert quant_ref.bf16_bits(np.array([scale], np.float32))[0] == g["fp8_scale_bf16"][i]
+        p, _, _, s32, z32 = quant_ref.promote_fp8_to_int4_rows(codes, scale)
+        np.testing.assert_array_equal(p.reshape(-1), g["i4_from_fp8_packed"][i])
+        np.testing.assert_array_equal(s32, g["i4_from_fp8_scale"][i])
+        np.testing.assert_array_equal(z32, g["i4_from_fp8_zero"][i])
+        p, _, _, s32, z32 = quant_ref.quantize_int4_rows(xs[i])
+        np.testing.assert_array_equal(p.reshape(-1), g["i4_from_full_packed"][i])
+        np.testing.assert_array_equal(s32, g["i4_from_full_scale"][i])
+        np.testing.assert_array_equal(z32, g["i4_from_full_zero"][i])
+
+
 def test_e4m3_encoder_matches_torch_on_all_bf16_magnitudes():
     # every bf16 value in the e4m3 range and beyond, both signs
     bits = np.arange(0, 0x7F80, dtype=np.uint32)
