@@ -8,7 +8,7 @@ from . import _native
 from ._native import OasisError, lib, version
 from .dit import OasisDiTB200
 from .kv_cache import KVCacheB200, attn_spatial, attn_temporal
-from .manager import KVCacheManagerB200, ProgressiveKVQuantizerB200
+from .manager import KVCacheManagerB200, ProgressiveKVQuantizerB200, RollingKVCacheB200
 from .oasis import (action_step_schedule, alphas_cumprod, generate, rollout_dpmpp,
                     sigmoid_beta_schedule, steps_for_action_magnitude)
 from .samplers import DPMSolverPPSampler, ddim_update, dpmpp2m_update
@@ -16,6 +16,7 @@ from .weights import pack_weights, param_shapes, random_state_dict, rope_tables
 
 __all__ = [
     "OasisDiTB200", "KVCacheB200", "KVCacheManagerB200", "ProgressiveKVQuantizerB200",
+    "RollingKVCacheB200",
     "DPMSolverPPSampler", "OasisError", "action_step_schedule", "alphas_cumprod", "attn_spatial", "attn_temporal",
     "ddim_update", "dpmpp2m_update", "generate", "lib", "pack_weights", "param_shapes",
     "random_state_dict", "rollout_dpmpp", "rope_tables", "sigmoid_beta_schedule", "steps_for_action_magnitude", "version",

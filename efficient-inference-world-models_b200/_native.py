@@ -87,6 +87,7 @@ SIGNATURES = {
                                     c_int, c_int, c_int, c_void_p]),
     "oasis_kv_store": (c_int, [c_void_p, c_int, c_int, c_int, POINTER(KvCache), c_int, c_int,
                                c_int, c_int, c_void_p]),
+    "oasis_kv_migrate": (c_int, [POINTER(KvCache), c_int, c_int, c_void_p]),
     "oasis_kv_load": (c_int, [POINTER(KvCache), c_int, c_int, c_int, c_void_p, c_void_p, c_void_p]),
     "oasis_dpmpp2m_update": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_longlong,
                                      c_longlong, c_float, c_float, c_int, c_void_p]),

@@ -195,6 +195,88 @@ int fill_store_params(KvStoreParams* p, const oasis_kv_cache_t* c) {
   return OASIS_OK;
 }
 
+// Age promotion of one frame (ProgressiveKVQuantizer.update_cache, progressive_quant.py:
+// 263-350) for every session and layer: the slot at (src_kind, src_idx) is re-quantised
+// into (dst_kind, dst_idx) with the store kernel's arithmetic.  The source values are
+// the bf16 entries, or for an FP8 entry promoted to INT4 the reference's dequantisation
+// with its default fp16 target: fp16(e4m3 x scale), the product exact in fp32 and
+// rounded once.  grid: (batch*layers, 2 [K,V], 16 heads); one CTA per 144 x 64 slice.
+__global__ void __launch_bounds__(kStoreThreads)
+    kv_migrate_kernel(KvStoreParams p, int src_kind, int src_idx, int dst_kind, int dst_idx) {
+  pdl_trigger();
+  pdl_wait();
+  const int bl = blockIdx.x;  // session * layers + layer
+  const bool is_v = blockIdx.y == 1;
+  const int h = blockIdx.z;
+  const __nv_bfloat16* sb = nullptr;
+  const uint8_t* sf = nullptr;
+  float fscale = 0.0f;
+  if (src_kind == OASIS_KV_BF16) {
+    sb = (is_v ? p.v_bf16 : p.k_bf16) + (static_cast<long long>(bl) * p.n_bf16 + src_idx) * OASIS_TOKENS *
+                                            OASIS_HIDDEN + h * 64;
+  } else {
+    const long long slot = static_cast<long long>(bl) * p.n_fp8 + src_idx;
+    sf = (is_v ? p.v_fp8 : p.k_fp8) + slot * OASIS_TOKENS * OASIS_HIDDEN + h * 64;
+    fscale = __bfloat162float((is_v ? p.v_fp8_scale : p.k_fp8_scale)[slot * OASIS_HEADS + h]);
+  }
+  // element (row r, column c) of the source slice as the value the reference quantises
+  auto value = [&](int r, int c) -> float {
+    if (sb) return __bfloat162float(sb[r * OASIS_HIDDEN + c]);
+    return __half2float(__float2half_rn(e4m3_to_float(sf[r * OASIS_HIDDEN + c]) * fscale));
+  };
+
+  if (dst_kind == OASIS_KV_FP8) {  // only from bf16 (a full-precision entry)
+    __shared__ float red[kStoreThreads / 32];
+    float amax = 0.0f;
+    for (int i = threadIdx.x; i < OASIS_TOKENS * 64; i += kStoreThreads)
+      amax = fmaxf(amax, fabsf(value(i >> 6, i & 63)));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
+    __syncthreads();
+    amax = red[0];
+#pragma unroll
+    for (int w = 1; w < kStoreThreads / 32; ++w) amax = fmaxf(amax, red[w]);
+    amax = fmaxf(amax, __bfloat162float(__float2bfloat16_rn(1e-12f)));
+    const float scale = bf16_round(__fdiv_rn(amax, 448.0f));
+    const long long slot = static_cast<long long>(bl) * p.n_fp8 + dst_idx;
+    uint8_t* dst = (is_v ? p.v_fp8 : p.k_fp8) + slot * OASIS_TOKENS * OASIS_HIDDEN + h * 64;
+    for (int i = threadIdx.x; i < OASIS_TOKENS * 64; i += kStoreThreads) {
+      const int r = i >> 6, c = i & 63;
+      dst[r * OASIS_HIDDEN + c] =
+          static_cast<uint8_t>(float_to_e4m3(bf16_round(__fdiv_rn(value(r, c), scale))));
+    }
+    if (threadIdx.x == 0)
+      (is_v ? p.v_fp8_scale : p.k_fp8_scale)[slot * OASIS_HEADS + h] = __float2bfloat16_rn(scale);
+    return;
+  }
+
+  // INT4: one warp per token row of this head; lane holds elements 2l, 2l+1
+  const long long slot = static_cast<long long>(bl) * p.n_int4 + dst_idx;
+  uint8_t* codes = is_v ? p.v_int4 : p.k_int4;
+  __half* sc = is_v ? p.v_i4_scale : p.k_i4_scale;
+  __half* zp = is_v ? p.v_i4_zero : p.k_i4_zero;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int r = warp; r < OASIS_TOKENS; r += kStoreThreads / 32) {
+    const float x0 = value(r, 2 * lane), x1 = value(r, 2 * lane + 1);
+    float mn = fminf(x0, x1), mx = fmaxf(x0, x1);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    }
+    const float scale = __fdiv_rn(fmaxf(__fsub_rn(mx, mn), 1e-12f), 15.0f);
+    const float q0 = fminf(fmaxf(rintf(__fdiv_rn(__fsub_rn(x0, mn), scale)), 0.0f), 15.0f);
+    const float q1 = fminf(fmaxf(rintf(__fdiv_rn(__fsub_rn(x1, mn), scale)), 0.0f), 15.0f);
+    const long long grp = (slot * OASIS_TOKENS + r) * OASIS_HEADS + h;
+    codes[grp * 32 + lane] = static_cast<uint8_t>((static_cast<uint32_t>(q0) << 4) | static_cast<uint32_t>(q1));
+    if (lane == 0) {
+      sc[grp] = __float2half_rn(scale);
+      zp[grp] = __float2half_rn(mn);
+    }
+  }
+}
+
 int validate_slots(const oasis_kv_cache_t* c, int slot0, int frames) {
   if (slot0 < 0 || frames < 0 || slot0 + frames > c->n_slots || c->n_slots > OASIS_MAX_FRAMES)
     return fail(OASIS_ERR_INVALID_ARG, "KV slot range outside the cache");
@@ -287,5 +369,25 @@ extern "C" int oasis_kv_load(const oasis_kv_cache_t* cache, int layer, int slot0
   dim3 grid(frames * cache->batch, 2);
   cudaError_t e = launch_pdl(kv_load_kernel, grid, dim3(256), 0, stream, p);
   if (e != cudaSuccess) return cuda_status(e, "kv_load_kernel");
+  return OASIS_OK;
+}
+
+extern "C" int oasis_kv_migrate(const oasis_kv_cache_t* cache, int src_slot, int dst_slot,
+                                cudaStream_t stream) {
+  using namespace oasis;
+  if (!cache || src_slot == dst_slot) return fail(OASIS_ERR_INVALID_ARG, "oasis_kv_migrate: bad args");
+  if (int s = validate_slots(cache, src_slot, 1)) return s;
+  if (int s = validate_slots(cache, dst_slot, 1)) return s;
+  const int sk = cache->slot_kind[src_slot], dk = cache->slot_kind[dst_slot];
+  if (!((sk == OASIS_KV_BF16 && (dk == OASIS_KV_FP8 || dk == OASIS_KV_INT4)) ||
+        (sk == OASIS_KV_FP8 && dk == OASIS_KV_INT4)))
+    return fail(OASIS_ERR_INVALID_ARG, "oasis_kv_migrate: promotions are bf16->fp8, bf16->int4, fp8->int4");
+  KvStoreParams p{};
+  fill_store_params(&p, cache);
+  dim3 grid(cache->batch * cache->layers, 2, OASIS_HEADS);
+  cudaError_t e = launch_pdl(kv_migrate_kernel, grid, dim3(kStoreThreads), 0, stream, p, sk,
+                             static_cast<int>(cache->slot_index[src_slot]), dk,
+                             static_cast<int>(cache->slot_index[dst_slot]));
+  if (e != cudaSuccess) return cuda_status(e, "kv_migrate_kernel");
   return OASIS_OK;
 }

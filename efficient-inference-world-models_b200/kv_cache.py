@@ -51,8 +51,18 @@ class KVCacheB200:
             index.append(counts[k])
             counts[k] += 1
         self.counts = counts
+        self._alloc_pools(counts)
+        s = self._pool_struct()
+        s.n_slots = len(kinds)
+        for i, (k, ix) in enumerate(zip(kinds, index)):
+            s.slot_kind[i] = k
+            s.slot_index[i] = ix
+        self.struct = s
+
+    def _alloc_pools(self, counts: Dict[int, int]) -> None:
+        """Zeroed storage for ``counts[kind]`` frame slots of each kind."""
         dev = self.device
-        lead = (batch, layers)
+        lead = (self.batch, self.layers)
         self.k_bf16 = self.v_bf16 = None
         self.k_fp8 = self.v_fp8 = self.k_fp8_scale = self.v_fp8_scale = None
         self.k_int4 = self.v_int4 = None
@@ -75,12 +85,12 @@ class KVCacheB200:
             self.k_i4_zero = torch.zeros_like(self.k_i4_scale)
             self.v_i4_scale = torch.zeros_like(self.k_i4_scale)
             self.v_i4_zero = torch.zeros_like(self.k_i4_scale)
+
+    def _pool_struct(self) -> "N.KvCache":
+        """A cache descriptor over this object's pools with no slots mapped yet."""
         s = N.KvCache()
-        s.batch, s.layers, s.n_slots = batch, layers, len(kinds)
-        s.n_bf16, s.n_fp8, s.n_int4 = counts[N.KV_BF16], counts[N.KV_FP8], counts[N.KV_INT4]
-        for i, (k, ix) in enumerate(zip(kinds, index)):
-            s.slot_kind[i] = k
-            s.slot_index[i] = ix
+        s.batch, s.layers, s.n_slots = self.batch, self.layers, 0
+        s.n_bf16, s.n_fp8, s.n_int4 = self.counts[N.KV_BF16], self.counts[N.KV_FP8], self.counts[N.KV_INT4]
 
         def ptr(t):
             return t.data_ptr() if t is not None else None
@@ -91,7 +101,7 @@ class KVCacheB200:
         s.k_int4, s.v_int4 = ptr(self.k_int4), ptr(self.v_int4)
         s.k_i4_scale, s.k_i4_zero = ptr(self.k_i4_scale), ptr(self.k_i4_zero)
         s.v_i4_scale, s.v_i4_zero = ptr(self.v_i4_scale), ptr(self.v_i4_zero)
-        self.struct = s
+        return s
 
     # -- configurations of the benchmark -----------------------------------------
     @classmethod

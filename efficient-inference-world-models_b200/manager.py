@@ -18,11 +18,13 @@ the reference's arithmetic.
 
 from __future__ import annotations
 
-from typing import Any, Dict, List, Optional
+import ctypes
+from typing import Any, Dict, List, Optional, Tuple
 
 import torch
 
-from .kv_cache import HEAD_DIM, HEADS, HIDDEN, TOKENS, KVCacheB200
+from . import _native as N
+from .kv_cache import HEAD_DIM, HEADS, HIDDEN, KIND_NAMES, TOKENS, KVCacheB200, _stream_ptr
 
 
 class ProgressiveKVQuantizerB200:
@@ -51,6 +53,103 @@ class ProgressiveKVQuantizerB200:
     def slot_kinds(self, n_past: int) -> List[str]:
         """Kinds of slots 0..n_past-1 where slot s holds a frame of age n_past - s."""
         return [self.precision_for_age(n_past - s) for s in range(n_past)]
+
+
+def _kv_rows(new_kv: Dict[str, torch.Tensor]) -> torch.Tensor:
+    """One frame's K/V of one layer, ``{"key", "value"}`` each (batch, heads, tokens,
+    head_dim) or (heads, tokens, head_dim), as bf16 rows [batch*144][K 1024 | V 1024]."""
+    k, v = new_kv["key"], new_kv["value"]
+    if k.dim() == 3:
+        k, v = k.unsqueeze(0), v.unsqueeze(0)
+    b = k.shape[0]
+    rows = torch.cat([k.permute(0, 2, 1, 3).reshape(b * TOKENS, HIDDEN),
+                      v.permute(0, 2, 1, 3).reshape(b * TOKENS, HIDDEN)], dim=1)
+    return rows.to(torch.bfloat16).contiguous()
+
+
+class RollingKVCacheB200(KVCacheB200):
+    """A rolling window of at most ``capacity`` cached frames that ages like the
+    reference's progressive cache: every ``append`` stores the new frame at full
+    precision (bf16) with age 0, drops the oldest frame once the window is full
+    (``manager.py:296-306``), adds one to every older frame's age and promotes the frames
+    whose tier changed, oldest first: bf16 -> FP8, bf16 -> INT4 or FP8 -> INT4, the last
+    through the fp16 dequantisation (``update_cache``, ``progressive_quant.py:263-350``,
+    with one kind per frame for K and V as in ``ProgressiveKVQuantizerB200``).
+
+    Frames live in per-kind pools sized for a full window (a promotion always finds the
+    slot its predecessor freed); logical slots 0 (oldest) .. n_slots-1 (newest) are
+    remapped on every append, so the object works wherever a :class:`KVCacheB200` does
+    (``OasisDiTB200.forward_cached``, ``attn_temporal``, ``load``)."""
+
+    def __init__(self, batch: int, layers: int, capacity: int,
+                 quantizer: "ProgressiveKVQuantizerB200", device="cuda"):
+        if not 1 <= capacity < N.MAX_FRAMES:
+            raise ValueError(f"capacity must be 1..{N.MAX_FRAMES - 1} past frames")
+        self.batch, self.layers, self.capacity = batch, layers, capacity
+        self.quantizer = quantizer
+        self.device = torch.device(device)
+        # a full window: the newest frame (age 0, bf16) and ages 1..capacity-1 by tier
+        tiers = ["bf16"] + [quantizer.precision_for_age(a) for a in range(1, capacity)]
+        self.counts = {N.KV_BF16: tiers.count("bf16"), N.KV_FP8: tiers.count("fp8"),
+                       N.KV_INT4: tiers.count("int4")}
+        self._alloc_pools(self.counts)
+        self._free = {k: list(range(n)) for k, n in self.counts.items()}
+        self.frames: List[Dict[str, int]] = []  # oldest first: {"age", "kind", "index"}
+        self._remap()
+
+    # -- logical slots -----------------------------------------------------------------
+    def _remap(self) -> None:
+        s = self._pool_struct()
+        s.n_slots = len(self.frames)
+        for i, f in enumerate(self.frames):
+            s.slot_kind[i] = f["kind"]
+            s.slot_index[i] = f["index"]
+        self.struct = s
+        names = {v: k for k, v in KIND_NAMES.items() if k != "fp16"}
+        self.slot_kinds = [names[f["kind"]] for f in self.frames]
+
+    def frame_slots(self) -> List[Tuple[str, int, int]]:
+        """(kind, pool index, age) of every cached frame, oldest first."""
+        return [(self.slot_kinds[i], f["index"], f["age"]) for i, f in enumerate(self.frames)]
+
+    def _take(self, kind: int) -> int:
+        if not self._free[kind]:
+            raise RuntimeError("rolling KV cache: no free slot of the promoted kind")
+        return self._free[kind].pop(0)
+
+    def _promote(self, f: Dict[str, int], kind: int, stream) -> None:
+        pair = self._pool_struct()
+        pair.n_slots = 2
+        pair.slot_kind[0], pair.slot_index[0] = f["kind"], f["index"]
+        dst = self._take(kind)
+        pair.slot_kind[1], pair.slot_index[1] = kind, dst
+        N.call("oasis_kv_migrate", ctypes.byref(pair), 0, 1, _stream_ptr(stream))
+        self._free[f["kind"]].append(f["index"])
+        f["kind"], f["index"] = kind, dst
+
+    # -- the progressive update ------------------------------------------------------------
+    def append(self, rows_per_layer, stream=None) -> None:
+        """Add one frame: ``rows_per_layer[layer]`` is that layer's K/V as bf16 rows
+        [batch*144][ld] with K in columns 0..1023 and V in 1024..2047, or a
+        ``{"key", "value"}`` dict as ``KVCacheManager.update`` takes."""
+        if len(rows_per_layer) != self.layers:
+            raise ValueError("one entry per layer")
+        if len(self.frames) == self.capacity:
+            old = self.frames.pop(0)
+            self._free[old["kind"]].append(old["index"])
+        rank = {N.KV_BF16: 0, N.KV_FP8: 1, N.KV_INT4: 2}
+        for f in self.frames:  # oldest first
+            f["age"] += 1
+            want = KIND_NAMES[self.quantizer.precision_for_age(f["age"])]
+            if rank[want] > rank[f["kind"]]:
+                self._promote(f, want, stream)
+        self.frames.append({"age": 0, "kind": N.KV_BF16, "index": self._take(N.KV_BF16)})
+        self._remap()
+        for layer in range(self.layers):
+            rows = rows_per_layer[layer]
+            if isinstance(rows, dict):
+                rows = _kv_rows(rows)
+            self.store(rows, layer, slot0=self.n_slots - 1, k_col=0, v_col=HIDDEN, stream=stream)
 
 
 class KVCacheManagerB200:
@@ -117,6 +216,20 @@ class KVCacheManagerB200:
             rows = torch.cat([k.permute(0, 2, 1, 3).reshape(b * TOKENS, HIDDEN),
                               v.permute(0, 2, 1, 3).reshape(b * TOKENS, HIDDEN)], dim=1)
             self.cache.store(rows.to(torch.bfloat16).contiguous(), layer, slot0=s, k_col=0, v_col=HIDDEN)
+        self._current_frame_idx = frame_idx
+
+    def append(self, new_kv: Dict[int, Dict[str, torch.Tensor]], frame_idx: int) -> None:
+        """The reference's progressive ``update`` (``manager.py:246-306`` with
+        ``progressive_quant.py:263-350``): append one frame's post-RoPE K/V for every
+        layer to a rolling window of ``max_frames - 1`` past frames (at most 31) that
+        ages and promotes its frames (:class:`RollingKVCacheB200`)."""
+        if not isinstance(self.cache, RollingKVCacheB200):
+            q = self.progressive_quantizer or ProgressiveKVQuantizerB200(
+                fp8_age_threshold=10 ** 6, int4_age_threshold=10 ** 6)
+            self.cache = RollingKVCacheB200(self.batch, self.num_layers,
+                                            min(self.max_frames - 1, N.MAX_FRAMES - 1), q,
+                                            device=self.device)
+        self.cache.append([new_kv[layer] for layer in range(self.num_layers)])
         self._current_frame_idx = frame_idx
 
     def get_kv_for_attention(self, layer_idx: int) -> Dict[str, torch.Tensor]:

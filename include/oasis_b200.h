@@ -237,6 +237,14 @@ int oasis_kv_store(const void* kv, int ld, int k_col, int v_col, const oasis_kv_
  * (progressive_quant.py:195-257); used by KV-manager retrieval calls. */
 int oasis_kv_load(const oasis_kv_cache_t* cache, int layer, int slot0, int frames,
                   void* k_out, void* v_out, cudaStream_t stream);
+/* Age promotion of one frame of a temporal KV cache (replaces the per-entry
+ * _promote_to_fp8 / _promote_to_int4 steps of ProgressiveKVQuantizer.update_cache,
+ * worldserve/optimizations/system_level/kv_cache/progressive_quant.py:263-350):
+ * re-quantises logical slot src_slot into logical slot dst_slot for every session and
+ * layer.  Allowed: bf16 -> FP8, bf16 -> INT4, FP8 -> INT4 (an FP8 entry is dequantised
+ * to fp16 first, as the reference does).  The two slots must map to different storage. */
+int oasis_kv_migrate(const oasis_kv_cache_t* cache, int src_slot, int dst_slot,
+                     cudaStream_t stream);
 
 /* DPM-Solver++ 2M v-prediction update of the newest frame of each session
  * (benchmarks/optimised/oasis_dpmpp_modal.py:143-164):
