@@ -103,6 +103,26 @@ def test_cached_forward_equals_full_forward_bf16(pkg, cuda):
     assert rel_l2(v_inc, v_full) < 1e-5
 
 
+def test_cached_forward_equals_full_forward_at_full_size(pkg, cuda):
+    """The same property at the size of the cached-forward benchmark configuration:
+    Oasis-500M (depth 16), 8 sessions, a 32-frame window whose first 31 frames are cached
+    in bf16.  The prefill runs the chained projections; the newest frame's incremental
+    forward reads all 31 cached frames."""
+    depth, B, T = 16, 8, 32
+    model = pkg.OasisDiTB200.from_state_dict(state(pkg, depth), device=cuda, depth=depth)
+    x, t, a = (z.to(cuda) for z in inputs(B, T, seed=41))
+    cache = pkg.KVCacheB200.uniform(B, depth, T - 1, "bf16", device=cuda)
+    model(x, t, a, kv_cache=cache)
+    x2, t2 = x.clone(), t.clone()
+    x2[:, -1] = torch.randn(B, 16, 18, 32, device=cuda)
+    t2[:, -1] = 321
+    v_full = model(x2, t2, a)[:, -1]
+    v_inc = model.forward_cached(x2[:, -1], t2[:, -1], a[:, -1], cache, n_past=T - 1)
+    torch.cuda.synchronize()
+    assert torch.isfinite(v_inc).all()
+    assert rel_l2(v_inc, v_full) < 1e-5
+
+
 def _oracle_incremental(sd, depth, x, t, a, kinds, x_new, t_new):
     """Oracle: prefill on the window, round-trip past K/V through the reference
     quantiser at the cache granularity, then the newest frame's forward."""
