@@ -123,6 +123,50 @@ def test_cached_forward_equals_full_forward_at_full_size(pkg, cuda):
     assert rel_l2(v_inc, v_full) < 1e-5
 
 
+@pytest.mark.parametrize("B,kinds", [(16, ["int4"] * 23 + ["bf16"] * 8), (8, ["fp8"] * 31)])
+def test_prefill_codes_bit_exact_at_full_size(pkg, cuda, B, kinds):
+    """The KV codes a full-size prefill writes (depth 16, 31 cached frames; the layouts of
+    the FP8 and INT4 cached-forward benchmark configurations) are the oracle's quantisation
+    of the K/V that the same, bit-deterministic prefill stores into a bf16 cache, on
+    sampled (session, layer, slot) pages."""
+    depth, T = 16, 32
+    model = pkg.OasisDiTB200.from_state_dict(state(pkg, depth), device=cuda, depth=depth)
+    x, t, a = (z.to(cuda) for z in inputs(B, T, seed=43))
+    ref = pkg.KVCacheB200.uniform(B, depth, T - 1, "bf16", device=cuda)
+    model(x, t, a, kv_cache=ref)
+    q = pkg.KVCacheB200(B, depth, kinds, device=cuda)
+    model(x, t, a, kv_cache=q)
+    torch.cuda.synchronize()
+    index, seen = [], {}
+    for k in kinds:
+        index.append(seen.get(k, 0))
+        seen[k] = seen.get(k, 0) + 1
+    g = torch.Generator().manual_seed(0)
+    for _ in range(6):
+        b = int(torch.randint(0, B, (1,), generator=g))
+        layer = int(torch.randint(0, depth, (1,), generator=g))
+        slot = int(torch.randint(0, T - 1, (1,), generator=g))
+        kind, idx = kinds[slot], index[slot]
+        for which in ("k", "v"):
+            page = getattr(ref, which + "_bf16")[b, layer, slot].float().cpu().numpy()  # (144, 1024)
+            if kind == "bf16":
+                assert torch.equal(getattr(q, which + "_bf16")[b, layer, idx],
+                                   getattr(ref, which + "_bf16")[b, layer, slot])
+                continue
+            for h in range(16):
+                sl = page[:, h * 64:(h + 1) * 64]
+                if kind == "fp8":
+                    codes, scale = quant_ref.quantize_to_fp8_bf16(sl)
+                    got = getattr(q, which + "_fp8")[b, layer, idx][:, h * 64:(h + 1) * 64].cpu().numpy()
+                    np.testing.assert_array_equal(got, codes)
+                    assert getattr(q, which + "_fp8_scale")[b, layer, idx, h].float().item() == scale
+                else:
+                    p, s16, z16, _, _ = quant_ref.quantize_int4_rows(sl)
+                    np.testing.assert_array_equal(getattr(q, which + "_int4")[b, layer, idx, :, h].cpu().numpy(), p)
+                    np.testing.assert_array_equal(getattr(q, which + "_i4_scale")[b, layer, idx, :, h].cpu().numpy(), s16)
+                    np.testing.assert_array_equal(getattr(q, which + "_i4_zero")[b, layer, idx, :, h].cpu().numpy(), z16)
+
+
 def _oracle_incremental(sd, depth, x, t, a, kinds, x_new, t_new):
     """Oracle: prefill on the window, round-trip past K/V through the reference
     quantiser at the cache granularity, then the newest frame's forward."""
