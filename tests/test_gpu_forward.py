@@ -167,6 +167,30 @@ def test_prefill_codes_bit_exact_at_full_size(pkg, cuda, B, kinds):
                     np.testing.assert_array_equal(getattr(q, which + "_i4_zero")[b, layer, idx, :, h].cpu().numpy(), z16)
 
 
+@pytest.mark.parametrize("B,kinds", [(16, ["int4"] * 23 + ["bf16"] * 8), (8, ["fp8"] * 31)])
+def test_fused_dequant_equals_dequantised_cache_at_full_size(pkg, cuda, B, kinds):
+    """The incremental forward over a quantised cache (K/V dequantised while staged into
+    shared memory) equals, bit for bit, the one over a bf16 cache holding the dequantised
+    pages (``load``), at the benchmark layouts (depth 16, 31 cached frames)."""
+    depth, T = 16, 32
+    model = pkg.OasisDiTB200.from_state_dict(state(pkg, depth), device=cuda, depth=depth)
+    x, t, a = (z.to(cuda) for z in inputs(B, T, seed=47))
+    q = pkg.KVCacheB200(B, depth, kinds, device=cuda)
+    model(x, t, a, kv_cache=q)
+    deq = pkg.KVCacheB200.uniform(B, depth, T - 1, "bf16", device=cuda)
+    for layer in range(depth):
+        k, v = q.load(layer)
+        deq.k_bf16[:, layer].copy_(k)
+        deq.v_bf16[:, layer].copy_(v)
+    x_new = torch.randn(B, 16, 18, 32, device=cuda)
+    t_new = torch.full((B,), 250, device=cuda)
+    v_q = model.forward_cached(x_new, t_new, a[:, -1], q, n_past=T - 1).clone()
+    v_d = model.forward_cached(x_new, t_new, a[:, -1], deq, n_past=T - 1)
+    torch.cuda.synchronize()
+    assert torch.isfinite(v_q).all()
+    assert torch.equal(v_q, v_d)  # the same dequantised values enter the same arithmetic
+
+
 def _oracle_incremental(sd, depth, x, t, a, kinds, x_new, t_new):
     """Oracle: prefill on the window, round-trip past K/V through the reference
     quantiser at the cache granularity, then the newest frame's forward."""
