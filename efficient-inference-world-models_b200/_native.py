@@ -50,16 +50,21 @@ class DiTWeights(Structure):
                 ("rope_spatial", c_void_p), ("rope_temporal", c_void_p)]
 
 
-class KvCache(Structure):
-    _fields_ = [("batch", c_int), ("layers", c_int), ("n_slots", c_int),
-                ("n_bf16", c_int), ("n_fp8", c_int), ("n_int4", c_int),
+class KvTensor(Structure):
+    """``oasis_kv_tensor_t``: the slot map and pools of the keys or of the values."""
+    _fields_ = [("n_bf16", c_int), ("n_fp8", c_int), ("n_int4", c_int),
                 ("slot_kind", c_uint8 * MAX_FRAMES), ("slot_index", c_uint8 * MAX_FRAMES),
-                ("k_bf16", c_void_p), ("v_bf16", c_void_p),
-                ("k_fp8", c_void_p), ("v_fp8", c_void_p),
-                ("k_fp8_scale", c_void_p), ("v_fp8_scale", c_void_p),
-                ("k_int4", c_void_p), ("v_int4", c_void_p),
-                ("k_i4_scale", c_void_p), ("k_i4_zero", c_void_p),
-                ("v_i4_scale", c_void_p), ("v_i4_zero", c_void_p)]
+                ("bf16", c_void_p), ("fp8", c_void_p), ("fp8_scale", c_void_p),
+                ("int4", c_void_p), ("i4_scale", c_void_p), ("i4_zero", c_void_p)]
+
+
+class KvCache(Structure):
+    """``oasis_kv_cache_t``: ``k`` the keys, ``v`` the values."""
+    _fields_ = [("batch", c_int), ("layers", c_int), ("n_slots", c_int),
+                ("k", KvTensor), ("v", KvTensor)]
+
+
+KV_KEYS, KV_VALUES = 1, 2
 
 
 # name -> (restype, argtypes); every symbol include/oasis_b200.h declares
@@ -87,7 +92,7 @@ SIGNATURES = {
                                     c_int, c_int, c_int, c_void_p]),
     "oasis_kv_store": (c_int, [c_void_p, c_int, c_int, c_int, POINTER(KvCache), c_int, c_int,
                                c_int, c_int, c_void_p]),
-    "oasis_kv_migrate": (c_int, [POINTER(KvCache), c_int, c_int, c_void_p]),
+    "oasis_kv_migrate": (c_int, [POINTER(KvCache), c_int, c_int, c_int, c_void_p]),
     "oasis_kv_load": (c_int, [POINTER(KvCache), c_int, c_int, c_int, c_void_p, c_void_p, c_void_p]),
     "oasis_dpmpp2m_update": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_longlong,
                                      c_longlong, c_float, c_float, c_int, c_void_p]),

@@ -280,14 +280,19 @@ __global__ void __launch_bounds__(kSpThreads, 2)
 }
 
 // ----------------------------------------------------------------------------------
-// temporal attention: one warp per (session, token, head); CTA = 4 heads of one token
+// temporal attention, several query frames: one warp per (session, token, head);
+// CTA = 4 heads of one token
 // ----------------------------------------------------------------------------------
-
 
 constexpr int kTpWarps = 4;
 constexpr int kTpRowsPerMat = 32;
 constexpr int kTpWarpSmem = 3 * kTpRowsPerMat * kSmemStride;  // bf16 elements
-constexpr int kTpSmem = kTpWarps * kTpWarpSmem * 2;             // 55,296 B
+constexpr int kTpTileBytes = kTpWarps * kTpWarpSmem * 2;        // 55,296 B
+// raw staging of quantised cached rows, per tensor: 32 rows x 256 B of codes (4 heads of
+// FP8; INT4 uses the first 128 B) + 32 x 16 B of per-row scale (8 B) and zero (8 B)
+constexpr int kTpRawCodes = kTpRowsPerMat * 256;
+constexpr int kTpRawTensor = kTpRawCodes + kTpRowsPerMat * 16;
+constexpr int kTpSmem = kTpTileBytes + 2 * kTpRawTensor;        // 72,704 B
 constexpr int kTpTmaTile = kTpRowsPerMat * 128;                   // 4 KB: 32 frames x 64 bf16
 constexpr int kTpTmaTiles = kTpWarps * 3 * kTpTmaTile;            // 48 KB
 constexpr int kTpSmemTma = kTpTmaTiles + 1024 + 64;               // + alignment slack, barrier
@@ -298,6 +303,16 @@ __device__ __forceinline__ float2 e4m3x2_to_float2(uint32_t two_codes) {
   const uint16_t v = static_cast<uint16_t>(two_codes);
   asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h) : "h"(v));
   return __half22float2(*reinterpret_cast<const __half2*>(&h));
+}
+
+// Dequantised values, rounded to bf16 once as the reference's bf16 dequantisation does:
+// FP8 code x scale (exact in fp32: 4 x 8 significant bits); INT4 code x scale + zero
+// (code x fp16 scale is exact in fp32, so fused and unfused forms agree).
+__device__ __forceinline__ float dq_fp8(float code_value, float scale) {
+  return bf16_round(code_value * scale);
+}
+__device__ __forceinline__ float dq_int4(uint32_t code, float scale, float zero) {
+  return bf16_round(__fmaf_rn(static_cast<float>(code), scale, zero));
 }
 
 // 8 codes -> 8 bf16, dequantised exactly as q.to(bf16) * scale in bf16 (one rounding)
@@ -314,22 +329,26 @@ __device__ __forceinline__ uint4 dequant_int4x8(uint32_t w, float scale, float z
 #pragma unroll
   for (int b = 0; b < 4; ++b) {
     const uint32_t byte = (w >> (8 * b)) & 0xFFu;
-    r[b] = pack_bf16x2(static_cast<float>(byte >> 4) * scale + zero,
-                       static_cast<float>(byte & 0xFu) * scale + zero);
+    r[b] = pack_bf16x2(__fmaf_rn(static_cast<float>(byte >> 4), scale, zero),
+                       __fmaf_rn(static_cast<float>(byte & 0xFu), scale, zero));
   }
   return make_uint4(r[0], r[1], r[2], r[3]);
 }
 
 // TMA = true: full-window call (no cached past): Q, K, V of the 4 heads arrive by 12
 // TMA tensor loads (box = 32 frames x 64 columns of one token) into 128B-swizzled
-// 4 KB tiles.  TMA = false: cached past frames, staged (and dequantised) by the threads.
+// 4 KB tiles.  TMA = false: cached past frames.  All rows are first copied
+// asynchronously (cp.async): bf16 rows straight into the tiles, FP8/INT4 codes and their
+// scales into a raw area, so every load of the CTA is in flight at once; the codes are
+// then dequantised from shared memory into the tiles.  Keys and values follow their own
+// slot maps.
 template <bool TMA>
 __global__ void __launch_bounds__(kTpWarps * 32)
     attn_temporal_kernel(const __grid_constant__ CUtensorMap tm_qkv,
                          const __grid_constant__ CUtensorMap tm_out,
                          const __nv_bfloat16* __restrict__ qkv, __nv_bfloat16* __restrict__ out,
-                         KvView kv, int layer, int q_frames, int q_pos0, int n_past, int n_kv,
-                         float scale_log2) {
+                         const __grid_constant__ KvView kv, int layer, int q_frames, int q_pos0,
+                         int n_past, int n_kv, float scale_log2) {
   pdl_trigger();
   extern __shared__ __align__(16) uint8_t sm_tp_raw[];
   uint8_t* sm_tp = TMA ? reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(sm_tp_raw) + 1023) &
@@ -369,69 +388,78 @@ __global__ void __launch_bounds__(kTpWarps * 32)
     }
     if (!mbar_wait(tbar, 0)) return;  // timeout recorded in the device error word
   } else {
-  // ---- cooperative staging: the 4 heads of one (session, token) are contiguous ----
-  // Q rows and live K/V rows: 3 x 512 B per frame (cp.async, 16-byte chunks)
-  for (int i = tid; i < q_frames * 32; i += kTpWarps * 32) {
-    const int t = i >> 5, c = i & 31;
-    const __nv_bfloat16* src = qkv + (static_cast<long long>(b * q_frames + t) * OASIS_TOKENS + p) * kQkvLd + hg * 256 + c * 8;
-    cp_async16(mat(c >> 3, 0) + t * kSmemStride + (c & 7) * 8, src);
+    uint8_t* raw = sm_tp + kTpTileBytes;  // [K | V] raw areas
+    // ---- phase 1: every copy in flight (the 4 heads of one (session, token) are contiguous) ----
+    // Q rows and live K/V rows: 3 x 512 B per frame, 16-byte chunks
+    for (int i = tid; i < q_frames * 32; i += kTpWarps * 32) {
+      const int t = i >> 5, c = i & 31;
+      const __nv_bfloat16* src = qkv + (static_cast<long long>(b * q_frames + t) * OASIS_TOKENS + p) * kQkvLd + hg * 256 + c * 8;
+      cp_async16(mat(c >> 3, 0) + t * kSmemStride + (c & 7) * 8, src);
+    }
+    for (int i = tid; i < n_live * 64; i += kTpWarps * 32) {
+      const int j = i >> 6, which = 1 + ((i >> 5) & 1), c = i & 31;
+      const __nv_bfloat16* src = qkv + (static_cast<long long>(b * q_frames + j) * OASIS_TOKENS + p) * kQkvLd +
+                                 which * OASIS_HIDDEN + hg * 256 + c * 8;
+      cp_async16(mat(c >> 3, which) + (n_past + j) * kSmemStride + (c & 7) * 8, src);
+    }
+    // cached rows, unit u (0..31) of the (slot, tensor) row: bf16 32 x 16 B; FP8 16 x 16 B
+    // of codes + the 4 heads' scales; INT4 8 x 16 B + the token's 4 scales and 4 zeros
+    for (int i = tid; i < n_past * 64; i += kTpWarps * 32) {
+      const int s = i >> 6, which = 1 + ((i >> 5) & 1), u = i & 31;
+      const KvTensor& t = kv.t[which - 1];
+      const int kind = t.kind[s];
+      uint8_t* rt = raw + (which - 1) * kTpRawTensor;
+      if (kind == OASIS_KV_BF16) {
+        const long long page = kv_page(b, kv.layers, layer, t.n_bf16, t.index[s]);
+        cp_async16(mat(u >> 3, which) + s * kSmemStride + (u & 7) * 8,
+                   t.bf16 + (page * OASIS_TOKENS + p) * OASIS_HIDDEN + hg * 256 + u * 8);
+      } else if (kind == OASIS_KV_FP8) {
+        const long long page = kv_page(b, kv.layers, layer, t.n_fp8, t.index[s]);
+        if (u < 16)
+          cp_async16(rt + s * 256 + u * 16, t.fp8 + (page * OASIS_TOKENS + p) * OASIS_HIDDEN + hg * 256 + u * 16);
+        else if (u == 16)
+          cp_async8(rt + kTpRawCodes + s * 16, t.fp8_scale + page * OASIS_HEADS + hg * 4);
+      } else {
+        const long long page = kv_page(b, kv.layers, layer, t.n_int4, t.index[s]);
+        const long long grp = (page * OASIS_TOKENS + p) * OASIS_HEADS + hg * 4;
+        if (u < 8)
+          cp_async16(rt + s * 256 + u * 16, t.int4 + grp * 32 + u * 16);
+        else if (u == 8)
+          cp_async8(rt + kTpRawCodes + s * 16, t.i4_scale + grp);
+        else if (u == 9)
+          cp_async8(rt + kTpRawCodes + s * 16 + 8, t.i4_zero + grp);
+      }
+    }
+    cp_async_wait_all();
+    __syncthreads();
+    // ---- phase 2: dequantise the raw rows into the tiles (8 elements per item) ----
+    for (int i = tid; i < n_past * 64; i += kTpWarps * 32) {
+      const int s = i >> 6, which = 1 + ((i >> 5) & 1), u = i & 31;
+      const int kind = kv.t[which - 1].kind[s];
+      if (kind == OASIS_KV_BF16) continue;
+      const uint8_t* rt = raw + (which - 1) * kTpRawTensor;
+      const int hh = u >> 3, c = u & 7;  // head, 8-element chunk
+      uint4 v;
+      if (kind == OASIS_KV_FP8) {
+        const uint2 w = *reinterpret_cast<const uint2*>(rt + s * 256 + hh * 64 + c * 8);
+        const float scale =
+            __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(rt + kTpRawCodes + s * 16)[hh]);
+        v = dequant_fp8x8(w.x, w.y, scale);
+      } else {
+        const uint32_t w = *reinterpret_cast<const uint32_t*>(rt + s * 256 + hh * 32 + c * 4);
+        const __half* aux = reinterpret_cast<const __half*>(rt + kTpRawCodes + s * 16);
+        v = dequant_int4x8(w, __half2float(aux[hh]), __half2float(aux[4 + hh]));
+      }
+      *reinterpret_cast<uint4*>(mat(hh, which) + s * kSmemStride + c * 8) = v;
+    }
+    // zero the padding rows the MMAs read (keeps masked products finite)
+    for (int i = tid; i < kTpWarps * 3 * 32 * 8; i += kTpWarps * 32) {
+      const int hh = i / (3 * 32 * 8), which = (i / (32 * 8)) % 3, r = (i >> 3) & 31, c = i & 7;
+      const bool pad = which == 0 ? (r >= q_frames && r < m_tiles * 16) : (r >= n_kv && r < n_pairs * 16);
+      if (pad) *reinterpret_cast<uint4*>(mat(hh, which) + r * kSmemStride + c * 8) = make_uint4(0, 0, 0, 0);
+    }
+    __syncthreads();
   }
-  for (int i = tid; i < n_live * 64; i += kTpWarps * 32) {
-    const int j = i >> 6, which = 1 + ((i >> 5) & 1), c = i & 31;
-    const __nv_bfloat16* src = qkv + (static_cast<long long>(b * q_frames + j) * OASIS_TOKENS + p) * kQkvLd +
-                               which * OASIS_HIDDEN + hg * 256 + c * 8;
-    cp_async16(mat(c >> 3, which) + (n_past + j) * kSmemStride + (c & 7) * 8, src);
-  }
-  // cached rows, one loop per storage kind so every thread has a unit of work:
-  //   bf16: 32 x 16-byte chunks per (slot, K|V) row of 4 heads (cp.async)
-  //   FP8 : 16 x 16-byte chunks of codes, dequantised through registers
-  //   INT4:  8 x 16-byte chunks of packed codes, dequantised through registers
-  for (int i = tid; i < n_past * 64; i += kTpWarps * 32) {
-    const int s = i >> 6, which = 1 + ((i >> 5) & 1), u = i & 31;
-    if (kv.kind[s] != OASIS_KV_BF16) continue;
-    const long long slot = (static_cast<long long>(b) * kv.layers + layer) * kv.n_bf16 + kv.index[s];
-    const __nv_bfloat16* src = (which == 2 ? kv.v_bf16 : kv.k_bf16) + (slot * OASIS_TOKENS + p) * OASIS_HIDDEN + hg * 256 + u * 8;
-    cp_async16(mat(u >> 3, which) + s * kSmemStride + (u & 7) * 8, src);
-  }
-  for (int i = tid; i < n_past * 32; i += kTpWarps * 32) {
-    const int s = i >> 5, which = 1 + ((i >> 4) & 1), u = i & 15;
-    if (kv.kind[s] != OASIS_KV_FP8) continue;
-    const bool is_v = which == 2;
-    const long long slot = (static_cast<long long>(b) * kv.layers + layer) * kv.n_fp8 + kv.index[s];
-    const uint4 w = *reinterpret_cast<const uint4*>((is_v ? kv.v_fp8 : kv.k_fp8) +
-                                                    (slot * OASIS_TOKENS + p) * OASIS_HIDDEN + hg * 256 + u * 16);
-    const int hh = u >> 2;
-    const float scale = __bfloat162float((is_v ? kv.v_fp8_scale : kv.k_fp8_scale)[slot * OASIS_HEADS + hg * 4 + hh]);
-    uint4* d = reinterpret_cast<uint4*>(mat(hh, which) + s * kSmemStride + (u & 3) * 16);
-    d[0] = dequant_fp8x8(w.x, w.y, scale);
-    d[1] = dequant_fp8x8(w.z, w.w, scale);
-  }
-  for (int i = tid; i < n_past * 16; i += kTpWarps * 32) {
-    const int s = i >> 4, which = 1 + ((i >> 3) & 1), u = i & 7;
-    if (kv.kind[s] != OASIS_KV_INT4) continue;
-    const bool is_v = which == 2;
-    const long long slot = (static_cast<long long>(b) * kv.layers + layer) * kv.n_int4 + kv.index[s];
-    const int hh = u >> 1;
-    const long long grp = (slot * OASIS_TOKENS + p) * OASIS_HEADS + hg * 4 + hh;
-    const uint4 w = *reinterpret_cast<const uint4*>((is_v ? kv.v_int4 : kv.k_int4) + grp * 32 + (u & 1) * 16);
-    const float scale = __half2float((is_v ? kv.v_i4_scale : kv.k_i4_scale)[grp]);
-    const float zero = __half2float((is_v ? kv.v_i4_zero : kv.k_i4_zero)[grp]);
-    uint4* d = reinterpret_cast<uint4*>(mat(hh, which) + s * kSmemStride + (u & 1) * 32);
-    d[0] = dequant_int4x8(w.x, scale, zero);
-    d[1] = dequant_int4x8(w.y, scale, zero);
-    d[2] = dequant_int4x8(w.z, scale, zero);
-    d[3] = dequant_int4x8(w.w, scale, zero);
-  }
-  // zero the padding rows the MMAs read (keeps masked products finite)
-  for (int i = tid; i < kTpWarps * 3 * 32 * 8; i += kTpWarps * 32) {
-    const int hh = i / (3 * 32 * 8), which = (i / (32 * 8)) % 3, r = (i >> 3) & 31, c = i & 7;
-    const bool pad = which == 0 ? (r >= q_frames && r < m_tiles * 16) : (r >= n_kv && r < n_pairs * 16);
-    if (pad) *reinterpret_cast<uint4*>(mat(hh, which) + r * kSmemStride + c * 8) = make_uint4(0, 0, 0, 0);
-  }
-  cp_async_wait_all();
-  __syncthreads();
-  }
-
   // 16-byte chunk `chunk` of row `row` of this warp's Q (0), K (1) or V (2) tile
   auto at = [&](int which, int row, int chunk) -> uint32_t {
     if constexpr (TMA)
@@ -563,6 +591,172 @@ __global__ void __launch_bounds__(kTpWarps * 32)
   }
 }
 
+
+// ----------------------------------------------------------------------------------
+// temporal attention of ONE query frame over cached frames (the incremental forward):
+// one CTA per (session, token, 8 heads), one warp per head, one lane per key frame.
+// ----------------------------------------------------------------------------------
+// Warp 0 issues one bulk copy per cached row (keys and values each in their slot's kind:
+// 1024 B bf16, 512 B FP8 codes, 256 B INT4 codes for 8 heads) and per row of scales,
+// plus the live Q, K and V rows, on two mbarriers (Q + keys, values), so the scores
+// start while the values are still in flight.  Scores: lane l accumulates
+// q[2l..2l+1] . k_j[2l..2l+1] for every key row j (each row read once, consecutive lanes
+// on consecutive bytes, dequantised in registers), then a 5-stage butterfly
+// transpose-reduce leaves the score of key l in lane l.  Softmax over the lanes with
+// shuffles; P is rounded to bf16 as the tensor-core path rounds it; O (dims 2l, 2l+1)
+// = sum_j bf16(p_j) v_j.  Memory-bound: the cached K/V bytes of one (session, token,
+// head group) move once.
+constexpr int kDecHeads = 8;
+constexpr int kDecThreads = kDecHeads * 32;
+constexpr int kDecMaxSmem = 96 * 1024;
+
+struct DecodeLayout {
+  // byte offsets in dynamic shared memory: codes of cached slot s (keys, values) and its
+  // scales (FP8: 8 bf16; INT4: 8 fp16 scales then 8 fp16 zeros)
+  uint32_t k_row[OASIS_MAX_FRAMES], v_row[OASIS_MAX_FRAMES];
+  uint32_t k_aux[OASIS_MAX_FRAMES], v_aux[OASIS_MAX_FRAMES];
+  uint32_t live;             // live Q | K | V rows of the query frame, 1 KB each
+  uint32_t k_bytes, v_bytes; // bytes expected on the two barriers
+  uint32_t total;
+  int live_kv;               // the query frame's own K/V is key n_past (n_kv = n_past + 1)
+};
+
+// Dequantised elements 2*lane, 2*lane+1 of head hh in one staged row of 8 heads.
+__device__ __forceinline__ float2 decode_pair(const uint8_t* row, const uint8_t* aux, int kind, int hh,
+                                              int lane) {
+  if (kind == OASIS_KV_BF16) {
+    const uint32_t w = *reinterpret_cast<const uint32_t*>(row + hh * 128 + lane * 4);
+    return make_float2(bf16_lo(w), bf16_hi(w));
+  }
+  if (kind == OASIS_KV_FP8) {
+    const uint32_t c = *reinterpret_cast<const uint16_t*>(row + hh * 64 + lane * 2);
+    const float scale = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(aux)[hh]);
+    const float2 f = e4m3x2_to_float2(c);
+    return make_float2(dq_fp8(f.x, scale), dq_fp8(f.y, scale));
+  }
+  const uint32_t byte = row[hh * 32 + lane];
+  const float scale = __half2float(reinterpret_cast<const __half*>(aux)[hh]);
+  const float zero = __half2float(reinterpret_cast<const __half*>(aux)[kDecHeads + hh]);
+  return make_float2(dq_int4(byte >> 4, scale, zero), dq_int4(byte & 0xFu, scale, zero));
+}
+
+__global__ void __launch_bounds__(kDecThreads)
+    attn_decode_kernel(const __nv_bfloat16* __restrict__ qkv, __nv_bfloat16* __restrict__ out,
+                       const __grid_constant__ KvView kv, const __grid_constant__ DecodeLayout lay,
+                       int layer, int q_pos, int n_past, float scale_log2) {
+  pdl_trigger();
+  extern __shared__ __align__(128) uint8_t sm_dec[];
+  __shared__ __align__(8) uint64_t bars[2];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int p = blockIdx.x, hg = blockIdx.y, b = blockIdx.z;
+  const int n_kv = n_past + lay.live_kv;
+  if (threadIdx.x == 0) {
+    mbar_init(&bars[0], 1);
+    mbar_init(&bars[1], 1);
+    mbar_fence_init();
+  }
+  __syncthreads();
+  pdl_wait();
+  if (warp == 0) {
+    if (lane == 0) {
+      mbar_arrive_expect_tx(&bars[0], lay.k_bytes);
+      mbar_arrive_expect_tx(&bars[1], lay.v_bytes);
+    }
+    __syncwarp();
+    if (lane < n_past) {  // lane s: the keys and values of cached slot s
+      const int s = lane;
+#pragma unroll
+      for (int which = 0; which < 2; ++which) {
+        const KvTensor& t = kv.t[which];
+        uint64_t* bar = &bars[which];
+        const uint32_t row_off = which ? lay.v_row[s] : lay.k_row[s];
+        const uint32_t aux_off = which ? lay.v_aux[s] : lay.k_aux[s];
+        const int kind = t.kind[s];
+        if (kind == OASIS_KV_BF16) {
+          const long long page = kv_page(b, kv.layers, layer, t.n_bf16, t.index[s]);
+          bulk_load(sm_dec + row_off, t.bf16 + (page * OASIS_TOKENS + p) * OASIS_HIDDEN + hg * kDecHeads * 64,
+                    kDecHeads * 128, bar);
+        } else if (kind == OASIS_KV_FP8) {
+          const long long page = kv_page(b, kv.layers, layer, t.n_fp8, t.index[s]);
+          bulk_load(sm_dec + row_off, t.fp8 + (page * OASIS_TOKENS + p) * OASIS_HIDDEN + hg * kDecHeads * 64,
+                    kDecHeads * 64, bar);
+          bulk_load(sm_dec + aux_off, t.fp8_scale + page * OASIS_HEADS + hg * kDecHeads, 16, bar);
+        } else {
+          const long long page = kv_page(b, kv.layers, layer, t.n_int4, t.index[s]);
+          const long long grp = (page * OASIS_TOKENS + p) * OASIS_HEADS + hg * kDecHeads;
+          bulk_load(sm_dec + row_off, t.int4 + grp * 32, kDecHeads * 32, bar);
+          bulk_load(sm_dec + aux_off, t.i4_scale + grp, 16, bar);
+          bulk_load(sm_dec + aux_off + 16, t.i4_zero + grp, 16, bar);
+        }
+      }
+    } else if (lane == 31) {  // the query frame's own q, k, v (bf16 rows of the QKV output)
+      const __nv_bfloat16* row = qkv + (static_cast<long long>(b) * OASIS_TOKENS + p) * kQkvLd + hg * kDecHeads * 64;
+      bulk_load(sm_dec + lay.live, row, kDecHeads * 128, &bars[0]);
+      if (lay.live_kv) {
+        bulk_load(sm_dec + lay.live + 1024, row + OASIS_HIDDEN, kDecHeads * 128, &bars[0]);
+        bulk_load(sm_dec + lay.live + 2048, row + 2 * OASIS_HIDDEN, kDecHeads * 128, &bars[1]);
+      }
+    }
+  }
+  const int hh = warp;  // head within the group
+  if (!mbar_wait(&bars[0], 0)) return;  // timeout recorded in the device error word
+  const uint32_t qw = *reinterpret_cast<const uint32_t*>(sm_dec + lay.live + hh * 128 + lane * 4);
+  const float q0 = bf16_lo(qw), q1 = bf16_hi(qw);
+  float part[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    part[j] = 0.0f;
+    if (j < n_past) {
+      const float2 k = decode_pair(sm_dec + lay.k_row[j], sm_dec + lay.k_aux[j], kv.t[0].kind[j], hh, lane);
+      part[j] = __fmaf_rn(q1, k.y, q0 * k.x);
+    } else if (j < n_kv) {
+      const float2 k = decode_pair(sm_dec + lay.live + 1024, nullptr, OASIS_KV_BF16, hh, lane);
+      part[j] = __fmaf_rn(q1, k.y, q0 * k.x);
+    }
+  }
+  // butterfly transpose-reduce: after the stage of width w, lane l holds w partial sums
+  // of the keys whose bits above log2(w) equal lane l's; the last leaves key l in lane l
+#pragma unroll
+  for (int w = 16; w >= 1; w >>= 1) {
+    const bool upper = (lane & w) != 0;
+#pragma unroll
+    for (int k = 0; k < w; ++k) {
+      const float send = upper ? part[k] : part[k + w];
+      const float keep = upper ? part[k + w] : part[k];
+      part[k] = keep + __shfl_xor_sync(0xffffffffu, send, w);
+    }
+  }
+  // causal mask: the query at window position q_pos sees keys 0..q_pos
+  const bool live_key = lane < n_kv && lane <= q_pos;
+  float mx = live_key ? part[0] : -INFINITY;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  const float pr = live_key ? exp2f(__fmaf_rn(part[0], scale_log2, -mx * scale_log2)) : 0.0f;
+  float sum = pr;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  const float pb = bf16_round(pr);  // the probability as the PV product sees it
+  if (!mbar_wait(&bars[1], 0)) return;
+  float o0 = 0.0f, o1 = 0.0f;
+#pragma unroll 4
+  for (int j = 0; j < n_past; ++j) {
+    const float pj = __shfl_sync(0xffffffffu, pb, j);
+    const float2 v = decode_pair(sm_dec + lay.v_row[j], sm_dec + lay.v_aux[j], kv.t[1].kind[j], hh, lane);
+    o0 = __fmaf_rn(pj, v.x, o0);
+    o1 = __fmaf_rn(pj, v.y, o1);
+  }
+  if (lay.live_kv) {
+    const float pj = __shfl_sync(0xffffffffu, pb, n_past);
+    const float2 v = decode_pair(sm_dec + lay.live + 2048, nullptr, OASIS_KV_BF16, hh, lane);
+    o0 = __fmaf_rn(pj, v.x, o0);
+    o1 = __fmaf_rn(pj, v.y, o1);
+  }
+  const float inv = 1.0f / sum;
+  __nv_bfloat16* orow = out + (static_cast<long long>(b) * OASIS_TOKENS + p) * OASIS_HIDDEN +
+                        (hg * kDecHeads + hh) * 64;
+  *reinterpret_cast<uint32_t*>(orow + 2 * lane) = pack_bf16x2(o0 * inv, o1 * inv);
+}
+
 // ----------------------------------------------------------------------------------
 // host launchers
 // ----------------------------------------------------------------------------------
@@ -594,42 +788,6 @@ int launch_attn_spatial(const void* qkv, void* out, int frames, cudaStream_t str
   return OASIS_OK;
 }
 
-int make_kv_view(const oasis_kv_cache_t* c, KvView* v) {
-  *v = KvView{};
-  if (!c) return OASIS_OK;
-  v->layers = c->layers;
-  v->n_bf16 = c->n_bf16;
-  v->n_fp8 = c->n_fp8;
-  v->n_int4 = c->n_int4;
-  for (int s = 0; s < OASIS_MAX_FRAMES; ++s) {
-    v->kind[s] = c->slot_kind[s];
-    v->index[s] = c->slot_index[s];
-  }
-  for (int s = 0; s < c->n_slots && s < OASIS_MAX_FRAMES; ++s) {
-    const int kind = c->slot_kind[s], idx = c->slot_index[s];
-    const bool ok = (kind == OASIS_KV_BF16 && idx < c->n_bf16 && c->k_bf16 && c->v_bf16) ||
-                    (kind == OASIS_KV_FP8 && idx < c->n_fp8 && c->k_fp8 && c->v_fp8 &&
-                     c->k_fp8_scale && c->v_fp8_scale) ||
-                    (kind == OASIS_KV_INT4 && idx < c->n_int4 && c->k_int4 && c->v_int4 &&
-                     c->k_i4_scale && c->k_i4_zero && c->v_i4_scale && c->v_i4_zero);
-    if (!ok) return fail(OASIS_ERR_INVALID_ARG, "KV cache slot " + std::to_string(s) +
-                                                    " has an invalid kind/index or missing pool");
-  }
-  v->k_bf16 = static_cast<const __nv_bfloat16*>(c->k_bf16);
-  v->v_bf16 = static_cast<const __nv_bfloat16*>(c->v_bf16);
-  v->k_fp8 = c->k_fp8;
-  v->v_fp8 = c->v_fp8;
-  v->k_fp8_scale = static_cast<const __nv_bfloat16*>(c->k_fp8_scale);
-  v->v_fp8_scale = static_cast<const __nv_bfloat16*>(c->v_fp8_scale);
-  v->k_int4 = c->k_int4;
-  v->v_int4 = c->v_int4;
-  v->k_i4_scale = static_cast<const __half*>(c->k_i4_scale);
-  v->k_i4_zero = static_cast<const __half*>(c->k_i4_zero);
-  v->v_i4_scale = static_cast<const __half*>(c->v_i4_scale);
-  v->v_i4_zero = static_cast<const __half*>(c->v_i4_zero);
-  return OASIS_OK;
-}
-
 int launch_attn_temporal(const void* qkv, const KvView& kv, int layer, void* out, int batch,
                          int q_frames, int q_pos0, int n_past, int n_kv, cudaStream_t stream) {
   static bool configured = false;
@@ -639,8 +797,43 @@ int launch_attn_temporal(const void* qkv, const KvView& kv, int layer, void* out
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(attn_temporal_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                kTpSmemTma);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               kDecMaxSmem);
     if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(attn_temporal)");
     configured = true;
+  }
+  if (q_frames == 1 && n_past > 0 && n_past < OASIS_MAX_FRAMES) {
+    // one query frame over cached slots: the decode kernel, shared memory sized for the
+    // kinds present (rows packed back to back, 16-byte aligned)
+    DecodeLayout lay{};
+    uint32_t off = 0;
+    lay.live_kv = n_kv > n_past ? 1 : 0;
+    lay.k_bytes = (1 + lay.live_kv) * kDecHeads * 128;  // live q (and k) rows
+    lay.v_bytes = lay.live_kv * kDecHeads * 128;        // live v row
+    for (int s = 0; s < n_past; ++s) {
+      for (int which = 0; which < 2; ++which) {
+        const int kind = kv.t[which].kind[s];
+        const uint32_t codes = kind == OASIS_KV_BF16 ? kDecHeads * 128 : (kind == OASIS_KV_FP8 ? kDecHeads * 64 : kDecHeads * 32);
+        const uint32_t aux = kind == OASIS_KV_BF16 ? 0u : (kind == OASIS_KV_FP8 ? 16u : 32u);
+        (which ? lay.v_row : lay.k_row)[s] = off;
+        off += codes;
+        (which ? lay.v_aux : lay.k_aux)[s] = off;
+        off += aux;
+        (which ? lay.v_bytes : lay.k_bytes) += codes + aux;
+      }
+    }
+    lay.live = off;
+    off += 3 * kDecHeads * 128;
+    lay.total = off;
+    if (lay.total > static_cast<uint32_t>(kDecMaxSmem))
+      return fail(OASIS_ERR_UNSUPPORTED, "attn_decode_kernel: shared memory layout too large");
+    dim3 grid(OASIS_TOKENS, OASIS_HEADS / kDecHeads, batch);
+    cudaError_t e = launch_pdl(attn_decode_kernel, grid, dim3(kDecThreads), lay.total, stream,
+                               static_cast<const __nv_bfloat16*>(qkv), static_cast<__nv_bfloat16*>(out),
+                               kv, lay, layer, q_pos0, n_past, kScaleLog2);
+    if (e != cudaSuccess) return cuda_status(e, "attn_decode_kernel");
+    return OASIS_OK;
   }
   dim3 grid(OASIS_TOKENS, OASIS_HEADS / kTpWarps, batch);
   CUtensorMap tm{}, tm_out{};

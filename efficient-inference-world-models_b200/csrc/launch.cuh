@@ -5,19 +5,30 @@
 
 namespace oasis {
 
-// By-value view of a KV cache handed to the temporal attention kernel.
-struct KvView {
-  int layers, n_bf16, n_fp8, n_int4;
+// By-value view of one tensor (keys or values) of a KV cache, handed to the kernels.
+struct KvTensor {
+  int n_bf16, n_fp8, n_int4;
   uint8_t kind[OASIS_MAX_FRAMES];
   uint8_t index[OASIS_MAX_FRAMES];
-  const __nv_bfloat16* k_bf16; const __nv_bfloat16* v_bf16;
-  const uint8_t* k_fp8; const uint8_t* v_fp8;
-  const __nv_bfloat16* k_fp8_scale; const __nv_bfloat16* v_fp8_scale;
-  const uint8_t* k_int4; const uint8_t* v_int4;
-  const __half* k_i4_scale; const __half* k_i4_zero;
-  const __half* v_i4_scale; const __half* v_i4_zero;
+  __nv_bfloat16* bf16;
+  uint8_t* fp8; __nv_bfloat16* fp8_scale;
+  uint8_t* int4; __half* i4_scale; __half* i4_zero;
 };
 
+// By-value view of a KV cache: t[0] the keys, t[1] the values.
+struct KvView {
+  int layers;
+  KvTensor t[2];
+};
+
+// Frame page (144 x 1024 elements, or 144 x 16 groups) of pool frame `idx` of session b,
+// layer `layer` in a pool of `n` frames.
+__host__ __device__ __forceinline__ long long kv_page(int b, int layers, int layer, int n, int idx) {
+  return (static_cast<long long>(b) * layers + layer) * n + idx;
+}
+
+// Fills `v` from `c` after checking that every slot of both tensors maps into a pool
+// that exists (c == NULL gives an empty view).
 int make_kv_view(const oasis_kv_cache_t* c, KvView* v);
 // bf16 tensor map of rank 2 or 3 (dims innermost first, byte strides of dims 1..),
 // 128-byte swizzled boxes.

@@ -71,6 +71,7 @@ class OasisDiTB200:
         self.device = torch.device(device)
         self.depth = weights.depth
         self._plans: Dict[Tuple[int, int], _Plan] = {}
+        self.kv_manager = None  # set by KVCacheManagerB200.wire_to_model
 
     # -- construction ----------------------------------------------------------
     @classmethod
@@ -100,7 +101,8 @@ class OasisDiTB200:
                 kv_cache=None, out: Optional[torch.Tensor] = None,
                 stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
         """Full-window forward.  ``kv_cache`` (a :class:`KVCacheB200`) additionally
-        receives the post-RoPE temporal K/V of frames 0..T-2 (prefill)."""
+        receives the post-RoPE temporal K/V of frames 0..T-2 (prefill); without one, a
+        wired KV manager (``KVCacheManagerB200.wire_to_model``) supplies its prefill cache."""
         if x.dim() != 5 or tuple(x.shape[2:]) != LATENT:
             raise ValueError(f"x must be (B, T, 16, 18, 32), got {tuple(x.shape)}")
         B, T = x.shape[:2]
@@ -116,6 +118,8 @@ class OasisDiTB200:
             ad = self._to_dev(external_cond, torch.float32)
         v = out if out is not None else torch.empty((B, T) + LATENT, device=self.device, dtype=torch.float32)
         p = self.plan(B, T)
+        if kv_cache is None and self.kv_manager is not None and T > 1:
+            kv_cache = self.kv_manager.cache_for_window(T - 1)
         cache = ctypes.byref(kv_cache.struct) if kv_cache is not None else None
         N.call("oasis_dit_forward", p.handle, xd.data_ptr(), td.data_ptr(),
                ad.data_ptr() if ad is not None else None, v.data_ptr(), cache, _stream_ptr(stream))

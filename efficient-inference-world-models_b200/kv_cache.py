@@ -35,72 +35,85 @@ def _stream_ptr(stream=None) -> int:
     return (stream or torch.cuda.current_stream()).cuda_stream
 
 
-class KVCacheB200:
-    """Device pools for ``batch`` sessions x ``layers`` blocks x ``len(slot_kinds)`` slots."""
+def _pool_map(kinds: Sequence[str]):
+    """Per-kind frame counts and each slot's index inside its kind's pool."""
+    counts = {N.KV_BF16: 0, N.KV_FP8: 0, N.KV_INT4: 0}
+    index = []
+    for k in kinds:
+        c = KIND_NAMES[k]
+        index.append(counts[c])
+        counts[c] += 1
+    return counts, index
 
-    def __init__(self, batch: int, layers: int, slot_kinds: Sequence[str], device="cuda"):
+
+class KVCacheB200:
+    """Device pools for ``batch`` sessions x ``layers`` blocks x ``len(slot_kinds)`` slots.
+
+    ``slot_kinds`` are the storage kinds of the key slots (slot 0 = oldest frame);
+    ``value_kinds`` those of the value slots (default: the same).  Keys and values have
+    their own pools, sized by their own kind counts, as the reference's progressive
+    quantiser keeps each in its own precision tier."""
+
+    def __init__(self, batch: int, layers: int, slot_kinds: Sequence[str], device="cuda",
+                 value_kinds: Optional[Sequence[str]] = None):
         if not 1 <= len(slot_kinds) <= N.MAX_FRAMES:
             raise ValueError("need 1..32 slots")
+        value_kinds = list(slot_kinds) if value_kinds is None else list(value_kinds)
+        if len(value_kinds) != len(slot_kinds):
+            raise ValueError("keys and values need the same number of slots")
         self.batch, self.layers = batch, layers
         self.device = torch.device(device)
         self.slot_kinds = [str(k) for k in slot_kinds]
-        kinds = [KIND_NAMES[k] for k in self.slot_kinds]
-        counts = {N.KV_BF16: 0, N.KV_FP8: 0, N.KV_INT4: 0}
-        index = []
-        for k in kinds:
-            index.append(counts[k])
-            counts[k] += 1
-        self.counts = counts
-        self._alloc_pools(counts)
+        self.value_kinds = [str(k) for k in value_kinds]
+        k_counts, k_index = _pool_map(self.slot_kinds)
+        v_counts, v_index = _pool_map(self.value_kinds)
+        self.counts = {"k": k_counts, "v": v_counts}
+        self._alloc_pools(k_counts, v_counts)
         s = self._pool_struct()
-        s.n_slots = len(kinds)
-        for i, (k, ix) in enumerate(zip(kinds, index)):
-            s.slot_kind[i] = k
-            s.slot_index[i] = ix
+        s.n_slots = len(self.slot_kinds)
+        for i in range(s.n_slots):
+            s.k.slot_kind[i], s.k.slot_index[i] = KIND_NAMES[self.slot_kinds[i]], k_index[i]
+            s.v.slot_kind[i], s.v.slot_index[i] = KIND_NAMES[self.value_kinds[i]], v_index[i]
         self.struct = s
 
-    def _alloc_pools(self, counts: Dict[int, int]) -> None:
-        """Zeroed storage for ``counts[kind]`` frame slots of each kind."""
+    _POOL_NAMES = ("bf16", "fp8", "fp8_scale", "int4", "i4_scale", "i4_zero")
+
+    def _alloc_pools(self, k_counts: Dict[int, int], v_counts: Dict[int, int]) -> None:
+        """Zeroed storage for ``counts[kind]`` frame slots of each kind, per tensor:
+        attributes ``k_bf16``, ``k_fp8``, ``k_fp8_scale``, ``k_int4``, ``k_i4_scale``,
+        ``k_i4_zero`` and the same with ``v_`` (None where a pool is empty)."""
         dev = self.device
         lead = (self.batch, self.layers)
-        self.k_bf16 = self.v_bf16 = None
-        self.k_fp8 = self.v_fp8 = self.k_fp8_scale = self.v_fp8_scale = None
-        self.k_int4 = self.v_int4 = None
-        self.k_i4_scale = self.k_i4_zero = self.v_i4_scale = self.v_i4_zero = None
-        if counts[N.KV_BF16]:
+        for which, counts in (("k", k_counts), ("v", v_counts)):
+            for name in self._POOL_NAMES:
+                setattr(self, f"{which}_{name}", None)
             n = counts[N.KV_BF16]
-            self.k_bf16 = torch.zeros(lead + (n, TOKENS, HIDDEN), dtype=torch.bfloat16, device=dev)
-            self.v_bf16 = torch.zeros_like(self.k_bf16)
-        if counts[N.KV_FP8]:
+            if n:
+                setattr(self, f"{which}_bf16", torch.zeros(lead + (n, TOKENS, HIDDEN), dtype=torch.bfloat16, device=dev))
             n = counts[N.KV_FP8]
-            self.k_fp8 = torch.zeros(lead + (n, TOKENS, HIDDEN), dtype=torch.uint8, device=dev)
-            self.v_fp8 = torch.zeros_like(self.k_fp8)
-            self.k_fp8_scale = torch.zeros(lead + (n, HEADS), dtype=torch.bfloat16, device=dev)
-            self.v_fp8_scale = torch.zeros_like(self.k_fp8_scale)
-        if counts[N.KV_INT4]:
+            if n:
+                setattr(self, f"{which}_fp8", torch.zeros(lead + (n, TOKENS, HIDDEN), dtype=torch.uint8, device=dev))
+                setattr(self, f"{which}_fp8_scale", torch.zeros(lead + (n, HEADS), dtype=torch.bfloat16, device=dev))
             n = counts[N.KV_INT4]
-            self.k_int4 = torch.zeros(lead + (n, TOKENS, HEADS, HEAD_DIM // 2), dtype=torch.uint8, device=dev)
-            self.v_int4 = torch.zeros_like(self.k_int4)
-            self.k_i4_scale = torch.zeros(lead + (n, TOKENS, HEADS), dtype=torch.float16, device=dev)
-            self.k_i4_zero = torch.zeros_like(self.k_i4_scale)
-            self.v_i4_scale = torch.zeros_like(self.k_i4_scale)
-            self.v_i4_zero = torch.zeros_like(self.k_i4_scale)
+            if n:
+                setattr(self, f"{which}_int4", torch.zeros(lead + (n, TOKENS, HEADS, HEAD_DIM // 2), dtype=torch.uint8, device=dev))
+                setattr(self, f"{which}_i4_scale", torch.zeros(lead + (n, TOKENS, HEADS), dtype=torch.float16, device=dev))
+                setattr(self, f"{which}_i4_zero", torch.zeros(lead + (n, TOKENS, HEADS), dtype=torch.float16, device=dev))
 
     def _pool_struct(self) -> "N.KvCache":
         """A cache descriptor over this object's pools with no slots mapped yet."""
         s = N.KvCache()
         s.batch, s.layers, s.n_slots = self.batch, self.layers, 0
-        s.n_bf16, s.n_fp8, s.n_int4 = self.counts[N.KV_BF16], self.counts[N.KV_FP8], self.counts[N.KV_INT4]
 
         def ptr(t):
             return t.data_ptr() if t is not None else None
 
-        s.k_bf16, s.v_bf16 = ptr(self.k_bf16), ptr(self.v_bf16)
-        s.k_fp8, s.v_fp8 = ptr(self.k_fp8), ptr(self.v_fp8)
-        s.k_fp8_scale, s.v_fp8_scale = ptr(self.k_fp8_scale), ptr(self.v_fp8_scale)
-        s.k_int4, s.v_int4 = ptr(self.k_int4), ptr(self.v_int4)
-        s.k_i4_scale, s.k_i4_zero = ptr(self.k_i4_scale), ptr(self.k_i4_zero)
-        s.v_i4_scale, s.v_i4_zero = ptr(self.v_i4_scale), ptr(self.v_i4_zero)
+        for which in ("k", "v"):
+            t = getattr(s, which)
+            counts = self.counts[which]
+            t.n_bf16, t.n_fp8, t.n_int4 = counts[N.KV_BF16], counts[N.KV_FP8], counts[N.KV_INT4]
+            for name in self._POOL_NAMES:
+                setattr(t, name, ptr(getattr(self, f"{which}_{name}")))
         return s
 
     # -- configurations of the benchmark -----------------------------------------
@@ -119,9 +132,13 @@ class KVCacheB200:
         return len(self.slot_kinds)
 
     def tensors(self) -> List[torch.Tensor]:
-        return [t for t in (self.k_bf16, self.v_bf16, self.k_fp8, self.v_fp8, self.k_fp8_scale,
-                            self.v_fp8_scale, self.k_int4, self.v_int4, self.k_i4_scale,
-                            self.k_i4_zero, self.v_i4_scale, self.v_i4_zero) if t is not None]
+        out = []
+        for which in ("k", "v"):
+            for name in self._POOL_NAMES:
+                t = getattr(self, f"{which}_{name}")
+                if t is not None:
+                    out.append(t)
+        return out
 
     @property
     def nbytes(self) -> int:

@@ -31,6 +31,16 @@ from typing import Any, Dict, List, Optional, Sequence, Union
 import torch
 
 from .kv_cache import KVCacheB200
+
+
+def _window_cache(B: int, depth: int, n_past: int, kv_kinds, device) -> KVCacheB200:
+    """Cache for the past frames of a window: ``kv_kinds(n_past)`` gives the slot kinds
+    (one list for keys and values, or a ``(key kinds, value kinds)`` pair such as
+    ``ProgressiveKVQuantizerB200.slot_kinds`` returns); bf16 when None."""
+    kinds = kv_kinds(n_past) if kv_kinds is not None else ["bf16"] * n_past
+    if isinstance(kinds, tuple):
+        return KVCacheB200(B, depth, kinds[0], device=device, value_kinds=kinds[1])
+    return KVCacheB200(B, depth, kinds, device=device)
 from . import _native as N
 from .samplers import FRAME_ELEMS, _stream_ptr, ddim_update
 
@@ -158,8 +168,7 @@ class _FrameGraph:
         self.v1 = torch.empty(B, LATENT_C, LATENT_H, LATENT_W, device=device)
         self.cache = None
         if use_cache and T > 1:
-            kinds = kv_kinds(T - 1) if kv_kinds is not None else ["bf16"] * (T - 1)
-            self.cache = KVCacheB200(B, dit.depth, kinds, device=device)
+            self.cache = _window_cache(B, dit.depth, T - 1, kv_kinds, device)
         self.levels = []
         for t, ab_t, ab_next in _solver_levels(steps, ab):
             tw = torch.full((B, T), stabilization_level - 1, dtype=torch.long, device=device)
@@ -243,8 +252,7 @@ def rollout_dpmpp(dit, prompt_latent: torch.Tensor, actions: torch.Tensor, num_f
         act = actions[:, start: i + 1].contiguous()
         t_win = torch.full((B, T), stabilization_level - 1, dtype=torch.long, device=device)
         if use_cache and T > 1 and (cache is None or cache.n_slots != T - 1):
-            kinds = kv_kinds(T - 1) if kv_kinds is not None else ["bf16"] * (T - 1)
-            cache = KVCacheB200(B, dit.depth, kinds, device=device)
+            cache = _window_cache(B, dit.depth, T - 1, kv_kinds, device)
         for k, (t, ab_t, ab_next) in enumerate(_solver_levels(steps_i, ab)):
             t_win[:, -1] = t
             if use_cache and T > 1 and k > 0:

@@ -94,7 +94,7 @@ class DPMSolverPPSampler:
                d1.data_ptr() if d1 is not None else None, d2.data_ptr() if d2 is not None else None,
                out.data_ptr(), x.numel(), h, c[0], c[1], c[2], _stream_ptr())
         self._history.append(d0.detach().clone())
-        return out
+        return out if latents.dtype == torch.float32 else out.to(latents.dtype)
 
     def wrap_oasis_loop(self, dit_fn: Callable, latents: torch.Tensor, timesteps: torch.Tensor):
         self.reset()

@@ -114,25 +114,37 @@ typedef struct {
 #define OASIS_KV_INT4 2   /* packed nibbles (element 2i high) + fp16 scale/zero
                              per (token, head) group of 64                      */
 
-/* Post-RoPE temporal K/V of past frames, for `batch` sessions x `layers`
- * blocks.  Slot s (0 <= s < n_slots) holds one frame; its storage kind and its
- * index inside that kind's pool are slot_kind[s] / slot_index[s] (shared by all
- * sessions and layers).  Pools (row-major, leading dims first):
- *   bf16: k_bf16/v_bf16   [batch][layers][n_bf16][144][1024] bf16
- *   fp8 : k_fp8/v_fp8     [batch][layers][n_fp8][144][1024] u8
- *         k_fp8_scale/..  [batch][layers][n_fp8][16] bf16
- *   int4: k_int4/v_int4   [batch][layers][n_int4][144][16][32] u8
- *         k_i4_scale, k_i4_zero, v_.. [batch][layers][n_int4][144][16] fp16
- * Unused pools may be NULL with count 0. */
+/* Bits of the `tensors` argument of oasis_kv_migrate. */
+#define OASIS_KV_KEYS   1
+#define OASIS_KV_VALUES 2
+
+/* One tensor (the keys or the values) of a temporal KV cache.  Logical slot s
+ * (0 <= s < n_slots of the cache; 0 = oldest frame) is stored in the pool of kind
+ * slot_kind[s], at frame index slot_index[s] of that pool (shared by all sessions and
+ * layers).  Keys and values carry separate maps and pools, so each sits in its own
+ * precision tier, as ProgressiveKVQuantizer ages them on separate thresholds
+ * (worldserve/optimizations/system_level/kv_cache/progressive_quant.py:92-98,310-322).
+ * Pools (row-major, leading dims first):
+ *   bf16: bf16       [batch][layers][n_bf16][144][1024] bf16
+ *   fp8 : fp8        [batch][layers][n_fp8][144][1024] e4m3fn codes
+ *         fp8_scale  [batch][layers][n_fp8][16] bf16
+ *   int4: int4       [batch][layers][n_int4][144][16][32] packed codes
+ *         i4_scale, i4_zero  [batch][layers][n_int4][144][16] fp16
+ * Unused pools may be NULL with count 0.  Every pool base must be 16-byte aligned. */
 typedef struct {
-  int batch, layers, n_slots;
   int n_bf16, n_fp8, n_int4;
   uint8_t slot_kind[OASIS_MAX_FRAMES];
   uint8_t slot_index[OASIS_MAX_FRAMES];
-  void* k_bf16; void* v_bf16;
-  uint8_t* k_fp8; uint8_t* v_fp8; void* k_fp8_scale; void* v_fp8_scale;
-  uint8_t* k_int4; uint8_t* v_int4;
-  void* k_i4_scale; void* k_i4_zero; void* v_i4_scale; void* v_i4_zero;
+  void* bf16;
+  uint8_t* fp8; void* fp8_scale;
+  uint8_t* int4; void* i4_scale; void* i4_zero;
+} oasis_kv_tensor_t;
+
+/* Post-RoPE temporal K/V of past frames, for `batch` sessions x `layers` blocks and
+ * `n_slots` frames (slot 0 = oldest). */
+typedef struct {
+  int batch, layers, n_slots;
+  oasis_kv_tensor_t k, v;
 } oasis_kv_cache_t;
 
 /* ------------------------------------------------------------------ forward plan */
@@ -152,7 +164,7 @@ void oasis_plan_destroy(oasis_plan_t* plan);
 /* Full-window forward: x fp32 [B][T][16][18][32], t int64 [B][T], act fp32
  * [B][T][25] (may be NULL: no external conditioning) -> v fp32 [B][T][16][18][32].
  * If `cache` is non-NULL, the post-RoPE temporal K/V of window frames
- * 0..T-2 are also stored into cache slots 0..T-2 in each slot's kind (FP8/INT4
+ * 0..T-2 are also stored into cache slots 0..T-2, keys and values each in its slot's kind (FP8/INT4
  * quantised exactly like ProgressiveKVQuantizer.quantize_to_fp8 / quantize_to_int4,
  * worldserve/optimizations/system_level/kv_cache/progressive_quant.py:113-193,
  * at the granularity above).  Replaces DiT.forward plus the KV capture of
@@ -225,7 +237,7 @@ int oasis_attn_temporal(const void* qkv, const oasis_kv_cache_t* cache, int laye
                         int n_kv, cudaStream_t stream);
 
 /* Quantise K/V of `frames` frames per session into cache slots
- * slot0..slot0+frames-1 (each in its slot kind) for one layer, from
+ * slot0..slot0+frames-1 (keys and values each in its slot kind) for one layer, from
  * kv bf16 [batch*frames*144][ld] where K is at column k_col and V at v_col.
  * Replaces ProgressiveKVQuantizer.quantize_to_fp8 / quantize_to_int4 applied
  * per frame-head slice / per token-head group (progressive_quant.py:113-193). */
@@ -240,10 +252,12 @@ int oasis_kv_load(const oasis_kv_cache_t* cache, int layer, int slot0, int frame
 /* Age promotion of one frame of a temporal KV cache (replaces the per-entry
  * _promote_to_fp8 / _promote_to_int4 steps of ProgressiveKVQuantizer.update_cache,
  * worldserve/optimizations/system_level/kv_cache/progressive_quant.py:263-350):
- * re-quantises logical slot src_slot into logical slot dst_slot for every session and
- * layer.  Allowed: bf16 -> FP8, bf16 -> INT4, FP8 -> INT4 (an FP8 entry is dequantised
- * to fp16 first, as the reference does).  The two slots must map to different storage. */
-int oasis_kv_migrate(const oasis_kv_cache_t* cache, int src_slot, int dst_slot,
+ * re-quantises logical slot src_slot into logical slot dst_slot, for every session and
+ * layer, of the keys (tensors & OASIS_KV_KEYS) and/or the values (OASIS_KV_VALUES),
+ * each through its own slot map.  Allowed per tensor: bf16 -> FP8, bf16 -> INT4,
+ * FP8 -> INT4 (an FP8 entry is dequantised to fp16 first, as the reference does).  The
+ * two slots of a tensor must map to different storage. */
+int oasis_kv_migrate(const oasis_kv_cache_t* cache, int tensors, int src_slot, int dst_slot,
                      cudaStream_t stream);
 
 /* DPM-Solver++ 2M v-prediction update of the newest frame of each session

@@ -169,3 +169,58 @@ def promote_fp8_to_int4_rows(codes: np.ndarray, scale) -> tuple:
     x16 = x.astype(np.float16).astype(np.float32)
     return quantize_int4_rows(x16)
 
+
+
+# ---------------------------------------------------------------- update_cache
+
+class UpdateCacheRef:
+    """``ProgressiveKVQuantizer.update_cache`` (progressive_quant.py:263-350) for one
+    stream of cache entries at the B200 cache's granularity (one 144 x 64 frame-head
+    slice per append; FP8 one scale per slice, INT4 one group per 64-element row).
+
+    Keys drop to FP8 at ``fp8_age`` and to INT4 at ``int4_age``; with
+    ``key_value_asymmetry`` the values use ``int(0.7 x)`` those ages (:92-98).  Each
+    append adds the new entries at full precision (age 0), then ages every older entry
+    by one and promotes it, oldest first: ``age >= int4_age`` and not INT4 -> INT4 (from
+    the entry's FP8 codes through the fp16 dequantisation, or from its full-precision
+    values); otherwise ``age >= fp8_age`` and full precision -> FP8.  ``window`` keeps
+    only the newest entries, as ``KVCacheManager.update`` trims its cache (manager.py:
+    296-306)."""
+
+    def __init__(self, fp8_age: int = 30, int4_age: int = 90, key_value_asymmetry: bool = True,
+                 window: int = 0):
+        self.thr = {"key": (fp8_age, int4_age)}
+        if key_value_asymmetry:
+            self.thr["value"] = (int(fp8_age * 0.7), int(int4_age * 0.7))
+        else:
+            self.thr["value"] = (fp8_age, int4_age)
+        self.window = window
+        self.entries = {"key": [], "value": []}
+        self.ages = []
+
+    def append(self, key: np.ndarray, value: np.ndarray) -> None:
+        for t, x in (("key", key), ("value", value)):
+            self.entries[t].append({"precision": "fp16", "x": np.asarray(x, np.float32).copy()})
+        self.ages.append(0)
+        for i in range(len(self.ages) - 1):
+            self.ages[i] += 1
+            for t in ("key", "value"):
+                fp8_age, int4_age = self.thr[t]
+                e = self.entries[t][i]
+                if self.ages[i] >= int4_age and e["precision"] != "int4":
+                    if e["precision"] == "fp8":
+                        p, s16, z16, s, z = promote_fp8_to_int4_rows(e["codes"], e["scale"])
+                    else:
+                        p, s16, z16, s, z = quantize_int4_rows(e["x"])
+                    e.update(precision="int4", packed=p, scale16=s16, zero16=z16, scale=s, zero=z)
+                elif self.ages[i] >= fp8_age and e["precision"] == "fp16":
+                    codes, scale = quantize_to_fp8_bf16(e["x"])
+                    e.update(precision="fp8", codes=codes, scale=scale)
+        if self.window and len(self.ages) > self.window:
+            drop = len(self.ages) - self.window
+            self.ages = self.ages[drop:]
+            for t in ("key", "value"):
+                self.entries[t] = self.entries[t][drop:]
+
+    def precisions(self, tensor: str):
+        return [e["precision"] for e in self.entries[tensor]]

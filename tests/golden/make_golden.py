@@ -2,7 +2,9 @@
 
 Run from the repository root in a container that has the reference checkout:
 
-    PYTHONPATH=/root/reference:. python tests/golden/make_golden.py
+    PYTHONPATH=<reference checkout>:. python tests/golden/make_golden.py [maker ...]
+
+(no argument: every fixture; otherwise only the named makers, e.g. ``update_cache``).
 
 Only this script reads the reference; the fixtures it writes are committed so the
 tests (CPU and GPU) never need the reference at run time.  Every fixture is
@@ -28,6 +30,14 @@ produced by calling the reference functions named below on seeded inputs:
   ``_promote_to_int4`` of an FP8 entry (``dequantize_fp8`` with its default fp16 target,
   then ``quantize_to_int4``) and of a full-precision entry (``quantize_to_int4``), with
   the cache's group of 64.
+* ``update_cache_golden.npz`` — ``ProgressiveKVQuantizer.update_cache`` itself with
+  ``key_value_asymmetry=True`` (values promoted at ``int(0.7 x)`` the key ages,
+  ``progressive_quant.py:92-98,263-350``), fed one bf16 (144, 64) key slice and one
+  value slice per frame; its INT4 group is set to the cache's 64 (one token-head row),
+  the granularity of the benchmark's INT4 cache.  Recorded: every entry's precision
+  after every append, and the final codes/scales/zeros of every entry, for thresholds
+  (fp8 3, int4 8) over 12 frames and (2, 2) over 5 frames (bf16 -> INT4 directly); and
+  the precisions alone for the reference defaults (30, 90) over 40 frames.
 """
 
 from __future__ import annotations
@@ -229,10 +239,60 @@ def make_cached_past():
                         q=q.numpy(), k=k.numpy(), v=v.numpy(), n_past=np.array(12), y=y.numpy())
 
 
+def _int4_group64(x, group_size=64):
+    """The reference quantiser's INT4 at the cache's group of 64 (one token-head row)."""
+    return ProgressiveKVQuantizer.quantize_to_int4(x, group_size=64)
+
+
+UPDATE_CACHE_CONFIGS = (("a", 3, 8, 12), ("b", 2, 2, 5), ("d", 30, 90, 40))
+PREC_CODE = {"fp16": 0, "fp8": 1, "int4": 2}
+
+
+def make_update_cache():
+    xs = quant_cases()
+    out = {}
+    for name, fp8_age, int4_age, n in UPDATE_CACHE_CONFIGS:
+        q = ProgressiveKVQuantizer(fp8_age_threshold=fp8_age, int4_age_threshold=int4_age,
+                                   key_value_asymmetry=True)
+        q.quantize_to_int4 = _int4_group64
+        hist = {t: np.full((n, n), -1, np.int8) for t in ("key", "value")}
+        for f in range(n):
+            if name == "d":  # precisions only: small entries
+                k = v = torch.zeros(2, 64).bfloat16()
+            else:
+                k, v = xs[f % len(xs)], xs[(f + 7) % len(xs)]
+            q.update_cache({}, {0: {"key": k, "value": v}}, f)
+            for t, entries in (("key", q._cache_k[0]), ("value", q._cache_v[0])):
+                hist[t][f, :f + 1] = [PREC_CODE[e.precision] for e in entries]
+        for t, entries in (("key", q._cache_k[0]), ("value", q._cache_v[0])):
+            out[f"{name}_{t}_hist"] = hist[t]
+            if name == "d":
+                continue
+            fp8_codes = np.zeros((n, 144, 64), np.uint8)
+            fp8_scale = np.zeros(n, np.uint16)
+            i4_packed = np.zeros((n, 144 * 32), np.uint8)
+            i4_scale = np.zeros((n, 144), np.float32)
+            i4_zero = np.zeros((n, 144), np.float32)
+            for i, e in enumerate(entries):
+                if e.precision == "fp8":
+                    fp8_codes[i] = e.data.view(torch.uint8).numpy()
+                    fp8_scale[i] = _bf16_bits(e.scale.reshape(1))[0]
+                elif e.precision == "int4":
+                    i4_packed[i] = e.data.numpy()
+                    i4_scale[i] = e.scale.numpy()
+                    i4_zero[i] = e.zero_point.numpy()
+            out.update({f"{name}_{t}_fp8_codes": fp8_codes, f"{name}_{t}_fp8_scale_bf16": fp8_scale,
+                        f"{name}_{t}_i4_packed": i4_packed, f"{name}_{t}_i4_scale": i4_scale,
+                        f"{name}_{t}_i4_zero": i4_zero})
+        out[f"{name}_thresholds"] = np.array([fp8_age, int4_age, n])
+    out["inputs"] = np.array("key of frame f: quant_golden inp_bf16[f % 18]; value: inp_bf16[(f + 7) % 18]")
+    np.savez_compressed(os.path.join(HERE, "update_cache_golden.npz"), **out)
+
+
+MAKERS = {"quant": make_quant, "sampler": make_sampler, "temporal_attn": make_temporal_attn,
+          "cached_past": make_cached_past, "promote": make_promote, "update_cache": make_update_cache}
+
 if __name__ == "__main__":
-    make_quant()
-    make_sampler()
-    make_temporal_attn()
-    make_cached_past()
-    make_promote()
+    for name in (sys.argv[1:] or list(MAKERS)):
+        MAKERS[name]()
     print("golden fixtures written to", HERE)

@@ -225,6 +225,88 @@ def test_attn_temporal_full_from_quantized_cache(pkg, cuda, kind, T):
     assert rel_l2(out.float(), ref) < 1e-2
 
 
+# keys and values in their own tiers (the reference's key/value asymmetry), one query frame
+@pytest.mark.parametrize("kinds,vkinds", [
+    (["int4"] * 3 + ["fp8"] * 3 + ["bf16"] * 2, ["int4"] * 5 + ["fp8"] * 2 + ["bf16"]),
+    (["fp8"] * 31, ["fp8"] * 31),
+    (["bf16"] * 31, ["fp8"] * 10 + ["bf16"] * 21),
+    (["fp8"] * 2 + ["bf16"] * 29, ["fp8"] * 11 + ["bf16"] * 20),
+    (["int4"] * 23 + ["bf16"] * 8, ["int4"] * 23 + ["bf16"] * 8)])
+def test_attn_decode_keys_values_in_own_tiers(pkg, cuda, kinds, vkinds):
+    """The one-query-frame kernel of the incremental forward: newest frame against cached
+    slots whose keys and values sit in different tiers, plus its own K/V, vs fp32 SDPA on
+    the dequantised cache."""
+    B, P = 3, len(kinds)
+    past = _kv_rows(B, P, cuda, 21)
+    cache = pkg.KVCacheB200(B, 1, kinds, device=cuda, value_kinds=vkinds)
+    cache.store(past, layer=0)
+    new = _qkv(B, cuda, 22)
+    out = pkg.attn_temporal(new, batch=B, q_frames=1, q_pos0=P, n_past=P, n_kv=P + 1, cache=cache, layer=0)
+    k, v = cache.load(0)
+    kp = k.float().reshape(B, P, TOK, 16, 64).permute(0, 2, 3, 1, 4).reshape(B * TOK, 16, P, 64)
+    vp = v.float().reshape(B, P, TOK, 16, 64).permute(0, 2, 3, 1, 4).reshape(B * TOK, 16, P, 64)
+    ref = _temporal_ref(new, B, 1, kp, vp, q_pos0=P)
+    torch.cuda.synchronize()
+    assert rel_l2(out.float(), ref) < 1e-2
+
+
+def test_attn_decode_all_keys_cached(pkg, cuda):
+    """One query frame whose keys all come from the cache (n_kv == n_past): the query at
+    window position P-1 sees cached slots 0..P-1 and nothing of its own row."""
+    B, P = 2, 9
+    past = _kv_rows(B, P, cuda, 31)
+    cache = pkg.KVCacheB200(B, 1, ["fp8"] * 4 + ["bf16"] * 5, device=cuda,
+                            value_kinds=["int4"] * 6 + ["bf16"] * 3)
+    cache.store(past, layer=0)
+    new = _qkv(B, cuda, 32)
+    out = pkg.attn_temporal(new, batch=B, q_frames=1, q_pos0=P - 1, n_past=P, n_kv=P, cache=cache, layer=0)
+    k, v = cache.load(0)
+    kp = k.float().reshape(B, P, TOK, 16, 64).permute(0, 2, 3, 1, 4).reshape(B * TOK, 16, P, 64)
+    vp = v.float().reshape(B, P, TOK, 16, 64).permute(0, 2, 3, 1, 4).reshape(B * TOK, 16, P, 64)
+    q = new.float().reshape(B, 1, TOK, 3, 16, 64)[:, :, :, 0].permute(0, 2, 3, 1, 4).reshape(B * TOK, 16, 1, 64)
+    ref = torch.nn.functional.scaled_dot_product_attention(q, kp, vp)
+    ref = ref.reshape(B, TOK, 16, 1, 64).permute(0, 3, 1, 2, 4).reshape(B * TOK, HID)
+    torch.cuda.synchronize()
+    assert rel_l2(out.float(), ref) < 1e-2
+
+
+# the isolated attention sweep (benchmark configuration 4) at its own sizes
+@pytest.mark.parametrize("frames", [256, 1024, 4096])
+def test_attn_spatial_sweep_sizes(pkg, cuda, frames):
+    qkv = _qkv(frames, cuda, 7 + frames)
+    out = pkg.attn_spatial(qkv)
+    q, k, v = (_heads(qkv[:, i * HID:(i + 1) * HID], frames) for i in range(3))
+    ref = torch.nn.functional.scaled_dot_product_attention(q, k, v)
+    ref = ref.permute(0, 2, 1, 3).reshape(frames * TOK, HID)
+    del q, k, v
+    torch.cuda.synchronize()
+    assert rel_l2(out.float(), ref) < 1e-2
+
+
+@pytest.mark.parametrize("kind", ["bf16", "fp8", "int4"])
+@pytest.mark.parametrize("T", [8, 16, 32])
+@pytest.mark.parametrize("B", [8, 32])
+def test_attn_temporal_sweep_sizes(pkg, cuda, B, T, kind):
+    """Causal T x T over B*144 sequences with bf16 K/V (full-window kernel) or every K/V
+    frame read from an FP8 / INT4 cache, vs fp32 SDPA on the (dequantised) inputs."""
+    qkv = _qkv(B * T, cuda, 300 + B + T)
+    if kind == "bf16":
+        out = pkg.attn_temporal(qkv, batch=B, q_frames=T)
+        ref = _temporal_ref(qkv, B, T)
+    else:
+        cache = pkg.KVCacheB200.uniform(B, 1, T, kind, device=cuda)
+        cache.store(qkv, layer=0)
+        out = pkg.attn_temporal(qkv, batch=B, q_frames=T, q_pos0=0, n_past=T, n_kv=T, cache=cache, layer=0)
+        k, v = cache.load(0)
+        deq = qkv.clone()
+        deq[:, HID:2 * HID] = k.reshape(B * T * TOK, HID)
+        deq[:, 2 * HID:] = v.reshape(B * T * TOK, HID)
+        del k, v, cache
+        ref = _temporal_ref(deq, B, T)
+    torch.cuda.synchronize()
+    assert rel_l2(out.float(), ref) < 1e-2
+
+
 # ----------------------------------------------------------------- samplers
 
 def test_dpmpp2m_and_ddim_update(pkg, cuda):

@@ -103,9 +103,35 @@ def test_progressive_policy_matches_reference_thresholds(pkg):
     q = pkg.ProgressiveKVQuantizerB200(fp8_age_threshold=3, int4_age_threshold=10,
                                        key_value_asymmetry=True)
     assert (q.v_fp8_age, q.v_int4_age) == (2, 7)  # int(0.7 * threshold), progressive_quant.py:93-95
-    kinds = q.slot_kinds(12)  # slot s holds a frame of age 12 - s
-    assert kinds[-1] == "bf16" and kinds[-2] == "fp8" and kinds[0] == "int4"
-    assert kinds.count("int4") == 6  # ages 12..7 (V reaches INT4 at 7)
+    keys, values = q.slot_kinds(12)  # slot s holds a frame of age 12 - s
+    # keys: INT4 at ages 12..10, FP8 at 9..3, bf16 at 2..1; values: INT4 at 12..7, FP8 at 6..2
+    assert keys == ["int4"] * 3 + ["fp8"] * 7 + ["bf16"] * 2
+    assert values == ["int4"] * 6 + ["fp8"] * 5 + ["bf16"]
+    assert q.precision_for_age(0, "value") == "bf16"  # a new entry is always full precision
+    sym = pkg.ProgressiveKVQuantizerB200(fp8_age_threshold=3, int4_age_threshold=10,
+                                         key_value_asymmetry=False)
+    assert sym.slot_kinds(12)[0] == sym.slot_kinds(12)[1] == keys
+
+
+def test_rolling_pool_sizes_follow_each_tensors_tiers(pkg):
+    """A full window of 32 frames at the reference defaults: keys FP8 from age 30 (2
+    frames), values FP8 from age 21 (11 frames); bf16 the rest, the newest frame included
+    (pool sizes of the rolling cache)."""
+    q = pkg.ProgressiveKVQuantizerB200()
+    counts = {}
+    for tensor in ("key", "value"):
+        tiers = [q.precision_for_age(a, tensor) for a in range(32)]
+        counts[tensor] = (tiers.count("bf16"), tiers.count("fp8"), tiers.count("int4"))
+    assert counts == {"key": (30, 2, 0), "value": (21, 11, 0)}
+
+
+def test_kv_struct_layout_matches_header(pkg):
+    """The ctypes mirror of oasis_kv_tensor_t / oasis_kv_cache_t has the C layout: one
+    slot map and six pool pointers per tensor, keys then values."""
+    import ctypes
+    N = pkg._native
+    assert ctypes.sizeof(N.KvTensor) == 128
+    assert (N.KvCache.k.offset, N.KvCache.v.offset, ctypes.sizeof(N.KvCache)) == (16, 144, 272)
 
 
 def test_action_step_schedule_buckets(pkg):

@@ -187,3 +187,40 @@ def test_cached_past_attention_equals_reference():
     q, k, v = (torch.from_numpy(g[n]) for n in ("q", "k", "v"))
     y = torch.nn.functional.scaled_dot_product_attention(q, k, v)
     np.testing.assert_allclose(y.numpy(), g["y"], rtol=0, atol=1e-6)
+
+
+# ----------------------------------------------------------------- update_cache (asymmetric)
+
+PREC = {0: "fp16", 1: "fp8", 2: "int4"}
+
+
+@pytest.mark.parametrize("name", ["a", "b", "d"])
+def test_update_cache_oracle_matches_reference_asymmetric(name):
+    """The oracle's update_cache, with the reference default key_value_asymmetry=True,
+    against the reference's own update_cache: every entry's precision after every
+    append, and (configs a, b) the final FP8 codes/scales and INT4 codes/scales/zeros."""
+    g = np.load(os.path.join(GOLD, "update_cache_golden.npz"))
+    xs = np.load(os.path.join(GOLD, "quant_golden.npz"))["inp_bf16"]
+    fp8_age, int4_age, n = (int(v) for v in g[f"{name}_thresholds"])
+    ref = quant_ref.UpdateCacheRef(fp8_age, int4_age, key_value_asymmetry=True)
+    for f in range(n):
+        if name == "d":
+            k = v = np.zeros((2, 64), np.float32)
+        else:
+            k = quant_ref.bf16_from_bits(xs[f % len(xs)])
+            v = quant_ref.bf16_from_bits(xs[(f + 7) % len(xs)])
+        ref.append(k, v)
+        for t in ("key", "value"):
+            want = [PREC[int(c)] for c in g[f"{name}_{t}_hist"][f, :f + 1]]
+            assert ref.precisions(t) == want, (name, f, t)
+    if name == "d":
+        return
+    for t in ("key", "value"):
+        for i, e in enumerate(ref.entries[t]):
+            if e["precision"] == "fp8":
+                np.testing.assert_array_equal(e["codes"], g[f"{name}_{t}_fp8_codes"][i])
+                assert quant_ref.bf16_bits(np.float32(e["scale"])) == g[f"{name}_{t}_fp8_scale_bf16"][i]
+            elif e["precision"] == "int4":
+                np.testing.assert_array_equal(e["packed"].reshape(-1), g[f"{name}_{t}_i4_packed"][i])
+                np.testing.assert_array_equal(e["scale"], g[f"{name}_{t}_i4_scale"][i])
+                np.testing.assert_array_equal(e["zero"], g[f"{name}_{t}_i4_zero"][i])
