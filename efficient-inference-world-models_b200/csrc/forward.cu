@@ -29,6 +29,9 @@ size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 struct Layout {
   size_t resid, hbuf, qkv, attn, mlp, cols, emb, h1a, silu, mod, cnt, total;
   size_t cnt_bytes;  // row-block counters of the residual GEMMs' LayerNorm tails
+  // split-K ordering counters of the residual GEMMs, right after the row-block counters:
+  // per sub-block two launches (out-proj, fc2) of at most ceil(M/128) x 8 tiles x 8 warps
+  size_t flag_words_per_launch;
 };
 
 // Row-block counters (one per 128-row block), zeroed at the start of every forward.
@@ -61,7 +64,8 @@ Layout layout_for(int F, int depth) {
   L.silu = take(static_cast<size_t>(F) * OASIS_HIDDEN * 2);
   L.mod = take(static_cast<size_t>(F) * mod_ld * 4);
   L.cnt_bytes = static_cast<size_t>(2 * depth) * kCountersPerSub * row_blocks(M) * 4;
-  L.cnt = take(L.cnt_bytes);
+  L.flag_words_per_launch = row_blocks(M) * 8 * 8;  // splits use tiles N >= 128 (<= 8 of them)
+  L.cnt = take(L.cnt_bytes + static_cast<size_t>(2 * depth) * 2 * L.flag_words_per_launch * 4);
   L.total = off;
   return L;
 }
@@ -84,6 +88,8 @@ struct oasis_plan {
   // out-proj, fc1, fc2 and the next QKV of a sub-block run as one chained launch
   // (gemm_chain_kernel) when all of them use CTA-pair 256-wide tiles
   bool chain = false;
+  // bytes of row-block counters and split-K counters zeroed at the start of a forward
+  size_t zero_bytes = 0;
   // timing
   bool timing = false;
   std::vector<cudaEvent_t> ev;
@@ -119,12 +125,15 @@ T* at(oasis_plan* p, size_t off) {
   return reinterpret_cast<T*>(p->ws + off);
 }
 
-// A projection GEMM over the M token rows: tile shape from choose_tiles.
+// A projection GEMM over the M token rows: tile shape from choose_tiles; the residual
+// GEMMs (out-proj, fc2) may split K.
 int make_proj(GemmOperands* g, const void* A, long long lda, const void* B, long long ldb, int M,
-              int N, int K) {
-  int bn = 256, ctas = 1;
-  choose_tiles(M, N, &bn, &ctas);
-  return make_gemm_operands(g, A, lda, B, ldb, M, N, K, bn, ctas);
+              int N, int K, bool residual = false) {
+  int bn = 256, ctas = 1, splits = 1;
+  choose_tiles(M, N, K, residual, &bn, &ctas, &splits);
+  if (int s = make_gemm_operands(g, A, lda, B, ldb, M, N, K, bn, ctas)) return s;
+  g->splits = splits;
+  return OASIS_OK;
 }
 
 int run_forward(oasis_plan* p, const float* x, const int64_t* t, const float* act, float* v,
@@ -142,12 +151,15 @@ int run_forward(oasis_plan* p, const float* x, const int64_t* t, const float* ac
   unsigned int* counters = at<unsigned int>(p, p->L.cnt);
   const size_t nblk = row_blocks(static_cast<size_t>(M));
   {
-    cudaError_t ce = cudaMemsetAsync(counters, 0, p->L.cnt_bytes, s);
+    cudaError_t ce = cudaMemsetAsync(counters, 0, p->zero_bytes, s);
     if (ce != cudaSuccess) return cuda_status(ce, "cudaMemsetAsync(row-block counters)");
   }
   // the residual GEMMs (out-proj, fc2) end with the LayerNorm + modulate that feeds the
   // next GEMM: shift/scale rows and counter slice for launch k
   auto cnt = [&](int j, int c) { return counters + (static_cast<size_t>(j) * kCountersPerSub + c) * nblk; };
+  // split-K counters of launch r (0 out-proj, 1 fc2) of sub-block j
+  unsigned int* flags0 = counters + p->L.cnt_bytes / 4;
+  auto flags = [&](int j, int r) { return flags0 + (static_cast<size_t>(j) * 2 + r) * p->L.flag_words_per_launch; };
   auto ln_tail = [&](EpiParams& ep, const float* shift, unsigned int* tiles_done) {
     ep.ln_out = static_cast<__nv_bfloat16*>(hbuf);
     ep.ln_shift = shift;
@@ -260,6 +272,7 @@ int run_forward(oasis_plan* p, const float* x, const int64_t* t, const float* ac
     eo.bias = sw.out_b;
     eo.gate = modj + 2 * OASIS_HIDDEN;
     eo.gate_ld = mld;
+    eo.split_flags = flags(j, 0);
     ln_tail(eo, modj + 3 * OASIS_HIDDEN, cnt(j, 0));
     EpiParams e1{};  // mlp = GELU(h W_1^T + b_1)
     e1.out = mlp;
@@ -271,6 +284,7 @@ int run_forward(oasis_plan* p, const float* x, const int64_t* t, const float* ac
     e2.bias = sw.fc2_b;
     e2.gate = modj + 5 * OASIS_HIDDEN;
     e2.gate_ld = mld;
+    e2.split_flags = flags(j, 1);
     ln_tail(e2, modj + OASIS_ADA_PER_SUB, cnt(j, 3));
     Timer tm(p, s, kFamGemm);
     if (chain) {
@@ -378,7 +392,7 @@ int plan_init(oasis_plan* p, const oasis_dit_weights_t* w, int batch, int frames
     if (!st) st = set_gemm_output(&p->qkv[j], p->ws + L.qkv, 3 * OASIS_HIDDEN, false);
     if (!st)
       st = make_proj(&p->out[j], p->ws + L.attn, OASIS_HIDDEN, s.out_w, OASIS_HIDDEN, M, OASIS_HIDDEN,
-                     OASIS_HIDDEN);
+                     OASIS_HIDDEN, true);
     if (!st) st = set_gemm_output(&p->out[j], p->ws + L.resid, OASIS_HIDDEN, true);
     if (!st)
       st = make_proj(&p->fc1[j], p->ws + L.hbuf, OASIS_HIDDEN, s.fc1_w, OASIS_HIDDEN, M,
@@ -386,10 +400,19 @@ int plan_init(oasis_plan* p, const oasis_dit_weights_t* w, int batch, int frames
     if (!st) st = set_gemm_output(&p->fc1[j], p->ws + L.mlp, OASIS_MLP_HIDDEN, false);
     if (!st)
       st = make_proj(&p->fc2[j], p->ws + L.mlp, OASIS_MLP_HIDDEN, s.fc2_w, OASIS_MLP_HIDDEN, M,
-                     OASIS_HIDDEN, OASIS_MLP_HIDDEN);
+                     OASIS_HIDDEN, OASIS_MLP_HIDDEN, true);
     if (!st) st = set_gemm_output(&p->fc2[j], p->ws + L.resid, OASIS_HIDDEN, true);
   }
   if (st) return st;
+  // zeroed per forward: the row-block counters, and split-K counters if any launch splits
+  p->zero_bytes = L.cnt_bytes;
+  for (int j = 0; j < 2 * w->depth; ++j)
+    if (p->out[j].splits > 1 || p->fc2[j].splits > 1) {
+      if (split_flag_count(p->out[j]) > L.flag_words_per_launch ||
+          split_flag_count(p->fc2[j]) > L.flag_words_per_launch)
+        return fail(OASIS_ERR_UNSUPPORTED, "oasis_plan_create: split-K counters exceed their region");
+      p->zero_bytes = L.cnt_bytes + static_cast<size_t>(2 * w->depth) * 2 * L.flag_words_per_launch * 4;
+    }
   p->chain = true;
   for (int j = 0; j < 2 * w->depth; ++j)
     for (const GemmOperands* g : {&p->qkv[j], &p->out[j], &p->fc1[j], &p->fc2[j]})

@@ -115,21 +115,30 @@ int launch_one(const GemmOperands& g, const EpiParams& ep, cudaStream_t stream, 
     if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(gemm)");
     configured = true;
   }
-  const int tiles = ((g.M + kGemmBM * CTAS - 1) / (kGemmBM * CTAS)) * ((g.N + BN - 1) / BN);
+  const int tiles = ((g.M + kGemmBM * CTAS - 1) / (kGemmBM * CTAS)) * ((g.N + BN - 1) / BN) *
+                    (g.splits > 1 ? g.splits : 1);
   int units = num_sms();
   if constexpr (CTAS == 2) units = max_pairs<BN, EPI>();
   if (max_ctas > 0 && max_ctas / CTAS < units) units = max_ctas / CTAS > 0 ? max_ctas / CTAS : 1;
   if (tiles < units) units = tiles;
   if (epi_uses_tma(EPI) && !g.has_d)
     return fail(OASIS_ERR_INVALID_ARG, "GEMM epilogue needs an output tensor map");
+  EpiParams epk = ep;
+  epk.k_splits = 1;
+  if (g.splits > 1) {
+    if (EPI != kEpiGateResid || CTAS != 1 || !ep.split_flags || (g.K / kGemmBK) % g.splits)
+      return fail(OASIS_ERR_INVALID_ARG, "GEMM K split needs the residual epilogue, single CTAs, "
+                                         "split counters and whole k-blocks per split");
+    epk.k_splits = g.splits;
+  }
   cudaError_t e;
   if constexpr (CTAS == 2)
     e = launch_pdl_cluster(gemm_tcgen05_kernel<BN, EPI, CTAS>, dim3(units * CTAS), dim3(kGemmThreads),
                            S::kSmemBytes, stream, CTAS, g.a, g.b, g.d, g.M, g.N, g.K,
-                           prefetch_flags(g), ep);
+                           prefetch_flags(g), epk);
   else
     e = launch_pdl(gemm_tcgen05_kernel<BN, EPI, CTAS>, dim3(units), dim3(kGemmThreads), S::kSmemBytes,
-                   stream, g.a, g.b, g.d, g.M, g.N, g.K, prefetch_flags(g), ep);
+                   stream, g.a, g.b, g.d, g.M, g.N, g.K, prefetch_flags(g), epk);
   if (e != cudaSuccess) return cuda_status(e, "gemm_tcgen05_kernel");
   return OASIS_OK;
 }
@@ -170,8 +179,8 @@ int make_gemm_operands(GemmOperands* g, const void* A, long long lda, const void
                        int M, int N, int K, int bn, int ctas) {
   if (M <= 0 || N <= 0 || K <= 0) return fail(OASIS_ERR_INVALID_ARG, "GEMM sizes must be positive");
   if (K % kGemmBK) return fail(OASIS_ERR_UNSUPPORTED, "GEMM K must be a multiple of 64");
-  if (bn != 32 && bn != 64 && bn != 128 && bn != 256)
-    return fail(OASIS_ERR_UNSUPPORTED, "GEMM tile N must be 32, 64, 128 or 256");
+  if (bn != 32 && bn != 64 && bn != 128 && bn != 192 && bn != 256)
+    return fail(OASIS_ERR_UNSUPPORTED, "GEMM tile N must be 32, 64, 128, 192 or 256");
   if (ctas != 1 && !(ctas == 2 && bn == 256))
     return fail(OASIS_ERR_UNSUPPORTED, "GEMM CTA pairs need tile N 256");
   *g = GemmOperands{};
@@ -183,6 +192,7 @@ int make_gemm_operands(GemmOperands* g, const void* A, long long lda, const void
   g->K = K;
   g->bn = bn;
   g->ctas = ctas;
+  g->splits = 1;
   g->has_d = false;
   g->b_is_weight = false;
   return OASIS_OK;
@@ -207,6 +217,7 @@ int launch_gemm(const GemmOperands& g, int epi, const EpiParams& ep, cudaStream_
     case 32: return dispatch_epi<32, 1>(g, epi, ep, stream, max_ctas);
     case 64: return dispatch_epi<64, 1>(g, epi, ep, stream, max_ctas);
     case 128: return dispatch_epi<128, 1>(g, epi, ep, stream, max_ctas);
+    case 192: return dispatch_epi<192, 1>(g, epi, ep, stream, max_ctas);
     case 256: return dispatch_epi<256, 1>(g, epi, ep, stream, max_ctas);
   }
   return fail(OASIS_ERR_UNSUPPORTED, "GEMM tile N");
@@ -267,25 +278,81 @@ int launch_chain(const ChainStep* steps, int n, cudaStream_t stream) {
   return OASIS_OK;
 }
 
-// CTA pairs on 256 x 256 tiles when there are about as many tiles as SM pairs or more
-// (each SM then stages half the B bytes per MMA: the N = 256 main loop stays
-// tensor-bound); otherwise single CTAs with the widest tile N that still gives every
-// SM work (at least 3/4 of a wave).
-void choose_tiles(int M, int N, int* bn, int* ctas) {
+namespace {
+
+// Estimated microseconds of an M x N x K bf16 GEMM on 128*ctas x bn tiles with K split
+// `splits` ways, `slots` units resident at once (SMs, or SM pairs).  Each unit streams
+// its A rows (16 KB per k-block) and its share of the B rows (bn/ctas x 128 B) through
+// one SM (at most ~150 GB/s) and issues 2*bn tensor cycles per k-block; the whole
+// launch moves A once per N tile and B once per M tile out of L2 (~10 TB/s); ~1.5 us
+// of pipeline fill and epilogue per unit; split k waits for split k-1's reduce-adds.
+double gemm_time_us(long long M, long long N, long long K, int bn, int ctas, int splits, int slots) {
+  const double clk_ghz = 1.8, sm_gbps = 150.0, l2_gbps = 10000.0, fixed_us = 1.5;
+  const long long m_tiles = (M + 128LL * ctas - 1) / (128LL * ctas);
+  const long long n_tiles = N / bn;
+  const long long units = m_tiles * n_tiles * splits;
+  const long long waves = (units + slots - 1) / slots;
+  const double kb = static_cast<double>(K / 64 / splits);
+  const double t_load = (16384.0 + (bn / ctas) * 128.0) / (sm_gbps * 1e3);
+  const double t_mma = 2.0 * bn / (clk_ghz * 1e3);
+  const double t_unit = kb * (t_load > t_mma ? t_load : t_mma) + fixed_us;
+  const double l2_bytes = 2.0 * M * K * n_tiles + 2.0 * N * K * m_tiles;
+  const double t_l2 = l2_bytes / (l2_gbps * 1e3) + fixed_us;
+  const double t = waves * t_unit > t_l2 ? waves * t_unit : t_l2;
+  return t + (splits - 1) * 0.7;
+}
+
+}  // namespace
+
+void choose_tiles(int M, int N, int K, bool allow_split, int* bn, int* ctas, int* splits) {
   const long long sms = num_sms();
-  const long long pair_m = (M + 2 * kGemmBM - 1) / (2 * kGemmBM);
-  if (N % 256 == 0 && 10 * pair_m * (N / 256) >= 9 * (sms / 2)) {
+  const int pairs = max_pairs<256, kEpiGateResid>();
+  *splits = 1;
+  if (N % 256 == 0) {
+    // CTA pairs on 256 x 256 tiles (the chained launch's tiles) where they fill the
+    // pair slots: enough tiles, and every wave at least 90 % full
+    const long long pair_m = (M + 2 * kGemmBM - 1) / (2 * kGemmBM);
+    const long long units = pair_m * (N / 256);
+    const long long waves = (units + pairs - 1) / pairs;
+    if (10 * units >= 9 * (sms / 2) && 10 * units >= 9 * waves * pairs) {
+      *bn = 256;
+      *ctas = 2;
+      return;
+    }
+  }
+  double best = 1e30;
+  *bn = 64;
+  *ctas = 1;
+  for (int b : {64, 128, 192, 256}) {
+    if (N % b) continue;
+    for (int s : {1, 2, 4}) {
+      if (s > 1 && (!allow_split || b < 128 || (K / kGemmBK) % s)) continue;
+      const double t = gemm_time_us(M, N, K, b, 1, s, static_cast<int>(sms));
+      if (t < best) {
+        best = t;
+        *bn = b;
+        *ctas = 1;
+        *splits = s;
+      }
+    }
+  }
+  if (N % 256 == 0 && gemm_time_us(M, N, K, 256, 2, 1, pairs) < best) {
     *bn = 256;
     *ctas = 2;
-    return;
+    *splits = 1;
   }
-  const long long mt = (M + kGemmBM - 1) / kGemmBM;
-  int b = 256;
-  for (; b > 64; b >>= 1)
-    if (N % b == 0 && 4 * mt * (N / b) >= 3 * sms) break;
-  while (b > 32 && N % b) b >>= 1;
-  *bn = b;
-  *ctas = 1;
+  if (N % *bn) {  // no candidate divides N: the widest power of two that does
+    int b = 256;
+    while (b > 32 && N % b) b >>= 1;
+    *bn = b;
+    *ctas = 1;
+    *splits = 1;
+  }
+}
+
+size_t split_flag_count(const GemmOperands& g) {
+  if (g.splits <= 1) return 0;
+  return static_cast<size_t>((g.M + kGemmBM - 1) / kGemmBM) * (g.N / g.bn) * kEpiWarps;
 }
 
 }  // namespace oasis
@@ -313,8 +380,8 @@ extern "C" int oasis_gemm_bf16(const void* A, const void* B, void* D, const floa
     return fail(OASIS_ERR_UNSUPPORTED, "oasis_gemm_bf16: N must be a multiple of 64 (bf16) / 32 (fp32)");
   if (!aligned16(D) || (epilogue == 0 ? (ldd % 8) : (ldd % 4)))
     return fail(OASIS_ERR_ALIGNMENT, "oasis_gemm_bf16: D must be 16-byte aligned rows");
-  int bn = 256, ctas = 1;
-  choose_tiles(M, N, &bn, &ctas);
+  int bn = 256, ctas = 1, splits = 1;
+  choose_tiles(M, N, K, false, &bn, &ctas, &splits);
   if (epilogue == 0 && bn < 64) bn = 64;  // the bf16 TMA-store box is 64 columns wide
   GemmOperands g;
   if (int s = make_gemm_operands(&g, A, lda, B, ldb, M, N, K, bn, ctas)) return s;

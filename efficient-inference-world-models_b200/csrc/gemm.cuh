@@ -64,6 +64,14 @@ struct EpiParams {
   const float* ln_scale;
   long long ln_mod_ld;
   unsigned int* ln_count;
+  // kEpiGateResid split along K (k_splits > 1, single-CTA tiles): every output tile is
+  // computed by k_splits units over equal K ranges; split s adds gate * acc_s (split 0 also
+  // gate * bias) into the residual.  The splits' reduce-adds of one tile are ordered by
+  // split_flags (one zeroed counter per output tile and epilogue warp: split s issues its
+  // reduce-adds after the counter reaches s and releases s + 1 once they completed), so
+  // the fp32 sum is formed in the same order on every run.
+  int k_splits;
+  unsigned int* split_flags;
 };
 
 constexpr int kGemmBM = 128;
@@ -81,7 +89,8 @@ struct GemmShape {
   static constexpr int kBBytes = (BN / CTAS) * kGemmBK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kStages = (192 * 1024) / kStageBytes > 8 ? 8 : (192 * 1024) / kStageBytes;
-  static constexpr int kTmemCols = 2 * BN;  // power of two >= 64 for BN in {32..256}
+  // two accumulator buffers of BN columns, allocated as a power of two >= 64
+  static constexpr int kTmemCols = 2 * BN <= 64 ? 64 : (2 * BN <= 128 ? 128 : (2 * BN <= 256 ? 256 : 512));
   static constexpr int kBarBytes = 1024;
   static constexpr int kEpiBytes = kEpiWarps * kEpiBufBytes;  // one TMA box per epilogue warp
   static constexpr int kSmemBytes =
@@ -205,7 +214,8 @@ __device__ __forceinline__ void epilogue_rows(const EpiParams& p, int M, int m, 
 // Elementwise math of the TMA epilogues on one thread's row segment (row m, columns
 // n0..n0+31), in registers.
 template <int EPI>
-__device__ __forceinline__ void epilogue_math(const EpiParams& p, int m, int n0, float (&v)[32]) {
+__device__ __forceinline__ void epilogue_math(const EpiParams& p, int m, int n0, float (&v)[32],
+                                              bool bias_on = true) {
   if (EPI == kEpiBiasGelu || EPI == kEpiStoreF32Bias) {
     if (EPI == kEpiStoreF32Bias && !p.bias) return;
     const float4* b4 = reinterpret_cast<const float4*>(p.bias + n0);
@@ -244,7 +254,7 @@ __device__ __forceinline__ void epilogue_math(const EpiParams& p, int m, int n0,
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const float4 g = g4[j];
-      const float4 b = b4[j];
+      const float4 b = bias_on ? b4[j] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
       v[4 * j + 0] = g.x * (v[4 * j + 0] + b.x);
       v[4 * j + 1] = g.y * (v[4 * j + 1] + b.y);
       v[4 * j + 2] = g.z * (v[4 * j + 2] + b.z);
@@ -299,8 +309,11 @@ template <int BN, int EPI, typename Release>
 __device__ __forceinline__ void epilogue_tile(const EpiParams& ep, const CUtensorMap* tmD, int M,
                                               int N, uint32_t taddr, int m0, int n0, int quarter,
                                               int half, int lane, uint8_t* buf, int& nbuf,
-                                              uint8_t* staging, Release release) {
+                                              uint8_t* staging, Release release, int split = 0,
+                                              unsigned int* split_flag = nullptr,
+                                              bool publish = false) {
   using G = EpiGeom<BN, EPI>;
+  bool ordered = split_flag == nullptr || split == 0;  // may issue its reduce-adds
   constexpr int COLS = G::COLS, NBLK = G::NBLK;
   const int m_row = m0 + quarter * 32 + lane;  // this thread's row
   const bool rows_live = m0 + quarter * 32 < M;
@@ -310,6 +323,7 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& ep, const CUtenso
   const int last_blk = (NBLK - 1 - half) >= 0 ? ((NBLK - 1 - half) / 2) * 2 + half : -1;
   if (last_blk < 0) {  // owns no columns of this tile
     release();
+    if (publish && lane == 0) red_release_add(split_flag, 1u);
     return;
   }
 #pragma unroll 1
@@ -331,9 +345,9 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& ep, const CUtenso
       if (lane == 0) bulk_wait_read<0>();
       __syncwarp();
     }
-    epilogue_math<EPI>(ep, m_op, nb, v);
+    epilogue_math<EPI>(ep, m_op, nb, v, split == 0);
     if (COLS == 64) {
-      epilogue_math<EPI>(ep, m_op, nb + 32, w);
+      epilogue_math<EPI>(ep, m_op, nb + 32, w, split == 0);
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         st_swizzled(box, lane, c, make_uint4(pack_bf16x2(v[8 * c + 0], v[8 * c + 1]),
@@ -354,6 +368,11 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& ep, const CUtenso
     fence_async_smem();
     __syncwarp();
     if (lane == 0) {
+      if (!ordered) {  // the previous split's reduce-adds of these rows must be complete
+        wait_count_geq(split_flag, static_cast<unsigned>(split));
+        fence_async_global();
+        ordered = true;
+      }
       if (EPI == kEpiGateResid)
         tma_reduce_add_2d(tmD, box, nb, m0 + quarter * 32);
       else
@@ -361,6 +380,11 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& ep, const CUtenso
       bulk_commit();
     }
     if (!staging) ++nbuf;
+  }
+  if (publish && lane == 0) {  // next split of this tile: these reduce-adds are complete
+    bulk_wait<0>();
+    fence_async_global();
+    red_release_add(split_flag, 1u);
   }
 }
 
@@ -437,8 +461,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int num_units = static_cast<int>(gridDim.x) / CTAS;
   const int num_m = (M + TILE_M - 1) / TILE_M;
   const int num_n = (N + BN - 1) / BN;
-  const int num_tiles = num_m * num_n;
-  const int num_kb = K / kGemmBK;
+  // kEpiGateResid may split K: unit = (output tile, split), the split fastest
+  const int splits = (EPI == kEpiGateResid && CTAS == 1 && ep.k_splits > 1) ? ep.k_splits : 1;
+  const int num_tiles = num_m * num_n * splits;
+  const int num_kb = K / kGemmBK / splits;  // k-blocks of one unit
+  auto unit_m0 = [&](int t) { return ((t / splits) % num_m) * TILE_M; };
+  auto unit_n0 = [&](int t) { return ((t / splits) / num_m) * BN; };
+  auto unit_kb0 = [&](int t) { return (t % splits) * num_kb; };
   const int a_row0 = static_cast<int>(rank) * kGemmBM;
   const int b_row0 = static_cast<int>(rank) * (BN / CTAS);
 
@@ -495,36 +524,39 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       int pre = 0;
       const bool pre_a = (prefetch_b & 2) != 0;
       if (prefetch_b && unit < num_tiles) {
-        const int m0 = (unit % num_m) * TILE_M;
-        const int n0 = (unit / num_m) * BN;
+        const int m0 = unit_m0(unit);
+        const int n0 = unit_n0(unit);
+        const int kb0 = unit_kb0(unit);
         pre = num_kb < STAGES ? num_kb : STAGES;
         for (int kb = 0; kb < pre; ++kb) {
           if (leader) mbar_arrive_expect_tx(&full_bar[kb], CTAS * S::kStageBytes);
           if (pre_a)
-            load(smem + kb * S::kStageBytes, &tmA, kb, kb * kGemmBK, m0 + a_row0);
+            load(smem + kb * S::kStageBytes, &tmA, kb, (kb0 + kb) * kGemmBK, m0 + a_row0);
           else
-            load(smem + kb * S::kStageBytes + S::kABytes, &tmB, kb, kb * kGemmBK, n0 + b_row0);
+            load(smem + kb * S::kStageBytes + S::kABytes, &tmB, kb, (kb0 + kb) * kGemmBK, n0 + b_row0);
         }
       }
       pdl_wait();
       for (int tile = unit; tile < num_tiles && !*abort_flag; tile += num_units) {
-        const int m0 = (tile % num_m) * TILE_M;
-        const int n0 = (tile / num_m) * BN;
+        const int m0 = unit_m0(tile);
+        const int n0 = unit_n0(tile);
+        const int kb0 = unit_kb0(tile);
         for (int kb = 0; kb < num_kb; ++kb) {
           uint8_t* sa = smem + stage * S::kStageBytes;
           uint8_t* sb = sa + S::kABytes;
+          const int kc = (kb0 + kb) * kGemmBK;
           if (pre > 0) {  // stage already armed and its weight tile in flight
             --pre;
             if (pre_a)
-              load(sb, &tmB, stage, kb * kGemmBK, n0 + b_row0);
+              load(sb, &tmB, stage, kc, n0 + b_row0);
             else
-              load(sa, &tmA, stage, kb * kGemmBK, m0 + a_row0);
+              load(sa, &tmA, stage, kc, m0 + a_row0);
           } else {
             // the stage is free once the MMAs that read it (in both CTAs) have completed
             if (!mbar_wait(&empty_bar[stage], phase ^ 1)) { *abort_flag = 1; break; }
             if (leader) mbar_arrive_expect_tx(&full_bar[stage], CTAS * S::kStageBytes);
-            load(sa, &tmA, stage, kb * kGemmBK, m0 + a_row0);
-            load(sb, &tmB, stage, kb * kGemmBK, n0 + b_row0);
+            load(sa, &tmA, stage, kc, m0 + a_row0);
+            load(sb, &tmB, stage, kc, n0 + b_row0);
           }
           last_phase[stage] = static_cast<int>(phase);
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
@@ -605,8 +637,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // instead of cycling one 4 KB buffer.
     static_assert(kEpiWarps * G::kWarpTileBytes <= STAGES * S::kStageBytes, "last-tile staging");
     for (int tile = unit; tile < num_tiles && !*abort_flag; tile += num_units, ++it) {
-      const int m0 = (tile % num_m) * TILE_M + a_row0;  // this CTA's accumulator rows
-      const int n0 = (tile / num_m) * BN;
+      const int m0 = unit_m0(tile) + a_row0;  // this CTA's accumulator rows
+      const int n0 = unit_n0(tile);
+      const int split = tile % splits;
       const int acc = it & 1;
       const uint32_t acc_phase = (it >> 1) & 1;
       if (epi_uses_tma(EPI))
@@ -627,8 +660,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             mbar_arrive(&tempty_bar[acc]);
         }
       };
+      // split-K: this warp's counter of the output tile orders the splits' reduce-adds
+      unsigned int* flag = splits > 1 ? ep.split_flags + (tile / splits) * kEpiWarps + half * 4 + quarter
+                                      : nullptr;
       epilogue_tile<BN, EPI>(ep, &tmD, M, N, taddr, m0, n0, quarter, half, lane, buf, nbuf,
-                             last_tile ? smem + (warp - 2) * G::kWarpTileBytes : nullptr, release);
+                             last_tile ? smem + (warp - 2) * G::kWarpTileBytes : nullptr, release,
+                             split, flag, flag != nullptr && split + 1 < splits);
     }
     if (epi_uses_tma(EPI) && lane == 0) bulk_wait<0>();  // all stores complete before exit
     __syncwarp();
@@ -641,13 +678,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (warp == 2 && lane == 0 && !*abort_flag) {
         const int nblk = (M + kGemmBM - 1) / kGemmBM;
         for (int tile = unit; tile < num_tiles; tile += num_units) {
-          const int q = ((tile % num_m) * TILE_M + a_row0) / kGemmBM;
+          const int q = (unit_m0(tile) + a_row0) / kGemmBM;
           if (q < nblk) red_release_add(ep.ln_count + q, 1u);
         }
       }
       // consume, staging rows in the now idle operand stages (16 KB per warp)
       static_assert(kEpiWarps * kLnRowsPerWarp * OASIS_HIDDEN * 4 <= STAGES * S::kStageBytes, "LN staging");
-      ln_rows_phase(ep, M, static_cast<unsigned>(num_n), warp - 2, lane,
+      ln_rows_phase(ep, M, static_cast<unsigned>(num_n * splits), warp - 2, lane,
                     reinterpret_cast<float4*>(smem + (warp - 2) * (kLnRowsPerWarp * OASIS_HIDDEN * 4)),
                     nullptr);
     }
@@ -1003,16 +1040,22 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 struct GemmOperands {
   CUtensorMap a, b, d;
   int M, N, K, bn;
-  int ctas;  // 1: one CTA per 128 x bn tile; 2: CTA pairs on 256 x 256 tiles
+  int ctas;    // 1: one CTA per 128 x bn tile; 2: CTA pairs on 256 x 256 tiles
+  int splits;  // > 1: K split into this many equal ranges (residual epilogue only)
   bool has_d;
   bool b_is_weight;  // B is never written by another kernel: may be prefetched early
   bool a_is_weight;  // the same for A (swap-AB GEMMs)
 };
 int make_gemm_operands(GemmOperands* g, const void* A, long long lda, const void* B, long long ldb,
                        int M, int N, int K, int bn, int ctas = 1);
-// Tile shape for an M x N x K projection on this GPU: CTA pairs where the tile count
-// fills the SM pairs, single CTAs otherwise.
-void choose_tiles(int M, int N, int* bn, int* ctas);
+// Tile shape for an M x N x K projection on this GPU: CTA pairs on 256 x 256 tiles where
+// the tile count fills the SM pairs in every wave; otherwise the (tile N, pairs or single
+// CTAs, K splits) of least estimated time (K splits only where allow_split: the residual
+// epilogue, whose reduce-add is linear in the accumulator).
+void choose_tiles(int M, int N, int K, bool allow_split, int* bn, int* ctas, int* splits);
+// Counters (unsigned ints, zeroed before the launch) a split-K launch of `g` orders its
+// reduce-adds with: one per output tile and epilogue warp.
+size_t split_flag_count(const GemmOperands& g);
 // Output tensor map for the TMA epilogues: D [M][N] with leading dim ldd, bf16 or fp32.
 int set_gemm_output(GemmOperands* g, void* D, long long ldd, bool f32);
 int launch_gemm(const GemmOperands& g, int epi, const EpiParams& ep, cudaStream_t stream,

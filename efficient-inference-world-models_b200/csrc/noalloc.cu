@@ -67,13 +67,17 @@ extern "C" int oasis_dit_forward_noalloc(const oasis_dit_weights_t* w, int batch
 
   std::lock_guard<std::mutex> lock(g_noalloc_mutex);
   NoAllocState& st = g_noalloc[dev];
-  if (!st.scratch) {
-    // first call on this device (the device is current here): the array's device
-    // address; the host-side name of a __device__ array is not a device pointer
-    e = cudaGetSymbolAddress(&st.scratch, g_noalloc_scratch);
-    if (e != cudaSuccess) {
-      st.scratch = nullptr;
-      return cuda_status(e, "oasis_dit_forward_noalloc(cudaGetSymbolAddress)");
+  {
+    // the array's device address on this device (current here); the host-side name of a
+    // __device__ array is not a device pointer.  Looked up on every call: after a device
+    // reset or in a new context the array can live elsewhere, and the cached plan's
+    // tensor maps point into it, so a changed address rebuilds the plan.
+    void* addr = nullptr;
+    e = cudaGetSymbolAddress(&addr, g_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_status(e, "oasis_dit_forward_noalloc(cudaGetSymbolAddress)");
+    if (addr != st.scratch) {
+      st.scratch = addr;
+      st.plan_valid = false;
     }
   }
   if (!st.plan_valid || st.key_batch != batch || st.key_frames != frames ||

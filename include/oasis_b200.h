@@ -196,8 +196,10 @@ int oasis_plan_get_timing(oasis_plan_t* plan, float* ms_per_family, int* launche
  * inputs and outputs, and uses as scratch a fixed 17 MiB file-scope device array of
  * this library, which every GPU that loads the library holds until the process exits.
  * Limit: batch * frames <= OASIS_NOALLOC_MAX_FRAMES; larger shapes are rejected with
- * OASIS_ERR_UNSUPPORTED.  The first call on a device looks up that array's device
- * address (cudaGetSymbolAddress), so make that first call before any stream capture.
+ * OASIS_ERR_UNSUPPORTED.  Each call looks up that array's device address on the current
+ * device (cudaGetSymbolAddress; after a device reset it may have moved, and the cached
+ * launch descriptors are rebuilt); the first call on a device also sets up those
+ * descriptors, so make that first call before any stream capture.
  * Calls share the one array: calls that overlap on the GPU (other streams, other host
  * threads) race.  No scratch byte has to start at zero: every byte the forward reads
  * is written earlier in the same call.  No counterpart in the reference (it has no
