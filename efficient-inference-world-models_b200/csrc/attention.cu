@@ -594,50 +594,69 @@ __global__ void __launch_bounds__(kTpWarps * 32)
 
 // ----------------------------------------------------------------------------------
 // temporal attention of ONE query frame over cached frames (the incremental forward):
-// one CTA per (session, token, 8 heads), one warp per head, one lane per key frame.
+// one CTA per (session, token, 8 heads), one warp per head, tensor cores (mma.sync
+// m16n8k16, f16 operands, fp32 accumulation) with the query in row 0.
 // ----------------------------------------------------------------------------------
-// Warp 0 issues one bulk copy per cached row (keys and values each in their slot's kind:
-// 1024 B bf16, 512 B FP8 codes, 256 B INT4 codes for 8 heads) and per row of scales,
-// plus the live Q, K and V rows, on two mbarriers (Q + keys, values), so the scores
-// start while the values are still in flight.  Scores: lane l accumulates
-// q[2l..2l+1] . k_j[2l..2l+1] for every key row j (each row read once, consecutive lanes
-// on consecutive bytes, dequantised in registers), then a 5-stage butterfly
-// transpose-reduce leaves the score of key l in lane l.  Softmax over the lanes with
-// shuffles; P is rounded to bf16 as the tensor-core path rounds it; O (dims 2l, 2l+1)
-// = sum_j bf16(p_j) v_j.  Memory-bound: the cached K/V bytes of one (session, token,
-// head group) move once.
+// Warp 0 brings every cached key and value row (8 heads: 1024 B bf16, 512 B FP8 codes,
+// 256 B INT4 codes), their scales and the live q/k/v rows into shared memory by bulk
+// copies on two mbarriers (q + keys, values), so the scores start while the values are
+// in flight.  The quantised codes are never expanded element by element: FP8 codes
+// become f16 by one cvt per pair (exact), INT4 codes by the 1024-offset f16 trick
+// (exact), bf16 rows by f32 -> f16 (exact in f16's normal range), and the per-frame
+// FP8 scale, the per-(token, head) INT4 scale and zero are applied to the fp32 scores
+// (s_j = scale_j * q.c_j [+ zero_j * sum(q)]) and to the probabilities
+// (p'_j = p_j * scale_j / max scale, plus sum_j p_j zero_j for INT4 values).  The head
+// dims are permuted inside each k-step so a thread's 16 dims of a key row are one
+// 16-byte load, and the output dims so its 8 dims of a value row are one load; the
+// row strides keep both load patterns free of shared-memory bank conflicts.
 constexpr int kDecHeads = 8;
 constexpr int kDecThreads = kDecHeads * 32;
 constexpr int kDecMaxSmem = 96 * 1024;
 
 struct DecodeLayout {
-  // byte offsets in dynamic shared memory: codes of cached slot s (keys, values) and its
-  // scales (FP8: 8 bf16; INT4: 8 fp16 scales then 8 fp16 zeros)
-  uint32_t k_row[OASIS_MAX_FRAMES], v_row[OASIS_MAX_FRAMES];
-  uint32_t k_aux[OASIS_MAX_FRAMES], v_aux[OASIS_MAX_FRAMES];
-  uint32_t live;             // live Q | K | V rows of the query frame, 1 KB each
-  uint32_t k_bytes, v_bytes; // bytes expected on the two barriers
+  uint32_t k_base, v_base;      // cached rows: slot s at base + s * stride
+  uint32_t k_stride, v_stride;
+  uint32_t k_aux, v_aux;        // per slot 32 B: FP8 8 bf16 scales; INT4 8 fp16 scales, 8 fp16 zeros
+  uint32_t live;                // q | k | v rows of the query frame, 1 KB each
+  uint32_t k_bytes, v_bytes;    // bytes expected on the two barriers
   uint32_t total;
-  int live_kv;               // the query frame's own K/V is key n_past (n_kv = n_past + 1)
+  unsigned long long k_kinds, v_kinds;  // 2 bits per cached slot
+  int live_kv;                  // the query frame's own K/V is key n_past
 };
 
-// Dequantised elements 2*lane, 2*lane+1 of head hh in one staged row of 8 heads.
-__device__ __forceinline__ float2 decode_pair(const uint8_t* row, const uint8_t* aux, int kind, int hh,
-                                              int lane) {
-  if (kind == OASIS_KV_BF16) {
-    const uint32_t w = *reinterpret_cast<const uint32_t*>(row + hh * 128 + lane * 4);
-    return make_float2(bf16_lo(w), bf16_hi(w));
-  }
-  if (kind == OASIS_KV_FP8) {
-    const uint32_t c = *reinterpret_cast<const uint16_t*>(row + hh * 64 + lane * 2);
-    const float scale = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(aux)[hh]);
-    const float2 f = e4m3x2_to_float2(c);
-    return make_float2(dq_fp8(f.x, scale), dq_fp8(f.y, scale));
-  }
-  const uint32_t byte = row[hh * 32 + lane];
-  const float scale = __half2float(reinterpret_cast<const __half*>(aux)[hh]);
-  const float zero = __half2float(reinterpret_cast<const __half*>(aux)[kDecHeads + hh]);
-  return make_float2(dq_int4(byte >> 4, scale, zero), dq_int4(byte & 0xFu, scale, zero));
+__device__ __forceinline__ int decode_kind(unsigned long long kinds, int j) {
+  return static_cast<int>((kinds >> (2 * j)) & 3ull);
+}
+__device__ __forceinline__ uint32_t f16x2_e4m3x2(uint32_t two_codes) {
+  uint32_t h;
+  const uint16_t v = static_cast<uint16_t>(two_codes);
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h) : "h"(v));
+  return h;
+}
+__device__ __forceinline__ uint32_t f16x2_bf16x2(uint32_t w) {
+  uint32_t h;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(h) : "f"(bf16_hi(w)), "f"(bf16_lo(w)));
+  return h;
+}
+// one packed byte of two INT4 codes (element 2i high) -> f16x2 (high nibble in the low half)
+__device__ __forceinline__ uint32_t f16x2_nibbles(uint32_t byte) {
+  const uint32_t biased = ((byte >> 4) & 0xFu) | ((byte & 0xFu) << 16) | 0x64006400u;  // 1024 + code
+  uint32_t h;
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(h) : "r"(biased), "r"(0x64006400u));
+  return h;
+}
+__device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
+  uint32_t h;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(h) : "f"(hi), "f"(lo));
+  return h;
+}
+__device__ __forceinline__ void mma_f16_16816(float (&c)[4], uint32_t a0, uint32_t a2, uint32_t b0,
+                                              uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
 }
 
 __global__ void __launch_bounds__(kDecThreads)
@@ -669,24 +688,24 @@ __global__ void __launch_bounds__(kDecThreads)
       for (int which = 0; which < 2; ++which) {
         const KvTensor& t = kv.t[which];
         uint64_t* bar = &bars[which];
-        const uint32_t row_off = which ? lay.v_row[s] : lay.k_row[s];
-        const uint32_t aux_off = which ? lay.v_aux[s] : lay.k_aux[s];
+        uint8_t* row = sm_dec + (which ? lay.v_base + s * lay.v_stride : lay.k_base + s * lay.k_stride);
+        uint8_t* aux = sm_dec + (which ? lay.v_aux : lay.k_aux) + s * 32;
         const int kind = t.kind[s];
         if (kind == OASIS_KV_BF16) {
           const long long page = kv_page(b, kv.layers, layer, t.n_bf16, t.index[s]);
-          bulk_load(sm_dec + row_off, t.bf16 + (page * OASIS_TOKENS + p) * OASIS_HIDDEN + hg * kDecHeads * 64,
+          bulk_load(row, t.bf16 + (page * OASIS_TOKENS + p) * OASIS_HIDDEN + hg * kDecHeads * 64,
                     kDecHeads * 128, bar);
         } else if (kind == OASIS_KV_FP8) {
           const long long page = kv_page(b, kv.layers, layer, t.n_fp8, t.index[s]);
-          bulk_load(sm_dec + row_off, t.fp8 + (page * OASIS_TOKENS + p) * OASIS_HIDDEN + hg * kDecHeads * 64,
+          bulk_load(row, t.fp8 + (page * OASIS_TOKENS + p) * OASIS_HIDDEN + hg * kDecHeads * 64,
                     kDecHeads * 64, bar);
-          bulk_load(sm_dec + aux_off, t.fp8_scale + page * OASIS_HEADS + hg * kDecHeads, 16, bar);
+          bulk_load(aux, t.fp8_scale + page * OASIS_HEADS + hg * kDecHeads, 16, bar);
         } else {
           const long long page = kv_page(b, kv.layers, layer, t.n_int4, t.index[s]);
           const long long grp = (page * OASIS_TOKENS + p) * OASIS_HEADS + hg * kDecHeads;
-          bulk_load(sm_dec + row_off, t.int4 + grp * 32, kDecHeads * 32, bar);
-          bulk_load(sm_dec + aux_off, t.i4_scale + grp, 16, bar);
-          bulk_load(sm_dec + aux_off + 16, t.i4_zero + grp, 16, bar);
+          bulk_load(row, t.int4 + grp * 32, kDecHeads * 32, bar);
+          bulk_load(aux, t.i4_scale + grp, 16, bar);
+          bulk_load(aux + 16, t.i4_zero + grp, 16, bar);
         }
       }
     } else if (lane == 31) {  // the query frame's own q, k, v (bf16 rows of the QKV output)
@@ -698,63 +717,202 @@ __global__ void __launch_bounds__(kDecThreads)
       }
     }
   }
-  const int hh = warp;  // head within the group
+  const int hh = warp;                   // head within the group
+  const int g = lane >> 2, c = lane & 3;  // mma fragment coordinates
   if (!mbar_wait(&bars[0], 0)) return;  // timeout recorded in the device error word
-  const uint32_t qw = *reinterpret_cast<const uint32_t*>(sm_dec + lay.live + hh * 128 + lane * 4);
-  const float q0 = bf16_lo(qw), q1 = bf16_hi(qw);
-  float part[32];
+
+  // ---- q as the A operand: row 0 only (lanes 0..3); lane c holds dims 16c..16c+15,
+  // k-step ks covering dims 16c + 4ks + {0,1} (a0) and + {2,3} (a2)
+  uint32_t qa[4][2];
+  float qsum = 0.0f;
 #pragma unroll
-  for (int j = 0; j < 32; ++j) {
-    part[j] = 0.0f;
+  for (int ks = 0; ks < 4; ++ks) qa[ks][0] = qa[ks][1] = 0u;
+  if (g == 0) {
+    const uint4* qp = reinterpret_cast<const uint4*>(sm_dec + lay.live + hh * 128 + 32 * c);
+    const uint4 x0 = qp[0], x1 = qp[1];
+    const uint32_t w[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks) {
+      qa[ks][0] = f16x2_bf16x2(w[2 * ks]);
+      qa[ks][1] = f16x2_bf16x2(w[2 * ks + 1]);
+      const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&qa[ks][0]));
+      const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&qa[ks][1]));
+      qsum += (f0.x + f0.y) + (f1.x + f1.y);
+    }
+  }
+  qsum += __shfl_xor_sync(0xffffffffu, qsum, 1);
+  qsum += __shfl_xor_sync(0xffffffffu, qsum, 2);
+
+  // ---- scores: n-tile nt holds keys 8nt..8nt+7; this thread supplies key 8nt + g
+  float sacc[4][4];
+#pragma unroll
+  for (int nt = 0; nt < 4; ++nt) {
+    sacc[nt][0] = sacc[nt][1] = sacc[nt][2] = sacc[nt][3] = 0.0f;
+    const int j = 8 * nt + g;
+    uint32_t kb[4][2];
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks) kb[ks][0] = kb[ks][1] = 0u;
+    const int kind = j < n_past ? decode_kind(lay.k_kinds, j) : (j < n_kv ? OASIS_KV_BF16 : -1);
+    const uint8_t* row = j < n_past ? sm_dec + lay.k_base + j * lay.k_stride : sm_dec + lay.live + 1024;
+    if (kind == OASIS_KV_FP8) {
+      const uint4 x = *reinterpret_cast<const uint4*>(row + hh * 64 + 16 * c);
+      const uint32_t w[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks) {
+        kb[ks][0] = f16x2_e4m3x2(w[ks] & 0xFFFFu);
+        kb[ks][1] = f16x2_e4m3x2(w[ks] >> 16);
+      }
+    } else if (kind == OASIS_KV_INT4) {
+      const uint2 x = *reinterpret_cast<const uint2*>(row + hh * 32 + 8 * c);
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks) {
+        const uint32_t h = ((ks < 2) ? x.x : x.y) >> (16 * (ks & 1));
+        kb[ks][0] = f16x2_nibbles(h & 0xFFu);
+        kb[ks][1] = f16x2_nibbles((h >> 8) & 0xFFu);
+      }
+    } else if (kind == OASIS_KV_BF16) {
+      const uint4* kp = reinterpret_cast<const uint4*>(row + hh * 128 + 32 * c);
+      const uint4 x0 = kp[0], x1 = kp[1];
+      const uint32_t w[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks) {
+        kb[ks][0] = f16x2_bf16x2(w[2 * ks]);
+        kb[ks][1] = f16x2_bf16x2(w[2 * ks + 1]);
+      }
+    }
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks) mma_f16_16816(sacc[nt], qa[ks][0], qa[ks][1], kb[ks][0], kb[ks][1]);
+  }
+
+  // ---- per key (row 0: lanes 0..3 hold keys 8nt + 2c + e): scales, mask, softmax
+  float sc[8], vm[8], vz[8];
+  float mx = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int nt = i >> 1, e = i & 1;
+    const int j = 8 * nt + 2 * c + e;
+    float s = sacc[nt][e];
+    vm[i] = 0.0f;
+    vz[i] = 0.0f;
     if (j < n_past) {
-      const float2 k = decode_pair(sm_dec + lay.k_row[j], sm_dec + lay.k_aux[j], kv.t[0].kind[j], hh, lane);
-      part[j] = __fmaf_rn(q1, k.y, q0 * k.x);
-    } else if (j < n_kv) {
-      const float2 k = decode_pair(sm_dec + lay.live + 1024, nullptr, OASIS_KV_BF16, hh, lane);
-      part[j] = __fmaf_rn(q1, k.y, q0 * k.x);
+      const int kk = decode_kind(lay.k_kinds, j);
+      const uint8_t* ka = sm_dec + lay.k_aux + j * 32;
+      if (kk == OASIS_KV_FP8) {
+        s *= __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(ka)[hh]);
+      } else if (kk == OASIS_KV_INT4) {
+        s = __fmaf_rn(s, __half2float(reinterpret_cast<const __half*>(ka)[hh]),
+                      __half2float(reinterpret_cast<const __half*>(ka + 16)[hh]) * qsum);
+      }
     }
+    const bool live = j < n_kv && j <= q_pos;
+    sc[i] = live ? s : -INFINITY;
+    mx = fmaxf(mx, sc[i]);
   }
-  // butterfly transpose-reduce: after the stage of width w, lane l holds w partial sums
-  // of the keys whose bits above log2(w) equal lane l's; the last leaves key l in lane l
+  mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+  mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+  float sum = 0.0f;
 #pragma unroll
-  for (int w = 16; w >= 1; w >>= 1) {
-    const bool upper = (lane & w) != 0;
-#pragma unroll
-    for (int k = 0; k < w; ++k) {
-      const float send = upper ? part[k] : part[k + w];
-      const float keep = upper ? part[k + w] : part[k];
-      part[k] = keep + __shfl_xor_sync(0xffffffffu, send, w);
-    }
+  for (int i = 0; i < 8; ++i) {
+    const float pr = sc[i] == -INFINITY ? 0.0f : exp2f(__fmaf_rn(sc[i], scale_log2, -mx * scale_log2));
+    sum += pr;
+    sc[i] = bf16_round(pr);  // the probability as the tensor-core path rounds it
   }
-  // causal mask: the query at window position q_pos sees keys 0..q_pos
-  const bool live_key = lane < n_kv && lane <= q_pos;
-  float mx = live_key ? part[0] : -INFINITY;
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  const float pr = live_key ? exp2f(__fmaf_rn(part[0], scale_log2, -mx * scale_log2)) : 0.0f;
-  float sum = pr;
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-  const float pb = bf16_round(pr);  // the probability as the PV product sees it
+  sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+  sum += __shfl_xor_sync(0xffffffffu, sum, 2);
   if (!mbar_wait(&bars[1], 0)) return;
-  float o0 = 0.0f, o1 = 0.0f;
-#pragma unroll 4
-  for (int j = 0; j < n_past; ++j) {
-    const float pj = __shfl_sync(0xffffffffu, pb, j);
-    const float2 v = decode_pair(sm_dec + lay.v_row[j], sm_dec + lay.v_aux[j], kv.t[1].kind[j], hh, lane);
-    o0 = __fmaf_rn(pj, v.x, o0);
-    o1 = __fmaf_rn(pj, v.y, o1);
+  // value multipliers: FP8 scale, INT4 scale (its zero adds sum_j p_j zero_j), bf16 1
+  float vmax = 0.0f, corr = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int j = 8 * (i >> 1) + 2 * c + (i & 1);
+    if (j >= n_kv) continue;
+    float m = 1.0f;
+    if (j < n_past) {
+      const int vk = decode_kind(lay.v_kinds, j);
+      const uint8_t* va = sm_dec + lay.v_aux + j * 32;
+      if (vk == OASIS_KV_FP8) {
+        m = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(va)[hh]);
+      } else if (vk == OASIS_KV_INT4) {
+        m = __half2float(reinterpret_cast<const __half*>(va)[hh]);
+        vz[i] = __half2float(reinterpret_cast<const __half*>(va + 16)[hh]);
+      }
+    }
+    vm[i] = m;
+    vmax = fmaxf(vmax, m);
+    corr = __fmaf_rn(sc[i], vz[i], corr);
   }
-  if (lay.live_kv) {
-    const float pj = __shfl_sync(0xffffffffu, pb, n_past);
-    const float2 v = decode_pair(sm_dec + lay.live + 2048, nullptr, OASIS_KV_BF16, hh, lane);
-    o0 = __fmaf_rn(pj, v.x, o0);
-    o1 = __fmaf_rn(pj, v.y, o1);
+  vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 1));
+  vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 2));
+  corr += __shfl_xor_sync(0xffffffffu, corr, 1);
+  corr += __shfl_xor_sync(0xffffffffu, corr, 2);
+  const float inv_vmax = vmax > 0.0f ? 1.0f / vmax : 0.0f;
+  // P' as the A operand of the two k-steps of keys (0..15, 16..31): row 0 only
+  uint32_t pa[2][2];
+#pragma unroll
+  for (int k2 = 0; k2 < 2; ++k2) {
+    pa[k2][0] = pa[k2][1] = 0u;
+    if (g == 0) {
+      const int i0 = 4 * k2, i1 = 4 * k2 + 2;  // n-tiles 2 k2 and 2 k2 + 1
+      pa[k2][0] = pack_f16x2(sc[i0] * vm[i0] * inv_vmax, sc[i0 + 1] * vm[i0 + 1] * inv_vmax);
+      pa[k2][1] = pack_f16x2(sc[i1] * vm[i1] * inv_vmax, sc[i1 + 1] * vm[i1 + 1] * inv_vmax);
+    }
   }
-  const float inv = 1.0f / sum;
-  __nv_bfloat16* orow = out + (static_cast<long long>(b) * OASIS_TOKENS + p) * OASIS_HIDDEN +
-                        (hg * kDecHeads + hh) * 64;
-  *reinterpret_cast<uint32_t*>(orow + 2 * lane) = pack_bf16x2(o0 * inv, o1 * inv);
+
+  // ---- O = P' V: n-tile nt2 column g is output dim 8g + nt2; this thread supplies keys
+  // 16 k2 + 2c + {0, 1, 8, 9}, dims 8g..8g+7 of each
+  float oacc[8][4];
+#pragma unroll
+  for (int n2 = 0; n2 < 8; ++n2) oacc[n2][0] = oacc[n2][1] = oacc[n2][2] = oacc[n2][3] = 0.0f;
+#pragma unroll
+  for (int k2 = 0; k2 < 2; ++k2) {
+    uint32_t F[4][4];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int j = 16 * k2 + 2 * c + (r & 1) + 8 * (r >> 1);
+      const int kind = j < n_past ? decode_kind(lay.v_kinds, j) : (j < n_kv ? OASIS_KV_BF16 : -1);
+      const uint8_t* row = j < n_past ? sm_dec + lay.v_base + j * lay.v_stride : sm_dec + lay.live + 2048;
+      F[r][0] = F[r][1] = F[r][2] = F[r][3] = 0u;
+      if (kind == OASIS_KV_FP8) {
+        const uint2 x = *reinterpret_cast<const uint2*>(row + hh * 64 + 8 * g);
+        F[r][0] = f16x2_e4m3x2(x.x & 0xFFFFu);
+        F[r][1] = f16x2_e4m3x2(x.x >> 16);
+        F[r][2] = f16x2_e4m3x2(x.y & 0xFFFFu);
+        F[r][3] = f16x2_e4m3x2(x.y >> 16);
+      } else if (kind == OASIS_KV_INT4) {
+        const uint32_t x = *reinterpret_cast<const uint32_t*>(row + hh * 32 + 4 * g);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) F[r][q] = f16x2_nibbles((x >> (8 * q)) & 0xFFu);
+      } else if (kind == OASIS_KV_BF16) {
+        const uint4 x = *reinterpret_cast<const uint4*>(row + hh * 128 + 16 * g);
+        F[r][0] = f16x2_bf16x2(x.x);
+        F[r][1] = f16x2_bf16x2(x.y);
+        F[r][2] = f16x2_bf16x2(x.z);
+        F[r][3] = f16x2_bf16x2(x.w);
+      }
+    }
+#pragma unroll
+    for (int n2 = 0; n2 < 8; ++n2) {
+      const uint32_t sel = (n2 & 1) ? 0x7632u : 0x5410u;
+      const uint32_t b0 = __byte_perm(F[0][n2 >> 1], F[1][n2 >> 1], sel);
+      const uint32_t b1 = __byte_perm(F[2][n2 >> 1], F[3][n2 >> 1], sel);
+      mma_f16_16816(oacc[n2], pa[k2][0], pa[k2][1], b0, b1);
+    }
+  }
+  if (g == 0) {
+    // lane c holds dims 16c + n2 (column 2c) and 16c + 8 + n2 (column 2c + 1)
+    const float inv = 1.0f / sum;
+    uint32_t o[8];
+#pragma unroll
+    for (int k = 0; k < 8; k += 2) {
+      const int d0 = k, d1 = k + 1;  // dims 16c + k, + k + 1 (both column 2c)
+      o[k / 2] = pack_bf16x2(__fmaf_rn(vmax, oacc[d0][0], corr) * inv, __fmaf_rn(vmax, oacc[d1][0], corr) * inv);
+      o[4 + k / 2] = pack_bf16x2(__fmaf_rn(vmax, oacc[d0][1], corr) * inv, __fmaf_rn(vmax, oacc[d1][1], corr) * inv);
+    }
+    uint4* orow = reinterpret_cast<uint4*>(out + (static_cast<long long>(b) * OASIS_TOKENS + p) * OASIS_HIDDEN +
+                                           (hg * kDecHeads + hh) * 64 + 16 * c);
+    orow[0] = make_uint4(o[0], o[1], o[2], o[3]);
+    orow[1] = make_uint4(o[4], o[5], o[6], o[7]);
+  }
 }
 
 // ----------------------------------------------------------------------------------
@@ -804,25 +962,44 @@ int launch_attn_temporal(const void* qkv, const KvView& kv, int layer, void* out
     configured = true;
   }
   if (q_frames == 1 && n_past > 0 && n_past < OASIS_MAX_FRAMES) {
-    // one query frame over cached slots: the decode kernel, shared memory sized for the
-    // kinds present (rows packed back to back, 16-byte aligned)
+    // one query frame over cached slots: the decode kernel.  Shared memory: cached key
+    // rows, value rows (uniform strides by the widest kind present, padded so the
+    // fragment loads are conflict-free), 32 B of scales per slot and tensor, the live rows
     DecodeLayout lay{};
-    uint32_t off = 0;
     lay.live_kv = n_kv > n_past ? 1 : 0;
+    int k_widest = OASIS_KV_INT4, v_widest = OASIS_KV_INT4;  // INT4 < FP8 < bf16 in bytes
+    auto wider = [](int a, int k) {
+      auto bytes = [](int kind) { return kind == OASIS_KV_BF16 ? 2 : (kind == OASIS_KV_FP8 ? 1 : 0); };
+      return bytes(k) > bytes(a) ? k : a;
+    };
+    auto codes = [](int kind) -> uint32_t {
+      return kind == OASIS_KV_BF16 ? kDecHeads * 128 : (kind == OASIS_KV_FP8 ? kDecHeads * 64 : kDecHeads * 32);
+    };
+    auto aux = [](int kind) -> uint32_t { return kind == OASIS_KV_BF16 ? 0u : (kind == OASIS_KV_FP8 ? 16u : 32u); };
     lay.k_bytes = (1 + lay.live_kv) * kDecHeads * 128;  // live q (and k) rows
     lay.v_bytes = lay.live_kv * kDecHeads * 128;        // live v row
     for (int s = 0; s < n_past; ++s) {
-      for (int which = 0; which < 2; ++which) {
-        const int kind = kv.t[which].kind[s];
-        const uint32_t codes = kind == OASIS_KV_BF16 ? kDecHeads * 128 : (kind == OASIS_KV_FP8 ? kDecHeads * 64 : kDecHeads * 32);
-        const uint32_t aux = kind == OASIS_KV_BF16 ? 0u : (kind == OASIS_KV_FP8 ? 16u : 32u);
-        (which ? lay.v_row : lay.k_row)[s] = off;
-        off += codes;
-        (which ? lay.v_aux : lay.k_aux)[s] = off;
-        off += aux;
-        (which ? lay.v_bytes : lay.k_bytes) += codes + aux;
-      }
+      const int kk = kv.t[0].kind[s], vk = kv.t[1].kind[s];
+      k_widest = wider(k_widest, kk);
+      v_widest = wider(v_widest, vk);
+      lay.k_kinds |= static_cast<unsigned long long>(kk) << (2 * s);
+      lay.v_kinds |= static_cast<unsigned long long>(vk) << (2 * s);
+      lay.k_bytes += codes(kk) + aux(kk);
+      lay.v_bytes += codes(vk) + aux(vk);
     }
+    // key rows: one 16-byte (FP8), 8-byte (INT4) or 2 x 16-byte (bf16) load per thread
+    // from 8 rows; value rows: 8-, 4- or 16-byte loads from 4 rows two apart
+    lay.k_stride = k_widest == OASIS_KV_BF16 ? 1040 : (k_widest == OASIS_KV_FP8 ? 576 : 288);
+    lay.v_stride = v_widest == OASIS_KV_BF16 ? 1040 : (v_widest == OASIS_KV_FP8 ? 528 : 272);
+    uint32_t off = 0;
+    lay.k_base = off;
+    off += n_past * lay.k_stride;
+    lay.v_base = off;
+    off += n_past * lay.v_stride;
+    lay.k_aux = off;
+    off += n_past * 32;
+    lay.v_aux = off;
+    off += n_past * 32;
     lay.live = off;
     off += 3 * kDecHeads * 128;
     lay.total = off;

@@ -171,9 +171,11 @@ def test_prefill_codes_bit_exact_at_full_size(pkg, cuda, B, kinds):
 
 @pytest.mark.parametrize("B,kinds", [(16, ["int4"] * 23 + ["bf16"] * 8), (8, ["fp8"] * 31)])
 def test_fused_dequant_equals_dequantised_cache_at_full_size(pkg, cuda, B, kinds):
-    """The incremental forward over a quantised cache (K/V dequantised while staged into
-    shared memory) equals, bit for bit, the one over a bf16 cache holding the dequantised
-    pages (``load``), at the benchmark layouts (depth 16, 31 cached frames)."""
+    """The incremental forward over a quantised cache (codes read by the attention kernel,
+    the FP8 scale / INT4 scale and zero applied to the scores and probabilities) equals
+    the one over a bf16 cache holding the dequantised pages (``load``, every element
+    rounded to bf16) to within that rounding, at the benchmark layouts (depth 16, 31
+    cached frames)."""
     depth, T = 16, 32
     model = pkg.OasisDiTB200.from_state_dict(state(pkg, depth), device=cuda, depth=depth)
     x, t, a = (z.to(cuda) for z in inputs(B, T, seed=47))
@@ -190,7 +192,10 @@ def test_fused_dequant_equals_dequantised_cache_at_full_size(pkg, cuda, B, kinds
     v_d = model.forward_cached(x_new, t_new, a[:, -1], deq, n_past=T - 1)
     torch.cuda.synchronize()
     assert torch.isfinite(v_q).all()
-    assert torch.equal(v_q, v_d)  # the same dequantised values enter the same arithmetic
+    err = rel_l2(v_q, v_d)
+    print(f"fused dequant vs dequantised bf16 cache: rel-L2 {err:.2e}")
+    # the only difference is the bf16 rounding of each dequantised K/V element (2^-9)
+    assert err < 5e-3
 
 
 def _oracle_incremental(sd, depth, x, t, a, kinds, x_new, t_new):
