@@ -22,6 +22,7 @@ import importlib
 import json
 import math
 import os
+import platform
 import statistics
 import subprocess
 import sys
@@ -103,7 +104,7 @@ class ClockSampler:
     def start(self):
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"],
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "50"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
@@ -149,52 +150,91 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------------------------ CPU baseline
+def cpu_model() -> str:
+    try:
+        with open("/proc/cpuinfo") as f:
+            for ln in f:
+                if ln.startswith("model name"):
+                    return ln.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return platform.processor() or "unknown"
+
+
 class CpuOracle:
-    """The fp32 PyTorch restatement of the reference forward on the host cores, at the
-    benchmark shape (B=1, T=32).  One sample = one SpatioTemporal block; a forward is
-    embed + final layer (timed once) + 16 blocks."""
+    """The fp32 PyTorch restatement of the reference forward (the oracle) on the host
+    cores, whole Oasis-500M forwards (depth 16) at B=1: the benchmark window (T=32) and
+    the reference's CPU configuration (T=4)."""
 
     def __init__(self, threads=None):
         from oracle.dit_ref import build_oracle
         pkg = importlib.import_module(PKG)
-        if threads:
-            torch.set_num_threads(threads)
+        torch.set_num_threads(threads or os.cpu_count() or 1)
         self.cores = torch.get_num_threads()
-        self.m = build_oracle(pkg.random_state_dict(seed=0, depth=1), depth=1)
+        self.m = build_oracle(pkg.random_state_dict(seed=0, depth=DEPTH), depth=DEPTH)
         g = torch.Generator().manual_seed(0)
-        x = torch.randn(1, WINDOW, *FRAME, generator=g)
-        t = torch.full((1, WINDOW), STAB_LEVEL - 1, dtype=torch.long)
-        a = synthetic_actions(g, 1, WINDOW)
-        with torch.no_grad():
-            s = time.perf_counter()
-            self.tok, self.c = self.m.embed(x, t, a)
-            e = time.perf_counter() - s
-            y = self.m.blocks[0](self.tok, self.c)  # warm-up
-            s = time.perf_counter()
-            self.m.unpatchify_out(y, self.c)
-            self.embed_final_s = e + time.perf_counter() - s
+        self.inputs = {}
+        for T in (WINDOW, 4):  # seeded N(0,1) latents, t ~ U{0..999}, actions as config 0
+            self.inputs[T] = (torch.randn(1, T, *FRAME, generator=g),
+                              torch.randint(0, 1000, (1, T), generator=g),
+                              synthetic_actions(g, 1, T))
 
-    def block_seconds(self):
+    def forward_seconds(self, T=WINDOW) -> float:
+        x, t, a = self.inputs[T]
         with torch.no_grad():
             s = time.perf_counter()
-            self.m.blocks[0](self.tok, self.c)
+            self.m(x, t, a)
             return time.perf_counter() - s
 
-    def rate(self, block_s):
-        return 1.0 / (self.embed_final_s + DEPTH * block_s)
 
-
-def cpu_oracle_rate(budget_s=12.0, threads=None):
-    """Forwards/s of the CPU oracle from ~budget_s of block samples."""
+def cpu_oracle_rate(budget_s=15.0, threads=None):
+    """Forwards/s of the CPU oracle: whole T=32 forwards for ~budget_s (at least 2), plus
+    three whole forwards of the reference's CPU configuration (B=1, T=4)."""
     o = CpuOracle(threads)
+    o.forward_seconds(4)
+    o.forward_seconds()  # warm-up
     times, start = [], time.perf_counter()
-    while len(times) < 2 or (time.perf_counter() - start < budget_s and len(times) < 64):
-        times.append(o.block_seconds())
-    blk = statistics.median(times)
-    return {"value": o.rate(blk), "unit": "forwards/s", "cores": o.cores, "kind": "port",
-            "sample": f"fp32 CPU oracle (PyTorch restatement of the reference forward): embed+final "
-                      f"once, {len(times)} SpatioTemporal blocks of a B=1 T=32 window (median "
-                      f"{blk:.3f} s each); forward = embed+final + 16 blocks"}
+    while len(times) < 2 or (time.perf_counter() - start < budget_s and len(times) < 20):
+        times.append(o.forward_seconds())
+    t4 = [o.forward_seconds(4) for _ in range(3)]
+    med = statistics.median(times)
+    return {"value": 1.0 / med, "unit": "forwards/s", "cores": o.cores, "kind": "port",
+            "cpu": cpu_model(),
+            "sample": f"{len(times)} whole fp32 forwards of the B=1 T=32 window (median {med:.3f} s) "
+                      f"by the oracle (PyTorch restatement of the reference forward)",
+            "config0_forwards_per_s": 1.0 / statistics.median(t4),
+            "config0": "B=1, T=4, fp32, seed 0: 3 whole forwards"}
+
+
+def library_bar(dev, steps=10):
+    """Same-box library comparator: the oracle (the reference forward restated in
+    PyTorch) cast to bf16 and run eagerly on this B200 (cuBLAS GEMMs, SDPA attention),
+    B=1 T=32 forwards/s.  A comparator only: nothing of it is on the product path."""
+    try:
+        from oracle.dit_ref import build_oracle
+        pkg = importlib.import_module(PKG)
+        m = build_oracle(pkg.random_state_dict(seed=0, depth=DEPTH), depth=DEPTH).to(dev, torch.bfloat16).eval()
+        g = torch.Generator().manual_seed(0)
+        x = torch.randn(1, WINDOW, *FRAME, generator=g).to(dev, torch.bfloat16)
+        t = torch.full((1, WINDOW), STAB_LEVEL - 1, dtype=torch.long, device=dev)
+        a = synthetic_actions(g, 1, WINDOW).to(dev, torch.bfloat16)
+        with torch.no_grad():
+            for _ in range(3):
+                m(x, t, a)
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(steps):
+                m(x, t, a)
+            e1.record()
+            torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / steps
+        del m
+        torch.cuda.empty_cache()
+        return {"value": 1000.0 / ms, "unit": "forwards/s", "ms_per_forward": ms,
+                "what": "oracle forward in bf16, eager PyTorch on this GPU (cuBLAS + SDPA), B=1 T=32"}
+    except Exception as e:  # a comparator, never required
+        return {"value": None, "error": str(e)[:200]}
 
 
 def workload_config(world, use_graph):
@@ -210,27 +250,31 @@ def workload_config(world, use_graph):
 
 
 def run_reference(args, rank, world):
+    """The reference arm: the oracle's whole fp32 forwards (B=1, T=32) on the host cores,
+    one forward per step (the reference's own forward is not in its tree)."""
     if rank != 0:
         return 0
-    torch.set_num_threads(os.cpu_count() or 1)
     steps, warmup = max(1, args.steps), max(0, args.warmup)
-    o = CpuOracle()
+    o = CpuOracle(os.cpu_count() or 1)
     for _ in range(warmup):
-        o.block_seconds()
-    times = [o.block_seconds() for _ in range(steps)]  # each step: one block sample
-    blk = statistics.median(times)
-    value = o.rate(blk)
+        o.forward_seconds()
+    times = [o.forward_seconds() for _ in range(steps)]
+    total = sum(times)
+    value = steps / total
+    t4 = [o.forward_seconds(4) for _ in range(3)]
     sample = (f"fp32 CPU oracle (PyTorch restatement of the reference forward; the upstream DiT is "
-              f"not in the reference tree): each step one SpatioTemporal block of a B=1 T=32 window "
-              f"(median {blk:.3f} s), forward = embed+final ({o.embed_final_s:.3f} s) + 16 blocks")
+              f"not in the reference tree): each step one whole B=1 T=32 forward "
+              f"(mean {total / steps:.3f} s, median {statistics.median(times):.3f} s)")
     line = {
         "impl": "reference", "metric": "Oasis-500M DiT forwards/s (T=32, bf16/FP8/INT4-KV)",
         "value": value, "unit": "forwards/s", "n_gpus": world, "steps": steps, "warmup": warmup,
-        "ms_per_step": 1000.0 / value, "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": 1000.0 * total / steps, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": workload_config(world, not args.no_graph),
         "cpu_baseline": {"value": value, "unit": "forwards/s", "cores": o.cores, "kind": "port",
-                         "sample": sample},
+                         "cpu": cpu_model(), "sample": sample,
+                         "config0_forwards_per_s": 1.0 / statistics.median(t4),
+                         "config0": "B=1, T=4, fp32, seed 0: 3 whole forwards"},
         "e2e": {"value": value, "unit": "forwards/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -343,7 +387,8 @@ def run_ours(args, rank, world, local_rank):
     e1.record()
     barrier()
     clk = clocks.stop()
-    ms_max = max_over_ranks(e0.elapsed_time(e1), dist, dev)
+    per_rank_ms = e0.elapsed_time(e1)
+    ms_max = max_over_ranks(per_rank_ms, dist, dev)
     value = whole_job_rate(B * args.steps, world, ms_max)
 
     # ---- e2e: public API, pinned host buffers, copies inside the timed region ----
@@ -383,26 +428,53 @@ def run_ours(args, rank, world, local_rank):
     h2d = hx.numel() * 4 + hts[0].numel() * 8 + ha.numel() * 4
     d2h = hout.numel() * 4
 
-    # ---- live per-family kernel timing (CUDA events on the launching stream) ----
-    model.set_timing(B, T, True)
-    n_prof = 3
-    for s in range(n_prof):
-        step_body(s % SOLVER_STEPS)
-    torch.cuda.synchronize()
-    fam = model.get_timing(B, T)
+    # ---- per-family kernel time inside a graph-replayed step: a second capture of the same
+    # step with timing events as graph nodes (the timed graphs carry none), replayed a few
+    # times; the families' times come from the last replay ----
+    M = B * T * TOKENS
+    fam_src = "graph"
+    n_prof = 1
+    try:
+        model.set_timing(B, T, True)
+        gt = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(stream):
+            with torch.cuda.graph(gt, stream=stream):
+                step_body(1)
+        for _ in range(5):
+            gt.replay()
+        torch.cuda.synchronize()
+        fam = model.get_timing(B, T)
+        del gt
+    except Exception:  # eager fallback: events on the launching stream
+        fam_src = "eager"
+        model.set_timing(B, T, True)
+        n_prof = 3
+        for s in range(n_prof):
+            step_body(s % SOLVER_STEPS)
+        torch.cuda.synchronize()
+        fam = model.get_timing(B, T)
     model.set_timing(B, T, False)
     gemm_ms, gemm_n = fam["gemm"]
-    M = B * T * TOKENS
     gemm_flops = LINEAR_FLOP_PER_TOKEN * M * n_prof
     achieved = gemm_flops / (gemm_ms / 1000.0) / 1e12 if gemm_ms > 0 else None
     peak = peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops"))
     traffic = load_traffic()
     per_fwd_ms = ms_max / args.steps
-    kv = {}
+    kv, sweep, lib = {}, [], None
     if rank == 0 and not args.skip_kv:
-        kv = kv_configs(pkg, model, dev, g)
+        kv = kv_configs(pkg, model, dev, g, peaks)
+    if rank == 0 and not args.skip_sweep:
+        sweep = attention_sweep(pkg, dev, peaks.get("hbm_gbs", 6650.0), reps=10)
+    if rank == 0 and world == 1 and not args.skip_cpu:
+        lib = library_bar(dev)
 
+    # every rank's own time and clocks, gathered outside the timed region
+    mine = {"rank": rank, "ms_per_step": per_rank_ms / args.steps, "sm_mhz": clk.get("sm_mhz"),
+            "power_w": clk.get("power_w"), "reasons": clk.get("reasons")}
+    per_rank = [mine]
     if dist is not None:
+        per_rank = [None] * world
+        dist.all_gather_object(per_rank, mine)
         dist.barrier()
     if rank == 0:
         cpu = None
@@ -429,6 +501,7 @@ def run_ours(args, rank, world, local_rank):
                          "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": (achieved / peak) if achieved else None,
                          "peak_source": f"{peak_src} bf16_tflops_sustained (kernel timed inside a long step)",
+                         "timed_in": f"{fam_src}-replayed step (CUDA events on the launching stream)",
                          "traffic": traffic.get("bytes_per_launch") if traffic else None,
                          "traffic_note": traffic.get("note") if traffic else "no ncu capture committed",
                          "algorithmic_flop_per_launch": gemm_flops / max(1, gemm_n),
@@ -436,8 +509,11 @@ def run_ours(args, rank, world, local_rank):
             "forward_tflops": LINEAR_FLOP_PER_TOKEN * M / (per_fwd_ms / 1000.0) / 1e12,
             "kernel_ms_per_forward": {k: round(vv[0] / n_prof, 4) for k, vv in fam.items()},
             "clocks": clk,
+            "per_rank": per_rank,
             "cpu_baseline": cpu,
+            "library_bar": lib,
             "kv_configs": kv,
+            "attention_sweep": sweep,
         }
         print(json.dumps(line), flush=True)
     graphs.clear()
@@ -446,10 +522,26 @@ def run_ours(args, rank, world, local_rank):
     return 0
 
 
-def kv_configs(pkg, model, dev, g):
-    """Secondary lines: incremental forwards/s with an FP8 cache (B=8) and a progressive
-    INT4 cache (B=16, newest 8 frames bf16), T=32 (31 cached frames)."""
+def _cached_call_flops(B):
+    """Algorithmic FLOPs of one incremental forward of B sessions (144 new tokens each):
+    the linear projections, the stacked adaLN GEMM, spatial attention over 144 tokens and
+    temporal attention of the new frame over the 32-frame window."""
+    tokens = B * TOKENS
+    ada = 2.0 * B * 1024 * (2 * DEPTH * 6144 + 2048)
+    spatial = 4.0 * TOKENS * TOKENS * 64 * 16 * B * DEPTH
+    temporal = 4.0 * WINDOW * 64 * 16 * tokens * DEPTH
+    return LINEAR_FLOP_PER_TOKEN * tokens + ada + spatial + temporal
+
+
+def kv_configs(pkg, model, dev, g, peaks):
+    """Incremental forwards/s with an FP8 cache (B=8), a progressive INT4 cache (B=16,
+    newest 8 frames bf16) and a bf16 cache (B=8), T=32 (31 cached frames), each with its
+    roofline: algorithmic bytes = every weight once + the whole cache, FLOPs as
+    _cached_call_flops."""
     out = {}
+    hbm = peaks.get("hbm_gbs", 6650.0)
+    tpk = peaks.get("bf16_tflops_sustained", 1400.0)
+    wbytes = model.weights.nbytes
     for name, B, kinds in (("fp8_b8", 8, ["fp8"] * 31),
                            ("int4_b16", 16, ["int4"] * 23 + ["bf16"] * 8),
                            ("bf16_b8", 8, ["bf16"] * 31)):
@@ -479,12 +571,86 @@ def kv_configs(pkg, model, dev, g):
             e1.record()
             torch.cuda.synchronize()
             ms = e0.elapsed_time(e1) / n
+            byts = wbytes + cache.nbytes
+            flops = _cached_call_flops(B)
             out[name] = {"forwards_per_s": B / (ms / 1000.0), "ms_per_call": ms, "batch": B,
                          "cached_frames": 31, "kv_bytes": cache.nbytes,
-                         "kv_bytes_bf16_equiv": cache.bf16_equivalent_bytes()}
+                         "kv_bytes_bf16_equiv": cache.bf16_equivalent_bytes(),
+                         "roofline": {"bytes": byts, "GBps": byts / ms / 1e6,
+                                      "frac_hbm": byts / ms / 1e6 / hbm, "flop": flops,
+                                      "TFLOPs": flops / ms / 1e9, "frac_tensor": flops / ms / 1e9 / tpk,
+                                      "note": "bytes = every weight once + the whole KV cache; "
+                                              "of measured hbm_gbs / bf16_tflops_sustained"}}
             del gr, cache
         except Exception as e:
             out[name] = {"error": str(e)[:200]}
+    return out
+
+
+def attention_sweep(pkg, dev, hbm, reps=20):
+    """The isolated attention sweep (benchmark configuration 4): spatial attention over
+    B*T frames of 144 tokens, causal temporal attention over T frames for B*144
+    sequences with bf16 K/V (full-window kernel) or every K/V frame from an FP8 / INT4
+    cache, and the one-query-frame kernel of the incremental forward (31 cached frames).
+    Bytes: q, k, v read and o written once (k, v at their stored width)."""
+    g = torch.Generator(device=dev).manual_seed(0)
+
+    def timeit(fn):
+        for _ in range(3):
+            fn()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / reps
+
+    out = []
+    for frames in (32, 256, 1024, 4096):
+        qkv = torch.randn(frames * TOKENS, 3072, device=dev, generator=g).bfloat16()
+        o = torch.empty(frames * TOKENS, 1024, device=dev).bfloat16()
+        ms = timeit(lambda: pkg.attn_spatial(qkv, out=o))
+        byts = frames * TOKENS * 1024 * 2 * 4
+        out.append({"case": f"spatial BT={frames}", "ms": ms, "GBps": byts / ms / 1e6,
+                    "frac_hbm": byts / ms / 1e6 / hbm,
+                    "tflops": 4 * 144 * 144 * 64 * 16 * frames / ms / 1e9})
+        del qkv, o
+    for T in (8, 16, 32):
+        for B in (1, 8, 32):
+            qkv = torch.randn(B * T * TOKENS, 3072, device=dev, generator=g).bfloat16()
+            o = torch.empty(B * T * TOKENS, 1024, device=dev).bfloat16()
+            for kind in ("bf16", "fp8", "int4"):
+                if kind == "bf16":
+                    fn = lambda: pkg.attn_temporal(qkv, batch=B, q_frames=T, out=o)
+                    kv_bytes = B * T * TOKENS * 1024 * 2 * 2
+                else:
+                    cache = pkg.KVCacheB200.uniform(B, 1, T, kind, device=dev)
+                    cache.store(qkv, layer=0)
+                    fn = lambda: pkg.attn_temporal(qkv, batch=B, q_frames=T, n_past=T, n_kv=T,
+                                                   cache=cache, layer=0, out=o)
+                    kv_bytes = cache.nbytes
+                ms = timeit(fn)
+                byts = kv_bytes + B * T * TOKENS * 1024 * 2 * 2  # + q read + o written
+                out.append({"case": f"temporal T={T} B={B} kv={kind}", "ms": ms,
+                            "GBps": byts / ms / 1e6, "frac_hbm": byts / ms / 1e6 / hbm})
+            del qkv, o
+    for B in (8, 32):
+        new = torch.randn(B * TOKENS, 3072, device=dev, generator=g).bfloat16()
+        o = torch.empty(B * TOKENS, 1024, device=dev).bfloat16()
+        past = torch.randn(B * 31 * TOKENS, 3072, device=dev, generator=g).bfloat16()
+        for kind in ("bf16", "fp8", "int4"):
+            cache = pkg.KVCacheB200.uniform(B, 1, 31, kind, device=dev)
+            cache.store(past, layer=0)
+            ms = timeit(lambda: pkg.attn_temporal(new, batch=B, q_frames=1, q_pos0=31, n_past=31,
+                                                  n_kv=32, cache=cache, layer=0, out=o))
+            byts = cache.nbytes + B * TOKENS * 1024 * 2 * 4  # + live q, k, v read + o written
+            out.append({"case": f"decode past=31 B={B} kv={kind}", "ms": ms, "GBps": byts / ms / 1e6,
+                        "frac_hbm": byts / ms / 1e6 / hbm})
+            del cache
+        del new, o, past
+    torch.cuda.empty_cache()
     return out
 
 
@@ -523,38 +689,8 @@ def run_isolated(args, local_rank):
         print(json.dumps({"case": f"gemm M={M} N={N} K={K}", "ms": ms, "tflops": tf,
                           "frac_burst": tf / peaks.get("bf16_tflops", 1590.0)}), flush=True)
         return 0
-    # attention sweep: spatial (B*T frames of 144 tokens) and causal temporal with
-    # bf16 / FP8 / INT4 K/V (every K/V frame read from the cache for the quantised kinds)
-    for frames in (32, 256, 1024, 4096):
-        qkv = torch.randn(frames * TOKENS, 3072, device=dev, generator=g).bfloat16()
-        out = torch.empty(frames * TOKENS, 1024, device=dev).bfloat16()
-        ms = timeit(lambda: pkg.attn_spatial(qkv, out=out), args.steps)
-        byts = frames * TOKENS * 1024 * 2 * 4
-        print(json.dumps({"case": f"spatial BT={frames}", "ms": ms, "GBps": byts / ms / 1e6,
-                          "frac_hbm": byts / ms / 1e6 / hbm,
-                          "tflops": 4 * 144 * 144 * 64 * 16 * frames / ms / 1e9}), flush=True)
-        del qkv, out
-    for T in (8, 16, 32):
-        for B in (1, 8, 32):
-            qkv = torch.randn(B * T * TOKENS, 3072, device=dev, generator=g).bfloat16()
-            out = torch.empty(B * T * TOKENS, 1024, device=dev).bfloat16()
-            for kind in ("bf16", "fp8", "int4"):
-                if kind == "bf16":
-                    fn = lambda: pkg.attn_temporal(qkv, batch=B, q_frames=T, out=out)
-                    kv_bytes = B * T * TOKENS * 1024 * 2 * 2
-                else:
-                    cache = pkg.KVCacheB200.uniform(B, 1, T, kind, device=dev)
-                    cache.store(qkv, layer=0)
-                    fn = lambda: pkg.attn_temporal(qkv, batch=B, q_frames=T, n_past=T, n_kv=T,
-                                                   cache=cache, layer=0, out=out)
-                    per = 1 if kind == "fp8" else 0.5
-                    kv_bytes = int(B * T * TOKENS * 1024 * 2 * per) + (
-                        B * T * 16 * 2 * 2 if kind == "fp8" else B * T * TOKENS * 16 * 2 * 2 * 2)
-                ms = timeit(fn, args.steps)
-                byts = kv_bytes + B * T * TOKENS * 1024 * 2 * 2  # + Q read + O write
-                print(json.dumps({"case": f"temporal T={T} B={B} kv={kind}", "ms": ms,
-                                  "GBps": byts / ms / 1e6, "frac_hbm": byts / ms / 1e6 / hbm}), flush=True)
-            del qkv, out
+    for line in attention_sweep(pkg, dev, hbm, reps=args.steps):
+        print(json.dumps(line), flush=True)
     return 0
 
 
@@ -567,6 +703,7 @@ def main():
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--skip-cpu", action="store_true")
     ap.add_argument("--skip-kv", action="store_true")
+    ap.add_argument("--skip-sweep", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=12.0)
     ap.add_argument("--isolated", choices=["attention", "gemm"], default=None)
     ap.add_argument("--M", type=int, default=36864)

@@ -112,11 +112,21 @@ struct Timer {
       idx = p->ev_used;
       p->ev_used += 2;
       p->ev_family[idx] = fam;
-      cudaEventRecord(p->ev[idx], s);
+      record(p->ev[idx]);
     }
   }
   ~Timer() {
-    if (idx >= 0) cudaEventRecord(p->ev[idx + 1], s);
+    if (idx >= 0) record(p->ev[idx + 1]);
+  }
+  // inside a stream capture the event becomes a record node of the graph, so the
+  // family times come from the replayed graph
+  void record(cudaEvent_t e) {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    cudaStreamIsCapturing(s, &cs);
+    if (cs == cudaStreamCaptureStatusActive)
+      cudaEventRecordWithFlags(e, s, cudaEventRecordExternal);
+    else
+      cudaEventRecord(e, s);
   }
 };
 

@@ -184,7 +184,9 @@ int oasis_dit_forward_cached(oasis_plan_t* plan, const float* x, const int64_t* 
                              int n_past, cudaStream_t stream);
 
 /* Per-kernel-family device time of the forwards run since the last reset
- * (CUDA events on the plan's stream; only while enabled).  families: 0 GEMM
+ * (CUDA events on the plan's stream; only while enabled).  A forward captured into a
+ * CUDA graph while enabled records its events as graph nodes: the times then come
+ * from the last replay of that graph.  families: 0 GEMM
  * projections, 1 adaLN GEMM, 2 spatial attention, 3 temporal attention,
  * 4 LayerNorm/modulate, 5 embeddings+final, 6 KV quantise. */
 int oasis_plan_set_timing(oasis_plan_t* plan, int enable);
