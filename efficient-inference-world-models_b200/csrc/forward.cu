@@ -11,6 +11,8 @@
 //   final LN+modulate -> 1024->64 GEMM with the unpatchify store into v.
 // All launches go to the caller's stream; nothing allocates or synchronises, so a
 // forward can be captured into a CUDA graph.
+#include <nvtx3/nvToolsExt.h>
+
 #include <cstring>
 #include <vector>
 
@@ -102,12 +104,20 @@ struct oasis_plan {
 namespace oasis {
 namespace {
 
+// NVTX range names of the kernel families (visible to Nsight tools; free otherwise).
+const char* const kFamilyNames[kFamilies] = {"oasis/gemm", "oasis/adaln_gemm", "oasis/spatial_attn",
+                                             "oasis/temporal_attn", "oasis/ln_modulate",
+                                             "oasis/embed_final", "oasis/kv_store"};
+
+// One launch group of a kernel family: an NVTX range around its host-side launches and,
+// while the plan's timing is enabled, CUDA events around it on the stream.
 struct Timer {
   oasis_plan* p;
   cudaStream_t s;
   int fam;
   int idx = -1;
   Timer(oasis_plan* p_, cudaStream_t s_, int fam_) : p(p_), s(s_), fam(fam_) {
+    nvtxRangePushA(kFamilyNames[fam]);
     if (p->timing && p->ev_used + 2 <= static_cast<int>(p->ev.size())) {
       idx = p->ev_used;
       p->ev_used += 2;
@@ -117,6 +127,7 @@ struct Timer {
   }
   ~Timer() {
     if (idx >= 0) record(p->ev[idx + 1]);
+    nvtxRangePop();
   }
   // inside a stream capture the event becomes a record node of the graph, so the
   // family times come from the replayed graph
