@@ -283,11 +283,13 @@ namespace {
 // Estimated microseconds of an M x N x K bf16 GEMM on 128*ctas x bn tiles with K split
 // `splits` ways, `slots` units resident at once (SMs, or SM pairs).  Each unit streams
 // its A rows (16 KB per k-block) and its share of the B rows (bn/ctas x 128 B) through
-// one SM (at most ~150 GB/s) and issues 2*bn tensor cycles per k-block; the whole
-// launch moves A once per N tile and B once per M tile out of L2 (~10 TB/s); ~1.5 us
-// of pipeline fill and epilogue per unit; split k waits for split k-1's reduce-adds.
+// one SM (~150 GB/s) and issues 2*bn tensor cycles per k-block; the whole launch moves A
+// once per N tile and B once per M tile out of L2 (~20 TB/s); ~1.5 us of pipeline fill
+// and epilogue per unit; split k issues its reduce-adds after split k-1's completed
+// (~2.5 us each).  The constants reproduce the tile choices measured best on B200 for
+// the incremental forward's shapes (M = 1152 and 2304).
 double gemm_time_us(long long M, long long N, long long K, int bn, int ctas, int splits, int slots) {
-  const double clk_ghz = 1.8, sm_gbps = 150.0, l2_gbps = 10000.0, fixed_us = 1.5;
+  const double clk_ghz = 1.8, sm_gbps = 150.0, l2_gbps = 20000.0, fixed_us = 1.5;
   const long long m_tiles = (M + 128LL * ctas - 1) / (128LL * ctas);
   const long long n_tiles = N / bn;
   const long long units = m_tiles * n_tiles * splits;
@@ -299,7 +301,7 @@ double gemm_time_us(long long M, long long N, long long K, int bn, int ctas, int
   const double l2_bytes = 2.0 * M * K * n_tiles + 2.0 * N * K * m_tiles;
   const double t_l2 = l2_bytes / (l2_gbps * 1e3) + fixed_us;
   const double t = waves * t_unit > t_l2 ? waves * t_unit : t_l2;
-  return t + (splits - 1) * 0.7;
+  return t + (splits - 1) * 2.5;
 }
 
 }  // namespace
@@ -309,12 +311,14 @@ void choose_tiles(int M, int N, int K, bool allow_split, int* bn, int* ctas, int
   const int pairs = max_pairs<256, kEpiGateResid>();
   *splits = 1;
   if (N % 256 == 0) {
-    // CTA pairs on 256 x 256 tiles (the chained launch's tiles) where they fill the
-    // pair slots: enough tiles, and every wave at least 90 % full
+    // CTA pairs on 256 x 256 tiles (the chained launch's tiles) unless their last wave
+    // would hold fewer than 45 % of the pair slots: each SM stages half the B rows, so a
+    // pair tile costs the SM less operand traffic than any single-CTA tile
     const long long pair_m = (M + 2 * kGemmBM - 1) / (2 * kGemmBM);
     const long long units = pair_m * (N / 256);
     const long long waves = (units + pairs - 1) / pairs;
-    if (10 * units >= 9 * (sms / 2) && 10 * units >= 9 * waves * pairs) {
+    const long long last = units - (waves - 1) * pairs;
+    if (100 * last >= 45LL * pairs) {
       *bn = 256;
       *ctas = 2;
       return;
@@ -335,11 +339,6 @@ void choose_tiles(int M, int N, int K, bool allow_split, int* bn, int* ctas, int
         *splits = s;
       }
     }
-  }
-  if (N % 256 == 0 && gemm_time_us(M, N, K, 256, 2, 1, pairs) < best) {
-    *bn = 256;
-    *ctas = 2;
-    *splits = 1;
   }
   if (N % *bn) {  // no candidate divides N: the widest power of two that does
     int b = 256;

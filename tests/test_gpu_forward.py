@@ -86,8 +86,39 @@ def test_forward_is_deterministic(pkg, cuda, B, T):
     assert torch.equal(v1, v2)
 
 
+# The incremental forward of the newest frame (a 1-frame plan) and the full-window forward
+# (a T-frame plan) compute the same function on the same K/V: cached-past reuse is exact
+# in exact arithmetic (oasis_persistent_kv_theory.py:24-112), and at the attention level
+# the two kernels agree to the last bit on all but a few elements (test below).  Their
+# projections run on different tile shapes (and the 1-frame plan splits K of the residual
+# GEMMs), which changes the fp32 accumulation bits; bf16 rounding of the activations turns
+# that into a spread of about 1e-3 between two equally accurate forwards.  So the forwards
+# are compared to each other at the bf16 spread and each to the fp32 oracle at the bar.
+BF16_SPREAD = 5e-3
+
+
+def test_decode_attention_equals_full_window_attention(pkg, cuda):
+    """Newest-frame attention over a bf16 cache of the first T-1 frames equals the
+    full-window kernel's newest frame on the same q/k/v (fp32 sums in another order)."""
+    for B, T in ((2, 6), (8, 32)):
+        g = torch.Generator(device=cuda).manual_seed(B * 100 + T)
+        qkv = torch.randn(B * T * 144, 3072, device=cuda, generator=g).bfloat16()
+        full = pkg.attn_temporal(qkv, batch=B, q_frames=T)
+        cache = pkg.KVCacheB200.uniform(B, 1, T - 1, "bf16", device=cuda)
+        frames = qkv.reshape(B, T, 144, 3072)
+        cache.store(frames[:, :T - 1].reshape(-1, 3072).contiguous(), layer=0)
+        dec = pkg.attn_temporal(frames[:, T - 1].reshape(-1, 3072).contiguous(), batch=B, q_frames=1,
+                                q_pos0=T - 1, n_past=T - 1, n_kv=T, cache=cache, layer=0)
+        last = full.reshape(B, T, 144, 1024)[:, T - 1].reshape(-1, 1024)
+        torch.cuda.synchronize()
+        assert rel_l2(dec, last) < 1e-4
+        assert (dec != last).float().mean().item() < 1e-3
+
+
 def test_cached_forward_equals_full_forward_bf16(pkg, cuda):
-    """Persistent past-frame reuse is exact (oasis_persistent_kv_theory.py:24-112)."""
+    """Persistent past-frame reuse (oasis_persistent_kv_theory.py:24-112): the incremental
+    forward of the newest frame against a bf16 cache of the prefill matches the full
+    forward's newest frame, and both match the fp32 oracle."""
     depth, B, T = 2, 2, 6
     model = pkg.OasisDiTB200.from_state_dict(state(pkg, depth), device=cuda, depth=depth)
     x, t, a = (z.to(cuda) for z in inputs(B, T, seed=21))
@@ -100,9 +131,11 @@ def test_cached_forward_equals_full_forward_bf16(pkg, cuda):
     v_full = model(x2, t2, a)[:, -1]
     v_inc = model.forward_cached(x2[:, -1], t2[:, -1], a[:, -1], cache, n_past=T - 1)
     torch.cuda.synchronize()
-    # same K/V and weights; the one-query-frame attention kernel only sums the scores and
-    # the probability-weighted values in another order than the full-window kernel
-    assert rel_l2(v_inc, v_full) < 1e-4
+    assert rel_l2(v_inc, v_full) < BF16_SPREAD
+    ref = build_oracle(state(pkg, depth), depth=depth)
+    with torch.no_grad():
+        v_ref = ref(x2.cpu(), t2.cpu(), a.cpu())[:, -1]
+    assert rel_l2(v_inc.cpu(), v_ref) <= 1e-2 and rel_l2(v_full.cpu(), v_ref) <= 1e-2
 
 
 def test_cached_forward_equals_full_forward_at_full_size(pkg, cuda):
@@ -122,7 +155,7 @@ def test_cached_forward_equals_full_forward_at_full_size(pkg, cuda):
     v_inc = model.forward_cached(x2[:, -1], t2[:, -1], a[:, -1], cache, n_past=T - 1)
     torch.cuda.synchronize()
     assert torch.isfinite(v_inc).all()
-    assert rel_l2(v_inc, v_full) < 1e-4  # summation order of the attention kernels only
+    assert rel_l2(v_inc, v_full) < BF16_SPREAD
 
 
 @pytest.mark.parametrize("B,kinds", [(16, ["int4"] * 23 + ["bf16"] * 8), (8, ["fp8"] * 31)])
@@ -259,7 +292,7 @@ def test_dpmpp_rollout_cached_matches_uncached(pkg, cuda):
     xb = pkg.rollout_dpmpp(model, prompt, acts, num_frames=4, solver_steps=3, use_cache=True, seed=1)
     torch.cuda.synchronize()
     assert torch.isfinite(xa).all()
-    assert rel_l2(xb, xa) < 1e-4
+    assert rel_l2(xb, xa) < BF16_SPREAD
 
 
 def test_dpmpp_rollout_with_action_step_schedule(pkg, cuda):
@@ -279,7 +312,7 @@ def test_dpmpp_rollout_with_action_step_schedule(pkg, cuda):
     xb = pkg.rollout_dpmpp(model, prompt, acts, num_frames=3, solver_steps=sched, use_cache=True, seed=3)
     torch.cuda.synchronize()
     assert torch.isfinite(xa).all()
-    assert rel_l2(xb, xa) < 1e-4
+    assert rel_l2(xb, xa) < BF16_SPREAD
 
 
 @pytest.mark.parametrize("use_cache", [False, True])
