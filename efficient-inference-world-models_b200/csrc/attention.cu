@@ -659,7 +659,82 @@ __device__ __forceinline__ void mma_f16_16816(float (&c)[4], uint32_t a0, uint32
       : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
 }
 
-__global__ void __launch_bounds__(kDecThreads)
+// Kinds of the decode kernel's template: one storage kind for every cached slot of a
+// tensor, or kDecMixed (per-slot kinds from the layout's 2-bit masks).
+constexpr int kDecMixed = 3;
+
+// f16 fragments of 16 dims (4 k-steps x 2 registers) of one key row of head hh: dims
+// 16c + 4ks + {0,1} in [ks][0], + {2,3} in [ks][1].  kind < 0: a key past the window (zeros).
+__device__ __forceinline__ void decode_key_frag(const uint8_t* row, int kind, int hh, int c,
+                                                uint32_t (&kb)[4][2]) {
+  if (kind == OASIS_KV_FP8) {
+    const uint4 x = *reinterpret_cast<const uint4*>(row + hh * 64 + 16 * c);
+    const uint32_t w[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks) {
+      kb[ks][0] = f16x2_e4m3x2(w[ks] & 0xFFFFu);
+      kb[ks][1] = f16x2_e4m3x2(w[ks] >> 16);
+    }
+  } else if (kind == OASIS_KV_INT4) {
+    const uint2 x = *reinterpret_cast<const uint2*>(row + hh * 32 + 8 * c);
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks) {
+      const uint32_t h = ((ks < 2) ? x.x : x.y) >> (16 * (ks & 1));
+      kb[ks][0] = f16x2_nibbles(h & 0xFFu);
+      kb[ks][1] = f16x2_nibbles((h >> 8) & 0xFFu);
+    }
+  } else if (kind == OASIS_KV_BF16) {
+    const uint4* kp = reinterpret_cast<const uint4*>(row + hh * 128 + 32 * c);
+    const uint4 x0 = kp[0], x1 = kp[1];
+    const uint32_t w[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks) {
+      kb[ks][0] = f16x2_bf16x2(w[2 * ks]);
+      kb[ks][1] = f16x2_bf16x2(w[2 * ks + 1]);
+    }
+  } else {
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks) kb[ks][0] = kb[ks][1] = 0u;
+  }
+}
+
+// f16 pairs of dims 8g..8g+7 of one value row of head hh (dims 8g + 2q, + 1 in F[q]).
+__device__ __forceinline__ void decode_value_row(const uint8_t* row, int kind, int hh, int g,
+                                                 uint32_t (&F)[4]) {
+  if (kind == OASIS_KV_FP8) {
+    const uint2 x = *reinterpret_cast<const uint2*>(row + hh * 64 + 8 * g);
+    F[0] = f16x2_e4m3x2(x.x & 0xFFFFu);
+    F[1] = f16x2_e4m3x2(x.x >> 16);
+    F[2] = f16x2_e4m3x2(x.y & 0xFFFFu);
+    F[3] = f16x2_e4m3x2(x.y >> 16);
+  } else if (kind == OASIS_KV_INT4) {
+    const uint32_t x = *reinterpret_cast<const uint32_t*>(row + hh * 32 + 4 * g);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) F[q] = f16x2_nibbles((x >> (8 * q)) & 0xFFu);
+  } else if (kind == OASIS_KV_BF16) {
+    const uint4 x = *reinterpret_cast<const uint4*>(row + hh * 128 + 16 * g);
+    F[0] = f16x2_bf16x2(x.x);
+    F[1] = f16x2_bf16x2(x.y);
+    F[2] = f16x2_bf16x2(x.z);
+    F[3] = f16x2_bf16x2(x.w);
+  } else {
+    F[0] = F[1] = F[2] = F[3] = 0u;
+  }
+}
+
+// Multiplier and offset of cached slot j's key (s_j = acc * mul + off * sum(q)) or value
+// (O += p_j * mul * codes, + p_j * off) for head hh: FP8 (scale, 0), INT4 (scale, zero),
+// bf16 (1, 0).
+__device__ __forceinline__ float2 decode_slot_scale(const uint8_t* aux, int kind, int hh) {
+  if (kind == OASIS_KV_FP8) return make_float2(__bfloat162float(reinterpret_cast<const __nv_bfloat16*>(aux)[hh]), 0.0f);
+  if (kind == OASIS_KV_INT4)
+    return make_float2(__half2float(reinterpret_cast<const __half*>(aux)[hh]),
+                       __half2float(reinterpret_cast<const __half*>(aux + 16)[hh]));
+  return make_float2(1.0f, 0.0f);
+}
+
+template <int KK, int VK>
+__global__ void __launch_bounds__(kDecThreads, 4)
     attn_decode_kernel(const __nv_bfloat16* __restrict__ qkv, __nv_bfloat16* __restrict__ out,
                        const __grid_constant__ KvView kv, const __grid_constant__ DecodeLayout lay,
                        int layer, int q_pos, int n_past, float scale_log2) {
@@ -690,18 +765,20 @@ __global__ void __launch_bounds__(kDecThreads)
         uint64_t* bar = &bars[which];
         uint8_t* row = sm_dec + (which ? lay.v_base + s * lay.v_stride : lay.k_base + s * lay.k_stride);
         uint8_t* aux = sm_dec + (which ? lay.v_aux : lay.k_aux) + s * 32;
-        const int kind = t.kind[s];
+        const int tk = which ? VK : KK;
+        const int kind = tk == kDecMixed ? static_cast<int>(t.kind[s]) : tk;
+        const int idx = t.index[s];
         if (kind == OASIS_KV_BF16) {
-          const long long page = kv_page(b, kv.layers, layer, t.n_bf16, t.index[s]);
+          const long long page = kv_page(b, kv.layers, layer, t.n_bf16, idx);
           bulk_load(row, t.bf16 + (page * OASIS_TOKENS + p) * OASIS_HIDDEN + hg * kDecHeads * 64,
                     kDecHeads * 128, bar);
         } else if (kind == OASIS_KV_FP8) {
-          const long long page = kv_page(b, kv.layers, layer, t.n_fp8, t.index[s]);
+          const long long page = kv_page(b, kv.layers, layer, t.n_fp8, idx);
           bulk_load(row, t.fp8 + (page * OASIS_TOKENS + p) * OASIS_HIDDEN + hg * kDecHeads * 64,
                     kDecHeads * 64, bar);
           bulk_load(aux, t.fp8_scale + page * OASIS_HEADS + hg * kDecHeads, 16, bar);
         } else {
-          const long long page = kv_page(b, kv.layers, layer, t.n_int4, t.index[s]);
+          const long long page = kv_page(b, kv.layers, layer, t.n_int4, idx);
           const long long grp = (page * OASIS_TOKENS + p) * OASIS_HEADS + hg * kDecHeads;
           bulk_load(row, t.int4 + grp * 32, kDecHeads * 32, bar);
           bulk_load(aux, t.i4_scale + grp, 16, bar);
@@ -719,6 +796,17 @@ __global__ void __launch_bounds__(kDecThreads)
   }
   const int hh = warp;                   // head within the group
   const int g = lane >> 2, c = lane & 3;  // mma fragment coordinates
+  // kind of a key / value slot j (a compile-time constant unless mixed; -1 past the window)
+  auto k_kind = [&](int j) -> int {
+    if (j >= n_kv) return -1;
+    if (j >= n_past) return OASIS_KV_BF16;
+    return KK == kDecMixed ? decode_kind(lay.k_kinds, j) : KK;
+  };
+  auto v_kind = [&](int j) -> int {
+    if (j >= n_kv) return -1;
+    if (j >= n_past) return OASIS_KV_BF16;
+    return VK == kDecMixed ? decode_kind(lay.v_kinds, j) : VK;
+  };
   if (!mbar_wait(&bars[0], 0)) return;  // timeout recorded in the device error word
 
   // ---- q as the A operand: row 0 only (lanes 0..3); lane c holds dims 16c..16c+15,
@@ -735,13 +823,21 @@ __global__ void __launch_bounds__(kDecThreads)
     for (int ks = 0; ks < 4; ++ks) {
       qa[ks][0] = f16x2_bf16x2(w[2 * ks]);
       qa[ks][1] = f16x2_bf16x2(w[2 * ks + 1]);
-      const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&qa[ks][0]));
-      const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&qa[ks][1]));
-      qsum += (f0.x + f0.y) + (f1.x + f1.y);
+      if (KK == OASIS_KV_INT4 || KK == kDecMixed) {
+        const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&qa[ks][0]));
+        const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&qa[ks][1]));
+        qsum += (f0.x + f0.y) + (f1.x + f1.y);
+      }
     }
   }
-  qsum += __shfl_xor_sync(0xffffffffu, qsum, 1);
-  qsum += __shfl_xor_sync(0xffffffffu, qsum, 2);
+  if (KK == OASIS_KV_INT4 || KK == kDecMixed) {
+    qsum += __shfl_xor_sync(0xffffffffu, qsum, 1);
+    qsum += __shfl_xor_sync(0xffffffffu, qsum, 2);
+  }
+  // lane j: multiplier / offset of key j (scale 1, offset 0 for bf16 and the live key)
+  float2 kscale = make_float2(1.0f, 0.0f);
+  if (KK != OASIS_KV_BF16 && lane < n_past)
+    kscale = decode_slot_scale(sm_dec + lay.k_aux + lane * 32, k_kind(lane), hh);
 
   // ---- scores: n-tile nt holds keys 8nt..8nt+7; this thread supplies key 8nt + g
   float sacc[4][4];
@@ -750,62 +846,25 @@ __global__ void __launch_bounds__(kDecThreads)
     sacc[nt][0] = sacc[nt][1] = sacc[nt][2] = sacc[nt][3] = 0.0f;
     const int j = 8 * nt + g;
     uint32_t kb[4][2];
-#pragma unroll
-    for (int ks = 0; ks < 4; ++ks) kb[ks][0] = kb[ks][1] = 0u;
-    const int kind = j < n_past ? decode_kind(lay.k_kinds, j) : (j < n_kv ? OASIS_KV_BF16 : -1);
-    const uint8_t* row = j < n_past ? sm_dec + lay.k_base + j * lay.k_stride : sm_dec + lay.live + 1024;
-    if (kind == OASIS_KV_FP8) {
-      const uint4 x = *reinterpret_cast<const uint4*>(row + hh * 64 + 16 * c);
-      const uint32_t w[4] = {x.x, x.y, x.z, x.w};
-#pragma unroll
-      for (int ks = 0; ks < 4; ++ks) {
-        kb[ks][0] = f16x2_e4m3x2(w[ks] & 0xFFFFu);
-        kb[ks][1] = f16x2_e4m3x2(w[ks] >> 16);
-      }
-    } else if (kind == OASIS_KV_INT4) {
-      const uint2 x = *reinterpret_cast<const uint2*>(row + hh * 32 + 8 * c);
-#pragma unroll
-      for (int ks = 0; ks < 4; ++ks) {
-        const uint32_t h = ((ks < 2) ? x.x : x.y) >> (16 * (ks & 1));
-        kb[ks][0] = f16x2_nibbles(h & 0xFFu);
-        kb[ks][1] = f16x2_nibbles((h >> 8) & 0xFFu);
-      }
-    } else if (kind == OASIS_KV_BF16) {
-      const uint4* kp = reinterpret_cast<const uint4*>(row + hh * 128 + 32 * c);
-      const uint4 x0 = kp[0], x1 = kp[1];
-      const uint32_t w[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-#pragma unroll
-      for (int ks = 0; ks < 4; ++ks) {
-        kb[ks][0] = f16x2_bf16x2(w[2 * ks]);
-        kb[ks][1] = f16x2_bf16x2(w[2 * ks + 1]);
-      }
-    }
+    decode_key_frag(j < n_past ? sm_dec + lay.k_base + j * lay.k_stride : sm_dec + lay.live + 1024,
+                    k_kind(j), hh, c, kb);
 #pragma unroll
     for (int ks = 0; ks < 4; ++ks) mma_f16_16816(sacc[nt], qa[ks][0], qa[ks][1], kb[ks][0], kb[ks][1]);
   }
 
-  // ---- per key (row 0: lanes 0..3 hold keys 8nt + 2c + e): scales, mask, softmax
-  float sc[8], vm[8], vz[8];
+  // ---- per key (row 0: lanes 0..3 hold keys 8nt + 2c + e): scale, mask, softmax
+  float sc[8];
   float mx = -INFINITY;
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
-    const int nt = i >> 1, e = i & 1;
-    const int j = 8 * nt + 2 * c + e;
-    float s = sacc[nt][e];
-    vm[i] = 0.0f;
-    vz[i] = 0.0f;
-    if (j < n_past) {
-      const int kk = decode_kind(lay.k_kinds, j);
-      const uint8_t* ka = sm_dec + lay.k_aux + j * 32;
-      if (kk == OASIS_KV_FP8) {
-        s *= __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(ka)[hh]);
-      } else if (kk == OASIS_KV_INT4) {
-        s = __fmaf_rn(s, __half2float(reinterpret_cast<const __half*>(ka)[hh]),
-                      __half2float(reinterpret_cast<const __half*>(ka + 16)[hh]) * qsum);
-      }
+    const int j = 8 * (i >> 1) + 2 * c + (i & 1);
+    float s = sacc[i >> 1][i & 1];
+    if (KK != OASIS_KV_BF16) {
+      const float mul = __shfl_sync(0xffffffffu, kscale.x, j);
+      const float off = __shfl_sync(0xffffffffu, kscale.y, j);
+      s = __fmaf_rn(s, mul, off * qsum);
     }
-    const bool live = j < n_kv && j <= q_pos;
-    sc[i] = live ? s : -INFINITY;
+    sc[i] = (j < n_kv && j <= q_pos) ? s : -INFINITY;
     mx = fmaxf(mx, sc[i]);
   }
   mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
@@ -820,41 +879,41 @@ __global__ void __launch_bounds__(kDecThreads)
   sum += __shfl_xor_sync(0xffffffffu, sum, 1);
   sum += __shfl_xor_sync(0xffffffffu, sum, 2);
   if (!mbar_wait(&bars[1], 0)) return;
-  // value multipliers: FP8 scale, INT4 scale (its zero adds sum_j p_j zero_j), bf16 1
-  float vmax = 0.0f, corr = 0.0f;
+  // value multipliers: lane j holds slot j's; their max over the window normalises P'
+  float2 vscale = make_float2(lane < n_kv ? 1.0f : 0.0f, 0.0f);
+  if (VK != OASIS_KV_BF16 && lane < n_past)
+    vscale = decode_slot_scale(sm_dec + lay.v_aux + lane * 32, v_kind(lane), hh);
+  float vmax = 1.0f, corr = 0.0f;
+  if (VK != OASIS_KV_BF16) {
+    vmax = vscale.x;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, o));
+  }
+  const float inv_vmax = vmax > 0.0f ? 1.0f / vmax : 0.0f;
+  float pv[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     const int j = 8 * (i >> 1) + 2 * c + (i & 1);
-    if (j >= n_kv) continue;
-    float m = 1.0f;
-    if (j < n_past) {
-      const int vk = decode_kind(lay.v_kinds, j);
-      const uint8_t* va = sm_dec + lay.v_aux + j * 32;
-      if (vk == OASIS_KV_FP8) {
-        m = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(va)[hh]);
-      } else if (vk == OASIS_KV_INT4) {
-        m = __half2float(reinterpret_cast<const __half*>(va)[hh]);
-        vz[i] = __half2float(reinterpret_cast<const __half*>(va + 16)[hh]);
-      }
+    pv[i] = sc[i];
+    if (VK != OASIS_KV_BF16) {
+      const float mul = __shfl_sync(0xffffffffu, vscale.x, j);
+      const float off = __shfl_sync(0xffffffffu, vscale.y, j);
+      pv[i] = sc[i] * mul * inv_vmax;
+      corr = __fmaf_rn(sc[i], off, corr);
     }
-    vm[i] = m;
-    vmax = fmaxf(vmax, m);
-    corr = __fmaf_rn(sc[i], vz[i], corr);
   }
-  vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 1));
-  vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 2));
-  corr += __shfl_xor_sync(0xffffffffu, corr, 1);
-  corr += __shfl_xor_sync(0xffffffffu, corr, 2);
-  const float inv_vmax = vmax > 0.0f ? 1.0f / vmax : 0.0f;
+  if (VK == OASIS_KV_INT4 || VK == kDecMixed) {
+    corr += __shfl_xor_sync(0xffffffffu, corr, 1);
+    corr += __shfl_xor_sync(0xffffffffu, corr, 2);
+  }
   // P' as the A operand of the two k-steps of keys (0..15, 16..31): row 0 only
   uint32_t pa[2][2];
 #pragma unroll
   for (int k2 = 0; k2 < 2; ++k2) {
     pa[k2][0] = pa[k2][1] = 0u;
     if (g == 0) {
-      const int i0 = 4 * k2, i1 = 4 * k2 + 2;  // n-tiles 2 k2 and 2 k2 + 1
-      pa[k2][0] = pack_f16x2(sc[i0] * vm[i0] * inv_vmax, sc[i0 + 1] * vm[i0 + 1] * inv_vmax);
-      pa[k2][1] = pack_f16x2(sc[i1] * vm[i1] * inv_vmax, sc[i1 + 1] * vm[i1 + 1] * inv_vmax);
+      pa[k2][0] = pack_f16x2(pv[4 * k2], pv[4 * k2 + 1]);
+      pa[k2][1] = pack_f16x2(pv[4 * k2 + 2], pv[4 * k2 + 3]);
     }
   }
 
@@ -869,26 +928,8 @@ __global__ void __launch_bounds__(kDecThreads)
 #pragma unroll
     for (int r = 0; r < 4; ++r) {
       const int j = 16 * k2 + 2 * c + (r & 1) + 8 * (r >> 1);
-      const int kind = j < n_past ? decode_kind(lay.v_kinds, j) : (j < n_kv ? OASIS_KV_BF16 : -1);
-      const uint8_t* row = j < n_past ? sm_dec + lay.v_base + j * lay.v_stride : sm_dec + lay.live + 2048;
-      F[r][0] = F[r][1] = F[r][2] = F[r][3] = 0u;
-      if (kind == OASIS_KV_FP8) {
-        const uint2 x = *reinterpret_cast<const uint2*>(row + hh * 64 + 8 * g);
-        F[r][0] = f16x2_e4m3x2(x.x & 0xFFFFu);
-        F[r][1] = f16x2_e4m3x2(x.x >> 16);
-        F[r][2] = f16x2_e4m3x2(x.y & 0xFFFFu);
-        F[r][3] = f16x2_e4m3x2(x.y >> 16);
-      } else if (kind == OASIS_KV_INT4) {
-        const uint32_t x = *reinterpret_cast<const uint32_t*>(row + hh * 32 + 4 * g);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) F[r][q] = f16x2_nibbles((x >> (8 * q)) & 0xFFu);
-      } else if (kind == OASIS_KV_BF16) {
-        const uint4 x = *reinterpret_cast<const uint4*>(row + hh * 128 + 16 * g);
-        F[r][0] = f16x2_bf16x2(x.x);
-        F[r][1] = f16x2_bf16x2(x.y);
-        F[r][2] = f16x2_bf16x2(x.z);
-        F[r][3] = f16x2_bf16x2(x.w);
-      }
+      decode_value_row(j < n_past ? sm_dec + lay.v_base + j * lay.v_stride : sm_dec + lay.live + 2048,
+                       v_kind(j), hh, g, F[r]);
     }
 #pragma unroll
     for (int n2 = 0; n2 < 8; ++n2) {
@@ -904,15 +945,35 @@ __global__ void __launch_bounds__(kDecThreads)
     uint32_t o[8];
 #pragma unroll
     for (int k = 0; k < 8; k += 2) {
-      const int d0 = k, d1 = k + 1;  // dims 16c + k, + k + 1 (both column 2c)
-      o[k / 2] = pack_bf16x2(__fmaf_rn(vmax, oacc[d0][0], corr) * inv, __fmaf_rn(vmax, oacc[d1][0], corr) * inv);
-      o[4 + k / 2] = pack_bf16x2(__fmaf_rn(vmax, oacc[d0][1], corr) * inv, __fmaf_rn(vmax, oacc[d1][1], corr) * inv);
+      o[k / 2] = pack_bf16x2(__fmaf_rn(vmax, oacc[k][0], corr) * inv, __fmaf_rn(vmax, oacc[k + 1][0], corr) * inv);
+      o[4 + k / 2] = pack_bf16x2(__fmaf_rn(vmax, oacc[k][1], corr) * inv, __fmaf_rn(vmax, oacc[k + 1][1], corr) * inv);
     }
     uint4* orow = reinterpret_cast<uint4*>(out + (static_cast<long long>(b) * OASIS_TOKENS + p) * OASIS_HIDDEN +
                                            (hg * kDecHeads + hh) * 64 + 16 * c);
     orow[0] = make_uint4(o[0], o[1], o[2], o[3]);
     orow[1] = make_uint4(o[4], o[5], o[6], o[7]);
   }
+}
+
+// decode kernel for (key kind, value kind), each a storage kind or kDecMixed
+using DecodeKernel = void (*)(const __nv_bfloat16*, __nv_bfloat16*, const KvView, const DecodeLayout, int,
+                              int, int, float);
+template <int KK>
+DecodeKernel decode_kernel_v(int vk) {
+  switch (vk) {
+    case OASIS_KV_BF16: return attn_decode_kernel<KK, OASIS_KV_BF16>;
+    case OASIS_KV_FP8: return attn_decode_kernel<KK, OASIS_KV_FP8>;
+    case OASIS_KV_INT4: return attn_decode_kernel<KK, OASIS_KV_INT4>;
+  }
+  return attn_decode_kernel<KK, kDecMixed>;
+}
+DecodeKernel decode_kernel(int kk, int vk) {
+  switch (kk) {
+    case OASIS_KV_BF16: return decode_kernel_v<OASIS_KV_BF16>(vk);
+    case OASIS_KV_FP8: return decode_kernel_v<OASIS_KV_FP8>(vk);
+    case OASIS_KV_INT4: return decode_kernel_v<OASIS_KV_INT4>(vk);
+  }
+  return decode_kernel_v<kDecMixed>(vk);
 }
 
 // ----------------------------------------------------------------------------------
@@ -955,9 +1016,10 @@ int launch_attn_temporal(const void* qkv, const KvView& kv, int layer, void* out
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(attn_temporal_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                kTpSmemTma);
-    if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               kDecMaxSmem);
+    for (int kk = 0; kk < 4 && e == cudaSuccess; ++kk)
+      for (int vk = 0; vk < 4 && e == cudaSuccess; ++vk)
+        e = cudaFuncSetAttribute(decode_kernel(kk, vk), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 kDecMaxSmem);
     if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(attn_temporal)");
     configured = true;
   }
@@ -1006,8 +1068,15 @@ int launch_attn_temporal(const void* qkv, const KvView& kv, int layer, void* out
     if (lay.total > static_cast<uint32_t>(kDecMaxSmem))
       return fail(OASIS_ERR_UNSUPPORTED, "attn_decode_kernel: shared memory layout too large");
     dim3 grid(OASIS_TOKENS, OASIS_HEADS / kDecHeads, batch);
-    cudaError_t e = launch_pdl(attn_decode_kernel, grid, dim3(kDecThreads), lay.total, stream,
-                               static_cast<const __nv_bfloat16*>(qkv), static_cast<__nv_bfloat16*>(out),
+    // one kind for every cached slot of a tensor selects a specialised kernel
+    auto uniform = [&](int which) {
+      const int k0 = kv.t[which].kind[0];
+      for (int s = 1; s < n_past; ++s)
+        if (kv.t[which].kind[s] != k0) return kDecMixed;
+      return k0;
+    };
+    cudaError_t e = launch_pdl(decode_kernel(uniform(0), uniform(1)), grid, dim3(kDecThreads), lay.total,
+                               stream, static_cast<const __nv_bfloat16*>(qkv), static_cast<__nv_bfloat16*>(out),
                                kv, lay, layer, q_pos0, n_past, kScaleLog2);
     if (e != cudaSuccess) return cuda_status(e, "attn_decode_kernel");
     return OASIS_OK;
