@@ -6,6 +6,8 @@
 // arrive post-RoPE from the QKV GEMM epilogue.  Temporal K/V may come from the
 // quantised cache: FP8/INT4 codes are dequantised while they are staged into
 // shared memory, so the cache is never materialised in bf16 in HBM.
+#include <algorithm>
+
 #include "launch.cuh"
 
 namespace oasis {
@@ -594,34 +596,40 @@ __global__ void __launch_bounds__(kTpWarps * 32)
 
 // ----------------------------------------------------------------------------------
 // temporal attention of ONE query frame over cached frames (the incremental forward):
-// one CTA per (session, token, 8 heads), one warp per head, tensor cores (mma.sync
-// m16n8k16, f16 operands, fp32 accumulation) with the query in row 0.
+// a persistent grid; each CTA walks work items (session, token, 8 heads), one warp per
+// head, with the next item's rows in flight while it computes the current one.
 // ----------------------------------------------------------------------------------
-// Warp 0 brings every cached key and value row (8 heads: 1024 B bf16, 512 B FP8 codes,
-// 256 B INT4 codes), their scales and the live q/k/v rows into shared memory by bulk
-// copies on two mbarriers (q + keys, values), so the scores start while the values are
-// in flight.  The quantised codes are never expanded element by element: FP8 codes
-// become f16 by one cvt per pair (exact), INT4 codes by the 1024-offset f16 trick
-// (exact), bf16 rows by f32 -> f16 (exact in f16's normal range), and the per-frame
-// FP8 scale, the per-(token, head) INT4 scale and zero are applied to the fp32 scores
-// (s_j = scale_j * q.c_j [+ zero_j * sum(q)]) and to the probabilities
-// (p'_j = p_j * scale_j / max scale, plus sum_j p_j zero_j for INT4 values).  The head
-// dims are permuted inside each k-step so a thread's 16 dims of a key row are one
-// 16-byte load, and the output dims so its 8 dims of a value row are one load; the
-// row strides keep both load patterns free of shared-memory bank conflicts.
+// Per item, warp 0 brings the cached key and value rows (8 heads: 1024 B bf16, 512 B FP8
+// codes, 256 B INT4 codes per slot) into one of two shared-memory stages by bulk copies
+// and the per-slot scales/zeros by plain loads, and the query frame's own q, k, v rows,
+// on two mbarriers (q + keys, values).  Scores and probability-weighted values of the
+// cached slots run on tensor cores (mma.sync m16n8k16, f16 operands, fp32 accumulation,
+// the query in row 0): FP8 codes become f16 by one cvt per pair (exact), INT4 codes by the
+// 1024-offset f16 trick (exact), bf16 rows by f32 -> f16; the FP8 scale and the INT4
+// scale and zero are applied to the fp32 scores (s_j = scale_j * q.c_j [+ zero_j sum(q)])
+// and to the probabilities (p'_j = p_j * scale_j / max scale, plus sum_j p_j zero_j).
+// The query frame's own key and value (bf16) are one more key on the CUDA cores.  Head
+// dims are permuted inside each k-step so a thread's 16 dims of a key row are one load,
+// and the output dims so its 8 dims of a value row are one load; each kind's rows sit in
+// their own region with a stride that keeps those loads free of bank conflicts.  Slots
+// past the cached frames map to rows zero-filled once, so the tiles need no branch.
 constexpr int kDecHeads = 8;
 constexpr int kDecThreads = kDecHeads * 32;
-constexpr int kDecMaxSmem = 96 * 1024;
+constexpr int kDecMaxStage = 112 * 1024;  // two stages must fit the 227 KB of a CTA
+// Kinds of the decode kernel's template: one storage kind for every cached slot of a
+// tensor, or kDecMixed (per-slot kinds and row offsets from the layout).
+constexpr int kDecMixed = 3;
 
 struct DecodeLayout {
-  uint32_t k_base, v_base;      // cached rows: slot s at base + s * stride
-  uint32_t k_stride, v_stride;
-  uint32_t k_aux, v_aux;        // per slot 32 B: FP8 8 bf16 scales; INT4 8 fp16 scales, 8 fp16 zeros
-  uint32_t live;                // q | k | v rows of the query frame, 1 KB each
-  uint32_t k_bytes, v_bytes;    // bytes expected on the two barriers
-  uint32_t total;
-  unsigned long long k_kinds, v_kinds;  // 2 bits per cached slot
-  int live_kv;                  // the query frame's own K/V is key n_past
+  uint32_t k_row[OASIS_MAX_FRAMES], v_row[OASIS_MAX_FRAMES];  // row of slot j in a stage
+  uint32_t k_base, v_base, k_stride, v_stride;  // uniform kinds: row j at base + j * stride
+  uint32_t aux;          // K scales of slot j at aux + 32 j, V scales at aux + 1024 + 32 j
+  uint32_t live;         // q | k | v rows of the query frame, 1 KB each
+  uint32_t stage_bytes;  // one pipeline stage (a multiple of 128)
+  uint32_t k_bytes, v_bytes;  // bulk-copy bytes of one item on the two barriers
+  unsigned long long k_kinds, v_kinds;  // 2 bits per slot 0..31 (slots past n_past: kind of their zero row)
+  int live_kv;           // the query frame's own K/V is a key (at window position n_past)
+  int items;             // batch * 144 tokens * 2 head groups
 };
 
 __device__ __forceinline__ int decode_kind(unsigned long long kinds, int j) {
@@ -658,13 +666,13 @@ __device__ __forceinline__ void mma_f16_16816(float (&c)[4], uint32_t a0, uint32
       : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
       : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
 }
-
-// Kinds of the decode kernel's template: one storage kind for every cached slot of a
-// tensor, or kDecMixed (per-slot kinds from the layout's 2-bit masks).
-constexpr int kDecMixed = 3;
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
 
 // f16 fragments of 16 dims (4 k-steps x 2 registers) of one key row of head hh: dims
-// 16c + 4ks + {0,1} in [ks][0], + {2,3} in [ks][1].  kind < 0: a key past the window (zeros).
+// 16c + 4ks + {0,1} in [ks][0], + {2,3} in [ks][1].
 __device__ __forceinline__ void decode_key_frag(const uint8_t* row, int kind, int hh, int c,
                                                 uint32_t (&kb)[4][2]) {
   if (kind == OASIS_KV_FP8) {
@@ -683,7 +691,7 @@ __device__ __forceinline__ void decode_key_frag(const uint8_t* row, int kind, in
       kb[ks][0] = f16x2_nibbles(h & 0xFFu);
       kb[ks][1] = f16x2_nibbles((h >> 8) & 0xFFu);
     }
-  } else if (kind == OASIS_KV_BF16) {
+  } else {
     const uint4* kp = reinterpret_cast<const uint4*>(row + hh * 128 + 32 * c);
     const uint4 x0 = kp[0], x1 = kp[1];
     const uint32_t w[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
@@ -692,9 +700,6 @@ __device__ __forceinline__ void decode_key_frag(const uint8_t* row, int kind, in
       kb[ks][0] = f16x2_bf16x2(w[2 * ks]);
       kb[ks][1] = f16x2_bf16x2(w[2 * ks + 1]);
     }
-  } else {
-#pragma unroll
-    for (int ks = 0; ks < 4; ++ks) kb[ks][0] = kb[ks][1] = 0u;
   }
 }
 
@@ -711,18 +716,16 @@ __device__ __forceinline__ void decode_value_row(const uint8_t* row, int kind, i
     const uint32_t x = *reinterpret_cast<const uint32_t*>(row + hh * 32 + 4 * g);
 #pragma unroll
     for (int q = 0; q < 4; ++q) F[q] = f16x2_nibbles((x >> (8 * q)) & 0xFFu);
-  } else if (kind == OASIS_KV_BF16) {
+  } else {
     const uint4 x = *reinterpret_cast<const uint4*>(row + hh * 128 + 16 * g);
     F[0] = f16x2_bf16x2(x.x);
     F[1] = f16x2_bf16x2(x.y);
     F[2] = f16x2_bf16x2(x.z);
     F[3] = f16x2_bf16x2(x.w);
-  } else {
-    F[0] = F[1] = F[2] = F[3] = 0u;
   }
 }
 
-// Multiplier and offset of cached slot j's key (s_j = acc * mul + off * sum(q)) or value
+// Multiplier and offset of a cached slot's key (s_j = acc * mul + off * sum(q)) or value
 // (O += p_j * mul * codes, + p_j * off) for head hh: FP8 (scale, 0), INT4 (scale, zero),
 // bf16 (1, 0).
 __device__ __forceinline__ float2 decode_slot_scale(const uint8_t* aux, int kind, int hh) {
@@ -734,27 +737,40 @@ __device__ __forceinline__ float2 decode_slot_scale(const uint8_t* aux, int kind
 }
 
 template <int KK, int VK>
-__global__ void __launch_bounds__(kDecThreads, 4)
+__global__ void __launch_bounds__(kDecThreads, 2)
     attn_decode_kernel(const __nv_bfloat16* __restrict__ qkv, __nv_bfloat16* __restrict__ out,
                        const __grid_constant__ KvView kv, const __grid_constant__ DecodeLayout lay,
                        int layer, int q_pos, int n_past, float scale_log2) {
   pdl_trigger();
   extern __shared__ __align__(128) uint8_t sm_dec[];
-  __shared__ __align__(8) uint64_t bars[2];
+  __shared__ __align__(8) uint64_t bars[2][2];  // [stage][keys, values]
+  __shared__ int abort_flag;                    // a bounded wait gave up: every warp stops
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int p = blockIdx.x, hg = blockIdx.y, b = blockIdx.z;
-  const int n_kv = n_past + lay.live_kv;
+  const int hh = warp;                   // head within the group
+  const int g = lane >> 2, c = lane & 3;  // mma fragment coordinates
   if (threadIdx.x == 0) {
-    mbar_init(&bars[0], 1);
-    mbar_init(&bars[1], 1);
+    abort_flag = 0;
+    for (int st = 0; st < 2; ++st) {
+      mbar_init(&bars[st][0], 1);
+      mbar_init(&bars[st][1], 1);
+    }
     mbar_fence_init();
   }
+  // both stages zero-filled once: rows of slots past the cached frames stay zero
+  for (uint32_t i = threadIdx.x * 16; i < 2 * lay.stage_bytes; i += kDecThreads * 16)
+    *reinterpret_cast<uint4*>(sm_dec + i) = make_uint4(0, 0, 0, 0);
+  fence_async_smem_cta();  // the zeros land before any bulk copy writes the same bytes
   __syncthreads();
   pdl_wait();
-  if (warp == 0) {
+
+  // warp 0: one item's rows into stage st
+  auto issue = [&](int item, int st) {
+    const int hg = item & 1, tok = item >> 1;
+    const int p = tok % OASIS_TOKENS, b = tok / OASIS_TOKENS;
+    uint8_t* stage = sm_dec + st * lay.stage_bytes;
     if (lane == 0) {
-      mbar_arrive_expect_tx(&bars[0], lay.k_bytes);
-      mbar_arrive_expect_tx(&bars[1], lay.v_bytes);
+      mbar_expect_tx(&bars[st][0], lay.k_bytes);
+      mbar_expect_tx(&bars[st][1], lay.v_bytes);
     }
     __syncwarp();
     if (lane < n_past) {  // lane s: the keys and values of cached slot s
@@ -762,9 +778,9 @@ __global__ void __launch_bounds__(kDecThreads, 4)
 #pragma unroll
       for (int which = 0; which < 2; ++which) {
         const KvTensor& t = kv.t[which];
-        uint64_t* bar = &bars[which];
-        uint8_t* row = sm_dec + (which ? lay.v_base + s * lay.v_stride : lay.k_base + s * lay.k_stride);
-        uint8_t* aux = sm_dec + (which ? lay.v_aux : lay.k_aux) + s * 32;
+        uint64_t* bar = &bars[st][which];
+        uint8_t* row = stage + (which ? lay.v_row[s] : lay.k_row[s]);
+        uint8_t* aux = stage + lay.aux + which * 1024 + s * 32;
         const int tk = which ? VK : KK;
         const int kind = tk == kDecMixed ? static_cast<int>(t.kind[s]) : tk;
         const int idx = t.index[s];
@@ -776,182 +792,222 @@ __global__ void __launch_bounds__(kDecThreads, 4)
           const long long page = kv_page(b, kv.layers, layer, t.n_fp8, idx);
           bulk_load(row, t.fp8 + (page * OASIS_TOKENS + p) * OASIS_HIDDEN + hg * kDecHeads * 64,
                     kDecHeads * 64, bar);
-          bulk_load(aux, t.fp8_scale + page * OASIS_HEADS + hg * kDecHeads, 16, bar);
+          *reinterpret_cast<uint4*>(aux) =
+              *reinterpret_cast<const uint4*>(t.fp8_scale + page * OASIS_HEADS + hg * kDecHeads);
         } else {
           const long long page = kv_page(b, kv.layers, layer, t.n_int4, idx);
           const long long grp = (page * OASIS_TOKENS + p) * OASIS_HEADS + hg * kDecHeads;
           bulk_load(row, t.int4 + grp * 32, kDecHeads * 32, bar);
-          bulk_load(aux, t.i4_scale + grp, 16, bar);
-          bulk_load(aux + 16, t.i4_zero + grp, 16, bar);
+          *reinterpret_cast<uint4*>(aux) = *reinterpret_cast<const uint4*>(t.i4_scale + grp);
+          *reinterpret_cast<uint4*>(aux + 16) = *reinterpret_cast<const uint4*>(t.i4_zero + grp);
         }
       }
     } else if (lane == 31) {  // the query frame's own q, k, v (bf16 rows of the QKV output)
       const __nv_bfloat16* row = qkv + (static_cast<long long>(b) * OASIS_TOKENS + p) * kQkvLd + hg * kDecHeads * 64;
-      bulk_load(sm_dec + lay.live, row, kDecHeads * 128, &bars[0]);
+      bulk_load(stage + lay.live, row, kDecHeads * 128, &bars[st][0]);
       if (lay.live_kv) {
-        bulk_load(sm_dec + lay.live + 1024, row + OASIS_HIDDEN, kDecHeads * 128, &bars[0]);
-        bulk_load(sm_dec + lay.live + 2048, row + 2 * OASIS_HIDDEN, kDecHeads * 128, &bars[1]);
+        bulk_load(stage + lay.live + 1024, row + OASIS_HIDDEN, kDecHeads * 128, &bars[st][0]);
+        bulk_load(stage + lay.live + 2048, row + 2 * OASIS_HIDDEN, kDecHeads * 128, &bars[st][1]);
       }
     }
-  }
-  const int hh = warp;                   // head within the group
-  const int g = lane >> 2, c = lane & 3;  // mma fragment coordinates
-  // kind of a key / value slot j (a compile-time constant unless mixed; -1 past the window)
-  auto k_kind = [&](int j) -> int {
-    if (j >= n_kv) return -1;
-    if (j >= n_past) return OASIS_KV_BF16;
-    return KK == kDecMixed ? decode_kind(lay.k_kinds, j) : KK;
+    __syncwarp();  // the scale stores of every lane before the arrivals release them
+    if (lane == 0) {
+      mbar_arrive(&bars[st][0]);
+      mbar_arrive(&bars[st][1]);
+    }
   };
-  auto v_kind = [&](int j) -> int {
-    if (j >= n_kv) return -1;
-    if (j >= n_past) return OASIS_KV_BF16;
-    return VK == kDecMixed ? decode_kind(lay.v_kinds, j) : VK;
-  };
-  if (!mbar_wait(&bars[0], 0)) return;  // timeout recorded in the device error word
+  auto k_kind = [&](int j) { return KK == kDecMixed ? decode_kind(lay.k_kinds, j) : KK; };
+  auto v_kind = [&](int j) { return VK == kDecMixed ? decode_kind(lay.v_kinds, j) : VK; };
+  auto k_row = [&](int j) { return KK == kDecMixed ? lay.k_row[j] : lay.k_base + j * lay.k_stride; };
+  auto v_row = [&](int j) { return VK == kDecMixed ? lay.v_row[j] : lay.v_base + j * lay.v_stride; };
+  const bool live_key = lay.live_kv && n_past <= q_pos;
 
-  // ---- q as the A operand: row 0 only (lanes 0..3); lane c holds dims 16c..16c+15,
-  // k-step ks covering dims 16c + 4ks + {0,1} (a0) and + {2,3} (a2)
-  uint32_t qa[4][2];
-  float qsum = 0.0f;
-#pragma unroll
-  for (int ks = 0; ks < 4; ++ks) qa[ks][0] = qa[ks][1] = 0u;
-  if (g == 0) {
-    const uint4* qp = reinterpret_cast<const uint4*>(sm_dec + lay.live + hh * 128 + 32 * c);
-    const uint4 x0 = qp[0], x1 = qp[1];
-    const uint32_t w[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-#pragma unroll
-    for (int ks = 0; ks < 4; ++ks) {
-      qa[ks][0] = f16x2_bf16x2(w[2 * ks]);
-      qa[ks][1] = f16x2_bf16x2(w[2 * ks + 1]);
-      if (KK == OASIS_KV_INT4 || KK == kDecMixed) {
-        const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&qa[ks][0]));
-        const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&qa[ks][1]));
-        qsum += (f0.x + f0.y) + (f1.x + f1.y);
-      }
-    }
-  }
-  if (KK == OASIS_KV_INT4 || KK == kDecMixed) {
-    qsum += __shfl_xor_sync(0xffffffffu, qsum, 1);
-    qsum += __shfl_xor_sync(0xffffffffu, qsum, 2);
-  }
-  // lane j: multiplier / offset of key j (scale 1, offset 0 for bf16 and the live key)
-  float2 kscale = make_float2(1.0f, 0.0f);
-  if (KK != OASIS_KV_BF16 && lane < n_past)
-    kscale = decode_slot_scale(sm_dec + lay.k_aux + lane * 32, k_kind(lane), hh);
+  int it = blockIdx.x;
+  if (warp == 0 && it < lay.items) issue(it, 0);
+  for (int k = 0; it < lay.items; ++k, it += gridDim.x) {
+    const int st = k & 1;
+    const uint32_t ph = (k >> 1) & 1;
+    const bool next = it + static_cast<int>(gridDim.x) < lay.items;
+    if (warp == 0 && next) issue(it + gridDim.x, st ^ 1);
+    const uint8_t* stage = sm_dec + st * lay.stage_bytes;
+    const int hg = it & 1, tok = it >> 1;
+    // a wait that gives up records a timeout in the device error word; the CTA then
+    // stops after this item (below), every warp at the same point
+    bool ok = mbar_wait(&bars[st][0], ph);
+    if (ok) {
 
-  // ---- scores: n-tile nt holds keys 8nt..8nt+7; this thread supplies key 8nt + g
-  float sacc[4][4];
+    // ---- the query: lane l holds dims 2l, 2l+1 (the live key's score); lanes 0..3 also
+    // hold the A operand (row 0), lane c dims 16c..16c+15 in k-step order
+    const uint32_t qw = *reinterpret_cast<const uint32_t*>(stage + lay.live + hh * 128 + 4 * lane);
+    float s_live = -INFINITY;
+    if (live_key) {
+      const uint32_t kw = *reinterpret_cast<const uint32_t*>(stage + lay.live + 1024 + hh * 128 + 4 * lane);
+      float d = __fmaf_rn(bf16_hi(qw), bf16_hi(kw), bf16_lo(qw) * bf16_lo(kw));
 #pragma unroll
-  for (int nt = 0; nt < 4; ++nt) {
-    sacc[nt][0] = sacc[nt][1] = sacc[nt][2] = sacc[nt][3] = 0.0f;
-    const int j = 8 * nt + g;
-    uint32_t kb[4][2];
-    decode_key_frag(j < n_past ? sm_dec + lay.k_base + j * lay.k_stride : sm_dec + lay.live + 1024,
-                    k_kind(j), hh, c, kb);
-#pragma unroll
-    for (int ks = 0; ks < 4; ++ks) mma_f16_16816(sacc[nt], qa[ks][0], qa[ks][1], kb[ks][0], kb[ks][1]);
-  }
-
-  // ---- per key (row 0: lanes 0..3 hold keys 8nt + 2c + e): scale, mask, softmax
-  float sc[8];
-  float mx = -INFINITY;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int j = 8 * (i >> 1) + 2 * c + (i & 1);
-    float s = sacc[i >> 1][i & 1];
-    if (KK != OASIS_KV_BF16) {
-      const float mul = __shfl_sync(0xffffffffu, kscale.x, j);
-      const float off = __shfl_sync(0xffffffffu, kscale.y, j);
-      s = __fmaf_rn(s, mul, off * qsum);
+      for (int o = 16; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+      s_live = d;
     }
-    sc[i] = (j < n_kv && j <= q_pos) ? s : -INFINITY;
-    mx = fmaxf(mx, sc[i]);
-  }
-  mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-  mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-  float sum = 0.0f;
+    uint32_t qa[4][2];
+    float qsum = 0.0f;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const float pr = sc[i] == -INFINITY ? 0.0f : exp2f(__fmaf_rn(sc[i], scale_log2, -mx * scale_log2));
-    sum += pr;
-    sc[i] = bf16_round(pr);  // the probability as the tensor-core path rounds it
-  }
-  sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-  sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-  if (!mbar_wait(&bars[1], 0)) return;
-  // value multipliers: lane j holds slot j's; their max over the window normalises P'
-  float2 vscale = make_float2(lane < n_kv ? 1.0f : 0.0f, 0.0f);
-  if (VK != OASIS_KV_BF16 && lane < n_past)
-    vscale = decode_slot_scale(sm_dec + lay.v_aux + lane * 32, v_kind(lane), hh);
-  float vmax = 1.0f, corr = 0.0f;
-  if (VK != OASIS_KV_BF16) {
-    vmax = vscale.x;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, o));
-  }
-  const float inv_vmax = vmax > 0.0f ? 1.0f / vmax : 0.0f;
-  float pv[8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int j = 8 * (i >> 1) + 2 * c + (i & 1);
-    pv[i] = sc[i];
-    if (VK != OASIS_KV_BF16) {
-      const float mul = __shfl_sync(0xffffffffu, vscale.x, j);
-      const float off = __shfl_sync(0xffffffffu, vscale.y, j);
-      pv[i] = sc[i] * mul * inv_vmax;
-      corr = __fmaf_rn(sc[i], off, corr);
-    }
-  }
-  if (VK == OASIS_KV_INT4 || VK == kDecMixed) {
-    corr += __shfl_xor_sync(0xffffffffu, corr, 1);
-    corr += __shfl_xor_sync(0xffffffffu, corr, 2);
-  }
-  // P' as the A operand of the two k-steps of keys (0..15, 16..31): row 0 only
-  uint32_t pa[2][2];
-#pragma unroll
-  for (int k2 = 0; k2 < 2; ++k2) {
-    pa[k2][0] = pa[k2][1] = 0u;
+    for (int ks = 0; ks < 4; ++ks) qa[ks][0] = qa[ks][1] = 0u;
     if (g == 0) {
-      pa[k2][0] = pack_f16x2(pv[4 * k2], pv[4 * k2 + 1]);
-      pa[k2][1] = pack_f16x2(pv[4 * k2 + 2], pv[4 * k2 + 3]);
+      const uint4* qp = reinterpret_cast<const uint4*>(stage + lay.live + hh * 128 + 32 * c);
+      const uint4 x0 = qp[0], x1 = qp[1];
+      const uint32_t w[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks) {
+        qa[ks][0] = f16x2_bf16x2(w[2 * ks]);
+        qa[ks][1] = f16x2_bf16x2(w[2 * ks + 1]);
+        if (KK == OASIS_KV_INT4 || KK == kDecMixed) {
+          const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&qa[ks][0]));
+          const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&qa[ks][1]));
+          qsum += (f0.x + f0.y) + (f1.x + f1.y);
+        }
+      }
     }
-  }
+    if (KK == OASIS_KV_INT4 || KK == kDecMixed) {
+      qsum += __shfl_xor_sync(0xffffffffu, qsum, 1);
+      qsum += __shfl_xor_sync(0xffffffffu, qsum, 2);
+    }
+    // lane j: multiplier / offset of cached key j
+    float2 kscale = make_float2(1.0f, 0.0f);
+    if (KK != OASIS_KV_BF16 && lane < n_past) kscale = decode_slot_scale(stage + lay.aux + lane * 32, k_kind(lane), hh);
 
-  // ---- O = P' V: n-tile nt2 column g is output dim 8g + nt2; this thread supplies keys
-  // 16 k2 + 2c + {0, 1, 8, 9}, dims 8g..8g+7 of each
-  float oacc[8][4];
+    // ---- cached scores: n-tile nt holds keys 8nt..8nt+7; this thread supplies key 8nt + g
+    float sacc[4][4];
 #pragma unroll
-  for (int n2 = 0; n2 < 8; ++n2) oacc[n2][0] = oacc[n2][1] = oacc[n2][2] = oacc[n2][3] = 0.0f;
+    for (int nt = 0; nt < 4; ++nt) {
+      sacc[nt][0] = sacc[nt][1] = sacc[nt][2] = sacc[nt][3] = 0.0f;
+      const int j = 8 * nt + g;
+      uint32_t kb[4][2];
+      decode_key_frag(stage + k_row(j), k_kind(j), hh, c, kb);
 #pragma unroll
-  for (int k2 = 0; k2 < 2; ++k2) {
-    uint32_t F[4][4];
-#pragma unroll
-    for (int r = 0; r < 4; ++r) {
-      const int j = 16 * k2 + 2 * c + (r & 1) + 8 * (r >> 1);
-      decode_value_row(j < n_past ? sm_dec + lay.v_base + j * lay.v_stride : sm_dec + lay.live + 2048,
-                       v_kind(j), hh, g, F[r]);
+      for (int ks = 0; ks < 4; ++ks) mma_f16_16816(sacc[nt], qa[ks][0], qa[ks][1], kb[ks][0], kb[ks][1]);
     }
+
+    // ---- softmax over the cached keys (row 0: lanes 0..3 hold keys 8nt + 2c + e) and the live key
+    float sc[8];
+    float mx = s_live;
 #pragma unroll
-    for (int n2 = 0; n2 < 8; ++n2) {
-      const uint32_t sel = (n2 & 1) ? 0x7632u : 0x5410u;
-      const uint32_t b0 = __byte_perm(F[0][n2 >> 1], F[1][n2 >> 1], sel);
-      const uint32_t b1 = __byte_perm(F[2][n2 >> 1], F[3][n2 >> 1], sel);
-      mma_f16_16816(oacc[n2], pa[k2][0], pa[k2][1], b0, b1);
+    for (int i = 0; i < 8; ++i) {
+      const int j = 8 * (i >> 1) + 2 * c + (i & 1);
+      float s = sacc[i >> 1][i & 1];
+      if (KK != OASIS_KV_BF16) {
+        const float mul = __shfl_sync(0xffffffffu, kscale.x, j);
+        if (KK == OASIS_KV_INT4 || KK == kDecMixed)
+          s = __fmaf_rn(s, mul, __shfl_sync(0xffffffffu, kscale.y, j) * qsum);
+        else
+          s *= mul;
+      }
+      sc[i] = (j < n_past && j <= q_pos) ? s : -INFINITY;
+      mx = fmaxf(mx, sc[i]);
     }
-  }
-  if (g == 0) {
-    // lane c holds dims 16c + n2 (column 2c) and 16c + 8 + n2 (column 2c + 1)
-    const float inv = 1.0f / sum;
-    uint32_t o[8];
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    const float mxs = mx * scale_log2;
+    float sum = 0.0f;
 #pragma unroll
-    for (int k = 0; k < 8; k += 2) {
-      o[k / 2] = pack_bf16x2(__fmaf_rn(vmax, oacc[k][0], corr) * inv, __fmaf_rn(vmax, oacc[k + 1][0], corr) * inv);
-      o[4 + k / 2] = pack_bf16x2(__fmaf_rn(vmax, oacc[k][1], corr) * inv, __fmaf_rn(vmax, oacc[k + 1][1], corr) * inv);
+    for (int i = 0; i < 8; ++i) {
+      const float pr = sc[i] == -INFINITY ? 0.0f : exp2f(__fmaf_rn(sc[i], scale_log2, -mxs));
+      sum += pr;
+      sc[i] = bf16_round(pr);  // the probability as the tensor-core path rounds it
     }
-    uint4* orow = reinterpret_cast<uint4*>(out + (static_cast<long long>(b) * OASIS_TOKENS + p) * OASIS_HIDDEN +
-                                           (hg * kDecHeads + hh) * 64 + 16 * c);
-    orow[0] = make_uint4(o[0], o[1], o[2], o[3]);
-    orow[1] = make_uint4(o[4], o[5], o[6], o[7]);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+    const float p_live = live_key ? exp2f(__fmaf_rn(s_live, scale_log2, -mxs)) : 0.0f;
+    sum += p_live;
+    const float pb_live = bf16_round(p_live);
+    ok = mbar_wait(&bars[st][1], ph);
+    if (ok) {
+    // value multipliers: lane j holds slot j's; their max normalises P'
+    float2 vscale = make_float2(lane < n_past ? 1.0f : 0.0f, 0.0f);
+    if (VK != OASIS_KV_BF16 && lane < n_past)
+      vscale = decode_slot_scale(stage + lay.aux + 1024 + lane * 32, v_kind(lane), hh);
+    float vmax = 1.0f, corr = 0.0f;
+    if (VK != OASIS_KV_BF16) {
+      vmax = vscale.x;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, o));
+    }
+    const float inv_vmax = 1.0f / vmax;
+    float pv[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int j = 8 * (i >> 1) + 2 * c + (i & 1);
+      pv[i] = sc[i];
+      if (VK != OASIS_KV_BF16) {
+        pv[i] = sc[i] * __shfl_sync(0xffffffffu, vscale.x, j) * inv_vmax;
+        if (VK == OASIS_KV_INT4 || VK == kDecMixed) corr = __fmaf_rn(sc[i], __shfl_sync(0xffffffffu, vscale.y, j), corr);
+      }
+    }
+    if (VK == OASIS_KV_INT4 || VK == kDecMixed) {
+      corr += __shfl_xor_sync(0xffffffffu, corr, 1);
+      corr += __shfl_xor_sync(0xffffffffu, corr, 2);
+    }
+    uint32_t pa[2][2];
+#pragma unroll
+    for (int k2 = 0; k2 < 2; ++k2) {
+      pa[k2][0] = pa[k2][1] = 0u;
+      if (g == 0) {
+        pa[k2][0] = pack_f16x2(pv[4 * k2], pv[4 * k2 + 1]);
+        pa[k2][1] = pack_f16x2(pv[4 * k2 + 2], pv[4 * k2 + 3]);
+      }
+    }
+
+    // ---- O = P' V: n-tile n2 column g is output dim 8g + n2; this thread supplies keys
+    // 16 k2 + 2c + {0, 1, 8, 9}, dims 8g..8g+7 of each
+    float oacc[8][4];
+#pragma unroll
+    for (int n2 = 0; n2 < 8; ++n2) oacc[n2][0] = oacc[n2][1] = oacc[n2][2] = oacc[n2][3] = 0.0f;
+#pragma unroll
+    for (int k2 = 0; k2 < 2; ++k2) {
+      uint32_t F[4][4];
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        const int j = 16 * k2 + 2 * c + (r & 1) + 8 * (r >> 1);
+        decode_value_row(stage + v_row(j), v_kind(j), hh, g, F[r]);
+      }
+#pragma unroll
+      for (int n2 = 0; n2 < 8; ++n2) {
+        const uint32_t sel = (n2 & 1) ? 0x7632u : 0x5410u;
+        const uint32_t b0 = __byte_perm(F[0][n2 >> 1], F[1][n2 >> 1], sel);
+        const uint32_t b1 = __byte_perm(F[2][n2 >> 1], F[3][n2 >> 1], sel);
+        mma_f16_16816(oacc[n2], pa[k2][0], pa[k2][1], b0, b1);
+      }
+    }
+    if (g == 0) {
+      // lane c holds dims 16c + n2 (column 2c) and 16c + 8 + n2 (column 2c + 1)
+      const float inv = 1.0f / sum;
+      const uint4* vl = reinterpret_cast<const uint4*>(stage + lay.live + 2048 + hh * 128 + 32 * c);
+      const uint4 v0 = vl[0], v1 = vl[1];
+      const uint32_t vw[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+      uint32_t o[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        // dims 16c + 2k, 16c + 2k + 1: accumulators of columns 2c (k < 4) / 2c + 1
+        const int n2 = (2 * k) & 7, col = k >> 2;
+        const float a0 = __fmaf_rn(vmax, oacc[n2][col], corr), a1 = __fmaf_rn(vmax, oacc[n2 + 1][col], corr);
+        o[k] = pack_bf16x2(__fmaf_rn(pb_live, bf16_lo(vw[k]), a0) * inv, __fmaf_rn(pb_live, bf16_hi(vw[k]), a1) * inv);
+      }
+      uint4* orow = reinterpret_cast<uint4*>(out + (static_cast<long long>(tok) * OASIS_HIDDEN) +
+                                             (hg * kDecHeads + hh) * 64 + 16 * c);
+      orow[0] = make_uint4(o[0], o[1], o[2], o[3]);
+      orow[1] = make_uint4(o[4], o[5], o[6], o[7]);
+    }
+    }  // values arrived
+    }  // keys arrived
+    if (!ok) abort_flag = 1;
+    __syncthreads();  // every warp is done with this stage before it is refilled
+    if (abort_flag) {
+      // the prefetched item's copies land (bounded) before the CTA exits
+      if (threadIdx.x == 0 && next) {
+        const uint32_t ph_next = ((k + 1) >> 1) & 1;
+        mbar_wait(&bars[st ^ 1][0], ph_next);
+        mbar_wait(&bars[st ^ 1][1], ph_next);
+      }
+      return;
+    }
   }
 }
 
@@ -1019,64 +1075,81 @@ int launch_attn_temporal(const void* qkv, const KvView& kv, int layer, void* out
     for (int kk = 0; kk < 4 && e == cudaSuccess; ++kk)
       for (int vk = 0; vk < 4 && e == cudaSuccess; ++vk)
         e = cudaFuncSetAttribute(decode_kernel(kk, vk), cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 kDecMaxSmem);
+                                 2 * kDecMaxStage);
     if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(attn_temporal)");
     configured = true;
   }
   if (q_frames == 1 && n_past > 0 && n_past < OASIS_MAX_FRAMES) {
-    // one query frame over cached slots: the decode kernel.  Shared memory: cached key
-    // rows, value rows (uniform strides by the widest kind present, padded so the
-    // fragment loads are conflict-free), 32 B of scales per slot and tensor, the live rows
+    // one query frame over cached slots: the persistent decode kernel.  A stage holds the
+    // key rows and the value rows of the 32 slots, each kind in its own region with a
+    // stride that keeps the fragment loads conflict-free (key rows: bf16 1040, FP8 576,
+    // INT4 288 B; value rows: 1040, 528, 272 B), 2 x 32 x 32 B of scales, the live rows.
+    // Slots past n_past take rows of the narrowest kind present, which stay zero.
     DecodeLayout lay{};
     lay.live_kv = n_kv > n_past ? 1 : 0;
-    int k_widest = OASIS_KV_INT4, v_widest = OASIS_KV_INT4;  // INT4 < FP8 < bf16 in bytes
-    auto wider = [](int a, int k) {
-      auto bytes = [](int kind) { return kind == OASIS_KV_BF16 ? 2 : (kind == OASIS_KV_FP8 ? 1 : 0); };
-      return bytes(k) > bytes(a) ? k : a;
-    };
+    lay.items = batch * OASIS_TOKENS * 2;
     auto codes = [](int kind) -> uint32_t {
       return kind == OASIS_KV_BF16 ? kDecHeads * 128 : (kind == OASIS_KV_FP8 ? kDecHeads * 64 : kDecHeads * 32);
     };
-    auto aux = [](int kind) -> uint32_t { return kind == OASIS_KV_BF16 ? 0u : (kind == OASIS_KV_FP8 ? 16u : 32u); };
-    lay.k_bytes = (1 + lay.live_kv) * kDecHeads * 128;  // live q (and k) rows
-    lay.v_bytes = lay.live_kv * kDecHeads * 128;        // live v row
-    for (int s = 0; s < n_past; ++s) {
-      const int kk = kv.t[0].kind[s], vk = kv.t[1].kind[s];
-      k_widest = wider(k_widest, kk);
-      v_widest = wider(v_widest, vk);
-      lay.k_kinds |= static_cast<unsigned long long>(kk) << (2 * s);
-      lay.v_kinds |= static_cast<unsigned long long>(vk) << (2 * s);
-      lay.k_bytes += codes(kk) + aux(kk);
-      lay.v_bytes += codes(vk) + aux(vk);
-    }
-    // key rows: one 16-byte (FP8), 8-byte (INT4) or 2 x 16-byte (bf16) load per thread
-    // from 8 rows; value rows: 8-, 4- or 16-byte loads from 4 rows two apart
-    lay.k_stride = k_widest == OASIS_KV_BF16 ? 1040 : (k_widest == OASIS_KV_FP8 ? 576 : 288);
-    lay.v_stride = v_widest == OASIS_KV_BF16 ? 1040 : (v_widest == OASIS_KV_FP8 ? 528 : 272);
+    const uint32_t k_strides[3] = {1040, 576, 288}, v_strides[3] = {1040, 528, 272};
     uint32_t off = 0;
-    lay.k_base = off;
-    off += n_past * lay.k_stride;
-    lay.v_base = off;
-    off += n_past * lay.v_stride;
-    lay.k_aux = off;
-    off += n_past * 32;
-    lay.v_aux = off;
-    off += n_past * 32;
+    int uniform[2];
+    for (int which = 0; which < 2; ++which) {
+      const KvTensor& t = kv.t[which];
+      const uint32_t* stride = which ? v_strides : k_strides;
+      int kinds[OASIS_MAX_FRAMES];
+      bool present[3] = {false, false, false};
+      for (int s = 0; s < n_past; ++s) {
+        kinds[s] = t.kind[s];
+        present[kinds[s]] = true;
+      }
+      int narrow = OASIS_KV_BF16;  // the kind with the smallest rows present
+      for (int k : {OASIS_KV_FP8, OASIS_KV_INT4})
+        if (present[k]) narrow = k;
+      for (int s = n_past; s < OASIS_MAX_FRAMES; ++s) kinds[s] = narrow;
+      uniform[which] = (present[0] + present[1] + present[2] == 1) ? narrow : kDecMixed;
+      uint32_t* rows = which ? lay.v_row : lay.k_row;
+      unsigned long long mask = 0;
+      for (int k : {OASIS_KV_BF16, OASIS_KV_FP8, OASIS_KV_INT4}) {  // one region per kind
+        for (int s = 0; s < OASIS_MAX_FRAMES; ++s)
+          if (kinds[s] == k) {
+            rows[s] = off;
+            off += stride[k];
+          }
+      }
+      for (int s = 0; s < OASIS_MAX_FRAMES; ++s) mask |= static_cast<unsigned long long>(kinds[s]) << (2 * s);
+      uint32_t bytes = 0;
+      for (int s = 0; s < n_past; ++s) bytes += codes(kinds[s]);
+      if (which) {
+        lay.v_kinds = mask;
+        lay.v_bytes = bytes + lay.live_kv * kDecHeads * 128;
+        lay.v_base = rows[0];
+        lay.v_stride = stride[narrow];
+      } else {
+        lay.k_kinds = mask;
+        lay.k_bytes = bytes + (1 + lay.live_kv) * kDecHeads * 128;
+        lay.k_base = rows[0];
+        lay.k_stride = stride[narrow];
+      }
+    }
+    lay.aux = off;
+    off += 2 * 1024;
     lay.live = off;
     off += 3 * kDecHeads * 128;
-    lay.total = off;
-    if (lay.total > static_cast<uint32_t>(kDecMaxSmem))
-      return fail(OASIS_ERR_UNSUPPORTED, "attn_decode_kernel: shared memory layout too large");
-    dim3 grid(OASIS_TOKENS, OASIS_HEADS / kDecHeads, batch);
-    // one kind for every cached slot of a tensor selects a specialised kernel
-    auto uniform = [&](int which) {
-      const int k0 = kv.t[which].kind[0];
-      for (int s = 1; s < n_past; ++s)
-        if (kv.t[which].kind[s] != k0) return kDecMixed;
-      return k0;
-    };
-    cudaError_t e = launch_pdl(decode_kernel(uniform(0), uniform(1)), grid, dim3(kDecThreads), lay.total,
-                               stream, static_cast<const __nv_bfloat16*>(qkv), static_cast<__nv_bfloat16*>(out),
+    lay.stage_bytes = (off + 127) & ~127u;
+    if (lay.stage_bytes > static_cast<uint32_t>(kDecMaxStage))
+      return fail(OASIS_ERR_UNSUPPORTED, "attn_decode_kernel: stage layout too large");
+    DecodeKernel kern = decode_kernel(uniform[0], uniform[1]);
+    const size_t smem = 2 * static_cast<size_t>(lay.stage_bytes);
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kDecThreads, smem) != cudaSuccess ||
+        per_sm < 1) {
+      cudaGetLastError();
+      per_sm = 1;
+    }
+    const int ctas = std::min(lay.items, per_sm * num_sms());
+    cudaError_t e = launch_pdl(kern, dim3(ctas), dim3(kDecThreads), smem, stream,
+                               static_cast<const __nv_bfloat16*>(qkv), static_cast<__nv_bfloat16*>(out),
                                kv, lay, layer, q_pos0, n_past, kScaleLog2);
     if (e != cudaSuccess) return cuda_status(e, "attn_decode_kernel");
     return OASIS_OK;

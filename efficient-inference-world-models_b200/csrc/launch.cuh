@@ -36,6 +36,8 @@ int encode_bf16_sw128(CUtensorMap* map, const void* base, int rank, const long l
                       const long long* strides_bytes, const int* box);
 int validate_slots(const oasis_kv_cache_t* c, int slot0, int frames);
 
+int num_sms();
+
 int launch_attn_spatial(const void* qkv, void* out, int frames, cudaStream_t stream);
 int launch_attn_temporal(const void* qkv, const KvView& kv, int layer, void* out, int batch,
                          int q_frames, int q_pos0, int n_past, int n_kv, cudaStream_t stream);
