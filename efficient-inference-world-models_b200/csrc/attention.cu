@@ -595,46 +595,79 @@ __global__ void __launch_bounds__(kTpWarps * 32)
 
 
 // ----------------------------------------------------------------------------------
-// temporal attention of ONE query frame over cached frames (the incremental forward):
-// a persistent grid; each CTA walks work items (session, token, 8 heads), one warp per
-// head, with the next item's rows in flight while it computes the current one.
+// temporal attention of ONE query frame over cached frames (the incremental forward)
 // ----------------------------------------------------------------------------------
-// Per item, warp 0 brings the cached key and value rows (8 heads: 1024 B bf16, 512 B FP8
-// codes, 256 B INT4 codes per slot) into one of two shared-memory stages by bulk copies
-// and the per-slot scales/zeros by plain loads, and the query frame's own q, k, v rows,
-// on two mbarriers (q + keys, values).  Scores and probability-weighted values of the
-// cached slots run on tensor cores (mma.sync m16n8k16, f16 operands, fp32 accumulation,
-// the query in row 0): FP8 codes become f16 by one cvt per pair (exact), INT4 codes by the
-// 1024-offset f16 trick (exact), bf16 rows by f32 -> f16; the FP8 scale and the INT4
-// scale and zero are applied to the fp32 scores (s_j = scale_j * q.c_j [+ zero_j sum(q)])
-// and to the probabilities (p'_j = p_j * scale_j / max scale, plus sum_j p_j zero_j).
-// The query frame's own key and value (bf16) are one more key on the CUDA cores.  Head
-// dims are permuted inside each k-step so a thread's 16 dims of a key row are one load,
-// and the output dims so its 8 dims of a value row are one load; each kind's rows sit in
-// their own region with a stride that keeps those loads free of bank conflicts.  Slots
-// past the cached frames map to rows zero-filled once, so the tiles need no branch.
-constexpr int kDecHeads = 8;
-constexpr int kDecThreads = kDecHeads * 32;
-constexpr int kDecMaxStage = 112 * 1024;  // two stages must fit the 227 KB of a CTA
+// One warp per (session, token, head): the head's 64-dim query row against up to 31
+// cached key rows plus the frame's own key.  Warps are independent (no shared memory, no
+// block barrier); a persistent grid walks the items, and each warp issues the next
+// item's loads straight into registers as soon as the current item's copies are used
+// (keys, query and key scales after the scores; values and value scales after P V), so
+// one item's rows are in flight while the warp computes the other.
+// Both products run on tensor cores (mma.sync m16n8k16, fp32 accumulation):
+//   scores  S[1 x 32] = q K^T: the query is row 0 of A, the keys are the B columns
+//           (n-tile nt = keys 8nt..8nt+7; thread (g, c) supplies key 8nt + g);
+//   output  O^T[64 x 1] = V^T P^T: V^T is A (m-tile mo = 16 dims; thread (g, c) supplies
+//           keys 16kv + 2c + {0, 1, 8, 9}, dims 8g..8g+7) and P^T is column 0 of B, which
+//           is where the score accumulators of lanes 0..3 already hold it.
+// Rows keep their storage format until the fragment is built: a tensor whose cached
+// slots are all bf16 feeds bf16 mma directly; FP8 codes become f16 by one cvt per pair
+// (exact); INT4 codes by the 1024-offset f16 trick on nibble pairs (exact).  Inside each
+// k-step the head dims are permuted so a thread's dims of a key row are one contiguous
+// load, and the query takes the same permutation.  FP8 scales and INT4 scale/zero apply
+// to the fp32 scores (s_j = scale_j q.c_j + zero_j sum(q)) and to the probabilities
+// (p'_j = p_j scale_j / max scale, plus sum_j p_j zero_j).  The frame's own key and value
+// (bf16 rows of the QKV output) are one more key on the CUDA cores.
+constexpr int kDecWarps = 8;
+constexpr int kDecThreads = kDecWarps * 32;
 // Kinds of the decode kernel's template: one storage kind for every cached slot of a
-// tensor, or kDecMixed (per-slot kinds and row offsets from the layout).
+// tensor, or kDecMixed (per-slot kinds from the layout).
 constexpr int kDecMixed = 3;
 
+struct DecodeTensor {
+  uint32_t slot_page[OASIS_MAX_FRAMES];  // layer * n_kind + pool index of slot j
+  unsigned long long kinds;              // 2 bits per slot (slots past n_past: any kind)
+  uint32_t session_pages[3];             // per kind: layers * n_kind, the pages of one session
+};
 struct DecodeLayout {
-  uint32_t k_row[OASIS_MAX_FRAMES], v_row[OASIS_MAX_FRAMES];  // row of slot j in a stage
-  uint32_t k_base, v_base, k_stride, v_stride;  // uniform kinds: row j at base + j * stride
-  uint32_t aux;          // K scales of slot j at aux + 32 j, V scales at aux + 1024 + 32 j
-  uint32_t live;         // q | k | v rows of the query frame, 1 KB each
-  uint32_t stage_bytes;  // one pipeline stage (a multiple of 128)
-  uint32_t k_bytes, v_bytes;  // bulk-copy bytes of one item on the two barriers
-  unsigned long long k_kinds, v_kinds;  // 2 bits per slot 0..31 (slots past n_past: kind of their zero row)
-  int live_kv;           // the query frame's own K/V is a key (at window position n_past)
-  int items;             // batch * 144 tokens * 2 head groups
+  DecodeTensor t[2];  // keys, values
+  int items;          // batch * 144 tokens * 16 heads
+  int live_kv;        // the query frame's own K/V is a key (at window position n_past)
 };
 
-__device__ __forceinline__ int decode_kind(unsigned long long kinds, int j) {
-  return static_cast<int>((kinds >> (2 * j)) & 3ull);
+// bytes of one token's 1024 elements / one head's 64 elements in a pool of `kind`
+__host__ __device__ constexpr uint32_t dec_row_bytes(int kind) {
+  return kind == OASIS_KV_BF16 ? 2048u : (kind == OASIS_KV_FP8 ? 1024u : 512u);
 }
+__host__ __device__ constexpr uint32_t dec_head_bytes(int kind) { return dec_row_bytes(kind) / 16; }
+
+__device__ __forceinline__ uint4 ldg_stream_v4(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
+  return r;
+}
+__device__ __forceinline__ uint2 ldg_stream_v2(const void* p) {
+  uint2 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];" : "=r"(r.x), "=r"(r.y) : "l"(p));
+  return r;
+}
+__device__ __forceinline__ uint32_t ldg_stream_u32(const void* p) {
+  uint32_t r;
+  asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(r) : "l"(p));
+  return r;
+}
+__device__ __forceinline__ uint32_t ldg_u16(const void* p) {
+  unsigned short r;
+  asm volatile("ld.global.nc.u16 %0, [%1];" : "=h"(r) : "l"(p));
+  return r;
+}
+// rows of the QKV output (written by the preceding kernel): coherent loads
+__device__ __forceinline__ uint4 ldg_v4(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
+  return r;
+}
+
 __device__ __forceinline__ uint32_t f16x2_e4m3x2(uint32_t two_codes) {
   uint32_t h;
   const uint16_t v = static_cast<uint16_t>(two_codes);
@@ -646,93 +679,200 @@ __device__ __forceinline__ uint32_t f16x2_bf16x2(uint32_t w) {
   asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(h) : "f"(bf16_hi(w)), "f"(bf16_lo(w)));
   return h;
 }
-// one packed byte of two INT4 codes (element 2i high) -> f16x2 (high nibble in the low half)
-__device__ __forceinline__ uint32_t f16x2_nibbles(uint32_t byte) {
-  const uint32_t biased = ((byte >> 4) & 0xFu) | ((byte & 0xFu) << 16) | 0x64006400u;  // 1024 + code
-  uint32_t h;
-  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(h) : "r"(biased), "r"(0x64006400u));
-  return h;
-}
 __device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
   uint32_t h;
   asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(h) : "f"(hi), "f"(lo));
   return h;
 }
-__device__ __forceinline__ void mma_f16_16816(float (&c)[4], uint32_t a0, uint32_t a2, uint32_t b0,
-                                              uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
-      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-      : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
+__device__ __forceinline__ uint32_t sub_1024(uint32_t biased) {
+  uint32_t h;
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(h) : "r"(biased), "r"(0x64006400u));
+  return h;
 }
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
-  asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
-               : "memory");
+// nibbles at bits s..s+3 and 16+s..19+s of u -> f16x2 (exact codes 0..15)
+__device__ __forceinline__ uint32_t nibble_pair(uint32_t u, int s) {
+  return sub_1024(((u >> s) & 0x000F000Fu) | 0x64006400u);
+}
+// one packed byte of two INT4 codes (element 2i high) -> f16x2 (element 2i in the low half)
+__device__ __forceinline__ uint32_t f16x2_nibbles(uint32_t byte) {
+  return sub_1024(((byte >> 4) & 0xFu) | ((byte & 0xFu) << 16) | 0x64006400u);
+}
+template <bool BF16>
+__device__ __forceinline__ void mma_16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                          uint32_t b0, uint32_t b1) {
+  if (BF16)
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
+        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+  else
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// f16 fragments of 16 dims (4 k-steps x 2 registers) of one key row of head hh: dims
-// 16c + 4ks + {0,1} in [ks][0], + {2,3} in [ks][1].
-__device__ __forceinline__ void decode_key_frag(const uint8_t* row, int kind, int hh, int c,
-                                                uint32_t (&kb)[4][2]) {
-  if (kind == OASIS_KV_FP8) {
-    const uint4 x = *reinterpret_cast<const uint4*>(row + hh * 64 + 16 * c);
-    const uint32_t w[4] = {x.x, x.y, x.z, x.w};
+// Key fragments of one key row (this thread's 16 dims, one contiguous chunk) for the 4
+// k-steps: kb[ks][0] pairs with the query's A register of columns 2c, 2c+1, kb[ks][1]
+// with columns 2c+8, 2c+9.  Dim order: bf16 and FP8 tensors take dims 16c + 4ks + {0,1}
+// and + {2,3} ("consecutive"); INT4 and mixed tensors take, for k = 0, 1, dims
+// 16c + 8k + {0,4}, {1,5} (k-step 2k) and {2,6}, {3,7} (k-step 2k+1) ("nibble" order,
+// the order in which a masked shift takes nibble pairs out of one 32-bit word).
+__device__ __forceinline__ void key_fragments_int4(uint32_t w0, uint32_t w1, uint32_t (&kb)[4][2]) {
+  const uint32_t w[2] = {w0, w1};
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    kb[2 * k][0] = nibble_pair(w[k], 4);       // elements 0, 4
+    kb[2 * k][1] = nibble_pair(w[k], 0);       // 1, 5
+    kb[2 * k + 1][0] = nibble_pair(w[k], 12);  // 2, 6
+    kb[2 * k + 1][1] = nibble_pair(w[k], 8);   // 3, 7
+  }
+}
+template <int KK, int KW>
+__device__ __forceinline__ void key_fragments(const uint32_t (&w)[KW], int kind, uint32_t (&kb)[4][2]) {
+  if constexpr (KK == OASIS_KV_BF16) {
 #pragma unroll
     for (int ks = 0; ks < 4; ++ks) {
-      kb[ks][0] = f16x2_e4m3x2(w[ks] & 0xFFFFu);
+      kb[ks][0] = w[2 * ks];
+      kb[ks][1] = w[2 * ks + 1];
+    }
+  } else if constexpr (KK == OASIS_KV_FP8) {
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks) {
+      kb[ks][0] = f16x2_e4m3x2(w[ks]);
       kb[ks][1] = f16x2_e4m3x2(w[ks] >> 16);
     }
-  } else if (kind == OASIS_KV_INT4) {
-    const uint2 x = *reinterpret_cast<const uint2*>(row + hh * 32 + 8 * c);
+  } else if constexpr (KK == OASIS_KV_INT4) {
+    key_fragments_int4(w[0], w[1], kb);
+  } else if (kind == OASIS_KV_INT4) {  // mixed tensor (8 words a row)
+    key_fragments_int4(w[0], w[1], kb);
+  } else if (kind == OASIS_KV_FP8) {  // mixed tensor, FP8 row in nibble order
 #pragma unroll
-    for (int ks = 0; ks < 4; ++ks) {
-      const uint32_t h = ((ks < 2) ? x.x : x.y) >> (16 * (ks & 1));
-      kb[ks][0] = f16x2_nibbles(h & 0xFFu);
-      kb[ks][1] = f16x2_nibbles((h >> 8) & 0xFFu);
+    for (int k = 0; k < 2; ++k) {
+      const uint32_t x = __byte_perm(w[2 * k], w[2 * k + 1], 0x5140);  // d0 d4 d1 d5
+      const uint32_t y = __byte_perm(w[2 * k], w[2 * k + 1], 0x7362);  // d2 d6 d3 d7
+      kb[2 * k][0] = f16x2_e4m3x2(x);
+      kb[2 * k][1] = f16x2_e4m3x2(x >> 16);
+      kb[2 * k + 1][0] = f16x2_e4m3x2(y);
+      kb[2 * k + 1][1] = f16x2_e4m3x2(y >> 16);
     }
-  } else {
-    const uint4* kp = reinterpret_cast<const uint4*>(row + hh * 128 + 32 * c);
-    const uint4 x0 = kp[0], x1 = kp[1];
-    const uint32_t w[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+  } else {  // mixed tensor, bf16 row in nibble order
 #pragma unroll
-    for (int ks = 0; ks < 4; ++ks) {
-      kb[ks][0] = f16x2_bf16x2(w[2 * ks]);
-      kb[ks][1] = f16x2_bf16x2(w[2 * ks + 1]);
+    for (int k = 0; k < 2; ++k) {
+      kb[2 * k][0] = f16x2_bf16x2(__byte_perm(w[4 * k], w[4 * k + 2], 0x5410));
+      kb[2 * k][1] = f16x2_bf16x2(__byte_perm(w[4 * k], w[4 * k + 2], 0x7632));
+      kb[2 * k + 1][0] = f16x2_bf16x2(__byte_perm(w[4 * k + 1], w[4 * k + 3], 0x5410));
+      kb[2 * k + 1][1] = f16x2_bf16x2(__byte_perm(w[4 * k + 1], w[4 * k + 3], 0x7632));
     }
   }
 }
 
-// f16 pairs of dims 8g..8g+7 of one value row of head hh (dims 8g + 2q, + 1 in F[q]).
-__device__ __forceinline__ void decode_value_row(const uint8_t* row, int kind, int hh, int g,
-                                                 uint32_t (&F)[4]) {
-  if (kind == OASIS_KV_FP8) {
-    const uint2 x = *reinterpret_cast<const uint2*>(row + hh * 64 + 8 * g);
-    F[0] = f16x2_e4m3x2(x.x & 0xFFFFu);
-    F[1] = f16x2_e4m3x2(x.x >> 16);
-    F[2] = f16x2_e4m3x2(x.y & 0xFFFFu);
-    F[3] = f16x2_e4m3x2(x.y >> 16);
-  } else if (kind == OASIS_KV_INT4) {
-    const uint32_t x = *reinterpret_cast<const uint32_t*>(row + hh * 32 + 4 * g);
+// f16x2 pairs of dims (2m, 2m+1), m = 0..3, of one value row's 8-dim chunk (mixed
+// tensors: 4 words a row)
+__device__ __forceinline__ void value_row_pairs(const uint32_t (&r)[4], int kind, uint32_t (&G)[4]) {
+  if (kind == OASIS_KV_BF16) {
 #pragma unroll
-    for (int q = 0; q < 4; ++q) F[q] = f16x2_nibbles((x >> (8 * q)) & 0xFFu);
+    for (int m = 0; m < 4; ++m) G[m] = f16x2_bf16x2(r[m]);
+  } else if (kind == OASIS_KV_FP8) {
+#pragma unroll
+    for (int m = 0; m < 2; ++m) {
+      G[2 * m] = f16x2_e4m3x2(r[m]);
+      G[2 * m + 1] = f16x2_e4m3x2(r[m] >> 16);
+    }
   } else {
-    const uint4 x = *reinterpret_cast<const uint4*>(row + hh * 128 + 16 * g);
-    F[0] = f16x2_bf16x2(x.x);
-    F[1] = f16x2_bf16x2(x.y);
-    F[2] = f16x2_bf16x2(x.z);
-    F[3] = f16x2_bf16x2(x.w);
+#pragma unroll
+    for (int m = 0; m < 4; ++m) G[m] = f16x2_nibbles((r[0] >> (8 * m)) & 0xFFu);
+  }
+}
+__device__ __forceinline__ void value_fragments_bf16(const uint32_t* r0, const uint32_t* r1, uint32_t (&F)[8]) {
+#pragma unroll
+  for (int m = 0; m < 4; ++m) {
+    F[2 * m] = __byte_perm(r0[m], r1[m], 0x5410);
+    F[2 * m + 1] = __byte_perm(r0[m], r1[m], 0x7632);
+  }
+}
+__device__ __forceinline__ void value_fragments_fp8(const uint32_t* r0, const uint32_t* r1, uint32_t (&F)[8]) {
+#pragma unroll
+  for (int m = 0; m < 2; ++m) {
+    const uint32_t x = __byte_perm(r0[m], r1[m], 0x5140);  // dims 4m of both keys, then 4m+1
+    const uint32_t y = __byte_perm(r0[m], r1[m], 0x7362);  // dims 4m+2, 4m+3
+    F[4 * m] = f16x2_e4m3x2(x);
+    F[4 * m + 1] = f16x2_e4m3x2(x >> 16);
+    F[4 * m + 2] = f16x2_e4m3x2(y);
+    F[4 * m + 3] = f16x2_e4m3x2(y >> 16);
+  }
+}
+__device__ __forceinline__ void value_fragments_int4(uint32_t r0, uint32_t r1, uint32_t (&F)[8]) {
+  const uint32_t x = __byte_perm(r0, r1, 0x5410);  // elements 0..3 of both keys
+  const uint32_t y = __byte_perm(r0, r1, 0x7632);  // elements 4..7
+  F[0] = nibble_pair(x, 4);
+  F[1] = nibble_pair(x, 0);
+  F[2] = nibble_pair(x, 12);
+  F[3] = nibble_pair(x, 8);
+  F[4] = nibble_pair(y, 4);
+  F[5] = nibble_pair(y, 0);
+  F[6] = nibble_pair(y, 12);
+  F[7] = nibble_pair(y, 8);
+}
+// V^T fragments of two keys (r0: key 2c [+8], r1: key 2c+1 [+8]): F[e] = the pair
+// (key 0, key 1) of dim 8g + e; bf16 pairs for a tensor of bf16 slots, else f16.
+template <int VK, int VW>
+__device__ __forceinline__ void value_fragments(const uint32_t (&r0)[VW], const uint32_t (&r1)[VW], int k0,
+                                                int k1, uint32_t (&F)[8]) {
+  if constexpr (VK == OASIS_KV_BF16) {
+    value_fragments_bf16(r0, r1, F);
+  } else if constexpr (VK == OASIS_KV_FP8) {
+    value_fragments_fp8(r0, r1, F);
+  } else if constexpr (VK == OASIS_KV_INT4) {
+    value_fragments_int4(r0[0], r1[0], F);
+  } else if (k0 != k1) {  // mixed tensor, two kinds: each row to f16 pairs, then interleave
+    uint32_t G0[4], G1[4];
+    value_row_pairs(r0, k0, G0);
+    value_row_pairs(r1, k1, G1);
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      F[2 * m] = __byte_perm(G0[m], G1[m], 0x5410);
+      F[2 * m + 1] = __byte_perm(G0[m], G1[m], 0x7632);
+    }
+  } else if (k0 == OASIS_KV_INT4) {
+    value_fragments_int4(r0[0], r1[0], F);
+  } else if (k0 == OASIS_KV_FP8) {
+    value_fragments_fp8(r0, r1, F);
+  } else {
+    value_fragments_bf16(r0, r1, F);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) F[e] = f16x2_bf16x2(F[e]);
   }
 }
 
-// Multiplier and offset of a cached slot's key (s_j = acc * mul + off * sum(q)) or value
-// (O += p_j * mul * codes, + p_j * off) for head hh: FP8 (scale, 0), INT4 (scale, zero),
-// bf16 (1, 0).
-__device__ __forceinline__ float2 decode_slot_scale(const uint8_t* aux, int kind, int hh) {
-  if (kind == OASIS_KV_FP8) return make_float2(__bfloat162float(reinterpret_cast<const __nv_bfloat16*>(aux)[hh]), 0.0f);
-  if (kind == OASIS_KV_INT4)
-    return make_float2(__half2float(reinterpret_cast<const __half*>(aux)[hh]),
-                       __half2float(reinterpret_cast<const __half*>(aux + 16)[hh]));
+// Pool bytes of (session b, token p, head h) in a tensor's pool of `kind`.
+__device__ __forceinline__ const uint8_t* dec_item_rows(const KvTensor& t, const DecodeTensor& d, int kind,
+                                                        int b, int p, int h) {
+  const uint8_t* pool = kind == OASIS_KV_BF16 ? reinterpret_cast<const uint8_t*>(t.bf16)
+                                              : (kind == OASIS_KV_FP8 ? t.fp8 : t.int4);
+  return pool + (static_cast<long long>(b) * d.session_pages[kind] * OASIS_TOKENS + p) * dec_row_bytes(kind) +
+         h * dec_head_bytes(kind);
+}
+// Scale / zero element index of (session b, token p, head h) for page 0 of the session:
+// FP8 per (page, head), INT4 per (page, token, head).
+__device__ __forceinline__ long long dec_item_scale(const DecodeTensor& d, int kind, int b, int p, int h) {
+  if (kind == OASIS_KV_FP8) return static_cast<long long>(b) * d.session_pages[kind] * OASIS_HEADS + h;
+  return (static_cast<long long>(b) * d.session_pages[kind] * OASIS_TOKENS + p) * OASIS_HEADS + h;
+}
+__device__ __forceinline__ uint32_t dec_slot_scale(int kind, uint32_t slot_page) {
+  return kind == OASIS_KV_FP8 ? slot_page * OASIS_HEADS : slot_page * (OASIS_TOKENS * OASIS_HEADS);
+}
+// a slot's (multiplier, offset) from its raw scale bits: FP8 bf16 scale; INT4 f16 scale |
+// f16 zero << 16; bf16 (1, 0); slots past n_past (dead, 0) - keys are masked anyway
+__device__ __forceinline__ float2 dec_scale(uint32_t raw, int kind, bool live) {
+  if (!live) return make_float2(0.0f, 0.0f);
+  if (kind == OASIS_KV_FP8) return make_float2(__uint_as_float(raw << 16), 0.0f);
+  if (kind == OASIS_KV_INT4) {
+    const __half2 h = *reinterpret_cast<const __half2*>(&raw);
+    return __half22float2(h);
+  }
   return make_float2(1.0f, 0.0f);
 }
 
@@ -740,153 +880,225 @@ template <int KK, int VK>
 __global__ void __launch_bounds__(kDecThreads, 2)
     attn_decode_kernel(const __nv_bfloat16* __restrict__ qkv, __nv_bfloat16* __restrict__ out,
                        const __grid_constant__ KvView kv, const __grid_constant__ DecodeLayout lay,
-                       int layer, int q_pos, int n_past, float scale_log2) {
+                       int q_pos, int n_past, float scale_log2) {
   pdl_trigger();
-  extern __shared__ __align__(128) uint8_t sm_dec[];
-  __shared__ __align__(8) uint64_t bars[2][2];  // [stage][keys, values]
-  __shared__ int abort_flag;                    // a bounded wait gave up: every warp stops
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int hh = warp;                   // head within the group
-  const int g = lane >> 2, c = lane & 3;  // mma fragment coordinates
-  if (threadIdx.x == 0) {
-    abort_flag = 0;
-    for (int st = 0; st < 2; ++st) {
-      mbar_init(&bars[st][0], 1);
-      mbar_init(&bars[st][1], 1);
-    }
-    mbar_fence_init();
-  }
-  // both stages zero-filled once: rows of slots past the cached frames stay zero
-  for (uint32_t i = threadIdx.x * 16; i < 2 * lay.stage_bytes; i += kDecThreads * 16)
-    *reinterpret_cast<uint4*>(sm_dec + i) = make_uint4(0, 0, 0, 0);
-  fence_async_smem_cta();  // the zeros land before any bulk copy writes the same bytes
-  __syncthreads();
-  pdl_wait();
-
-  // warp 0: one item's rows into stage st
-  auto issue = [&](int item, int st) {
-    const int hg = item & 1, tok = item >> 1;
-    const int p = tok % OASIS_TOKENS, b = tok / OASIS_TOKENS;
-    uint8_t* stage = sm_dec + st * lay.stage_bytes;
-    if (lane == 0) {
-      mbar_expect_tx(&bars[st][0], lay.k_bytes);
-      mbar_expect_tx(&bars[st][1], lay.v_bytes);
-    }
-    __syncwarp();
-    if (lane < n_past) {  // lane s: the keys and values of cached slot s
-      const int s = lane;
-#pragma unroll
-      for (int which = 0; which < 2; ++which) {
-        const KvTensor& t = kv.t[which];
-        uint64_t* bar = &bars[st][which];
-        uint8_t* row = stage + (which ? lay.v_row[s] : lay.k_row[s]);
-        uint8_t* aux = stage + lay.aux + which * 1024 + s * 32;
-        const int tk = which ? VK : KK;
-        const int kind = tk == kDecMixed ? static_cast<int>(t.kind[s]) : tk;
-        const int idx = t.index[s];
-        if (kind == OASIS_KV_BF16) {
-          const long long page = kv_page(b, kv.layers, layer, t.n_bf16, idx);
-          bulk_load(row, t.bf16 + (page * OASIS_TOKENS + p) * OASIS_HIDDEN + hg * kDecHeads * 64,
-                    kDecHeads * 128, bar);
-        } else if (kind == OASIS_KV_FP8) {
-          const long long page = kv_page(b, kv.layers, layer, t.n_fp8, idx);
-          bulk_load(row, t.fp8 + (page * OASIS_TOKENS + p) * OASIS_HIDDEN + hg * kDecHeads * 64,
-                    kDecHeads * 64, bar);
-          *reinterpret_cast<uint4*>(aux) =
-              *reinterpret_cast<const uint4*>(t.fp8_scale + page * OASIS_HEADS + hg * kDecHeads);
-        } else {
-          const long long page = kv_page(b, kv.layers, layer, t.n_int4, idx);
-          const long long grp = (page * OASIS_TOKENS + p) * OASIS_HEADS + hg * kDecHeads;
-          bulk_load(row, t.int4 + grp * 32, kDecHeads * 32, bar);
-          *reinterpret_cast<uint4*>(aux) = *reinterpret_cast<const uint4*>(t.i4_scale + grp);
-          *reinterpret_cast<uint4*>(aux + 16) = *reinterpret_cast<const uint4*>(t.i4_zero + grp);
-        }
-      }
-    } else if (lane == 31) {  // the query frame's own q, k, v (bf16 rows of the QKV output)
-      const __nv_bfloat16* row = qkv + (static_cast<long long>(b) * OASIS_TOKENS + p) * kQkvLd + hg * kDecHeads * 64;
-      bulk_load(stage + lay.live, row, kDecHeads * 128, &bars[st][0]);
-      if (lay.live_kv) {
-        bulk_load(stage + lay.live + 1024, row + OASIS_HIDDEN, kDecHeads * 128, &bars[st][0]);
-        bulk_load(stage + lay.live + 2048, row + 2 * OASIS_HIDDEN, kDecHeads * 128, &bars[st][1]);
-      }
-    }
-    __syncwarp();  // the scale stores of every lane before the arrivals release them
-    if (lane == 0) {
-      mbar_arrive(&bars[st][0]);
-      mbar_arrive(&bars[st][1]);
-    }
+  constexpr int KW = KK == OASIS_KV_FP8 ? 4 : (KK == OASIS_KV_INT4 ? 2 : 8);  // words per key chunk
+  constexpr int VW = VK == OASIS_KV_FP8 ? 2 : (VK == OASIS_KV_INT4 ? 1 : 4);  // words per value chunk
+  constexpr bool kNibble = KK == OASIS_KV_INT4 || KK == kDecMixed;          // key dim order
+  constexpr bool kZeroK = KK == OASIS_KV_INT4 || KK == kDecMixed;           // keys may carry zeros
+  constexpr bool kZeroV = VK == OASIS_KV_INT4 || VK == kDecMixed;
+  const int lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
+  const KvTensor& tk = kv.t[0];
+  const KvTensor& tv = kv.t[1];
+  const DecodeTensor& dk = lay.t[0];
+  const DecodeTensor& dv = lay.t[1];
+  auto kind_of = [&](const DecodeTensor& d, int tmpl, int j) {
+    return tmpl == kDecMixed ? static_cast<int>((d.kinds >> (2 * j)) & 3ull) : tmpl;
   };
-  auto k_kind = [&](int j) { return KK == kDecMixed ? decode_kind(lay.k_kinds, j) : KK; };
-  auto v_kind = [&](int j) { return VK == kDecMixed ? decode_kind(lay.v_kinds, j) : VK; };
-  auto k_row = [&](int j) { return KK == kDecMixed ? lay.k_row[j] : lay.k_base + j * lay.k_stride; };
-  auto v_row = [&](int j) { return VK == kDecMixed ? lay.v_row[j] : lay.v_base + j * lay.v_stride; };
+
+  // ---- loop-invariant parts of this lane's addresses
+  // key rows r = 0..3: key 8r + g, dims 16c..16c+15
+  uint32_t koff[4];
+  int kkind[4];
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    const int j = 8 * r + g;
+    kkind[r] = kind_of(dk, KK, j);
+    koff[r] = dk.slot_page[j] * (OASIS_TOKENS * dec_row_bytes(kkind[r])) + c * (dec_head_bytes(kkind[r]) / 4);
+  }
+  // value rows q = 0..7: key 16 (q >> 2) + 2c + 8 ((q >> 1) & 1) + (q & 1), dims 8g..8g+7
+  uint32_t voff[8];
+  int vkind[8];
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    const int j = 16 * (q >> 2) + 2 * c + 8 * ((q >> 1) & 1) + (q & 1);
+    vkind[q] = kind_of(dv, VK, j);
+    voff[q] = dv.slot_page[j] * (OASIS_TOKENS * dec_row_bytes(vkind[q])) + g * (dec_head_bytes(vkind[q]) / 8);
+  }
+  // scales of slot `lane`
+  const bool slot_live = lane < n_past;
+  const int ks_kind = kind_of(dk, KK, lane), vs_kind = kind_of(dv, VK, lane);
+  const uint32_t ks_off = dec_slot_scale(ks_kind, dk.slot_page[lane]);
+  const uint32_t vs_off = dec_slot_scale(vs_kind, dv.slot_page[lane]);
   const bool live_key = lay.live_kv && n_past <= q_pos;
 
-  int it = blockIdx.x;
-  if (warp == 0 && it < lay.items) issue(it, 0);
-  for (int k = 0; it < lay.items; ++k, it += gridDim.x) {
-    const int st = k & 1;
-    const uint32_t ph = (k >> 1) & 1;
-    const bool next = it + static_cast<int>(gridDim.x) < lay.items;
-    if (warp == 0 && next) issue(it + gridDim.x, st ^ 1);
-    const uint8_t* stage = sm_dec + st * lay.stage_bytes;
-    const int hg = it & 1, tok = it >> 1;
-    // a wait that gives up records a timeout in the device error word; the CTA then
-    // stops after this item (below), every warp at the same point
-    bool ok = mbar_wait(&bars[st][0], ph);
-    if (ok) {
+  const int warps_total = gridDim.x * kDecWarps;
+  int it = blockIdx.x * kDecWarps + (threadIdx.x >> 5);
+  pdl_wait();
+  if (it >= lay.items) return;
 
-    // ---- the query: lane l holds dims 2l, 2l+1 (the live key's score); lanes 0..3 also
-    // hold the A operand (row 0), lane c dims 16c..16c+15 in k-step order
-    const uint32_t qw = *reinterpret_cast<const uint32_t*>(stage + lay.live + hh * 128 + 4 * lane);
-    float s_live = -INFINITY;
-    if (live_key) {
-      const uint32_t kw = *reinterpret_cast<const uint32_t*>(stage + lay.live + 1024 + hh * 128 + 4 * lane);
-      float d = __fmaf_rn(bf16_hi(qw), bf16_hi(kw), bf16_lo(qw) * bf16_lo(kw));
+  // ---- per-item loads (registers)
+  uint32_t kr[4][KW], qraw[8], klraw[8], ks_raw;
+  uint32_t vr[8][VW], vlraw[4], vs_raw;
+  auto load_keys = [&](int item) {
+    const int h = item & 15, tok = item >> 4;
+    const int p = tok % OASIS_TOKENS, b = tok / OASIS_TOKENS;
+    const uint8_t* base[3];
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
-      s_live = d;
-    }
-    uint32_t qa[4][2];
-    float qsum = 0.0f;
+    for (int k = 0; k < 3; ++k)
+      base[k] = (KK == kDecMixed || KK == k) ? dec_item_rows(tk, dk, k, b, p, h) : nullptr;
 #pragma unroll
-    for (int ks = 0; ks < 4; ++ks) qa[ks][0] = qa[ks][1] = 0u;
-    if (g == 0) {
-      const uint4* qp = reinterpret_cast<const uint4*>(stage + lay.live + hh * 128 + 32 * c);
-      const uint4 x0 = qp[0], x1 = qp[1];
-      const uint32_t w[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+    for (int r = 0; r < 4; ++r) {
+      const int kind = kkind[r];
 #pragma unroll
-      for (int ks = 0; ks < 4; ++ks) {
-        qa[ks][0] = f16x2_bf16x2(w[2 * ks]);
-        qa[ks][1] = f16x2_bf16x2(w[2 * ks + 1]);
-        if (KK == OASIS_KV_INT4 || KK == kDecMixed) {
-          const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&qa[ks][0]));
-          const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&qa[ks][1]));
-          qsum += (f0.x + f0.y) + (f1.x + f1.y);
+      for (int w = 0; w < KW; ++w) kr[r][w] = 0u;
+      if (8 * r + g < n_past) {
+        const uint8_t* src = base[kind] + koff[r];
+        if (kind == OASIS_KV_BF16) {
+          const uint4 x0 = ldg_stream_v4(src), x1 = ldg_stream_v4(src + 16);
+          const uint32_t v[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+          for (int w = 0; w < KW; ++w) kr[r][w] = v[w];
+        } else if (kind == OASIS_KV_FP8) {
+          const uint4 x = ldg_stream_v4(src);
+          const uint32_t v[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+          for (int w = 0; w < (KW < 4 ? KW : 4); ++w) kr[r][w] = v[w];
+        } else {
+          const uint2 x = ldg_stream_v2(src);
+          kr[r][0] = x.x;
+          kr[r][1] = x.y;
         }
       }
     }
-    if (KK == OASIS_KV_INT4 || KK == kDecMixed) {
+    // the query frame's q (lanes 0..3: dims 16c..16c+15) and its own key
+    const __nv_bfloat16* row = qkv + (static_cast<long long>(b) * OASIS_TOKENS + p) * kQkvLd + h * 64 + 16 * c;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) qraw[w] = klraw[w] = 0u;
+    if (g == 0) {
+      const uint4 a = ldg_v4(row), a1 = ldg_v4(row + 8);
+      qraw[0] = a.x; qraw[1] = a.y; qraw[2] = a.z; qraw[3] = a.w;
+      qraw[4] = a1.x; qraw[5] = a1.y; qraw[6] = a1.z; qraw[7] = a1.w;
+      if (live_key) {
+        const uint4 k0 = ldg_v4(row + OASIS_HIDDEN), k1 = ldg_v4(row + OASIS_HIDDEN + 8);
+        klraw[0] = k0.x; klraw[1] = k0.y; klraw[2] = k0.z; klraw[3] = k0.w;
+        klraw[4] = k1.x; klraw[5] = k1.y; klraw[6] = k1.z; klraw[7] = k1.w;
+      }
+    }
+    ks_raw = 0u;
+    if (KK != OASIS_KV_BF16 && slot_live) {
+      if (ks_kind == OASIS_KV_FP8) {
+        ks_raw = ldg_u16(tk.fp8_scale + dec_item_scale(dk, OASIS_KV_FP8, b, p, h) + ks_off);
+      } else if (ks_kind == OASIS_KV_INT4) {
+        const long long e = dec_item_scale(dk, OASIS_KV_INT4, b, p, h) + ks_off;
+        ks_raw = ldg_u16(tk.i4_scale + e) | (ldg_u16(tk.i4_zero + e) << 16);
+      }
+    }
+  };
+  auto load_values = [&](int item) {
+    const int h = item & 15, tok = item >> 4;
+    const int p = tok % OASIS_TOKENS, b = tok / OASIS_TOKENS;
+    const uint8_t* base[3];
+#pragma unroll
+    for (int k = 0; k < 3; ++k)
+      base[k] = (VK == kDecMixed || VK == k) ? dec_item_rows(tv, dv, k, b, p, h) : nullptr;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const int kind = vkind[q];
+      const int j = 16 * (q >> 2) + 2 * c + 8 * ((q >> 1) & 1) + (q & 1);
+#pragma unroll
+      for (int w = 0; w < VW; ++w) vr[q][w] = 0u;
+      if (j < n_past) {
+        const uint8_t* src = base[kind] + voff[q];
+        if (kind == OASIS_KV_BF16) {
+          const uint4 x = ldg_stream_v4(src);
+          const uint32_t v[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+          for (int w = 0; w < VW; ++w) vr[q][w] = v[w];
+        } else if (kind == OASIS_KV_FP8) {
+          const uint2 x = ldg_stream_v2(src);
+          vr[q][0] = x.x;
+          if (VW > 1) vr[q][VW > 1 ? 1 : 0] = x.y;
+        } else {
+          vr[q][0] = ldg_stream_u32(src);
+        }
+      }
+    }
+    // the frame's own value (lanes c == 0: dims 8g..8g+7)
+    vlraw[0] = vlraw[1] = vlraw[2] = vlraw[3] = 0u;
+    if (c == 0 && live_key) {
+      const uint4 v = ldg_v4(qkv + (static_cast<long long>(b) * OASIS_TOKENS + p) * kQkvLd + 2 * OASIS_HIDDEN +
+                             h * 64 + 8 * g);
+      vlraw[0] = v.x; vlraw[1] = v.y; vlraw[2] = v.z; vlraw[3] = v.w;
+    }
+    vs_raw = 0u;
+    if (VK != OASIS_KV_BF16 && slot_live) {
+      if (vs_kind == OASIS_KV_FP8) {
+        vs_raw = ldg_u16(tv.fp8_scale + dec_item_scale(dv, OASIS_KV_FP8, b, p, h) + vs_off);
+      } else if (vs_kind == OASIS_KV_INT4) {
+        const long long e = dec_item_scale(dv, OASIS_KV_INT4, b, p, h) + vs_off;
+        vs_raw = ldg_u16(tv.i4_scale + e) | (ldg_u16(tv.i4_zero + e) << 16);
+      }
+    }
+  };
+
+  load_keys(it);
+  load_values(it);
+  for (; it < lay.items; it += warps_total) {
+    const int nx = it + warps_total;
+    const int h = it & 15, tok = it >> 4;
+
+    // ---- the query as row 0 of A (lanes 0..3 hold it; other rows are don't-care)
+    uint32_t qa[4][2];
+    if (KK == OASIS_KV_BF16) {
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks) {
+        qa[ks][0] = qraw[2 * ks];
+        qa[ks][1] = qraw[2 * ks + 1];
+      }
+    } else if (!kNibble) {
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks) {
+        qa[ks][0] = f16x2_bf16x2(qraw[2 * ks]);
+        qa[ks][1] = f16x2_bf16x2(qraw[2 * ks + 1]);
+      }
+    } else {
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        qa[2 * k][0] = pack_f16x2(bf16_lo(qraw[4 * k]), bf16_lo(qraw[4 * k + 2]));
+        qa[2 * k][1] = pack_f16x2(bf16_hi(qraw[4 * k]), bf16_hi(qraw[4 * k + 2]));
+        qa[2 * k + 1][0] = pack_f16x2(bf16_lo(qraw[4 * k + 1]), bf16_lo(qraw[4 * k + 3]));
+        qa[2 * k + 1][1] = pack_f16x2(bf16_hi(qraw[4 * k + 1]), bf16_hi(qraw[4 * k + 3]));
+      }
+    }
+    float qsum = 0.0f;
+    if (kZeroK) {
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks) {
+        const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&qa[ks][0]));
+        const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&qa[ks][1]));
+        qsum += (f0.x + f0.y) + (f1.x + f1.y);
+      }
       qsum += __shfl_xor_sync(0xffffffffu, qsum, 1);
       qsum += __shfl_xor_sync(0xffffffffu, qsum, 2);
     }
-    // lane j: multiplier / offset of cached key j
-    float2 kscale = make_float2(1.0f, 0.0f);
-    if (KK != OASIS_KV_BF16 && lane < n_past) kscale = decode_slot_scale(stage + lay.aux + lane * 32, k_kind(lane), hh);
+    // the frame's own key on the CUDA cores (lanes 0..3, 16 dims each)
+    float s_live = -INFINITY;
+    if (live_key) {
+      float d = 0.0f;
+#pragma unroll
+      for (int w = 0; w < 8; ++w)
+        d = __fmaf_rn(bf16_hi(qraw[w]), bf16_hi(klraw[w]), __fmaf_rn(bf16_lo(qraw[w]), bf16_lo(klraw[w]), d));
+      d += __shfl_xor_sync(0xffffffffu, d, 1);
+      d += __shfl_xor_sync(0xffffffffu, d, 2);
+      s_live = d;
+    }
 
-    // ---- cached scores: n-tile nt holds keys 8nt..8nt+7; this thread supplies key 8nt + g
+    // ---- cached scores
     float sacc[4][4];
 #pragma unroll
     for (int nt = 0; nt < 4; ++nt) {
       sacc[nt][0] = sacc[nt][1] = sacc[nt][2] = sacc[nt][3] = 0.0f;
-      const int j = 8 * nt + g;
       uint32_t kb[4][2];
-      decode_key_frag(stage + k_row(j), k_kind(j), hh, c, kb);
+      key_fragments<KK, KW>(kr[nt], kkind[nt], kb);
 #pragma unroll
-      for (int ks = 0; ks < 4; ++ks) mma_f16_16816(sacc[nt], qa[ks][0], qa[ks][1], kb[ks][0], kb[ks][1]);
+      for (int ks = 0; ks < 4; ++ks)
+        mma_16816<KK == OASIS_KV_BF16>(sacc[nt], qa[ks][0], 0u, qa[ks][1], 0u, kb[ks][0], kb[ks][1]);
     }
+    const float2 kscale = KK == OASIS_KV_BF16 ? make_float2(1.0f, 0.0f) : dec_scale(ks_raw, ks_kind, slot_live);
+    if (nx < lay.items) load_keys(nx);  // the next item's keys, query, key scales
 
-    // ---- softmax over the cached keys (row 0: lanes 0..3 hold keys 8nt + 2c + e) and the live key
+    // ---- softmax over the cached keys (lanes 0..3 hold keys 8nt + 2c + e) and the live key
     float sc[8];
     float mx = s_live;
 #pragma unroll
@@ -895,10 +1107,7 @@ __global__ void __launch_bounds__(kDecThreads, 2)
       float s = sacc[i >> 1][i & 1];
       if (KK != OASIS_KV_BF16) {
         const float mul = __shfl_sync(0xffffffffu, kscale.x, j);
-        if (KK == OASIS_KV_INT4 || KK == kDecMixed)
-          s = __fmaf_rn(s, mul, __shfl_sync(0xffffffffu, kscale.y, j) * qsum);
-        else
-          s *= mul;
+        s = kZeroK ? __fmaf_rn(s, mul, __shfl_sync(0xffffffffu, kscale.y, j) * qsum) : s * mul;
       }
       sc[i] = (j < n_past && j <= q_pos) ? s : -INFINITY;
       mx = fmaxf(mx, sc[i]);
@@ -918,102 +1127,84 @@ __global__ void __launch_bounds__(kDecThreads, 2)
     const float p_live = live_key ? exp2f(__fmaf_rn(s_live, scale_log2, -mxs)) : 0.0f;
     sum += p_live;
     const float pb_live = bf16_round(p_live);
-    ok = mbar_wait(&bars[st][1], ph);
-    if (ok) {
-    // value multipliers: lane j holds slot j's; their max normalises P'
-    float2 vscale = make_float2(lane < n_past ? 1.0f : 0.0f, 0.0f);
-    if (VK != OASIS_KV_BF16 && lane < n_past)
-      vscale = decode_slot_scale(stage + lay.aux + 1024 + lane * 32, v_kind(lane), hh);
+
+    // ---- P' (value multipliers folded in, normalised by their max) as B column 0
+    const float2 vscale = VK == OASIS_KV_BF16 ? make_float2(1.0f, 0.0f) : dec_scale(vs_raw, vs_kind, slot_live);
     float vmax = 1.0f, corr = 0.0f;
     if (VK != OASIS_KV_BF16) {
       vmax = vscale.x;
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, o));
+      vmax = fmaxf(vmax, 1e-30f);
     }
     const float inv_vmax = 1.0f / vmax;
-    float pv[8];
+    uint32_t pb[2][2];
+    {
+      float pv[8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int j = 8 * (i >> 1) + 2 * c + (i & 1);
-      pv[i] = sc[i];
-      if (VK != OASIS_KV_BF16) {
-        pv[i] = sc[i] * __shfl_sync(0xffffffffu, vscale.x, j) * inv_vmax;
-        if (VK == OASIS_KV_INT4 || VK == kDecMixed) corr = __fmaf_rn(sc[i], __shfl_sync(0xffffffffu, vscale.y, j), corr);
+      for (int i = 0; i < 8; ++i) {
+        const int j = 8 * (i >> 1) + 2 * c + (i & 1);
+        pv[i] = sc[i];
+        if (VK != OASIS_KV_BF16) {
+          pv[i] = sc[i] * __shfl_sync(0xffffffffu, vscale.x, j) * inv_vmax;
+          if (kZeroV) corr = __fmaf_rn(sc[i], __shfl_sync(0xffffffffu, vscale.y, j), corr);
+        }
+      }
+#pragma unroll
+      for (int kv2 = 0; kv2 < 2; ++kv2) {
+        if (VK == OASIS_KV_BF16) {
+          pb[kv2][0] = pack_bf16x2(pv[4 * kv2], pv[4 * kv2 + 1]);
+          pb[kv2][1] = pack_bf16x2(pv[4 * kv2 + 2], pv[4 * kv2 + 3]);
+        } else {
+          pb[kv2][0] = pack_f16x2(pv[4 * kv2], pv[4 * kv2 + 1]);
+          pb[kv2][1] = pack_f16x2(pv[4 * kv2 + 2], pv[4 * kv2 + 3]);
+        }
       }
     }
-    if (VK == OASIS_KV_INT4 || VK == kDecMixed) {
+    if (kZeroV) {
       corr += __shfl_xor_sync(0xffffffffu, corr, 1);
       corr += __shfl_xor_sync(0xffffffffu, corr, 2);
     }
-    uint32_t pa[2][2];
-#pragma unroll
-    for (int k2 = 0; k2 < 2; ++k2) {
-      pa[k2][0] = pa[k2][1] = 0u;
-      if (g == 0) {
-        pa[k2][0] = pack_f16x2(pv[4 * k2], pv[4 * k2 + 1]);
-        pa[k2][1] = pack_f16x2(pv[4 * k2 + 2], pv[4 * k2 + 3]);
-      }
-    }
 
-    // ---- O = P' V: n-tile n2 column g is output dim 8g + n2; this thread supplies keys
-    // 16 k2 + 2c + {0, 1, 8, 9}, dims 8g..8g+7 of each
-    float oacc[8][4];
+    // ---- O^T = V^T P^T: m-tile mo rows g / g+8 are dims 8g + 2mo / 8g + 2mo + 1
+    float oacc[4][4];
 #pragma unroll
-    for (int n2 = 0; n2 < 8; ++n2) oacc[n2][0] = oacc[n2][1] = oacc[n2][2] = oacc[n2][3] = 0.0f;
+    for (int mo = 0; mo < 4; ++mo) oacc[mo][0] = oacc[mo][1] = oacc[mo][2] = oacc[mo][3] = 0.0f;
 #pragma unroll
-    for (int k2 = 0; k2 < 2; ++k2) {
-      uint32_t F[4][4];
+    for (int kv2 = 0; kv2 < 2; ++kv2) {
+      uint32_t F[2][8];
 #pragma unroll
-      for (int r = 0; r < 4; ++r) {
-        const int j = 16 * k2 + 2 * c + (r & 1) + 8 * (r >> 1);
-        decode_value_row(stage + v_row(j), v_kind(j), hh, g, F[r]);
-      }
+      for (int pr = 0; pr < 2; ++pr)
+        value_fragments<VK, VW>(vr[4 * kv2 + 2 * pr], vr[4 * kv2 + 2 * pr + 1], vkind[4 * kv2 + 2 * pr],
+                                vkind[4 * kv2 + 2 * pr + 1], F[pr]);
 #pragma unroll
-      for (int n2 = 0; n2 < 8; ++n2) {
-        const uint32_t sel = (n2 & 1) ? 0x7632u : 0x5410u;
-        const uint32_t b0 = __byte_perm(F[0][n2 >> 1], F[1][n2 >> 1], sel);
-        const uint32_t b1 = __byte_perm(F[2][n2 >> 1], F[3][n2 >> 1], sel);
-        mma_f16_16816(oacc[n2], pa[k2][0], pa[k2][1], b0, b1);
-      }
+      for (int mo = 0; mo < 4; ++mo)
+        mma_16816<VK == OASIS_KV_BF16>(oacc[mo], F[0][2 * mo], F[0][2 * mo + 1], F[1][2 * mo], F[1][2 * mo + 1],
+                                       pb[kv2][0], pb[kv2][1]);
     }
-    if (g == 0) {
-      // lane c holds dims 16c + n2 (column 2c) and 16c + 8 + n2 (column 2c + 1)
-      const float inv = 1.0f / sum;
-      const uint4* vl = reinterpret_cast<const uint4*>(stage + lay.live + 2048 + hh * 128 + 32 * c);
-      const uint4 v0 = vl[0], v1 = vl[1];
-      const uint32_t vw[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-      uint32_t o[8];
+    const uint32_t vl[4] = {vlraw[0], vlraw[1], vlraw[2], vlraw[3]};
+    if (nx < lay.items) load_values(nx);  // the next item's values, own value, value scales
+
+    // ---- epilogue: lanes c == 0 hold dims 8g..8g+7 (column 0 of C)
+    const float inv = __shfl_sync(0xffffffffu, 1.0f / sum, 0);
+    const float corr0 = __shfl_sync(0xffffffffu, corr, 0);
+    const float pl = __shfl_sync(0xffffffffu, pb_live, 0);
+    if (c == 0) {
+      uint32_t o[4];
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        // dims 16c + 2k, 16c + 2k + 1: accumulators of columns 2c (k < 4) / 2c + 1
-        const int n2 = (2 * k) & 7, col = k >> 2;
-        const float a0 = __fmaf_rn(vmax, oacc[n2][col], corr), a1 = __fmaf_rn(vmax, oacc[n2 + 1][col], corr);
-        o[k] = pack_bf16x2(__fmaf_rn(pb_live, bf16_lo(vw[k]), a0) * inv, __fmaf_rn(pb_live, bf16_hi(vw[k]), a1) * inv);
+      for (int mo = 0; mo < 4; ++mo) {
+        const float a0 = __fmaf_rn(vmax, oacc[mo][0], corr0), a1 = __fmaf_rn(vmax, oacc[mo][2], corr0);
+        o[mo] = pack_bf16x2(__fmaf_rn(pl, bf16_lo(vl[mo]), a0) * inv, __fmaf_rn(pl, bf16_hi(vl[mo]), a1) * inv);
       }
-      uint4* orow = reinterpret_cast<uint4*>(out + (static_cast<long long>(tok) * OASIS_HIDDEN) +
-                                             (hg * kDecHeads + hh) * 64 + 16 * c);
-      orow[0] = make_uint4(o[0], o[1], o[2], o[3]);
-      orow[1] = make_uint4(o[4], o[5], o[6], o[7]);
-    }
-    }  // values arrived
-    }  // keys arrived
-    if (!ok) abort_flag = 1;
-    __syncthreads();  // every warp is done with this stage before it is refilled
-    if (abort_flag) {
-      // the prefetched item's copies land (bounded) before the CTA exits
-      if (threadIdx.x == 0 && next) {
-        const uint32_t ph_next = ((k + 1) >> 1) & 1;
-        mbar_wait(&bars[st ^ 1][0], ph_next);
-        mbar_wait(&bars[st ^ 1][1], ph_next);
-      }
-      return;
+      *reinterpret_cast<uint4*>(out + static_cast<long long>(tok) * OASIS_HIDDEN + h * 64 + 8 * g) =
+          make_uint4(o[0], o[1], o[2], o[3]);
     }
   }
 }
 
 // decode kernel for (key kind, value kind), each a storage kind or kDecMixed
-using DecodeKernel = void (*)(const __nv_bfloat16*, __nv_bfloat16*, const KvView, const DecodeLayout, int,
-                              int, int, float);
+using DecodeKernel = void (*)(const __nv_bfloat16*, __nv_bfloat16*, const KvView, const DecodeLayout, int, int,
+                              float);
 template <int KK>
 DecodeKernel decode_kernel_v(int vk) {
   switch (vk) {
@@ -1072,85 +1263,47 @@ int launch_attn_temporal(const void* qkv, const KvView& kv, int layer, void* out
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(attn_temporal_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                kTpSmemTma);
-    for (int kk = 0; kk < 4 && e == cudaSuccess; ++kk)
-      for (int vk = 0; vk < 4 && e == cudaSuccess; ++vk)
-        e = cudaFuncSetAttribute(decode_kernel(kk, vk), cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 2 * kDecMaxStage);
     if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(attn_temporal)");
     configured = true;
   }
   if (q_frames == 1 && n_past > 0 && n_past < OASIS_MAX_FRAMES) {
-    // one query frame over cached slots: the persistent decode kernel.  A stage holds the
-    // key rows and the value rows of the 32 slots, each kind in its own region with a
-    // stride that keeps the fragment loads conflict-free (key rows: bf16 1040, FP8 576,
-    // INT4 288 B; value rows: 1040, 528, 272 B), 2 x 32 x 32 B of scales, the live rows.
-    // Slots past n_past take rows of the narrowest kind present, which stay zero.
+    // one query frame over cached slots: the warp-per-head decode kernel
     DecodeLayout lay{};
     lay.live_kv = n_kv > n_past ? 1 : 0;
-    lay.items = batch * OASIS_TOKENS * 2;
-    auto codes = [](int kind) -> uint32_t {
-      return kind == OASIS_KV_BF16 ? kDecHeads * 128 : (kind == OASIS_KV_FP8 ? kDecHeads * 64 : kDecHeads * 32);
-    };
-    const uint32_t k_strides[3] = {1040, 576, 288}, v_strides[3] = {1040, 528, 272};
-    uint32_t off = 0;
+    lay.items = batch * OASIS_TOKENS * OASIS_HEADS;
     int uniform[2];
     for (int which = 0; which < 2; ++which) {
       const KvTensor& t = kv.t[which];
-      const uint32_t* stride = which ? v_strides : k_strides;
-      int kinds[OASIS_MAX_FRAMES];
+      DecodeTensor& d = lay.t[which];
+      const int n_kind[3] = {t.n_bf16, t.n_fp8, t.n_int4};
+      for (int k = 0; k < 3; ++k) {
+        d.session_pages[k] = static_cast<uint32_t>(kv.layers * n_kind[k]);
+        // a slot's row offset (pages x 144 rows x row bytes) is a 32-bit lane register
+        if (static_cast<unsigned long long>(kv.layers) * n_kind[k] * OASIS_TOKENS * dec_row_bytes(k) >= (1ull << 32))
+          return fail(OASIS_ERR_UNSUPPORTED, "attn_decode_kernel: one session's pool exceeds 4 GiB");
+      }
       bool present[3] = {false, false, false};
       for (int s = 0; s < n_past; ++s) {
-        kinds[s] = t.kind[s];
-        present[kinds[s]] = true;
+        const int k = t.kind[s];
+        present[k] = true;
+        d.slot_page[s] = static_cast<uint32_t>(layer * n_kind[k] + t.index[s]);
+        d.kinds |= static_cast<unsigned long long>(k) << (2 * s);
       }
-      int narrow = OASIS_KV_BF16;  // the kind with the smallest rows present
-      for (int k : {OASIS_KV_FP8, OASIS_KV_INT4})
-        if (present[k]) narrow = k;
-      for (int s = n_past; s < OASIS_MAX_FRAMES; ++s) kinds[s] = narrow;
-      uniform[which] = (present[0] + present[1] + present[2] == 1) ? narrow : kDecMixed;
-      uint32_t* rows = which ? lay.v_row : lay.k_row;
-      unsigned long long mask = 0;
-      for (int k : {OASIS_KV_BF16, OASIS_KV_FP8, OASIS_KV_INT4}) {  // one region per kind
-        for (int s = 0; s < OASIS_MAX_FRAMES; ++s)
-          if (kinds[s] == k) {
-            rows[s] = off;
-            off += stride[k];
-          }
-      }
-      for (int s = 0; s < OASIS_MAX_FRAMES; ++s) mask |= static_cast<unsigned long long>(kinds[s]) << (2 * s);
-      uint32_t bytes = 0;
-      for (int s = 0; s < n_past; ++s) bytes += codes(kinds[s]);
-      if (which) {
-        lay.v_kinds = mask;
-        lay.v_bytes = bytes + lay.live_kv * kDecHeads * 128;
-        lay.v_base = rows[0];
-        lay.v_stride = stride[narrow];
-      } else {
-        lay.k_kinds = mask;
-        lay.k_bytes = bytes + (1 + lay.live_kv) * kDecHeads * 128;
-        lay.k_base = rows[0];
-        lay.k_stride = stride[narrow];
-      }
+      uniform[which] = present[0] + present[1] + present[2] == 1 ? (present[0] ? 0 : present[1] ? 1 : 2) : kDecMixed;
+      for (int s = n_past; s < OASIS_MAX_FRAMES; ++s)  // dead slots: never loaded
+        d.kinds |= static_cast<unsigned long long>(uniform[which] == kDecMixed ? 0 : uniform[which]) << (2 * s);
     }
-    lay.aux = off;
-    off += 2 * 1024;
-    lay.live = off;
-    off += 3 * kDecHeads * 128;
-    lay.stage_bytes = (off + 127) & ~127u;
-    if (lay.stage_bytes > static_cast<uint32_t>(kDecMaxStage))
-      return fail(OASIS_ERR_UNSUPPORTED, "attn_decode_kernel: stage layout too large");
     DecodeKernel kern = decode_kernel(uniform[0], uniform[1]);
-    const size_t smem = 2 * static_cast<size_t>(lay.stage_bytes);
     int per_sm = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kDecThreads, smem) != cudaSuccess ||
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kDecThreads, 0) != cudaSuccess ||
         per_sm < 1) {
       cudaGetLastError();
       per_sm = 1;
     }
-    const int ctas = std::min(lay.items, per_sm * num_sms());
-    cudaError_t e = launch_pdl(kern, dim3(ctas), dim3(kDecThreads), smem, stream,
+    const int ctas = std::min((lay.items + kDecWarps - 1) / kDecWarps, per_sm * num_sms());
+    cudaError_t e = launch_pdl(kern, dim3(ctas), dim3(kDecThreads), 0, stream,
                                static_cast<const __nv_bfloat16*>(qkv), static_cast<__nv_bfloat16*>(out),
-                               kv, lay, layer, q_pos0, n_past, kScaleLog2);
+                               kv, lay, q_pos0, n_past, kScaleLog2);
     if (e != cudaSuccess) return cuda_status(e, "attn_decode_kernel");
     return OASIS_OK;
   }
