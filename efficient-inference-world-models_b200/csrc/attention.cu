@@ -617,7 +617,7 @@ __global__ void __launch_bounds__(kTpWarps * 32)
 // to the fp32 scores (s_j = scale_j q.c_j + zero_j sum(q)) and to the probabilities
 // (p'_j = p_j scale_j / max scale, plus sum_j p_j zero_j).  The frame's own key and value
 // (bf16 rows of the QKV output) are one more key on the CUDA cores.
-constexpr int kDecWarps = 4;
+constexpr int kDecWarps = 8;
 constexpr int kDecThreads = kDecWarps * 32;
 // Kinds of the decode kernel's template: one storage kind for every cached slot of a
 // tensor, or kDecMixed (per-slot kinds from the layout).
@@ -639,6 +639,34 @@ __host__ __device__ constexpr uint32_t dec_row_bytes(int kind) {
   return kind == OASIS_KV_BF16 ? 2048u : (kind == OASIS_KV_FP8 ? 1024u : 512u);
 }
 __host__ __device__ constexpr uint32_t dec_head_bytes(int kind) { return dec_row_bytes(kind) / 16; }
+
+__device__ __forceinline__ uint4 ldg_stream_v4(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
+  return r;
+}
+__device__ __forceinline__ uint2 ldg_stream_v2(const void* p) {
+  uint2 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];" : "=r"(r.x), "=r"(r.y) : "l"(p));
+  return r;
+}
+__device__ __forceinline__ uint32_t ldg_stream_u32(const void* p) {
+  uint32_t r;
+  asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(r) : "l"(p));
+  return r;
+}
+__device__ __forceinline__ uint32_t ldg_u16(const void* p) {
+  unsigned short r;
+  asm volatile("ld.global.nc.u16 %0, [%1];" : "=h"(r) : "l"(p));
+  return r;
+}
+// rows of the QKV output (written by the preceding kernel): coherent loads
+__device__ __forceinline__ uint4 ldg_v4(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
+  return r;
+}
 
 __device__ __forceinline__ uint32_t f16x2_e4m3x2(uint32_t two_codes) {
   uint32_t h;
@@ -848,61 +876,18 @@ __device__ __forceinline__ float2 dec_scale(uint32_t raw, int kind, bool live) {
   return make_float2(1.0f, 0.0f);
 }
 
-// zero-filling asynchronous copies: `valid` false writes zeros and reads nothing
-template <int BYTES>
-__device__ __forceinline__ void cp_async_zfill(void* smem, const void* src, bool valid) {
-  if constexpr (BYTES == 16)
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem)), "l"(src),
-                 "r"(valid ? 16 : 0) : "memory");
-  else
-    asm volatile("cp.async.ca.shared.global [%0], [%1], %2, %3;" ::"r"(smem_u32(smem)), "l"(src), "n"(BYTES),
-                 "r"(valid ? BYTES : 0) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
-
-// One warp's pipeline stage: every thread copies, and later reads, only its own chunks,
-// so the stages need no barrier.  Key chunks [row r][lane], value chunks [row q][lane],
-// the query frame's q and own key (lanes 0..3), own value (lanes c == 0), and four scale
-// words per lane (slot `lane`: key scale, key zero, value scale, value zero; the 4-byte
-// word holding the 2-byte value).
-__host__ __device__ constexpr int dec_key_chunk(int kk) { return kk == OASIS_KV_FP8 ? 16 : (kk == OASIS_KV_INT4 ? 8 : 32); }
-__host__ __device__ constexpr int dec_value_chunk(int vk) { return vk == OASIS_KV_FP8 ? 8 : (vk == OASIS_KV_INT4 ? 4 : 16); }
-__host__ __device__ constexpr int dec_stage_bytes(int kk, int vk) {
-  return 4 * 32 * dec_key_chunk(kk) + 8 * 32 * dec_value_chunk(vk) + 4 * 64 + 8 * 16 + 32 * 16;
-}
 template <int KK, int VK>
-struct DecodeStage {
-  static constexpr int kKB = dec_key_chunk(KK);    // key chunk bytes (32: two 16-byte planes)
-  static constexpr int kVB = dec_value_chunk(VK);  // value chunk bytes
-  static constexpr int kKeys = 0;                  // [row][plane][lane] x 16 B, or [row][lane] x 8 B
-  static constexpr int kValues = kKeys + 4 * 32 * kKB;  // [row][lane] x kVB
-  static constexpr int kQuery = kValues + 8 * 32 * kVB;  // [c][q 32 B | own key 32 B]
-  static constexpr int kOwnValue = kQuery + 4 * 64;      // [g][16 B]
-  static constexpr int kScales = kOwnValue + 8 * 16;     // [lane][4 words]
-  static constexpr int kBytes = kScales + 32 * 16;
-  static_assert(kBytes == dec_stage_bytes(KK, VK), "stage layout");
-  __device__ static constexpr int key(int r, int plane, int lane) {
-    return kKB >= 16 ? kKeys + ((r * (kKB / 16) + plane) * 32 + lane) * 16 : kKeys + (r * 32 + lane) * kKB;
-  }
-};
-constexpr int kDecStages = 3;  // the item computed + two in flight
-
-template <int KK, int VK>
-__global__ void __launch_bounds__(kDecThreads)
+__global__ void __launch_bounds__(kDecThreads, 2)
     attn_decode_kernel(const __nv_bfloat16* __restrict__ qkv, __nv_bfloat16* __restrict__ out,
                        const __grid_constant__ KvView kv, const __grid_constant__ DecodeLayout lay,
                        int q_pos, int n_past, float scale_log2) {
   pdl_trigger();
-  using St = DecodeStage<KK, VK>;
-  constexpr int KW = St::kKB / 4, VW = St::kVB / 4;                   // words per chunk
-  constexpr bool kNibble = KK == OASIS_KV_INT4 || KK == kDecMixed;  // key dim order
-  constexpr bool kZeroK = KK == OASIS_KV_INT4 || KK == kDecMixed;   // keys may carry zeros
+  constexpr int KW = KK == OASIS_KV_FP8 ? 4 : (KK == OASIS_KV_INT4 ? 2 : 8);  // words per key chunk
+  constexpr int VW = VK == OASIS_KV_FP8 ? 2 : (VK == OASIS_KV_INT4 ? 1 : 4);  // words per value chunk
+  constexpr bool kNibble = KK == OASIS_KV_INT4 || KK == kDecMixed;          // key dim order
+  constexpr bool kZeroK = KK == OASIS_KV_INT4 || KK == kDecMixed;           // keys may carry zeros
   constexpr bool kZeroV = VK == OASIS_KV_INT4 || VK == kDecMixed;
-  extern __shared__ __align__(16) uint8_t sm_dec[];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
-  uint8_t* stages = sm_dec + warp * (kDecStages * St::kBytes);
+  const int lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
   const KvTensor& tk = kv.t[0];
   const KvTensor& tv = kv.t[1];
   const DecodeTensor& dk = lay.t[0];
@@ -938,115 +923,122 @@ __global__ void __launch_bounds__(kDecThreads)
   const bool live_key = lay.live_kv && n_past <= q_pos;
 
   const int warps_total = gridDim.x * kDecWarps;
-  const int first = blockIdx.x * kDecWarps + warp;
+  int it = blockIdx.x * kDecWarps + (threadIdx.x >> 5);
   pdl_wait();
-  if (first >= lay.items) return;
+  if (it >= lay.items) return;
 
-  // ---- one item's copies into stage st (one commit group per call, empty past the end)
-  auto issue = [&](int item, int st) {
-    if (item < lay.items) {
-      uint8_t* s = stages + st * St::kBytes;
-      const int h = item & 15, tok = item >> 4;
-      const int p = tok % OASIS_TOKENS, b = tok / OASIS_TOKENS;
-      const uint8_t* kbase[3];
-      const uint8_t* vbase[3];
+  // ---- per-item loads (registers)
+  uint32_t kr[4][KW], qraw[8], klraw[8], ks_raw;
+  uint32_t vr[8][VW], vlraw[4], vs_raw;
+  auto load_keys = [&](int item) {
+    const int h = item & 15, tok = item >> 4;
+    const int p = tok % OASIS_TOKENS, b = tok / OASIS_TOKENS;
+    const uint8_t* base[3];
 #pragma unroll
-      for (int k = 0; k < 3; ++k) {
-        kbase[k] = (KK == kDecMixed || KK == k) ? dec_item_rows(tk, dk, k, b, p, h) : nullptr;
-        vbase[k] = (VK == kDecMixed || VK == k) ? dec_item_rows(tv, dv, k, b, p, h) : nullptr;
-      }
+    for (int k = 0; k < 3; ++k)
+      base[k] = (KK == kDecMixed || KK == k) ? dec_item_rows(tk, dk, k, b, p, h) : nullptr;
 #pragma unroll
-      for (int r = 0; r < 4; ++r) {
-        const int kind = kkind[r];
-        const bool ok = 8 * r + g < n_past;
-        const uint8_t* src = ok ? kbase[kind] + koff[r] : reinterpret_cast<const uint8_t*>(qkv);
+    for (int r = 0; r < 4; ++r) {
+      const int kind = kkind[r];
+#pragma unroll
+      for (int w = 0; w < KW; ++w) kr[r][w] = 0u;
+      if (8 * r + g < n_past) {
+        const uint8_t* src = base[kind] + koff[r];
         if (kind == OASIS_KV_BF16) {
-          cp_async_zfill<16>(s + St::key(r, 0, lane), src, ok);
-          cp_async_zfill<16>(s + St::key(r, 1, lane), src + 16, ok);
-        } else if (kind == OASIS_KV_FP8) {
-          cp_async_zfill<16>(s + St::key(r, 0, lane), src, ok);
-        } else {
-          cp_async_zfill<8>(s + St::key(r, 0, lane), src, ok);
-        }
-      }
+          const uint4 x0 = ldg_stream_v4(src), x1 = ldg_stream_v4(src + 16);
+          const uint32_t v[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
 #pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        const int kind = vkind[q];
-        const bool ok = 16 * (q >> 2) + 2 * c + 8 * ((q >> 1) & 1) + (q & 1) < n_past;
-        uint8_t* dst = s + St::kValues + (q * 32 + lane) * St::kVB;
-        const uint8_t* src = ok ? vbase[kind] + voff[q] : reinterpret_cast<const uint8_t*>(qkv);
-        if (kind == OASIS_KV_BF16) cp_async_zfill<16>(dst, src, ok);
-        else if (kind == OASIS_KV_FP8) cp_async_zfill<8>(dst, src, ok);
-        else cp_async_zfill<4>(dst, src, ok);
-      }
-      const __nv_bfloat16* row = qkv + (static_cast<long long>(b) * OASIS_TOKENS + p) * kQkvLd + h * 64;
-      if (g == 0) {  // q and the frame's own key, dims 16c..16c+15
-        uint8_t* dst = s + St::kQuery + c * 64;
-        cp_async_zfill<16>(dst, row + 16 * c, true);
-        cp_async_zfill<16>(dst + 16, row + 16 * c + 8, true);
-        cp_async_zfill<16>(dst + 32, row + OASIS_HIDDEN + 16 * c, live_key);
-        cp_async_zfill<16>(dst + 48, row + OASIS_HIDDEN + 16 * c + 8, live_key);
-      }
-      if (c == 0)  // the frame's own value, dims 8g..8g+7
-        cp_async_zfill<16>(s + St::kOwnValue + g * 16, row + 2 * OASIS_HIDDEN + 8 * g, live_key);
-      uint8_t* sc = s + St::kScales + lane * 16;
-      if (KK != OASIS_KV_BF16) {
-        const uint8_t* src = reinterpret_cast<const uint8_t*>(qkv);
-        bool ok = false, zero = false;
-        long long e = 0;
-        if (slot_live && ks_kind == OASIS_KV_FP8) {
-          e = (dec_item_scale(dk, OASIS_KV_FP8, b, p, h) + ks_off) & ~1ll;
-          src = reinterpret_cast<const uint8_t*>(tk.fp8_scale + e);
-          ok = true;
-        } else if (slot_live && ks_kind == OASIS_KV_INT4) {
-          e = (dec_item_scale(dk, OASIS_KV_INT4, b, p, h) + ks_off) & ~1ll;
-          src = reinterpret_cast<const uint8_t*>(tk.i4_scale + e);
-          ok = zero = true;
+          for (int w = 0; w < KW; ++w) kr[r][w] = v[w];
+        } else if (kind == OASIS_KV_FP8) {
+          const uint4 x = ldg_stream_v4(src);
+          const uint32_t v[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+          for (int w = 0; w < (KW < 4 ? KW : 4); ++w) kr[r][w] = v[w];
+        } else {
+          const uint2 x = ldg_stream_v2(src);
+          kr[r][0] = x.x;
+          kr[r][1] = x.y;
         }
-        cp_async_zfill<4>(sc, src, ok);
-        if (kZeroK)
-          cp_async_zfill<4>(sc + 4, zero ? reinterpret_cast<const uint8_t*>(tk.i4_zero + e) : src, zero);
-      }
-      if (VK != OASIS_KV_BF16) {
-        const uint8_t* src = reinterpret_cast<const uint8_t*>(qkv);
-        bool ok = false, zero = false;
-        long long e = 0;
-        if (slot_live && vs_kind == OASIS_KV_FP8) {
-          e = (dec_item_scale(dv, OASIS_KV_FP8, b, p, h) + vs_off) & ~1ll;
-          src = reinterpret_cast<const uint8_t*>(tv.fp8_scale + e);
-          ok = true;
-        } else if (slot_live && vs_kind == OASIS_KV_INT4) {
-          e = (dec_item_scale(dv, OASIS_KV_INT4, b, p, h) + vs_off) & ~1ll;
-          src = reinterpret_cast<const uint8_t*>(tv.i4_scale + e);
-          ok = zero = true;
-        }
-        cp_async_zfill<4>(sc + 8, src, ok);
-        if (kZeroV)
-          cp_async_zfill<4>(sc + 12, zero ? reinterpret_cast<const uint8_t*>(tv.i4_zero + e) : src, zero);
       }
     }
-    cp_async_commit();
+    // the query frame's q (lanes 0..3: dims 16c..16c+15) and its own key
+    const __nv_bfloat16* row = qkv + (static_cast<long long>(b) * OASIS_TOKENS + p) * kQkvLd + h * 64 + 16 * c;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) qraw[w] = klraw[w] = 0u;
+    if (g == 0) {
+      const uint4 a = ldg_v4(row), a1 = ldg_v4(row + 8);
+      qraw[0] = a.x; qraw[1] = a.y; qraw[2] = a.z; qraw[3] = a.w;
+      qraw[4] = a1.x; qraw[5] = a1.y; qraw[6] = a1.z; qraw[7] = a1.w;
+      if (live_key) {
+        const uint4 k0 = ldg_v4(row + OASIS_HIDDEN), k1 = ldg_v4(row + OASIS_HIDDEN + 8);
+        klraw[0] = k0.x; klraw[1] = k0.y; klraw[2] = k0.z; klraw[3] = k0.w;
+        klraw[4] = k1.x; klraw[5] = k1.y; klraw[6] = k1.z; klraw[7] = k1.w;
+      }
+    }
+    ks_raw = 0u;
+    if (KK != OASIS_KV_BF16 && slot_live) {
+      if (ks_kind == OASIS_KV_FP8) {
+        ks_raw = ldg_u16(tk.fp8_scale + dec_item_scale(dk, OASIS_KV_FP8, b, p, h) + ks_off);
+      } else if (ks_kind == OASIS_KV_INT4) {
+        const long long e = dec_item_scale(dk, OASIS_KV_INT4, b, p, h) + ks_off;
+        ks_raw = ldg_u16(tk.i4_scale + e) | (ldg_u16(tk.i4_zero + e) << 16);
+      }
+    }
+  };
+  auto load_values = [&](int item) {
+    const int h = item & 15, tok = item >> 4;
+    const int p = tok % OASIS_TOKENS, b = tok / OASIS_TOKENS;
+    const uint8_t* base[3];
+#pragma unroll
+    for (int k = 0; k < 3; ++k)
+      base[k] = (VK == kDecMixed || VK == k) ? dec_item_rows(tv, dv, k, b, p, h) : nullptr;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const int kind = vkind[q];
+      const int j = 16 * (q >> 2) + 2 * c + 8 * ((q >> 1) & 1) + (q & 1);
+#pragma unroll
+      for (int w = 0; w < VW; ++w) vr[q][w] = 0u;
+      if (j < n_past) {
+        const uint8_t* src = base[kind] + voff[q];
+        if (kind == OASIS_KV_BF16) {
+          const uint4 x = ldg_stream_v4(src);
+          const uint32_t v[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+          for (int w = 0; w < VW; ++w) vr[q][w] = v[w];
+        } else if (kind == OASIS_KV_FP8) {
+          const uint2 x = ldg_stream_v2(src);
+          vr[q][0] = x.x;
+          if (VW > 1) vr[q][VW > 1 ? 1 : 0] = x.y;
+        } else {
+          vr[q][0] = ldg_stream_u32(src);
+        }
+      }
+    }
+    // the frame's own value (lanes c == 0: dims 8g..8g+7)
+    vlraw[0] = vlraw[1] = vlraw[2] = vlraw[3] = 0u;
+    if (c == 0 && live_key) {
+      const uint4 v = ldg_v4(qkv + (static_cast<long long>(b) * OASIS_TOKENS + p) * kQkvLd + 2 * OASIS_HIDDEN +
+                             h * 64 + 8 * g);
+      vlraw[0] = v.x; vlraw[1] = v.y; vlraw[2] = v.z; vlraw[3] = v.w;
+    }
+    vs_raw = 0u;
+    if (VK != OASIS_KV_BF16 && slot_live) {
+      if (vs_kind == OASIS_KV_FP8) {
+        vs_raw = ldg_u16(tv.fp8_scale + dec_item_scale(dv, OASIS_KV_FP8, b, p, h) + vs_off);
+      } else if (vs_kind == OASIS_KV_INT4) {
+        const long long e = dec_item_scale(dv, OASIS_KV_INT4, b, p, h) + vs_off;
+        vs_raw = ldg_u16(tv.i4_scale + e) | (ldg_u16(tv.i4_zero + e) << 16);
+      }
+    }
   };
 
-#pragma unroll
-  for (int k = 0; k < kDecStages - 1; ++k) issue(first + k * warps_total, k);
-  int st = 0;
-  for (int it = first; it < lay.items; it += warps_total) {
-    issue(it + (kDecStages - 1) * warps_total, st == 0 ? kDecStages - 1 : st - 1);
-    cp_async_wait<kDecStages - 1>();  // this thread's copies of item `it` have landed
-    const uint8_t* s = stages + st * St::kBytes;
-    st = st == kDecStages - 1 ? 0 : st + 1;
+  load_keys(it);
+  load_values(it);
+  for (; it < lay.items; it += warps_total) {
+    const int nx = it + warps_total;
     const int h = it & 15, tok = it >> 4;
-    const int hsel = 16 * (h & 1);  // half of a scale word holding head h's value
 
     // ---- the query as row 0 of A (lanes 0..3 hold it; other rows are don't-care)
-    uint32_t qraw[8], klraw[8];
-    {
-      const uint4* qp = reinterpret_cast<const uint4*>(s + St::kQuery + c * 64);
-      const uint4 a0 = qp[0], a1 = qp[1];
-      qraw[0] = a0.x; qraw[1] = a0.y; qraw[2] = a0.z; qraw[3] = a0.w;
-      qraw[4] = a1.x; qraw[5] = a1.y; qraw[6] = a1.z; qraw[7] = a1.w;
-    }
     uint32_t qa[4][2];
     if (KK == OASIS_KV_BF16) {
 #pragma unroll
@@ -1083,10 +1075,6 @@ __global__ void __launch_bounds__(kDecThreads)
     // the frame's own key on the CUDA cores (lanes 0..3, 16 dims each)
     float s_live = -INFINITY;
     if (live_key) {
-      const uint4* kp = reinterpret_cast<const uint4*>(s + St::kQuery + c * 64 + 32);
-      const uint4 k0 = kp[0], k1 = kp[1];
-      klraw[0] = k0.x; klraw[1] = k0.y; klraw[2] = k0.z; klraw[3] = k0.w;
-      klraw[4] = k1.x; klraw[5] = k1.y; klraw[6] = k1.z; klraw[7] = k1.w;
       float d = 0.0f;
 #pragma unroll
       for (int w = 0; w < 8; ++w)
@@ -1101,31 +1089,14 @@ __global__ void __launch_bounds__(kDecThreads)
 #pragma unroll
     for (int nt = 0; nt < 4; ++nt) {
       sacc[nt][0] = sacc[nt][1] = sacc[nt][2] = sacc[nt][3] = 0.0f;
-      uint32_t kr[KW];
-      const uint8_t* kp = s + St::key(nt, 0, lane);
-      if constexpr (KW == 8) {
-        const uint4 x0 = *reinterpret_cast<const uint4*>(kp);
-        const uint4 x1 = *reinterpret_cast<const uint4*>(s + St::key(nt, 1, lane));
-        kr[0] = x0.x; kr[1] = x0.y; kr[2] = x0.z; kr[3] = x0.w;
-        kr[4] = x1.x; kr[5] = x1.y; kr[6] = x1.z; kr[7] = x1.w;
-      } else if constexpr (KW == 4) {
-        const uint4 x = reinterpret_cast<const uint4*>(kp)[0];
-        kr[0] = x.x; kr[1] = x.y; kr[2] = x.z; kr[3] = x.w;
-      } else {
-        const uint2 x = reinterpret_cast<const uint2*>(kp)[0];
-        kr[0] = x.x; kr[1] = x.y;
-      }
       uint32_t kb[4][2];
-      key_fragments<KK, KW>(kr, kkind[nt], kb);
+      key_fragments<KK, KW>(kr[nt], kkind[nt], kb);
 #pragma unroll
       for (int ks = 0; ks < 4; ++ks)
         mma_16816<KK == OASIS_KV_BF16>(sacc[nt], qa[ks][0], 0u, qa[ks][1], 0u, kb[ks][0], kb[ks][1]);
     }
-    const uint4 scw = *reinterpret_cast<const uint4*>(s + St::kScales + lane * 16);
-    const float2 kscale =
-        KK == OASIS_KV_BF16 ? make_float2(1.0f, 0.0f)
-                            : dec_scale(((scw.x >> hsel) & 0xFFFFu) | (((scw.y >> hsel) & 0xFFFFu) << 16), ks_kind,
-                                        slot_live);
+    const float2 kscale = KK == OASIS_KV_BF16 ? make_float2(1.0f, 0.0f) : dec_scale(ks_raw, ks_kind, slot_live);
+    if (nx < lay.items) load_keys(nx);  // the next item's keys, query, key scales
 
     // ---- softmax over the cached keys (lanes 0..3 hold keys 8nt + 2c + e) and the live key
     float sc[8];
@@ -1133,12 +1104,12 @@ __global__ void __launch_bounds__(kDecThreads)
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const int j = 8 * (i >> 1) + 2 * c + (i & 1);
-      float sv = sacc[i >> 1][i & 1];
+      float s = sacc[i >> 1][i & 1];
       if (KK != OASIS_KV_BF16) {
         const float mul = __shfl_sync(0xffffffffu, kscale.x, j);
-        sv = kZeroK ? __fmaf_rn(sv, mul, __shfl_sync(0xffffffffu, kscale.y, j) * qsum) : sv * mul;
+        s = kZeroK ? __fmaf_rn(s, mul, __shfl_sync(0xffffffffu, kscale.y, j) * qsum) : s * mul;
       }
-      sc[i] = (j < n_past && j <= q_pos) ? sv : -INFINITY;
+      sc[i] = (j < n_past && j <= q_pos) ? s : -INFINITY;
       mx = fmaxf(mx, sc[i]);
     }
     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
@@ -1158,10 +1129,7 @@ __global__ void __launch_bounds__(kDecThreads)
     const float pb_live = bf16_round(p_live);
 
     // ---- P' (value multipliers folded in, normalised by their max) as B column 0
-    const float2 vscale =
-        VK == OASIS_KV_BF16 ? make_float2(1.0f, 0.0f)
-                            : dec_scale(((scw.z >> hsel) & 0xFFFFu) | (((scw.w >> hsel) & 0xFFFFu) << 16), vs_kind,
-                                        slot_live);
+    const float2 vscale = VK == OASIS_KV_BF16 ? make_float2(1.0f, 0.0f) : dec_scale(vs_raw, vs_kind, slot_live);
     float vmax = 1.0f, corr = 0.0f;
     if (VK != OASIS_KV_BF16) {
       vmax = vscale.x;
@@ -1204,38 +1172,24 @@ __global__ void __launch_bounds__(kDecThreads)
     for (int mo = 0; mo < 4; ++mo) oacc[mo][0] = oacc[mo][1] = oacc[mo][2] = oacc[mo][3] = 0.0f;
 #pragma unroll
     for (int kv2 = 0; kv2 < 2; ++kv2) {
-      uint32_t vr[4][VW];
-#pragma unroll
-      for (int r = 0; r < 4; ++r) {
-        const uint8_t* vp = s + St::kValues + ((4 * kv2 + r) * 32 + lane) * St::kVB;
-        if constexpr (VW == 4) {
-          const uint4 x = *reinterpret_cast<const uint4*>(vp);
-          vr[r][0] = x.x; vr[r][1] = x.y; vr[r][2] = x.z; vr[r][3] = x.w;
-        } else if constexpr (VW == 2) {
-          const uint2 x = *reinterpret_cast<const uint2*>(vp);
-          vr[r][0] = x.x; vr[r][1] = x.y;
-        } else {
-          vr[r][0] = *reinterpret_cast<const uint32_t*>(vp);
-        }
-      }
       uint32_t F[2][8];
 #pragma unroll
       for (int pr = 0; pr < 2; ++pr)
-        value_fragments<VK, VW>(vr[2 * pr], vr[2 * pr + 1], vkind[4 * kv2 + 2 * pr], vkind[4 * kv2 + 2 * pr + 1],
-                                F[pr]);
+        value_fragments<VK, VW>(vr[4 * kv2 + 2 * pr], vr[4 * kv2 + 2 * pr + 1], vkind[4 * kv2 + 2 * pr],
+                                vkind[4 * kv2 + 2 * pr + 1], F[pr]);
 #pragma unroll
       for (int mo = 0; mo < 4; ++mo)
         mma_16816<VK == OASIS_KV_BF16>(oacc[mo], F[0][2 * mo], F[0][2 * mo + 1], F[1][2 * mo], F[1][2 * mo + 1],
                                        pb[kv2][0], pb[kv2][1]);
     }
+    const uint32_t vl[4] = {vlraw[0], vlraw[1], vlraw[2], vlraw[3]};
+    if (nx < lay.items) load_values(nx);  // the next item's values, own value, value scales
 
     // ---- epilogue: lanes c == 0 hold dims 8g..8g+7 (column 0 of C)
     const float inv = __shfl_sync(0xffffffffu, 1.0f / sum, 0);
     const float corr0 = __shfl_sync(0xffffffffu, corr, 0);
     const float pl = __shfl_sync(0xffffffffu, pb_live, 0);
     if (c == 0) {
-      const uint4 v = *reinterpret_cast<const uint4*>(s + St::kOwnValue + g * 16);
-      const uint32_t vl[4] = {v.x, v.y, v.z, v.w};
       uint32_t o[4];
 #pragma unroll
       for (int mo = 0; mo < 4; ++mo) {
@@ -1246,7 +1200,6 @@ __global__ void __launch_bounds__(kDecThreads)
           make_uint4(o[0], o[1], o[2], o[3]);
     }
   }
-  cp_async_wait<0>();  // no copy outlives the warp
 }
 
 // decode kernel for (key kind, value kind), each a storage kind or kDecMixed
@@ -1310,10 +1263,6 @@ int launch_attn_temporal(const void* qkv, const KvView& kv, int layer, void* out
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(attn_temporal_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                kTpSmemTma);
-    for (int kk = 0; kk < 4 && e == cudaSuccess; ++kk)
-      for (int vk = 0; vk < 4 && e == cudaSuccess; ++vk)
-        e = cudaFuncSetAttribute(decode_kernel(kk, vk), cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 kDecWarps * kDecStages * dec_stage_bytes(kk, vk));
     if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(attn_temporal)");
     configured = true;
   }
@@ -1345,15 +1294,14 @@ int launch_attn_temporal(const void* qkv, const KvView& kv, int layer, void* out
         d.kinds |= static_cast<unsigned long long>(uniform[which] == kDecMixed ? 0 : uniform[which]) << (2 * s);
     }
     DecodeKernel kern = decode_kernel(uniform[0], uniform[1]);
-    const size_t smem = static_cast<size_t>(kDecWarps) * kDecStages * dec_stage_bytes(uniform[0], uniform[1]);
     int per_sm = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kDecThreads, smem) != cudaSuccess ||
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kDecThreads, 0) != cudaSuccess ||
         per_sm < 1) {
       cudaGetLastError();
       per_sm = 1;
     }
     const int ctas = std::min((lay.items + kDecWarps - 1) / kDecWarps, per_sm * num_sms());
-    cudaError_t e = launch_pdl(kern, dim3(ctas), dim3(kDecThreads), smem, stream,
+    cudaError_t e = launch_pdl(kern, dim3(ctas), dim3(kDecThreads), 0, stream,
                                static_cast<const __nv_bfloat16*>(qkv), static_cast<__nv_bfloat16*>(out),
                                kv, lay, q_pos0, n_past, kScaleLog2);
     if (e != cudaSuccess) return cuda_status(e, "attn_decode_kernel");
