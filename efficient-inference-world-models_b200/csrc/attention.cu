@@ -628,8 +628,13 @@ struct DecodeTensor {
   unsigned long long kinds;              // 2 bits per slot (slots past n_past: any kind)
   uint32_t session_pages[3];             // per kind: layers * n_kind, the pages of one session
 };
+// Key positions 0..31 of the tiles hold the cached slots in an order the host picks:
+// slot order when every slot of a tensor has one kind, else grouped so that each 8-key
+// n-tile holds one (key kind, value kind) pair, which keeps the kind branches uniform
+// across the warp.  Softmax and P V do not depend on the order.
 struct DecodeLayout {
-  DecodeTensor t[2];  // keys, values
+  DecodeTensor t[2];  // keys, values, indexed by key position
+  uint32_t valid;     // positions holding a cached slot at or before the query's window position
   int items;          // batch * 144 tokens * 16 heads
   int live_kv;        // the query frame's own K/V is a key (at window position n_past)
 };
@@ -876,8 +881,12 @@ __device__ __forceinline__ float2 dec_scale(uint32_t raw, int kind, bool live) {
   return make_float2(1.0f, 0.0f);
 }
 
+// CTAs per SM the register budget is sized for: two for one storage kind per tensor;
+// mixed tensors keep their row kinds and three row pointers live, and take the registers
+// of one CTA (no spills) rather than spill inside the item loop
+__host__ __device__ constexpr int dec_min_ctas(int kk, int vk) { return kk == kDecMixed || vk == kDecMixed ? 1 : 2; }
 template <int KK, int VK>
-__global__ void __launch_bounds__(kDecThreads, 2)
+__global__ void __launch_bounds__(kDecThreads, dec_min_ctas(KK, VK))
     attn_decode_kernel(const __nv_bfloat16* __restrict__ qkv, __nv_bfloat16* __restrict__ out,
                        const __grid_constant__ KvView kv, const __grid_constant__ DecodeLayout lay,
                        int q_pos, int n_past, float scale_log2) {
@@ -899,28 +908,33 @@ __global__ void __launch_bounds__(kDecThreads, 2)
   // ---- loop-invariant parts of this lane's addresses
   // key rows r = 0..3: key 8r + g, dims 16c..16c+15
   uint32_t koff[4];
-  int kkind[4];
+  uint32_t kpack = 0;  // 2 bits per row: its kind (mixed tensors)
 #pragma unroll
   for (int r = 0; r < 4; ++r) {
-    const int j = 8 * r + g;
-    kkind[r] = kind_of(dk, KK, j);
-    koff[r] = dk.slot_page[j] * (OASIS_TOKENS * dec_row_bytes(kkind[r])) + c * (dec_head_bytes(kkind[r]) / 4);
+    const int j = 8 * r + g, kind = kind_of(dk, KK, j);
+    kpack |= static_cast<uint32_t>(kind) << (2 * r);
+    koff[r] = dk.slot_page[j] * (OASIS_TOKENS * dec_row_bytes(kind)) + c * (dec_head_bytes(kind) / 4);
   }
+  auto kkind = [&](int r) { return KK == kDecMixed ? static_cast<int>((kpack >> (2 * r)) & 3u) : KK; };
   // value rows q = 0..7: key 16 (q >> 2) + 2c + 8 ((q >> 1) & 1) + (q & 1), dims 8g..8g+7
   uint32_t voff[8];
-  int vkind[8];
+  uint32_t vpack = 0;
 #pragma unroll
   for (int q = 0; q < 8; ++q) {
-    const int j = 16 * (q >> 2) + 2 * c + 8 * ((q >> 1) & 1) + (q & 1);
-    vkind[q] = kind_of(dv, VK, j);
-    voff[q] = dv.slot_page[j] * (OASIS_TOKENS * dec_row_bytes(vkind[q])) + g * (dec_head_bytes(vkind[q]) / 8);
+    const int j = 16 * (q >> 2) + 2 * c + 8 * ((q >> 1) & 1) + (q & 1), kind = kind_of(dv, VK, j);
+    vpack |= static_cast<uint32_t>(kind) << (2 * q);
+    voff[q] = dv.slot_page[j] * (OASIS_TOKENS * dec_row_bytes(kind)) + g * (dec_head_bytes(kind) / 8);
   }
+  auto vkind = [&](int q) { return VK == kDecMixed ? static_cast<int>((vpack >> (2 * q)) & 3u) : VK; };
   // scales of slot `lane`
-  const bool slot_live = lane < n_past;
+  const bool slot_live = (lay.valid >> lane) & 1u;
   const int ks_kind = kind_of(dk, KK, lane), vs_kind = kind_of(dv, VK, lane);
   const uint32_t ks_off = dec_slot_scale(ks_kind, dk.slot_page[lane]);
   const uint32_t vs_off = dec_slot_scale(vs_kind, dv.slot_page[lane]);
   const bool live_key = lay.live_kv && n_past <= q_pos;
+  uint32_t smask = 0;  // score i of lanes 0..3 (position 8 (i >> 1) + 2c + (i & 1)) is a cached key
+#pragma unroll
+  for (int i = 0; i < 8; ++i) smask |= ((lay.valid >> (8 * (i >> 1) + 2 * c + (i & 1))) & 1u) << i;
 
   const int warps_total = gridDim.x * kDecWarps;
   int it = blockIdx.x * kDecWarps + (threadIdx.x >> 5);
@@ -933,17 +947,16 @@ __global__ void __launch_bounds__(kDecThreads, 2)
   auto load_keys = [&](int item) {
     const int h = item & 15, tok = item >> 4;
     const int p = tok % OASIS_TOKENS, b = tok / OASIS_TOKENS;
-    const uint8_t* base[3];
-#pragma unroll
-    for (int k = 0; k < 3; ++k)
-      base[k] = (KK == kDecMixed || KK == k) ? dec_item_rows(tk, dk, k, b, p, h) : nullptr;
+    const uint8_t* base0 = (KK == kDecMixed || KK == 0) ? dec_item_rows(tk, dk, 0, b, p, h) : nullptr;
+    const uint8_t* base1 = (KK == kDecMixed || KK == 1) ? dec_item_rows(tk, dk, 1, b, p, h) : nullptr;
+    const uint8_t* base2 = (KK == kDecMixed || KK == 2) ? dec_item_rows(tk, dk, 2, b, p, h) : nullptr;
 #pragma unroll
     for (int r = 0; r < 4; ++r) {
-      const int kind = kkind[r];
+      const int kind = kkind(r);
 #pragma unroll
       for (int w = 0; w < KW; ++w) kr[r][w] = 0u;
-      if (8 * r + g < n_past) {
-        const uint8_t* src = base[kind] + koff[r];
+      if ((lay.valid >> (8 * r + g)) & 1u) {
+        const uint8_t* src = (kind == 0 ? base0 : (kind == 1 ? base1 : base2)) + koff[r];
         if (kind == OASIS_KV_BF16) {
           const uint4 x0 = ldg_stream_v4(src), x1 = ldg_stream_v4(src + 16);
           const uint32_t v[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
@@ -988,18 +1001,17 @@ __global__ void __launch_bounds__(kDecThreads, 2)
   auto load_values = [&](int item) {
     const int h = item & 15, tok = item >> 4;
     const int p = tok % OASIS_TOKENS, b = tok / OASIS_TOKENS;
-    const uint8_t* base[3];
-#pragma unroll
-    for (int k = 0; k < 3; ++k)
-      base[k] = (VK == kDecMixed || VK == k) ? dec_item_rows(tv, dv, k, b, p, h) : nullptr;
+    const uint8_t* base0 = (VK == kDecMixed || VK == 0) ? dec_item_rows(tv, dv, 0, b, p, h) : nullptr;
+    const uint8_t* base1 = (VK == kDecMixed || VK == 1) ? dec_item_rows(tv, dv, 1, b, p, h) : nullptr;
+    const uint8_t* base2 = (VK == kDecMixed || VK == 2) ? dec_item_rows(tv, dv, 2, b, p, h) : nullptr;
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
-      const int kind = vkind[q];
+      const int kind = vkind(q);
       const int j = 16 * (q >> 2) + 2 * c + 8 * ((q >> 1) & 1) + (q & 1);
 #pragma unroll
       for (int w = 0; w < VW; ++w) vr[q][w] = 0u;
-      if (j < n_past) {
-        const uint8_t* src = base[kind] + voff[q];
+      if ((lay.valid >> j) & 1u) {
+        const uint8_t* src = (kind == 0 ? base0 : (kind == 1 ? base1 : base2)) + voff[q];
         if (kind == OASIS_KV_BF16) {
           const uint4 x = ldg_stream_v4(src);
           const uint32_t v[4] = {x.x, x.y, x.z, x.w};
@@ -1090,7 +1102,7 @@ __global__ void __launch_bounds__(kDecThreads, 2)
     for (int nt = 0; nt < 4; ++nt) {
       sacc[nt][0] = sacc[nt][1] = sacc[nt][2] = sacc[nt][3] = 0.0f;
       uint32_t kb[4][2];
-      key_fragments<KK, KW>(kr[nt], kkind[nt], kb);
+      key_fragments<KK, KW>(kr[nt], kkind(nt), kb);
 #pragma unroll
       for (int ks = 0; ks < 4; ++ks)
         mma_16816<KK == OASIS_KV_BF16>(sacc[nt], qa[ks][0], 0u, qa[ks][1], 0u, kb[ks][0], kb[ks][1]);
@@ -1109,7 +1121,7 @@ __global__ void __launch_bounds__(kDecThreads, 2)
         const float mul = __shfl_sync(0xffffffffu, kscale.x, j);
         s = kZeroK ? __fmaf_rn(s, mul, __shfl_sync(0xffffffffu, kscale.y, j) * qsum) : s * mul;
       }
-      sc[i] = (j < n_past && j <= q_pos) ? s : -INFINITY;
+      sc[i] = (smask >> i) & 1u ? s : -INFINITY;
       mx = fmaxf(mx, sc[i]);
     }
     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
@@ -1175,8 +1187,8 @@ __global__ void __launch_bounds__(kDecThreads, 2)
       uint32_t F[2][8];
 #pragma unroll
       for (int pr = 0; pr < 2; ++pr)
-        value_fragments<VK, VW>(vr[4 * kv2 + 2 * pr], vr[4 * kv2 + 2 * pr + 1], vkind[4 * kv2 + 2 * pr],
-                                vkind[4 * kv2 + 2 * pr + 1], F[pr]);
+        value_fragments<VK, VW>(vr[4 * kv2 + 2 * pr], vr[4 * kv2 + 2 * pr + 1], vkind(4 * kv2 + 2 * pr),
+                                vkind(4 * kv2 + 2 * pr + 1), F[pr]);
 #pragma unroll
       for (int mo = 0; mo < 4; ++mo)
         mma_16816<VK == OASIS_KV_BF16>(oacc[mo], F[0][2 * mo], F[0][2 * mo + 1], F[1][2 * mo], F[1][2 * mo + 1],
@@ -1271,7 +1283,58 @@ int launch_attn_temporal(const void* qkv, const KvView& kv, int layer, void* out
     DecodeLayout lay{};
     lay.live_kv = n_kv > n_past ? 1 : 0;
     lay.items = batch * OASIS_TOKENS * OASIS_HEADS;
+    // key position of each cached slot
+    int kinds[2][OASIS_MAX_FRAMES];
+    bool present[2][3] = {{false, false, false}, {false, false, false}};
+    for (int which = 0; which < 2; ++which)
+      for (int s = 0; s < n_past; ++s) {
+        kinds[which][s] = kv.t[which].kind[s];
+        present[which][kinds[which][s]] = true;
+      }
     int uniform[2];
+    for (int which = 0; which < 2; ++which) {
+      const bool* pr = present[which];
+      uniform[which] = pr[0] + pr[1] + pr[2] == 1 ? (pr[0] ? 0 : (pr[1] ? 1 : 2)) : kDecMixed;
+    }
+    int pos_slot[OASIS_MAX_FRAMES];  // slot at each key position, -1: none
+    int pos_kind[2][OASIS_MAX_FRAMES];
+    for (int j = 0; j < OASIS_MAX_FRAMES; ++j) {
+      pos_slot[j] = j < n_past ? j : -1;
+      for (int which = 0; which < 2; ++which)
+        pos_kind[which][j] = j < n_past ? kinds[which][j] : (uniform[which] == kDecMixed ? 0 : uniform[which]);
+    }
+    if (uniform[0] == kDecMixed || uniform[1] == kDecMixed) {
+      // group the slots by (key kind, value kind), each group from an n-tile boundary,
+      // when the groups fit the 4 n-tiles
+      int combo_of[OASIS_MAX_FRAMES], count[9] = {0}, tiles = 0;
+      for (int s = 0; s < n_past; ++s) {
+        combo_of[s] = 3 * kinds[0][s] + kinds[1][s];
+        ++count[combo_of[s]];
+      }
+      for (int cb = 0; cb < 9; ++cb) tiles += (count[cb] + 7) / 8;
+      if (tiles <= OASIS_MAX_FRAMES / 8) {
+        int next = 0;
+        for (int cb = 0; cb < 9; ++cb) {
+          if (!count[cb]) continue;
+          const int start = next;
+          for (int s = 0; s < n_past; ++s)
+            if (combo_of[s] == cb) pos_slot[next++] = s;
+          next = start + 8 * ((count[cb] + 7) / 8);
+          for (int j = start; j < next; ++j) {
+            if (j >= start + count[cb]) pos_slot[j] = -1;
+            pos_kind[0][j] = cb / 3;
+            pos_kind[1][j] = cb % 3;
+          }
+        }
+        for (int j = next; j < OASIS_MAX_FRAMES; ++j) {  // trailing dead tiles: kinds of the last group
+          pos_slot[j] = -1;
+          pos_kind[0][j] = pos_kind[0][next - 1];
+          pos_kind[1][j] = pos_kind[1][next - 1];
+        }
+      }
+    }
+    for (int j = 0; j < OASIS_MAX_FRAMES; ++j)
+      if (pos_slot[j] >= 0 && pos_slot[j] <= q_pos0) lay.valid |= 1u << j;
     for (int which = 0; which < 2; ++which) {
       const KvTensor& t = kv.t[which];
       DecodeTensor& d = lay.t[which];
@@ -1282,16 +1345,10 @@ int launch_attn_temporal(const void* qkv, const KvView& kv, int layer, void* out
         if (static_cast<unsigned long long>(kv.layers) * n_kind[k] * OASIS_TOKENS * dec_row_bytes(k) >= (1ull << 32))
           return fail(OASIS_ERR_UNSUPPORTED, "attn_decode_kernel: one session's pool exceeds 4 GiB");
       }
-      bool present[3] = {false, false, false};
-      for (int s = 0; s < n_past; ++s) {
-        const int k = t.kind[s];
-        present[k] = true;
-        d.slot_page[s] = static_cast<uint32_t>(layer * n_kind[k] + t.index[s]);
-        d.kinds |= static_cast<unsigned long long>(k) << (2 * s);
+      for (int j = 0; j < OASIS_MAX_FRAMES; ++j) {
+        d.kinds |= static_cast<unsigned long long>(pos_kind[which][j]) << (2 * j);
+        if (pos_slot[j] >= 0) d.slot_page[j] = static_cast<uint32_t>(layer * n_kind[pos_kind[which][j]] + t.index[pos_slot[j]]);
       }
-      uniform[which] = present[0] + present[1] + present[2] == 1 ? (present[0] ? 0 : present[1] ? 1 : 2) : kDecMixed;
-      for (int s = n_past; s < OASIS_MAX_FRAMES; ++s)  // dead slots: never loaded
-        d.kinds |= static_cast<unsigned long long>(uniform[which] == kDecMixed ? 0 : uniform[which]) << (2 * s);
     }
     DecodeKernel kern = decode_kernel(uniform[0], uniform[1]);
     int per_sm = 0;

@@ -231,7 +231,10 @@ def test_attn_temporal_full_from_quantized_cache(pkg, cuda, kind, T):
     (["fp8"] * 31, ["fp8"] * 31),
     (["bf16"] * 31, ["fp8"] * 10 + ["bf16"] * 21),
     (["fp8"] * 2 + ["bf16"] * 29, ["fp8"] * 11 + ["bf16"] * 20),
-    (["int4"] * 23 + ["bf16"] * 8, ["int4"] * 23 + ["bf16"] * 8)])
+    (["int4"] * 23 + ["bf16"] * 8, ["int4"] * 23 + ["bf16"] * 8),
+    # kinds interleaved: the kernel regroups the slots into kind-uniform key tiles
+    (["int4", "bf16"] * 8, ["int4", "bf16"] * 8),
+    (["fp8", "int4"] * 10 + ["bf16"], ["fp8"] * 20 + ["bf16"])])
 def test_attn_decode_keys_values_in_own_tiers(pkg, cuda, kinds, vkinds):
     """The one-query-frame kernel of the incremental forward: newest frame against cached
     slots whose keys and values sit in different tiers, plus its own K/V, vs fp32 SDPA on
