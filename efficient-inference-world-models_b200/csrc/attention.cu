@@ -622,6 +622,17 @@ constexpr int kDecThreads = kDecWarps * 32;
 // Kinds of the decode kernel's template: one storage kind for every cached slot of a
 // tensor, or kDecMixed (per-slot kinds from the layout).
 constexpr int kDecMixed = 3;
+// ... or 4 + 3a + b (a != b): kind a at the key positions below the layout's split, kind b
+// from it on (two kind-uniform runs of tiles: the kind branches fold at compile time)
+constexpr int kDecSplit = 4;
+__host__ __device__ constexpr int dec_split_code(int a, int b) { return kDecSplit + 3 * a + b; }
+__host__ __device__ constexpr int dec_split_a(int code) { return (code - kDecSplit) / 3; }
+__host__ __device__ constexpr int dec_split_b(int code) { return (code - kDecSplit) % 3; }
+// whether a template kind code can hold rows of storage kind `kind`
+__host__ __device__ constexpr bool dec_has(int code, int kind) {
+  return code == kind || code == kDecMixed ||
+         (code >= kDecSplit && (dec_split_a(code) == kind || dec_split_b(code) == kind));
+}
 
 struct DecodeTensor {
   uint32_t slot_page[OASIS_MAX_FRAMES];  // layer * n_kind + pool index of slot j
@@ -635,6 +646,7 @@ struct DecodeTensor {
 struct DecodeLayout {
   DecodeTensor t[2];  // keys, values, indexed by key position
   uint32_t valid;     // positions holding a cached slot at or before the query's window position
+  int split;          // split kind codes: first position of the second kind (a multiple of 8)
   int items;          // batch * 144 tokens * 16 heads
   int live_kv;        // the query frame's own K/V is a key (at window position n_past)
 };
@@ -885,6 +897,12 @@ __device__ __forceinline__ float2 dec_scale(uint32_t raw, int kind, bool live) {
 // mixed tensors keep their row kinds and three row pointers live, and take the registers
 // of one CTA (no spills) rather than spill inside the item loop
 __host__ __device__ constexpr int dec_min_ctas(int kk, int vk) { return kk == kDecMixed || vk == kDecMixed ? 1 : 2; }
+// storage kind of key position j under template kind code `code`
+__device__ __forceinline__ int dec_position_kind(int code, const DecodeTensor& d, int split, int j) {
+  if (code == kDecMixed) return static_cast<int>((d.kinds >> (2 * j)) & 3ull);
+  if (code >= kDecSplit) return j < split ? dec_split_a(code) : dec_split_b(code);
+  return code;
+}
 template <int KK, int VK>
 __global__ void __launch_bounds__(kDecThreads, dec_min_ctas(KK, VK))
     attn_decode_kernel(const __nv_bfloat16* __restrict__ qkv, __nv_bfloat16* __restrict__ out,
@@ -893,17 +911,15 @@ __global__ void __launch_bounds__(kDecThreads, dec_min_ctas(KK, VK))
   pdl_trigger();
   constexpr int KW = KK == OASIS_KV_FP8 ? 4 : (KK == OASIS_KV_INT4 ? 2 : 8);  // words per key chunk
   constexpr int VW = VK == OASIS_KV_FP8 ? 2 : (VK == OASIS_KV_INT4 ? 1 : 4);  // words per value chunk
-  constexpr bool kNibble = KK == OASIS_KV_INT4 || KK == kDecMixed;          // key dim order
-  constexpr bool kZeroK = KK == OASIS_KV_INT4 || KK == kDecMixed;           // keys may carry zeros
-  constexpr bool kZeroV = VK == OASIS_KV_INT4 || VK == kDecMixed;
+  constexpr bool kNibble = KK == OASIS_KV_INT4 || KK >= kDecMixed;  // key dim order
+  constexpr bool kZeroK = dec_has(KK, OASIS_KV_INT4);               // keys may carry zeros
+  constexpr bool kZeroV = dec_has(VK, OASIS_KV_INT4);
   const int lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
   const KvTensor& tk = kv.t[0];
   const KvTensor& tv = kv.t[1];
   const DecodeTensor& dk = lay.t[0];
   const DecodeTensor& dv = lay.t[1];
-  auto kind_of = [&](const DecodeTensor& d, int tmpl, int j) {
-    return tmpl == kDecMixed ? static_cast<int>((d.kinds >> (2 * j)) & 3ull) : tmpl;
-  };
+  auto kind_of = [&](const DecodeTensor& d, int tmpl, int j) { return dec_position_kind(tmpl, d, lay.split, j); };
 
   // ---- loop-invariant parts of this lane's addresses
   // key rows r = 0..3: key 8r + g, dims 16c..16c+15
@@ -915,7 +931,10 @@ __global__ void __launch_bounds__(kDecThreads, dec_min_ctas(KK, VK))
     kpack |= static_cast<uint32_t>(kind) << (2 * r);
     koff[r] = dk.slot_page[j] * (OASIS_TOKENS * dec_row_bytes(kind)) + c * (dec_head_bytes(kind) / 4);
   }
-  auto kkind = [&](int r) { return KK == kDecMixed ? static_cast<int>((kpack >> (2 * r)) & 3u) : KK; };
+  auto kkind = [&](int r) {
+    if constexpr (KK >= kDecSplit) return 8 * r + g < lay.split ? dec_split_a(KK) : dec_split_b(KK);
+    return KK == kDecMixed ? static_cast<int>((kpack >> (2 * r)) & 3u) : KK;
+  };
   // value rows q = 0..7: key 16 (q >> 2) + 2c + 8 ((q >> 1) & 1) + (q & 1), dims 8g..8g+7
   uint32_t voff[8];
   uint32_t vpack = 0;
@@ -925,7 +944,11 @@ __global__ void __launch_bounds__(kDecThreads, dec_min_ctas(KK, VK))
     vpack |= static_cast<uint32_t>(kind) << (2 * q);
     voff[q] = dv.slot_page[j] * (OASIS_TOKENS * dec_row_bytes(kind)) + g * (dec_head_bytes(kind) / 8);
   }
-  auto vkind = [&](int q) { return VK == kDecMixed ? static_cast<int>((vpack >> (2 * q)) & 3u) : VK; };
+  auto vkind = [&](int q) {
+    if constexpr (VK >= kDecSplit)
+      return 16 * (q >> 2) + 8 * ((q >> 1) & 1) < lay.split ? dec_split_a(VK) : dec_split_b(VK);
+    return VK == kDecMixed ? static_cast<int>((vpack >> (2 * q)) & 3u) : VK;
+  };
   // scales of slot `lane`
   const bool slot_live = (lay.valid >> lane) & 1u;
   const int ks_kind = kind_of(dk, KK, lane), vs_kind = kind_of(dv, VK, lane);
@@ -947,9 +970,9 @@ __global__ void __launch_bounds__(kDecThreads, dec_min_ctas(KK, VK))
   auto load_keys = [&](int item) {
     const int h = item & 15, tok = item >> 4;
     const int p = tok % OASIS_TOKENS, b = tok / OASIS_TOKENS;
-    const uint8_t* base0 = (KK == kDecMixed || KK == 0) ? dec_item_rows(tk, dk, 0, b, p, h) : nullptr;
-    const uint8_t* base1 = (KK == kDecMixed || KK == 1) ? dec_item_rows(tk, dk, 1, b, p, h) : nullptr;
-    const uint8_t* base2 = (KK == kDecMixed || KK == 2) ? dec_item_rows(tk, dk, 2, b, p, h) : nullptr;
+    const uint8_t* base0 = dec_has(KK, 0) ? dec_item_rows(tk, dk, 0, b, p, h) : nullptr;
+    const uint8_t* base1 = dec_has(KK, 1) ? dec_item_rows(tk, dk, 1, b, p, h) : nullptr;
+    const uint8_t* base2 = dec_has(KK, 2) ? dec_item_rows(tk, dk, 2, b, p, h) : nullptr;
 #pragma unroll
     for (int r = 0; r < 4; ++r) {
       const int kind = kkind(r);
@@ -1001,9 +1024,9 @@ __global__ void __launch_bounds__(kDecThreads, dec_min_ctas(KK, VK))
   auto load_values = [&](int item) {
     const int h = item & 15, tok = item >> 4;
     const int p = tok % OASIS_TOKENS, b = tok / OASIS_TOKENS;
-    const uint8_t* base0 = (VK == kDecMixed || VK == 0) ? dec_item_rows(tv, dv, 0, b, p, h) : nullptr;
-    const uint8_t* base1 = (VK == kDecMixed || VK == 1) ? dec_item_rows(tv, dv, 1, b, p, h) : nullptr;
-    const uint8_t* base2 = (VK == kDecMixed || VK == 2) ? dec_item_rows(tv, dv, 2, b, p, h) : nullptr;
+    const uint8_t* base0 = dec_has(VK, 0) ? dec_item_rows(tv, dv, 0, b, p, h) : nullptr;
+    const uint8_t* base1 = dec_has(VK, 1) ? dec_item_rows(tv, dv, 1, b, p, h) : nullptr;
+    const uint8_t* base2 = dec_has(VK, 2) ? dec_item_rows(tv, dv, 2, b, p, h) : nullptr;
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
       const int kind = vkind(q);
@@ -1227,6 +1250,16 @@ DecodeKernel decode_kernel_v(int vk) {
   return attn_decode_kernel<KK, kDecMixed>;
 }
 DecodeKernel decode_kernel(int kk, int vk) {
+  if (kk >= kDecSplit && kk == vk) {
+    switch (kk - kDecSplit) {
+      case 1: return attn_decode_kernel<kDecSplit + 1, kDecSplit + 1>;  // bf16 | FP8
+      case 2: return attn_decode_kernel<kDecSplit + 2, kDecSplit + 2>;  // bf16 | INT4
+      case 3: return attn_decode_kernel<kDecSplit + 3, kDecSplit + 3>;  // FP8 | bf16
+      case 5: return attn_decode_kernel<kDecSplit + 5, kDecSplit + 5>;  // FP8 | INT4
+      case 6: return attn_decode_kernel<kDecSplit + 6, kDecSplit + 6>;  // INT4 | bf16
+      case 7: return attn_decode_kernel<kDecSplit + 7, kDecSplit + 7>;  // INT4 | FP8
+    }
+  }
   switch (kk) {
     case OASIS_KV_BF16: return decode_kernel_v<OASIS_KV_BF16>(vk);
     case OASIS_KV_FP8: return decode_kernel_v<OASIS_KV_FP8>(vk);
@@ -1335,6 +1368,20 @@ int launch_attn_temporal(const void* qkv, const KvView& kv, int layer, void* out
     }
     for (int j = 0; j < OASIS_MAX_FRAMES; ++j)
       if (pos_slot[j] >= 0 && pos_slot[j] <= q_pos0) lay.valid |= 1u << j;
+    // two kind-uniform runs of tiles, the same for keys and values: the split kernels
+    if (uniform[0] == kDecMixed && uniform[1] == kDecMixed) {
+      int split = 0;
+      while (split < OASIS_MAX_FRAMES && pos_kind[0][split] == pos_kind[0][0] && pos_kind[1][split] == pos_kind[1][0])
+        ++split;
+      bool two_runs = split % 8 == 0 && split < OASIS_MAX_FRAMES && pos_kind[0][0] == pos_kind[1][0] &&
+                      pos_kind[0][split] == pos_kind[1][split] && pos_kind[0][split] != pos_kind[0][0];
+      for (int j = split; two_runs && j < OASIS_MAX_FRAMES; ++j)
+        two_runs = pos_kind[0][j] == pos_kind[0][split] && pos_kind[1][j] == pos_kind[1][split];
+      if (two_runs) {
+        uniform[0] = uniform[1] = dec_split_code(pos_kind[0][0], pos_kind[0][split]);
+        lay.split = split;
+      }
+    }
     for (int which = 0; which < 2; ++which) {
       const KvTensor& t = kv.t[which];
       DecodeTensor& d = lay.t[which];
