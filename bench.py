@@ -206,21 +206,95 @@ def cpu_oracle_rate(budget_s=15.0, threads=None):
             "config0": "B=1, T=4, fp32, seed 0: 3 whole forwards"}
 
 
-def library_bar(dev, steps=10):
-    """Same-box library comparator: the oracle (the reference forward restated in
-    PyTorch) cast to bf16 and run eagerly on this B200 (cuBLAS GEMMs, SDPA attention),
-    B=1 T=32 forwards/s.  A comparator only: nothing of it is on the product path."""
+class TorchBf16DiT:
+    """Same-box library comparator: the Oasis DiT-S/2 forward written directly in eager
+    PyTorch bf16 (cuBLAS GEMMs, SDPA attention, axial / temporal RoPE tables on the GPU) on
+    the same random weights.  A comparator only: nothing of it is on the product path."""
+
+    def __init__(self, sd, depth, dev):
+        bf = torch.bfloat16
+        self.w = {k: v.to(dev, bf) for k, v in sd.items()}
+        self.depth = depth
+
+        def angles(pos, freqs):  # (n,) x (f,) -> (n, 2f), pairs interleaved
+            return (pos[:, None] * freqs).repeat_interleave(2, dim=-1)
+
+        # spatial: 16 "pixel" frequencies per axis over linspace(-1, 1) positions, H then W
+        pf = torch.linspace(1.0, 128.0, 16, device=dev) * math.pi
+        ah = angles(torch.linspace(-1.0, 1.0, 9, device=dev), pf)
+        aw = angles(torch.linspace(-1.0, 1.0, 16, device=dev), pf)
+        sp = torch.cat([ah[:, None, :].expand(9, 16, 32), aw[None, :, :].expand(9, 16, 32)], -1).reshape(144, 64)
+        self.s_cos, self.s_sin = sp.cos().to(bf), sp.sin().to(bf)
+        # temporal: 32 "lang" frequencies over frame positions 0..31
+        lf = 1.0 / (10000.0 ** (torch.arange(0, 64, 2, device=dev).float() / 64))
+        tp = angles(torch.arange(WINDOW, device=dev).float(), lf)
+        self.t_cos, self.t_sin = tp.cos().to(bf), tp.sin().to(bf)
+
+    @staticmethod
+    def _rope(x, cos, sin):
+        a, b = x.unflatten(-1, (-1, 2)).unbind(-1)
+        return x * cos + torch.stack((-b, a), dim=-1).flatten(-2) * sin
+
+    def _sub(self, x, c, i, kind):
+        F = torch.nn.functional
+        w, p = self.w, f"blocks.{i}.{kind}_"
+        B, T = x.shape[:2]
+        mod = F.linear(F.silu(c), w[p + "adaLN_modulation.1.weight"], w[p + "adaLN_modulation.1.bias"])
+        sh1, sc1, g1, sh2, sc2, g2 = mod[:, :, None, :].chunk(6, dim=-1)
+        h = F.layer_norm(x, (1024,), eps=1e-6) * (1 + sc1) + sh1
+        q, k, v = F.linear(h, w[p + "attn.to_qkv.weight"]).view(B, T, 144, 3, 16, 64).unbind(3)
+        if kind == "s":
+            q, k, v = (z.reshape(B * T, 144, 16, 64).transpose(1, 2) for z in (q, k, v))
+            q, k = self._rope(q, self.s_cos, self.s_sin), self._rope(k, self.s_cos, self.s_sin)
+            o = F.scaled_dot_product_attention(q, k, v).transpose(1, 2).reshape(B, T, 144, 1024)
+        else:
+            q, k, v = (z.permute(0, 2, 3, 1, 4).reshape(B * 144, 16, T, 64) for z in (q, k, v))
+            cos, sin = self.t_cos[:T], self.t_sin[:T]
+            q, k = self._rope(q, cos, sin), self._rope(k, cos, sin)
+            o = F.scaled_dot_product_attention(q, k, v, is_causal=True)
+            o = o.reshape(B, 144, 16, T, 64).permute(0, 3, 1, 2, 4).reshape(B, T, 144, 1024)
+        x = x + g1 * F.linear(o, w[p + "attn.to_out.weight"], w[p + "attn.to_out.bias"])
+        h = F.layer_norm(x, (1024,), eps=1e-6) * (1 + sc2) + sh2
+        h = F.gelu(F.linear(h, w[p + "mlp.fc1.weight"], w[p + "mlp.fc1.bias"]), approximate="tanh")
+        return x + g2 * F.linear(h, w[p + "mlp.fc2.weight"], w[p + "mlp.fc2.bias"])
+
+    def __call__(self, x, t, a):
+        F = torch.nn.functional
+        w = self.w
+        B, T = x.shape[:2]
+        tok = F.conv2d(x.reshape(B * T, 16, 18, 32).to(torch.bfloat16), w["x_embedder.proj.weight"],
+                       w["x_embedder.proj.bias"], stride=2)
+        tok = tok.permute(0, 2, 3, 1).reshape(B, T, 144, 1024)
+        half = 128
+        freqs = torch.exp(-math.log(10000.0) * torch.arange(half, device=x.device).float() / half)
+        args = t.reshape(-1, 1).float() * freqs[None]
+        temb = torch.cat([torch.cos(args), torch.sin(args)], dim=-1).to(torch.bfloat16)
+        temb = F.linear(F.silu(F.linear(temb, w["t_embedder.mlp.0.weight"], w["t_embedder.mlp.0.bias"])),
+                        w["t_embedder.mlp.2.weight"], w["t_embedder.mlp.2.bias"])
+        c = temb.reshape(B, T, 1024) + F.linear(a.to(torch.bfloat16), w["external_cond.weight"], w["external_cond.bias"])
+        for i in range(self.depth):
+            tok = self._sub(self._sub(tok, c, i, "s"), c, i, "t")
+        shift, scale = F.linear(F.silu(c), w["final_layer.adaLN_modulation.1.weight"],
+                                w["final_layer.adaLN_modulation.1.bias"])[:, :, None, :].chunk(2, dim=-1)
+        y = F.linear(F.layer_norm(tok, (1024,), eps=1e-6) * (1 + scale) + shift, w["final_layer.linear.weight"],
+                     w["final_layer.linear.bias"])
+        y = y.reshape(B * T, 9, 16, 2, 2, 16)
+        return torch.einsum("nhwpqc->nchpwq", y).reshape(B, T, 16, 18, 32)
+
+
+def library_bar(dev, model, steps=10):
+    """Same-box library comparator (TorchBf16DiT), B=1 T=32 forwards/s, with the rel-L2 of
+    its v against this package's forward on the same inputs."""
     try:
-        from oracle.dit_ref import build_oracle
         pkg = importlib.import_module(PKG)
-        m = build_oracle(pkg.random_state_dict(seed=0, depth=DEPTH), depth=DEPTH).to(dev, torch.bfloat16).eval()
+        m = TorchBf16DiT(pkg.random_state_dict(seed=0, depth=DEPTH), DEPTH, dev)
         g = torch.Generator().manual_seed(0)
-        x = torch.randn(1, WINDOW, *FRAME, generator=g).to(dev, torch.bfloat16)
+        x = torch.randn(1, WINDOW, *FRAME, generator=g).to(dev)
         t = torch.full((1, WINDOW), STAB_LEVEL - 1, dtype=torch.long, device=dev)
-        a = synthetic_actions(g, 1, WINDOW).to(dev, torch.bfloat16)
+        a = synthetic_actions(g, 1, WINDOW).to(dev)
         with torch.no_grad():
             for _ in range(3):
-                m(x, t, a)
+                v_lib = m(x, t, a)
             torch.cuda.synchronize()
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record()
@@ -228,11 +302,14 @@ def library_bar(dev, steps=10):
                 m(x, t, a)
             e1.record()
             torch.cuda.synchronize()
+            v_ours = model(x, t, a)
+            rel = ((v_lib.float() - v_ours.float()).norm() / v_ours.float().norm()).item()
         ms = e0.elapsed_time(e1) / steps
         del m
         torch.cuda.empty_cache()
-        return {"value": 1000.0 / ms, "unit": "forwards/s", "ms_per_forward": ms,
-                "what": "oracle forward in bf16, eager PyTorch on this GPU (cuBLAS + SDPA), B=1 T=32"}
+        return {"value": 1000.0 / ms, "unit": "forwards/s", "ms_per_forward": ms, "rel_l2_vs_b200_path": rel,
+                "what": "the same DiT forward in eager PyTorch bf16 on this GPU (cuBLAS + SDPA), B=1 T=32, "
+                        "same random weights"}
     except Exception as e:  # a comparator, never required
         return {"value": None, "error": str(e)[:200]}
 
@@ -466,7 +543,7 @@ def run_ours(args, rank, world, local_rank):
     if rank == 0 and not args.skip_sweep:
         sweep = attention_sweep(pkg, dev, peaks.get("hbm_gbs", 6650.0), reps=10)
     if rank == 0 and world == 1 and not args.skip_cpu:
-        lib = library_bar(dev)
+        lib = library_bar(dev, model)
 
     # every rank's own time and clocks, gathered outside the timed region
     mine = {"rank": rank, "ms_per_step": per_rank_ms / args.steps, "sm_mhz": clk.get("sm_mhz"),
