@@ -311,14 +311,15 @@ void choose_tiles(int M, int N, int K, bool allow_split, int* bn, int* ctas, int
   const int pairs = max_pairs<256, kEpiGateResid>();
   *splits = 1;
   if (N % 256 == 0) {
-    // CTA pairs on 256 x 256 tiles (the chained launch's tiles) unless their last wave
-    // would hold fewer than 45 % of the pair slots: each SM stages half the B rows, so a
-    // pair tile costs the SM less operand traffic than any single-CTA tile
+    // CTA pairs on 256 x 256 tiles (the chained launch's tiles) unless they run in fewer
+    // than four waves, the last of them under 45 % full: each SM stages half the B rows,
+    // so a pair tile costs the SM less operand traffic than any single-CTA tile, and from
+    // four waves on a partly filled last wave costs less than leaving the pairs
     const long long pair_m = (M + 2 * kGemmBM - 1) / (2 * kGemmBM);
     const long long units = pair_m * (N / 256);
     const long long waves = (units + pairs - 1) / pairs;
     const long long last = units - (waves - 1) * pairs;
-    if (100 * last >= 45LL * pairs) {
+    if (waves >= 4 || 100 * last >= 45LL * pairs) {
       *bn = 256;
       *ctas = 2;
       return;
