@@ -664,13 +664,17 @@ def kv_configs(pkg, model, dev, g, peaks):
     return out
 
 
-def attention_sweep(pkg, dev, hbm, reps=20):
+def attention_sweep(pkg, dev, hbm, reps=20, only=None):
     """The isolated attention sweep (benchmark configuration 4): spatial attention over
     B*T frames of 144 tokens, causal temporal attention over T frames for B*144
     sequences with bf16 K/V (full-window kernel) or every K/V frame from an FP8 / INT4
     cache, and the one-query-frame kernel of the incremental forward (31 cached frames).
-    Bytes: q, k, v read and o written once (k, v at their stored width)."""
+    Bytes: q, k, v read and o written once (k, v at their stored width).  `only`: run just
+    the cases whose name contains it."""
     g = torch.Generator(device=dev).manual_seed(0)
+
+    def wanted(case):
+        return only is None or only in case
 
     def timeit(fn):
         for _ in range(3):
@@ -686,6 +690,8 @@ def attention_sweep(pkg, dev, hbm, reps=20):
 
     out = []
     for frames in (32, 256, 1024, 4096):
+        if not wanted(f"spatial BT={frames}"):
+            continue
         qkv = torch.randn(frames * TOKENS, 3072, device=dev, generator=g).bfloat16()
         o = torch.empty(frames * TOKENS, 1024, device=dev).bfloat16()
         ms = timeit(lambda: pkg.attn_spatial(qkv, out=o))
@@ -696,9 +702,12 @@ def attention_sweep(pkg, dev, hbm, reps=20):
         del qkv, o
     for T in (8, 16, 32):
         for B in (1, 8, 32):
+            kinds = [k for k in ("bf16", "fp8", "int4") if wanted(f"temporal T={T} B={B} kv={k}")]
+            if not kinds:
+                continue
             qkv = torch.randn(B * T * TOKENS, 3072, device=dev, generator=g).bfloat16()
             o = torch.empty(B * T * TOKENS, 1024, device=dev).bfloat16()
-            for kind in ("bf16", "fp8", "int4"):
+            for kind in kinds:
                 if kind == "bf16":
                     fn = lambda: pkg.attn_temporal(qkv, batch=B, q_frames=T, out=o)
                     kv_bytes = B * T * TOKENS * 1024 * 2 * 2
@@ -714,10 +723,13 @@ def attention_sweep(pkg, dev, hbm, reps=20):
                             "GBps": byts / ms / 1e6, "frac_hbm": byts / ms / 1e6 / hbm})
             del qkv, o
     for B in (8, 32):
+        kinds = [k for k in ("bf16", "fp8", "int4") if wanted(f"decode past=31 B={B} kv={k}")]
+        if not kinds:
+            continue
         new = torch.randn(B * TOKENS, 3072, device=dev, generator=g).bfloat16()
         o = torch.empty(B * TOKENS, 1024, device=dev).bfloat16()
         past = torch.randn(B * 31 * TOKENS, 3072, device=dev, generator=g).bfloat16()
-        for kind in ("bf16", "fp8", "int4"):
+        for kind in kinds:
             cache = pkg.KVCacheB200.uniform(B, 1, 31, kind, device=dev)
             cache.store(past, layer=0)
             ms = timeit(lambda: pkg.attn_temporal(new, batch=B, q_frames=1, q_pos0=31, n_past=31,
@@ -766,7 +778,26 @@ def run_isolated(args, local_rank):
         print(json.dumps({"case": f"gemm M={M} N={N} K={K}", "ms": ms, "tflops": tf,
                           "frac_burst": tf / peaks.get("bf16_tflops", 1590.0)}), flush=True)
         return 0
-    for line in attention_sweep(pkg, dev, hbm, reps=args.steps):
+    if args.isolated == "cached":
+        # prefill of a B-session window into a cache of one kind, then `steps` incremental
+        # forwards of the newest frame over the 31 cached frames (eager launches)
+        B = args.batch
+        model = pkg.OasisDiTB200.random(seed=0, depth=DEPTH, device=dev)
+        gh = torch.Generator().manual_seed(0)
+        x = torch.randn(B, WINDOW, *FRAME, generator=gh).to(dev)
+        t = torch.full((B, WINDOW), STAB_LEVEL - 1, dtype=torch.long, device=dev)
+        a = synthetic_actions(gh, B, WINDOW).to(dev)
+        kinds = (["int4"] * 23 + ["bf16"] * 8) if args.kv == "progressive" else [args.kv] * (WINDOW - 1)
+        cache = pkg.KVCacheB200(B, DEPTH, kinds, device=dev)
+        model(x, t, a, kv_cache=cache)
+        xn, an = x[:, -1].contiguous(), a[:, -1].contiguous()
+        tn = torch.full((B,), 599, dtype=torch.long, device=dev)
+        vout = torch.empty(B, *FRAME, device=dev)
+        ms = timeit(lambda: model.forward_cached(xn, tn, an, cache, n_past=WINDOW - 1, out=vout), args.steps)
+        print(json.dumps({"case": f"cached forward B={B} kv={args.kv} past=31", "ms": ms,
+                          "forwards_per_s": B / (ms / 1e3), "launch": "eager"}), flush=True)
+        return 0
+    for line in attention_sweep(pkg, dev, hbm, reps=args.steps, only=args.case):
         print(json.dumps(line), flush=True)
     return 0
 
@@ -782,7 +813,11 @@ def main():
     ap.add_argument("--skip-kv", action="store_true")
     ap.add_argument("--skip-sweep", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=12.0)
-    ap.add_argument("--isolated", choices=["attention", "gemm"], default=None)
+    ap.add_argument("--isolated", choices=["attention", "gemm", "cached"], default=None)
+    ap.add_argument("--case", default=None, help="--isolated attention: cases whose name contains this")
+    ap.add_argument("--batch", type=int, default=8, help="--isolated cached: sessions")
+    ap.add_argument("--kv", default="fp8", choices=["bf16", "fp8", "int4", "progressive"],
+                    help="--isolated cached: cache kind (progressive: 23 INT4 + 8 bf16 frames)")
     ap.add_argument("--M", type=int, default=36864)
     ap.add_argument("--N", type=int, default=1024)
     ap.add_argument("--K", type=int, default=4096)
