@@ -454,11 +454,13 @@ __global__ void __launch_bounds__(kTpWarps * 32)
       }
       *reinterpret_cast<uint4*>(mat(hh, which) + s * kSmemStride + c * 8) = v;
     }
-    // zero the padding rows the MMAs read (keeps masked products finite)
-    for (int i = tid; i < kTpWarps * 3 * 32 * 8; i += kTpWarps * 32) {
-      const int hh = i / (3 * 32 * 8), which = (i / (32 * 8)) % 3, r = (i >> 3) & 31, c = i & 7;
-      const bool pad = which == 0 ? (r >= q_frames && r < m_tiles * 16) : (r >= n_kv && r < n_pairs * 16);
-      if (pad) *reinterpret_cast<uint4*>(mat(hh, which) + r * kSmemStride + c * 8) = make_uint4(0, 0, 0, 0);
+    // zero the padding rows the MMAs read (keeps masked products finite), if there are any
+    if (q_frames < m_tiles * 16 || n_kv < n_pairs * 16) {
+      for (int i = tid; i < kTpWarps * 3 * 32 * 8; i += kTpWarps * 32) {
+        const int hh = i / (3 * 32 * 8), which = (i / (32 * 8)) % 3, r = (i >> 3) & 31, c = i & 7;
+        const bool pad = which == 0 ? (r >= q_frames && r < m_tiles * 16) : (r >= n_kv && r < n_pairs * 16);
+        if (pad) *reinterpret_cast<uint4*>(mat(hh, which) + r * kSmemStride + c * 8) = make_uint4(0, 0, 0, 0);
+      }
     }
     __syncthreads();
   }
@@ -1269,6 +1271,313 @@ DecodeKernel decode_kernel(int kk, int vk) {
 }
 
 // ----------------------------------------------------------------------------------
+// temporal attention of several query frames whose keys and values all come from cache
+// slots of one kind per tensor (no live frames: the isolated sweep's case)
+// ----------------------------------------------------------------------------------
+// One warp per (session, token, head, 16-query tile).  The key and value fragments come
+// straight from the cache into registers and are converted there, as in the one-query-frame
+// kernel (same fragment layouts and head-dim orders); the query tile is the A operand of the
+// scores, whose accumulators are the A operand of P V (no shuffle), and the softmax of the
+// 16 rows uses every lane (rows g and g + 8 of each lane quad).
+constexpr int kWcWarps = 4;
+
+struct WindowLayout {
+  DecodeTensor t[2];  // keys, values by slot
+  int items;          // batch * 144 tokens * 16 heads * m_tiles
+  int m_tiles;        // 16-row query tiles (1 or 2)
+};
+
+template <int KK, int VK>
+__global__ void __launch_bounds__(kWcWarps * 32, 4)
+    attn_window_cached_kernel(const __nv_bfloat16* __restrict__ qkv, __nv_bfloat16* __restrict__ out,
+                              const __grid_constant__ KvView kv, const __grid_constant__ WindowLayout lay,
+                              int q_frames, int q_pos0, int n_past, float scale_log2) {
+  pdl_trigger();
+  constexpr int KW = KK == OASIS_KV_FP8 ? 4 : (KK == OASIS_KV_INT4 ? 2 : 8);
+  constexpr int VW = VK == OASIS_KV_FP8 ? 2 : (VK == OASIS_KV_INT4 ? 1 : 4);
+  constexpr bool kNibble = KK == OASIS_KV_INT4;
+  const int lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
+  const int item = blockIdx.x * kWcWarps + (threadIdx.x >> 5);
+  const KvTensor& tk = kv.t[0];
+  const KvTensor& tv = kv.t[1];
+  const DecodeTensor& dk = lay.t[0];
+  const DecodeTensor& dv = lay.t[1];
+  pdl_wait();
+  if (item >= lay.items) return;
+  const int mt = item % lay.m_tiles, rest = item / lay.m_tiles;
+  const int h = rest & 15, tok = rest >> 4;
+  const int p = tok % OASIS_TOKENS, b = tok / OASIS_TOKENS;
+
+  // ---- loads: keys 8r + g (dims 16c..), values 16kv + 2c + {0,1,8,9} (dims 8g..), query rows
+  uint32_t kr[4][KW], vr[8][VW], q0[8], q1[8];
+  {
+    const uint8_t* kb = dec_item_rows(tk, dk, KK, b, p, h);
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int j = 8 * r + g;
+#pragma unroll
+      for (int w = 0; w < KW; ++w) kr[r][w] = 0u;
+      if (j < n_past) {
+        const uint8_t* src = kb + dk.slot_page[j] * (OASIS_TOKENS * dec_row_bytes(KK)) + c * (dec_head_bytes(KK) / 4);
+        if (KK == OASIS_KV_INT4) {
+          const uint2 x = *reinterpret_cast<const uint2*>(src);
+          kr[r][0] = x.x;
+          kr[r][KW > 1 ? 1 : 0] = x.y;
+        } else {
+#pragma unroll
+          for (int w4 = 0; w4 < KW / 4; ++w4) {
+            const uint4 x = __ldg(reinterpret_cast<const uint4*>(src) + w4);
+            kr[r][4 * w4] = x.x; kr[r][4 * w4 + 1] = x.y; kr[r][4 * w4 + 2] = x.z; kr[r][4 * w4 + 3] = x.w;
+          }
+        }
+      }
+    }
+    const uint8_t* vb = dec_item_rows(tv, dv, VK, b, p, h);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const int j = 16 * (q >> 2) + 2 * c + 8 * ((q >> 1) & 1) + (q & 1);
+#pragma unroll
+      for (int w = 0; w < VW; ++w) vr[q][w] = 0u;
+      if (j < n_past) {
+        const uint8_t* src = vb + dv.slot_page[j] * (OASIS_TOKENS * dec_row_bytes(VK)) + g * (dec_head_bytes(VK) / 8);
+        if (VW == 4) {
+          const uint4 x = __ldg(reinterpret_cast<const uint4*>(src));
+          vr[q][0] = x.x; vr[q][VW > 1 ? 1 : 0] = x.y; vr[q][VW > 2 ? 2 : 0] = x.z; vr[q][VW > 3 ? 3 : 0] = x.w;
+        } else if (VW == 2) {
+          const uint2 x = __ldg(reinterpret_cast<const uint2*>(src));
+          vr[q][0] = x.x; vr[q][VW > 1 ? 1 : 0] = x.y;
+        } else {
+          vr[q][0] = __ldg(reinterpret_cast<const uint32_t*>(src));
+        }
+      }
+    }
+    const int t0 = 16 * mt + g, t1 = t0 + 8;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) q0[w] = q1[w] = 0u;
+    if (t0 < q_frames) {
+      const uint4* src = reinterpret_cast<const uint4*>(
+          qkv + (static_cast<long long>(b * q_frames + t0) * OASIS_TOKENS + p) * kQkvLd + h * 64 + 16 * c);
+      const uint4 x0 = src[0], x1 = src[1];
+      q0[0] = x0.x; q0[1] = x0.y; q0[2] = x0.z; q0[3] = x0.w; q0[4] = x1.x; q0[5] = x1.y; q0[6] = x1.z; q0[7] = x1.w;
+    }
+    if (t1 < q_frames) {
+      const uint4* src = reinterpret_cast<const uint4*>(
+          qkv + (static_cast<long long>(b * q_frames + t1) * OASIS_TOKENS + p) * kQkvLd + h * 64 + 16 * c);
+      const uint4 x0 = src[0], x1 = src[1];
+      q1[0] = x0.x; q1[1] = x0.y; q1[2] = x0.z; q1[3] = x0.w; q1[4] = x1.x; q1[5] = x1.y; q1[6] = x1.z; q1[7] = x1.w;
+    }
+  }
+  // scales of slot `lane`
+  const bool slot_live = lane < n_past;
+  float2 kscale = make_float2(1.0f, 0.0f), vscale = make_float2(slot_live ? 1.0f : 0.0f, 0.0f);
+  if (KK != OASIS_KV_BF16 && slot_live) {
+    const long long e = dec_item_scale(dk, KK, b, p, h) + dec_slot_scale(KK, dk.slot_page[lane]);
+    const uint32_t raw = KK == OASIS_KV_FP8
+                             ? static_cast<uint32_t>(__ldg(reinterpret_cast<const unsigned short*>(tk.fp8_scale) + e))
+                             : static_cast<uint32_t>(__ldg(reinterpret_cast<const unsigned short*>(tk.i4_scale) + e)) |
+                                   (static_cast<uint32_t>(__ldg(reinterpret_cast<const unsigned short*>(tk.i4_zero) + e)) << 16);
+    kscale = dec_scale(raw, KK, true);
+  }
+  if (VK != OASIS_KV_BF16 && slot_live) {
+    const long long e = dec_item_scale(dv, VK, b, p, h) + dec_slot_scale(VK, dv.slot_page[lane]);
+    const uint32_t raw = VK == OASIS_KV_FP8
+                             ? static_cast<uint32_t>(__ldg(reinterpret_cast<const unsigned short*>(tv.fp8_scale) + e))
+                             : static_cast<uint32_t>(__ldg(reinterpret_cast<const unsigned short*>(tv.i4_scale) + e)) |
+                                   (static_cast<uint32_t>(__ldg(reinterpret_cast<const unsigned short*>(tv.i4_zero) + e)) << 16);
+    vscale = dec_scale(raw, VK, true);
+  }
+
+  // ---- the query tile as A (rows g, g + 8), in the keys' head-dim order
+  uint32_t qa[4][4];
+  if (KK == OASIS_KV_BF16) {
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks) {
+      qa[ks][0] = q0[2 * ks]; qa[ks][1] = q1[2 * ks]; qa[ks][2] = q0[2 * ks + 1]; qa[ks][3] = q1[2 * ks + 1];
+    }
+  } else if (!kNibble) {
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks) {
+      qa[ks][0] = f16x2_bf16x2(q0[2 * ks]); qa[ks][1] = f16x2_bf16x2(q1[2 * ks]);
+      qa[ks][2] = f16x2_bf16x2(q0[2 * ks + 1]); qa[ks][3] = f16x2_bf16x2(q1[2 * ks + 1]);
+    }
+  } else {
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      qa[2 * k][0] = pack_f16x2(bf16_lo(q0[4 * k]), bf16_lo(q0[4 * k + 2]));
+      qa[2 * k][1] = pack_f16x2(bf16_lo(q1[4 * k]), bf16_lo(q1[4 * k + 2]));
+      qa[2 * k][2] = pack_f16x2(bf16_hi(q0[4 * k]), bf16_hi(q0[4 * k + 2]));
+      qa[2 * k][3] = pack_f16x2(bf16_hi(q1[4 * k]), bf16_hi(q1[4 * k + 2]));
+      qa[2 * k + 1][0] = pack_f16x2(bf16_lo(q0[4 * k + 1]), bf16_lo(q0[4 * k + 3]));
+      qa[2 * k + 1][1] = pack_f16x2(bf16_lo(q1[4 * k + 1]), bf16_lo(q1[4 * k + 3]));
+      qa[2 * k + 1][2] = pack_f16x2(bf16_hi(q0[4 * k + 1]), bf16_hi(q0[4 * k + 3]));
+      qa[2 * k + 1][3] = pack_f16x2(bf16_hi(q1[4 * k + 1]), bf16_hi(q1[4 * k + 3]));
+    }
+  }
+  float qs0 = 0.0f, qs1 = 0.0f;  // sum of each row's f16 query (INT4 zero term)
+  if (KK == OASIS_KV_INT4) {
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks) {
+      const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&qa[ks][0]));
+      const float2 a2 = __half22float2(*reinterpret_cast<const __half2*>(&qa[ks][2]));
+      const float2 bq = __half22float2(*reinterpret_cast<const __half2*>(&qa[ks][1]));
+      const float2 b2 = __half22float2(*reinterpret_cast<const __half2*>(&qa[ks][3]));
+      qs0 += (a.x + a.y) + (a2.x + a2.y);
+      qs1 += (bq.x + bq.y) + (b2.x + b2.y);
+    }
+    qs0 += __shfl_xor_sync(0xffffffffu, qs0, 1);
+    qs0 += __shfl_xor_sync(0xffffffffu, qs0, 2);
+    qs1 += __shfl_xor_sync(0xffffffffu, qs1, 1);
+    qs1 += __shfl_xor_sync(0xffffffffu, qs1, 2);
+  }
+
+  // ---- scores: s[nt][e] row g, s[nt][2 + e] row g + 8, key 8nt + 2c + e
+  float s[4][4];
+#pragma unroll
+  for (int nt = 0; nt < 4; ++nt) {
+    s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.0f;
+    uint32_t kb[4][2];
+    key_fragments<KK, KW>(kr[nt], KK, kb);
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks)
+      mma_16816<KK == OASIS_KV_BF16>(s[nt], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], kb[ks][0], kb[ks][1]);
+  }
+  const int qp0 = q_pos0 + 16 * mt + g, qp1 = qp0 + 8;  // window positions of the two rows
+  float mx0 = -1e30f, mx1 = -1e30f;  // finite floor: a fully masked row gives 0, not NaN
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int nt = i >> 1, e = i & 1, j = 8 * nt + 2 * c + e;
+    float a = s[nt][e], bb = s[nt][2 + e];
+    if (KK != OASIS_KV_BF16) {
+      const float mul = __shfl_sync(0xffffffffu, kscale.x, j);
+      if (KK == OASIS_KV_INT4) {
+        const float off = __shfl_sync(0xffffffffu, kscale.y, j);
+        a = __fmaf_rn(a, mul, off * qs0);
+        bb = __fmaf_rn(bb, mul, off * qs1);
+      } else {
+        a *= mul;
+        bb *= mul;
+      }
+    }
+    s[nt][e] = (j < n_past && j <= qp0) ? a : -INFINITY;
+    s[nt][2 + e] = (j < n_past && j <= qp1) ? bb : -INFINITY;
+    mx0 = fmaxf(mx0, s[nt][e]);
+    mx1 = fmaxf(mx1, s[nt][2 + e]);
+  }
+  mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+  mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+  mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+  mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+  const float o0 = mx0 * scale_log2, o1 = mx1 * scale_log2;
+  float sum0 = 0.0f, sum1 = 0.0f;
+  float vmax = 1.0f, inv_vmax = 1.0f;
+  if (VK != OASIS_KV_BF16) {
+    vmax = vscale.x;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, o));
+    vmax = fmaxf(vmax, 1e-30f);
+    inv_vmax = 1.0f / vmax;
+  }
+  const float vmul = vscale.x * inv_vmax;  // slot `lane`'s value multiplier over the max
+  float corr0 = 0.0f, corr1 = 0.0f;
+  uint32_t pa[2][4];  // P' as the A operand of P V, k-step kv: keys 16kv..16kv+15
+#pragma unroll
+  for (int nt = 0; nt < 4; ++nt) {
+    float pr[4];
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      pr[e] = exp2f(__fmaf_rn(s[nt][e], scale_log2, -o0));
+      pr[2 + e] = exp2f(__fmaf_rn(s[nt][2 + e], scale_log2, -o1));
+      sum0 += pr[e];
+      sum1 += pr[2 + e];
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) pr[e] = bf16_round(pr[e]);  // P as the tensor-core path rounds it
+    if (VK != OASIS_KV_BF16) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int j = 8 * nt + 2 * c + e;
+        const float m = __shfl_sync(0xffffffffu, vmul, j);
+        if (VK == OASIS_KV_INT4) {
+          const float z = __shfl_sync(0xffffffffu, vscale.y, j);
+          corr0 = __fmaf_rn(pr[e], z, corr0);
+          corr1 = __fmaf_rn(pr[2 + e], z, corr1);
+        }
+        pr[e] *= m;
+        pr[2 + e] *= m;
+      }
+      pa[nt >> 1][2 * (nt & 1)] = pack_f16x2(pr[0], pr[1]);
+      pa[nt >> 1][2 * (nt & 1) + 1] = pack_f16x2(pr[2], pr[3]);
+    } else {
+      pa[nt >> 1][2 * (nt & 1)] = pack_bf16x2(pr[0], pr[1]);
+      pa[nt >> 1][2 * (nt & 1) + 1] = pack_bf16x2(pr[2], pr[3]);
+    }
+  }
+  sum0 += __shfl_xor_sync(0xffffffffu, sum0, 1);
+  sum0 += __shfl_xor_sync(0xffffffffu, sum0, 2);
+  sum1 += __shfl_xor_sync(0xffffffffu, sum1, 1);
+  sum1 += __shfl_xor_sync(0xffffffffu, sum1, 2);
+  if (VK == OASIS_KV_INT4) {
+    corr0 += __shfl_xor_sync(0xffffffffu, corr0, 1);
+    corr0 += __shfl_xor_sync(0xffffffffu, corr0, 2);
+    corr1 += __shfl_xor_sync(0xffffffffu, corr1, 1);
+    corr1 += __shfl_xor_sync(0xffffffffu, corr1, 2);
+  }
+
+  // ---- O = P' V: n-tile n column 2c / 2c + 1 are dims 16c + n / 16c + 8 + n
+  float o[8][4];
+#pragma unroll
+  for (int n = 0; n < 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.0f;
+#pragma unroll
+  for (int kv2 = 0; kv2 < 2; ++kv2) {
+    uint32_t F[2][8];
+#pragma unroll
+    for (int pr = 0; pr < 2; ++pr)
+      value_fragments<VK, VW>(vr[4 * kv2 + 2 * pr], vr[4 * kv2 + 2 * pr + 1], VK, VK, F[pr]);
+#pragma unroll
+    for (int n = 0; n < 8; ++n)
+      mma_16816<VK == OASIS_KV_BF16>(o[n], pa[kv2][0], pa[kv2][1], pa[kv2][2], pa[kv2][3], F[0][n], F[1][n]);
+  }
+  const float inv0 = 1.0f / sum0, inv1 = 1.0f / sum1;
+  const int t0 = 16 * mt + g, t1 = t0 + 8;
+#pragma unroll
+  for (int half = 0; half < 2; ++half) {
+    const int t = half ? t1 : t0;
+    if (t >= q_frames) continue;
+    const float inv = half ? inv1 : inv0, corr = half ? corr1 : corr0;
+    uint32_t w[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      // dims 16c + 2k, + 1: n-tiles 2k, 2k + 1 (mod 8) of column 2c (k < 4) or 2c + 1
+      const int n = (2 * k) & 7, col = k >> 2;
+      const float a0 = __fmaf_rn(vmax, o[n][2 * half + col], corr), a1 = __fmaf_rn(vmax, o[n + 1][2 * half + col], corr);
+      w[k] = pack_bf16x2(a0 * inv, a1 * inv);
+    }
+    uint4* dst = reinterpret_cast<uint4*>(out + (static_cast<long long>(b * q_frames + t) * OASIS_TOKENS + p) * OASIS_HIDDEN +
+                                          h * 64 + 16 * c);
+    dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+    dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+  }
+}
+
+using WindowKernel = void (*)(const __nv_bfloat16*, __nv_bfloat16*, const KvView, const WindowLayout, int, int,
+                              int, float);
+template <int KK>
+WindowKernel window_kernel_v(int vk) {
+  switch (vk) {
+    case OASIS_KV_FP8: return attn_window_cached_kernel<KK, OASIS_KV_FP8>;
+    case OASIS_KV_INT4: return attn_window_cached_kernel<KK, OASIS_KV_INT4>;
+  }
+  return attn_window_cached_kernel<KK, OASIS_KV_BF16>;
+}
+WindowKernel window_kernel(int kk, int vk) {
+  switch (kk) {
+    case OASIS_KV_FP8: return window_kernel_v<OASIS_KV_FP8>(vk);
+    case OASIS_KV_INT4: return window_kernel_v<OASIS_KV_INT4>(vk);
+  }
+  return window_kernel_v<OASIS_KV_BF16>(vk);
+}
+
+// ----------------------------------------------------------------------------------
 // host launchers
 // ----------------------------------------------------------------------------------
 constexpr float kScaleLog2 = 0.125f * 1.4426950408889634f;  // (1/sqrt(64)) * log2(e)
@@ -1410,6 +1719,40 @@ int launch_attn_temporal(const void* qkv, const KvView& kv, int layer, void* out
                                kv, lay, q_pos0, n_past, kScaleLog2);
     if (e != cudaSuccess) return cuda_status(e, "attn_decode_kernel");
     return OASIS_OK;
+  }
+  if (q_frames > 1 && n_past > 0 && n_kv == n_past) {
+    // several query frames, every key and value from cache slots: the register-fragment
+    // window kernel when each tensor's slots share one kind
+    int uniform[2] = {-1, -1};
+    for (int which = 0; which < 2; ++which) {
+      const KvTensor& t = kv.t[which];
+      uniform[which] = t.kind[0];
+      for (int s = 1; s < n_past; ++s)
+        if (t.kind[s] != uniform[which]) uniform[which] = -1;
+    }
+    if (uniform[0] >= 0 && uniform[1] >= 0) {
+      WindowLayout lay{};
+      lay.m_tiles = (q_frames + 15) / 16;
+      lay.items = batch * OASIS_TOKENS * OASIS_HEADS * lay.m_tiles;
+      for (int which = 0; which < 2; ++which) {
+        const KvTensor& t = kv.t[which];
+        DecodeTensor& d = lay.t[which];
+        const int n_kind[3] = {t.n_bf16, t.n_fp8, t.n_int4};
+        for (int k = 0; k < 3; ++k) {
+          d.session_pages[k] = static_cast<uint32_t>(kv.layers * n_kind[k]);
+          if (static_cast<unsigned long long>(kv.layers) * n_kind[k] * OASIS_TOKENS * dec_row_bytes(k) >= (1ull << 32))
+            return fail(OASIS_ERR_UNSUPPORTED, "attn_window_cached_kernel: one session's pool exceeds 4 GiB");
+        }
+        for (int s = 0; s < n_past; ++s)
+          d.slot_page[s] = static_cast<uint32_t>(layer * n_kind[uniform[which]] + t.index[s]);
+      }
+      const int ctas = (lay.items + kWcWarps - 1) / kWcWarps;
+      cudaError_t e = launch_pdl(window_kernel(uniform[0], uniform[1]), dim3(ctas), dim3(kWcWarps * 32), 0, stream,
+                                 static_cast<const __nv_bfloat16*>(qkv), static_cast<__nv_bfloat16*>(out), kv, lay,
+                                 q_frames, q_pos0, n_past, kScaleLog2);
+      if (e != cudaSuccess) return cuda_status(e, "attn_window_cached_kernel");
+      return OASIS_OK;
+    }
   }
   dim3 grid(OASIS_TOKENS, OASIS_HEADS / kTpWarps, batch);
   CUtensorMap tm{}, tm_out{};

@@ -225,6 +225,35 @@ def test_attn_temporal_full_from_quantized_cache(pkg, cuda, kind, T):
     assert rel_l2(out.float(), ref) < 1e-2
 
 
+@pytest.mark.parametrize("kinds,vkinds,q_frames,q_pos0", [
+    (["bf16"] * 16, ["bf16"] * 16, 16, 0),
+    (["fp8"] * 32, ["int4"] * 32, 8, 24),
+    (["int4"] * 32, ["bf16"] * 32, 20, 12),
+    (["int4"] * 16 + ["bf16"] * 16, ["int4"] * 16 + ["bf16"] * 16, 32, 0)])
+def test_attn_window_from_cache(pkg, cuda, kinds, vkinds, q_frames, q_pos0):
+    """Several query frames with every key and value from the cache: one kind per tensor runs
+    the register-fragment window kernel, mixed kinds the staging kernel; vs fp32 SDPA over
+    the dequantised cache, causal at window positions q_pos0.."""
+    B, P = 3, len(kinds)
+    past = _kv_rows(B, P, cuda, 400 + P)
+    cache = pkg.KVCacheB200(B, 1, kinds, device=cuda, value_kinds=vkinds)
+    cache.store(past, layer=0)
+    new = _qkv(B * q_frames, cuda, 401)
+    out = pkg.attn_temporal(new, batch=B, q_frames=q_frames, q_pos0=q_pos0, n_past=P, n_kv=P, cache=cache,
+                            layer=0)
+    k, v = cache.load(0)
+    kp = k.float().reshape(B, P, TOK, 16, 64).permute(0, 2, 3, 1, 4).reshape(B * TOK, 16, P, 64)
+    vp = v.float().reshape(B, P, TOK, 16, 64).permute(0, 2, 3, 1, 4).reshape(B * TOK, 16, P, 64)
+    q = new.float().reshape(B, q_frames, TOK, 3, 16, 64)[:, :, :, 0]
+    q = q.permute(0, 2, 3, 1, 4).reshape(B * TOK, 16, q_frames, 64)
+    pos_q = torch.arange(q_frames, device=cuda) + q_pos0
+    mask = torch.arange(P, device=cuda)[None, :] <= pos_q[:, None]
+    ref = torch.nn.functional.scaled_dot_product_attention(q, kp, vp, attn_mask=mask)
+    ref = ref.reshape(B, TOK, 16, q_frames, 64).permute(0, 3, 1, 2, 4).reshape(B * q_frames * TOK, HID)
+    torch.cuda.synchronize()
+    assert rel_l2(out.float(), ref) < 1e-2
+
+
 # keys and values in their own tiers (the reference's key/value asymmetry), one query frame
 @pytest.mark.parametrize("kinds,vkinds", [
     (["int4"] * 3 + ["fp8"] * 3 + ["bf16"] * 2, ["int4"] * 5 + ["fp8"] * 2 + ["bf16"]),
