@@ -1274,7 +1274,7 @@ DecodeKernel decode_kernel(int kk, int vk) {
 // temporal attention of several query frames whose keys and values all come from cache
 // slots of one kind per tensor (no live frames: the isolated sweep's case)
 // ----------------------------------------------------------------------------------
-// One warp per (session, token, head, 16-query tile).  The key and value fragments come
+// One warp per (session, token, head), its 16-query tiles in turn.  The key and value fragments come
 // straight from the cache into registers and are converted there, as in the one-query-frame
 // kernel (same fragment layouts and head-dim orders); the query tile is the A operand of the
 // scores, whose accumulators are the A operand of P V (no shuffle), and the softmax of the
@@ -1283,12 +1283,12 @@ constexpr int kWcWarps = 4;
 
 struct WindowLayout {
   DecodeTensor t[2];  // keys, values by slot
-  int items;          // batch * 144 tokens * 16 heads * m_tiles
-  int m_tiles;        // 16-row query tiles (1 or 2)
+  int items;          // batch * 144 tokens * 16 heads
+  int m_tiles;        // 16-row query tiles per item (1 or 2)
 };
 
 template <int KK, int VK>
-__global__ void __launch_bounds__(kWcWarps * 32, 4)
+__global__ void __launch_bounds__(kWcWarps * 32, 3)
     attn_window_cached_kernel(const __nv_bfloat16* __restrict__ qkv, __nv_bfloat16* __restrict__ out,
                               const __grid_constant__ KvView kv, const __grid_constant__ WindowLayout lay,
                               int q_frames, int q_pos0, int n_past, float scale_log2) {
@@ -1304,8 +1304,7 @@ __global__ void __launch_bounds__(kWcWarps * 32, 4)
   const DecodeTensor& dv = lay.t[1];
   pdl_wait();
   if (item >= lay.items) return;
-  const int mt = item % lay.m_tiles, rest = item / lay.m_tiles;
-  const int h = rest & 15, tok = rest >> 4;
+  const int h = item & 15, tok = item >> 4;
   const int p = tok % OASIS_TOKENS, b = tok / OASIS_TOKENS;
 
   // ---- loads: keys 8r + g (dims 16c..), values 16kv + 2c + {0,1,8,9} (dims 8g..), query rows
@@ -1351,6 +1350,9 @@ __global__ void __launch_bounds__(kWcWarps * 32, 4)
         }
       }
     }
+  }
+  // query rows t0 = 16 mt + g and t1 = t0 + 8 of query tile mt (zero past q_frames)
+  auto load_q = [&](int mt) {
     const int t0 = 16 * mt + g, t1 = t0 + 8;
 #pragma unroll
     for (int w = 0; w < 8; ++w) q0[w] = q1[w] = 0u;
@@ -1366,7 +1368,8 @@ __global__ void __launch_bounds__(kWcWarps * 32, 4)
       const uint4 x0 = src[0], x1 = src[1];
       q1[0] = x0.x; q1[1] = x0.y; q1[2] = x0.z; q1[3] = x0.w; q1[4] = x1.x; q1[5] = x1.y; q1[6] = x1.z; q1[7] = x1.w;
     }
-  }
+  };
+  load_q(0);
   // scales of slot `lane`
   const bool slot_live = lane < n_past;
   float2 kscale = make_float2(1.0f, 0.0f), vscale = make_float2(slot_live ? 1.0f : 0.0f, 0.0f);
@@ -1387,6 +1390,16 @@ __global__ void __launch_bounds__(kWcWarps * 32, 4)
     vscale = dec_scale(raw, VK, true);
   }
 
+  float vmax = 1.0f, inv_vmax = 1.0f;
+  if (VK != OASIS_KV_BF16) {
+    vmax = vscale.x;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, o));
+    vmax = fmaxf(vmax, 1e-30f);
+    inv_vmax = 1.0f / vmax;
+  }
+  const float vmul = vscale.x * inv_vmax;  // slot `lane`'s value multiplier over the max
+  for (int mt = 0; mt < lay.m_tiles; ++mt) {
   // ---- the query tile as A (rows g, g + 8), in the keys' head-dim order
   uint32_t qa[4][4];
   if (KK == OASIS_KV_BF16) {
@@ -1468,16 +1481,8 @@ __global__ void __launch_bounds__(kWcWarps * 32, 4)
   mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
   mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
   const float o0 = mx0 * scale_log2, o1 = mx1 * scale_log2;
+  if (mt + 1 < lay.m_tiles) load_q(mt + 1);  // the next tile's rows load under this tile's math
   float sum0 = 0.0f, sum1 = 0.0f;
-  float vmax = 1.0f, inv_vmax = 1.0f;
-  if (VK != OASIS_KV_BF16) {
-    vmax = vscale.x;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, o));
-    vmax = fmaxf(vmax, 1e-30f);
-    inv_vmax = 1.0f / vmax;
-  }
-  const float vmul = vscale.x * inv_vmax;  // slot `lane`'s value multiplier over the max
   float corr0 = 0.0f, corr1 = 0.0f;
   uint32_t pa[2][4];  // P' as the A operand of P V, k-step kv: keys 16kv..16kv+15
 #pragma unroll
@@ -1557,6 +1562,7 @@ __global__ void __launch_bounds__(kWcWarps * 32, 4)
     dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
     dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
   }
+  }  // query tiles
 }
 
 using WindowKernel = void (*)(const __nv_bfloat16*, __nv_bfloat16*, const KvView, const WindowLayout, int, int,
@@ -1733,7 +1739,7 @@ int launch_attn_temporal(const void* qkv, const KvView& kv, int layer, void* out
     if (uniform[0] >= 0 && uniform[1] >= 0) {
       WindowLayout lay{};
       lay.m_tiles = (q_frames + 15) / 16;
-      lay.items = batch * OASIS_TOKENS * OASIS_HEADS * lay.m_tiles;
+      lay.items = batch * OASIS_TOKENS * OASIS_HEADS;
       for (int which = 0; which < 2; ++which) {
         const KvTensor& t = kv.t[which];
         DecodeTensor& d = lay.t[which];
