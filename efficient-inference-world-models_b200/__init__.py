@@ -12,12 +12,13 @@ from .manager import KVCacheManagerB200, ProgressiveKVQuantizerB200, RollingKVCa
 from .oasis import (action_step_schedule, alphas_cumprod, generate, rollout_dpmpp,
                     sigmoid_beta_schedule, steps_for_action_magnitude)
 from .samplers import DPMSolverPPSampler, ddim_update, dpmpp2m_update
+from .vae import OasisVAEDecoderB200, random_vae_state_dict, vae_param_shapes
 from .weights import pack_weights, param_shapes, random_state_dict, rope_tables
 
 __all__ = [
-    "OasisDiTB200", "KVCacheB200", "KVCacheManagerB200", "ProgressiveKVQuantizerB200",
+    "OasisDiTB200", "OasisVAEDecoderB200", "KVCacheB200", "KVCacheManagerB200", "ProgressiveKVQuantizerB200",
     "RollingKVCacheB200",
     "DPMSolverPPSampler", "OasisError", "action_step_schedule", "alphas_cumprod", "attn_spatial", "attn_temporal",
     "ddim_update", "dpmpp2m_update", "generate", "lib", "pack_weights", "param_shapes",
-    "random_state_dict", "rollout_dpmpp", "rope_tables", "sigmoid_beta_schedule", "steps_for_action_magnitude", "version",
+    "random_state_dict", "random_vae_state_dict", "rollout_dpmpp", "rope_tables", "sigmoid_beta_schedule", "steps_for_action_magnitude", "vae_param_shapes", "version",
 ]

@@ -66,6 +66,24 @@ class KvCache(Structure):
 
 KV_KEYS, KV_VALUES = 1, 2
 
+VAE_MAX_DEPTH = 12
+VAE_PRED_LD = 1216
+
+
+class VaeBlock(Structure):
+    """``oasis_vae_block_t``: one pre-norm block of the latent decoder."""
+    _fields_ = [("ln1_shift", c_void_p), ("ln1_scale", c_void_p), ("qkv_w", c_void_p),
+                ("proj_w", c_void_p), ("proj_b", c_void_p), ("ln2_shift", c_void_p),
+                ("ln2_scale", c_void_p), ("fc1_w", c_void_p), ("fc1_b", c_void_p),
+                ("fc2_w", c_void_p), ("fc2_b", c_void_p)]
+
+
+class VaeWeights(Structure):
+    """``oasis_vae_weights_t``."""
+    _fields_ = [("depth", c_int), ("post_w", c_void_p), ("post_b", c_void_p),
+                ("blk", VaeBlock * VAE_MAX_DEPTH), ("norm_shift", c_void_p), ("norm_scale", c_void_p),
+                ("pred_w", c_void_p), ("pred_b", c_void_p), ("rope", c_void_p), ("ones", c_void_p)]
+
 
 # name -> (restype, argtypes); every symbol include/oasis_b200.h declares
 SIGNATURES = {
@@ -98,6 +116,10 @@ SIGNATURES = {
                                      c_longlong, c_float, c_float, c_int, c_void_p]),
     "oasis_ab_update": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_longlong,
                                 c_float, c_float, c_float, c_float, c_void_p]),
+    "oasis_vae_workspace_size": (c_size_t, [c_int, c_int]),
+    "oasis_vae_plan_create": (c_int, [POINTER(VaeWeights), c_int, c_void_p, c_size_t, POINTER(c_void_p)]),
+    "oasis_vae_plan_destroy": (None, [c_void_p]),
+    "oasis_vae_decode": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p]),
 }
 
 _LIB = None

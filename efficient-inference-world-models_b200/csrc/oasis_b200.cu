@@ -6,4 +6,5 @@
 #include "kv.cu"
 #include "elementwise.cu"
 #include "forward.cu"
+#include "vae.cu"
 #include "noalloc.cu"

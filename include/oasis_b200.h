@@ -284,6 +284,57 @@ int oasis_ab_update(const float* x, const float* d0, const float* d1, const floa
                     float* out, long long n, float h, float c0, float c1, float c2,
                     cudaStream_t stream);
 
+/* ------------------------------------------------------------------ VAE decode */
+/* The latent decoder behind `vae.decode(z)` of the Oasis rollout
+ * (worldserve/models/oasis.py:237-245): z (frames, 576, 16) fp32 latents (already divided
+ * by the VAE scale) -> RGB (frames, 3, 360, 640) fp32 in [-1, 1].  The decoder is a ViT of
+ * width 1024 (16 heads x 64) over the 18 x 32 token grid, patch 20: Linear(16 -> 1024),
+ * `depth` pre-norm blocks (affine LayerNorm eps 1e-6; bias-free QKV with axial RoPE;
+ * non-causal attention; output projection; MLP 1024 -> 4096 -> 1024, GELU(tanh)), a final
+ * affine LayerNorm and Linear(1024 -> 20*20*3) unpatchified to pixels (upstream open-oasis
+ * vae.py is not in the reference tree; these are the restated choices). */
+#define OASIS_VAE_MAX_DEPTH 12
+#define OASIS_VAE_PRED_LD 1216 /* predictor rows: 1200 padded to a multiple of 64       */
+
+typedef struct {
+  /* LayerNorms as (1 + scale) * x_hat + shift: shift = bias, scale = weight - 1      */
+  const float* ln1_shift; const float* ln1_scale;   /* fp32 [1024] each                */
+  const void*  qkv_w;     /* bf16 [3072][1024] (no bias)                             */
+  const void*  proj_w;    /* bf16 [1024][1024]                                       */
+  const float* proj_b;    /* fp32 [1024]                                             */
+  const float* ln2_shift; const float* ln2_scale;
+  const void*  fc1_w;     /* bf16 [4096][1024]                                       */
+  const float* fc1_b;     /* fp32 [4096]                                             */
+  const void*  fc2_w;     /* bf16 [1024][4096]                                       */
+  const float* fc2_b;     /* fp32 [1024]                                             */
+} oasis_vae_block_t;
+
+typedef struct {
+  int depth;              /* decoder blocks (12)                                     */
+  const void*  post_w;    /* bf16 [1024][64]: Linear(16 -> 1024) weight, K zero-padded */
+  const float* post_b;    /* fp32 [1024]                                             */
+  oasis_vae_block_t blk[OASIS_VAE_MAX_DEPTH];
+  const float* norm_shift; const float* norm_scale; /* final LayerNorm              */
+  const void*  pred_w;    /* bf16 [1216][1024]: Linear(1024 -> 1200), rows 1200.. zero;
+                             output column (p*20 + q)*3 + c                          */
+  const float* pred_b;    /* fp32 [1216]                                             */
+  const float* rope;      /* fp32 [576][32][2] (cos, sin): pairs 0..15 H axis, 16..31 W */
+  const float* ones;      /* fp32 [1024] of 1.0 (the residual gate of the epilogue)  */
+} oasis_vae_weights_t;
+
+typedef struct oasis_vae_plan oasis_vae_plan_t;
+
+/* Workspace bytes of a decode of `frames` frames (0 on invalid arguments). */
+size_t oasis_vae_workspace_size(int frames, int depth);
+/* Plan for `frames` frames over caller-owned weights and workspace (encodes tensor maps
+ * on the host; allocates no device memory). */
+int oasis_vae_plan_create(const oasis_vae_weights_t* w, int frames, void* workspace,
+                          size_t workspace_bytes, oasis_vae_plan_t** out);
+void oasis_vae_plan_destroy(oasis_vae_plan_t* plan);
+/* Decode: z fp32 [frames][576][16] -> out fp32 [frames][3][360][640] (16-byte aligned).
+ * Enqueues on `stream`, allocates nothing; one decode per plan at a time. */
+int oasis_vae_decode(oasis_vae_plan_t* plan, const float* z, float* out, cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

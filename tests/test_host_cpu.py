@@ -146,3 +146,16 @@ def test_action_step_schedule_buckets(pkg):
     a[0, 3, 23:] = -0.2        # camera only, idle (L1 = 0.4)
     a[1] = 9.0                 # other sessions do not change the schedule
     assert pkg.action_step_schedule(a) == [2, 3, 5, 2]
+
+
+def test_vae_oracle_shapes_and_names(pkg):
+    """The package's decoder parameters are the oracle's, and the oracle decodes
+    (frames, 576, 16) latents into (frames, 3, 360, 640) frames."""
+    from oracle import vae_ref
+    sd = pkg.random_vae_state_dict(seed=0, depth=1)
+    assert {k: tuple(v.shape) for k, v in sd.items()} == vae_ref.param_shapes(1)
+    assert torch.allclose(pkg.vae.vae_rope_table(), vae_ref.rope_table())
+    out = vae_ref.decode(sd, torch.randn(2, 576, 16), depth=1)
+    assert out.shape == (2, 3, 360, 640) and torch.isfinite(out).all()
+    assert pkg.lib().oasis_vae_workspace_size(1, 12) > 0
+    assert pkg.lib().oasis_vae_workspace_size(1, 13) == 0
