@@ -540,8 +540,10 @@ def run_ours(args, rank, world, local_rank):
     kv, sweep, lib = {}, [], None
     if rank == 0 and not args.skip_kv:
         kv = kv_configs(pkg, model, dev, g, peaks)
+    vae = {}
     if rank == 0 and not args.skip_sweep:
         sweep = attention_sweep(pkg, dev, peaks.get("hbm_gbs", 6650.0), reps=10)
+        vae = vae_decode_bench(pkg, dev, peaks)
     if rank == 0 and world == 1 and not args.skip_cpu:
         lib = library_bar(dev, model)
 
@@ -591,6 +593,7 @@ def run_ours(args, rank, world, local_rank):
             "library_bar": lib,
             "kv_configs": kv,
             "attention_sweep": sweep,
+            "vae_decode": vae,
         }
         print(json.dumps(line), flush=True)
     graphs.clear()
@@ -661,6 +664,36 @@ def kv_configs(pkg, model, dev, g, peaks):
             del gr, cache
         except Exception as e:
             out[name] = {"error": str(e)[:200]}
+    return out
+
+
+def vae_decode_bench(pkg, dev, peaks, reps=10):
+    """Latent decoder (`vae.decode`): the newest frame of a session (1 frame) and a whole
+    32-frame window, frames/s with the tensor roofline of its projections + attention."""
+    out = {}
+    try:
+        dec = pkg.OasisVAEDecoderB200.random(seed=0, depth=12, device=dev)
+        tpk = peaks.get("bf16_tflops_sustained", 1400.0)
+        for F in (1, 32):
+            z = torch.randn(F, 576, 16, device=dev, generator=torch.Generator(device=dev).manual_seed(F))
+            o = torch.empty(F, 3, 360, 640, device=dev)
+            for _ in range(3):
+                dec.decode(z, out=o)
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(reps):
+                dec.decode(z, out=o)
+            e1.record()
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1) / reps
+            flop = F * 576 * 12 * 2 * (12 * 1024 * 1024) + F * 12 * 16 * 4 * 576 * 576 * 64
+            out[f"frames_{F}"] = {"frames_per_s": F / (ms / 1e3), "ms": ms, "tflops": flop / ms / 1e9,
+                                  "frac_tensor": flop / ms / 1e9 / tpk}
+        del dec
+        torch.cuda.empty_cache()
+    except Exception as e:  # an extra line, never required
+        out = {"error": str(e)[:200]}
     return out
 
 
