@@ -1287,6 +1287,25 @@ struct WindowLayout {
   int m_tiles;        // 16-row query tiles per item (1 or 2)
 };
 
+// Loads of cached key / value chunks that stay in registers for every query tile: volatile,
+// so the compiler keeps the values rather than issuing the load again for a later tile.
+__device__ __forceinline__ uint4 ldg_keep_v4(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
+  return r;
+}
+__device__ __forceinline__ uint2 ldg_keep_v2(const void* p) {
+  uint2 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];" : "=r"(r.x), "=r"(r.y) : "l"(p));
+  return r;
+}
+__device__ __forceinline__ uint32_t ldg_keep_u32(const void* p) {
+  uint32_t r;
+  asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(r) : "l"(p));
+  return r;
+}
+
 template <int KK, int VK>
 __global__ void __launch_bounds__(kWcWarps * 32, 3)
     attn_window_cached_kernel(const __nv_bfloat16* __restrict__ qkv, __nv_bfloat16* __restrict__ out,
@@ -1319,13 +1338,13 @@ __global__ void __launch_bounds__(kWcWarps * 32, 3)
       if (j < n_past) {
         const uint8_t* src = kb + dk.slot_page[j] * (OASIS_TOKENS * dec_row_bytes(KK)) + c * (dec_head_bytes(KK) / 4);
         if (KK == OASIS_KV_INT4) {
-          const uint2 x = *reinterpret_cast<const uint2*>(src);
+          const uint2 x = ldg_keep_v2(src);
           kr[r][0] = x.x;
           kr[r][KW > 1 ? 1 : 0] = x.y;
         } else {
 #pragma unroll
           for (int w4 = 0; w4 < KW / 4; ++w4) {
-            const uint4 x = __ldg(reinterpret_cast<const uint4*>(src) + w4);
+            const uint4 x = ldg_keep_v4(src + 16 * w4);
             kr[r][4 * w4] = x.x; kr[r][4 * w4 + 1] = x.y; kr[r][4 * w4 + 2] = x.z; kr[r][4 * w4 + 3] = x.w;
           }
         }
@@ -1340,13 +1359,13 @@ __global__ void __launch_bounds__(kWcWarps * 32, 3)
       if (j < n_past) {
         const uint8_t* src = vb + dv.slot_page[j] * (OASIS_TOKENS * dec_row_bytes(VK)) + g * (dec_head_bytes(VK) / 8);
         if (VW == 4) {
-          const uint4 x = __ldg(reinterpret_cast<const uint4*>(src));
+          const uint4 x = ldg_keep_v4(src);
           vr[q][0] = x.x; vr[q][VW > 1 ? 1 : 0] = x.y; vr[q][VW > 2 ? 2 : 0] = x.z; vr[q][VW > 3 ? 3 : 0] = x.w;
         } else if (VW == 2) {
-          const uint2 x = __ldg(reinterpret_cast<const uint2*>(src));
+          const uint2 x = ldg_keep_v2(src);
           vr[q][0] = x.x; vr[q][VW > 1 ? 1 : 0] = x.y;
         } else {
-          vr[q][0] = __ldg(reinterpret_cast<const uint32_t*>(src));
+          vr[q][0] = ldg_keep_u32(src);
         }
       }
     }
