@@ -703,6 +703,13 @@ __device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
   asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(h) : "f"(hi), "f"(lo));
   return h;
 }
+// 2^x by the SFU (ex2.approx; 2^-inf = +0, results below the normal range flush to 0: the
+// probabilities they would give are far below a bf16 ulp of the row sum)
+__device__ __forceinline__ float ex2_ftz(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 __device__ __forceinline__ uint32_t sub_1024(uint32_t biased) {
   uint32_t h;
   asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(h) : "r"(biased), "r"(0x64006400u));
@@ -1151,17 +1158,18 @@ __global__ void __launch_bounds__(kDecThreads, dec_min_ctas(KK, VK))
     }
     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-    const float mxs = mx * scale_log2;
+    // a finite floor: masked scores (-inf) then give 2^-inf = 0 with no select
+    const float mxs = fmaxf(mx, -1e30f) * scale_log2;
     float sum = 0.0f;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      const float pr = sc[i] == -INFINITY ? 0.0f : exp2f(__fmaf_rn(sc[i], scale_log2, -mxs));
+      const float pr = ex2_ftz(__fmaf_rn(sc[i], scale_log2, -mxs));
       sum += pr;
       sc[i] = bf16_round(pr);  // the probability as the tensor-core path rounds it
     }
     sum += __shfl_xor_sync(0xffffffffu, sum, 1);
     sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-    const float p_live = live_key ? exp2f(__fmaf_rn(s_live, scale_log2, -mxs)) : 0.0f;
+    const float p_live = ex2_ftz(__fmaf_rn(s_live, scale_log2, -mxs));  // 0 without the live key
     sum += p_live;
     const float pb_live = bf16_round(p_live);
 
@@ -1509,8 +1517,8 @@ __global__ void __launch_bounds__(kWcWarps * 32, 3)
     float pr[4];
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
-      pr[e] = exp2f(__fmaf_rn(s[nt][e], scale_log2, -o0));
-      pr[2 + e] = exp2f(__fmaf_rn(s[nt][2 + e], scale_log2, -o1));
+      pr[e] = ex2_ftz(__fmaf_rn(s[nt][e], scale_log2, -o0));
+      pr[2 + e] = ex2_ftz(__fmaf_rn(s[nt][2 + e], scale_log2, -o1));
       sum0 += pr[e];
       sum1 += pr[2 + e];
     }
