@@ -1128,16 +1128,18 @@ __global__ void __launch_bounds__(kDecThreads, dec_min_ctas(KK, VK))
       s_live = d;
     }
 
-    // ---- cached scores
+    // ---- cached scores (n-tiles without a cached key are skipped: the warp agrees)
     float sacc[4][4];
 #pragma unroll
     for (int nt = 0; nt < 4; ++nt) {
       sacc[nt][0] = sacc[nt][1] = sacc[nt][2] = sacc[nt][3] = 0.0f;
-      uint32_t kb[4][2];
-      key_fragments<KK, KW>(kr[nt], kkind(nt), kb);
+      if ((lay.valid >> (8 * nt)) & 0xFFu) {
+        uint32_t kb[4][2];
+        key_fragments<KK, KW>(kr[nt], kkind(nt), kb);
 #pragma unroll
-      for (int ks = 0; ks < 4; ++ks)
-        mma_16816<KK == OASIS_KV_BF16>(sacc[nt], qa[ks][0], 0u, qa[ks][1], 0u, kb[ks][0], kb[ks][1]);
+        for (int ks = 0; ks < 4; ++ks)
+          mma_16816<KK == OASIS_KV_BF16>(sacc[nt], qa[ks][0], 0u, qa[ks][1], 0u, kb[ks][0], kb[ks][1]);
+      }
     }
     const float2 kscale = KK == OASIS_KV_BF16 ? make_float2(1.0f, 0.0f) : dec_scale(ks_raw, ks_kind, slot_live);
     if (nx < lay.items) load_keys(nx);  // the next item's keys, query, key scales
@@ -1217,6 +1219,7 @@ __global__ void __launch_bounds__(kDecThreads, dec_min_ctas(KK, VK))
     for (int mo = 0; mo < 4; ++mo) oacc[mo][0] = oacc[mo][1] = oacc[mo][2] = oacc[mo][3] = 0.0f;
 #pragma unroll
     for (int kv2 = 0; kv2 < 2; ++kv2) {
+      if (!((lay.valid >> (16 * kv2)) & 0xFFFFu)) continue;  // no cached key in these 16
       uint32_t F[2][8];
 #pragma unroll
       for (int pr = 0; pr < 2; ++pr)
@@ -1470,16 +1473,21 @@ __global__ void __launch_bounds__(kWcWarps * 32, 3)
     qs1 += __shfl_xor_sync(0xffffffffu, qs1, 2);
   }
 
-  // ---- scores: s[nt][e] row g, s[nt][2 + e] row g + 8, key 8nt + 2c + e
+  // ---- scores: s[nt][e] row g, s[nt][2 + e] row g + 8, key 8nt + 2c + e.  Keys from
+  // `vis` on are masked for every row of the tile (past the cache or the tile's last
+  // window position): their n-tiles and P V k-steps are skipped (the warp agrees).
+  const int vis = min(n_past, q_pos0 + 16 * mt + 16);
   float s[4][4];
 #pragma unroll
   for (int nt = 0; nt < 4; ++nt) {
     s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.0f;
-    uint32_t kb[4][2];
-    key_fragments<KK, KW>(kr[nt], KK, kb);
+    if (8 * nt < vis) {
+      uint32_t kb[4][2];
+      key_fragments<KK, KW>(kr[nt], KK, kb);
 #pragma unroll
-    for (int ks = 0; ks < 4; ++ks)
-      mma_16816<KK == OASIS_KV_BF16>(s[nt], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], kb[ks][0], kb[ks][1]);
+      for (int ks = 0; ks < 4; ++ks)
+        mma_16816<KK == OASIS_KV_BF16>(s[nt], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], kb[ks][0], kb[ks][1]);
+    }
   }
   const int qp0 = q_pos0 + 16 * mt + g, qp1 = qp0 + 8;  // window positions of the two rows
   float mx0 = -1e30f, mx1 = -1e30f;  // finite floor: a fully masked row gives 0, not NaN
@@ -1561,6 +1569,7 @@ __global__ void __launch_bounds__(kWcWarps * 32, 3)
   for (int n = 0; n < 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.0f;
 #pragma unroll
   for (int kv2 = 0; kv2 < 2; ++kv2) {
+    if (16 * kv2 >= vis) continue;  // every probability of these keys is 0
     uint32_t F[2][8];
 #pragma unroll
     for (int pr = 0; pr < 2; ++pr)

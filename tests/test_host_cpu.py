@@ -159,3 +159,20 @@ def test_vae_oracle_shapes_and_names(pkg):
     assert out.shape == (2, 3, 360, 640) and torch.isfinite(out).all()
     assert pkg.lib().oasis_vae_workspace_size(1, 12) > 0
     assert pkg.lib().oasis_vae_workspace_size(1, 13) == 0
+
+
+def test_vae_invalid_arguments_are_reported_not_fatal(pkg):
+    L = pkg.lib()
+    h = ctypes.c_void_p()
+    assert L.oasis_vae_plan_create(None, 1, None, 0, ctypes.byref(h)) == 1
+    w = pkg._native.VaeWeights()
+    w.depth = 12
+    assert L.oasis_vae_plan_create(ctypes.byref(w), 0, ctypes.c_void_p(256), 1 << 30, ctypes.byref(h)) == 1
+    assert b"frames" in L.oasis_last_error()
+    w.depth = 13
+    assert L.oasis_vae_plan_create(ctypes.byref(w), 1, ctypes.c_void_p(256), 1 << 30, ctypes.byref(h)) == 1
+    w.depth = 12
+    need = L.oasis_vae_workspace_size(1, 12)
+    assert L.oasis_vae_plan_create(ctypes.byref(w), 1, ctypes.c_void_p(256), need - 1, ctypes.byref(h)) == 3
+    assert L.oasis_vae_decode(None, ctypes.c_void_p(16), ctypes.c_void_p(16), None) == 1
+    assert not h.value  # no plan was handed out
