@@ -1317,8 +1317,10 @@ __device__ __forceinline__ uint32_t ldg_keep_u32(const void* p) {
   return r;
 }
 
-template <int KK, int VK>
-__global__ void __launch_bounds__(kWcWarps * 32, 3)
+// MT: query tiles per warp (1: windows of up to 16 query frames, sized for four CTAs per
+// SM; 2: the second tile's rows load under the first tile's math, three CTAs per SM)
+template <int KK, int VK, int MT>
+__global__ void __launch_bounds__(kWcWarps * 32, MT == 1 ? 4 : 3)
     attn_window_cached_kernel(const __nv_bfloat16* __restrict__ qkv, __nv_bfloat16* __restrict__ out,
                               const __grid_constant__ KvView kv, const __grid_constant__ WindowLayout lay,
                               int q_frames, int q_pos0, int n_past, float scale_log2) {
@@ -1429,7 +1431,7 @@ __global__ void __launch_bounds__(kWcWarps * 32, 3)
     inv_vmax = 1.0f / vmax;
   }
   const float vmul = vscale.x * inv_vmax;  // slot `lane`'s value multiplier over the max
-  for (int mt = 0; mt < lay.m_tiles; ++mt) {
+  for (int mt = 0; mt < (MT == 1 ? 1 : lay.m_tiles); ++mt) {
   // ---- the query tile as A (rows g, g + 8), in the keys' head-dim order
   uint32_t qa[4][4];
   if (KK == OASIS_KV_BF16) {
@@ -1516,7 +1518,7 @@ __global__ void __launch_bounds__(kWcWarps * 32, 3)
   mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
   mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
   const float o0 = mx0 * scale_log2, o1 = mx1 * scale_log2;
-  if (mt + 1 < lay.m_tiles) load_q(mt + 1);  // the next tile's rows load under this tile's math
+  if (MT > 1 && mt + 1 < lay.m_tiles) load_q(mt + 1);  // the next tile's rows load under this tile's math
   float sum0 = 0.0f, sum1 = 0.0f;
   float corr0 = 0.0f, corr1 = 0.0f;
   uint32_t pa[2][4];  // P' as the A operand of P V, k-step kv: keys 16kv..16kv+15
@@ -1603,20 +1605,24 @@ __global__ void __launch_bounds__(kWcWarps * 32, 3)
 
 using WindowKernel = void (*)(const __nv_bfloat16*, __nv_bfloat16*, const KvView, const WindowLayout, int, int,
                               int, float);
-template <int KK>
+template <int KK, int MT>
 WindowKernel window_kernel_v(int vk) {
   switch (vk) {
-    case OASIS_KV_FP8: return attn_window_cached_kernel<KK, OASIS_KV_FP8>;
-    case OASIS_KV_INT4: return attn_window_cached_kernel<KK, OASIS_KV_INT4>;
+    case OASIS_KV_FP8: return attn_window_cached_kernel<KK, OASIS_KV_FP8, MT>;
+    case OASIS_KV_INT4: return attn_window_cached_kernel<KK, OASIS_KV_INT4, MT>;
   }
-  return attn_window_cached_kernel<KK, OASIS_KV_BF16>;
+  return attn_window_cached_kernel<KK, OASIS_KV_BF16, MT>;
 }
-WindowKernel window_kernel(int kk, int vk) {
+template <int MT>
+WindowKernel window_kernel_m(int kk, int vk) {
   switch (kk) {
-    case OASIS_KV_FP8: return window_kernel_v<OASIS_KV_FP8>(vk);
-    case OASIS_KV_INT4: return window_kernel_v<OASIS_KV_INT4>(vk);
+    case OASIS_KV_FP8: return window_kernel_v<OASIS_KV_FP8, MT>(vk);
+    case OASIS_KV_INT4: return window_kernel_v<OASIS_KV_INT4, MT>(vk);
   }
-  return window_kernel_v<OASIS_KV_BF16>(vk);
+  return window_kernel_v<OASIS_KV_BF16, MT>(vk);
+}
+WindowKernel window_kernel(int kk, int vk, int m_tiles) {
+  return m_tiles == 1 ? window_kernel_m<1>(kk, vk) : window_kernel_m<2>(kk, vk);
 }
 
 // ----------------------------------------------------------------------------------
@@ -1789,7 +1795,7 @@ int launch_attn_temporal(const void* qkv, const KvView& kv, int layer, void* out
           d.slot_page[s] = static_cast<uint32_t>(layer * n_kind[uniform[which]] + t.index[s]);
       }
       const int ctas = (lay.items + kWcWarps - 1) / kWcWarps;
-      cudaError_t e = launch_pdl(window_kernel(uniform[0], uniform[1]), dim3(ctas), dim3(kWcWarps * 32), 0, stream,
+      cudaError_t e = launch_pdl(window_kernel(uniform[0], uniform[1], lay.m_tiles), dim3(ctas), dim3(kWcWarps * 32), 0, stream,
                                  static_cast<const __nv_bfloat16*>(qkv), static_cast<__nv_bfloat16*>(out), kv, lay,
                                  q_frames, q_pos0, n_past, kScaleLog2);
       if (e != cudaSuccess) return cuda_status(e, "attn_window_cached_kernel");
