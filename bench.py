@@ -816,6 +816,15 @@ def run_isolated(args, local_rank):
         print(json.dumps({"case": f"gemm M={M} N={N} K={K}", "ms": ms, "tflops": tf,
                           "frac_burst": tf / peaks.get("bf16_tflops", 1590.0)}), flush=True)
         return 0
+    if args.isolated == "vae":
+        # the latent decoder (12 blocks, random init) on `--batch` frames, eager launches
+        dec = pkg.OasisVAEDecoderB200.random(seed=0, depth=12, device=dev)
+        F = args.batch
+        z = torch.randn(F, 576, 16, device=dev, generator=g)
+        o = torch.empty(F, 3, 360, 640, device=dev)
+        ms = timeit(lambda: dec.decode(z, out=o), args.steps)
+        print(json.dumps({"case": f"vae decode frames={F}", "ms": ms, "frames_per_s": F / (ms / 1e3)}), flush=True)
+        return 0
     if args.isolated == "cached":
         # prefill of a B-session window into a cache of one kind, then `steps` incremental
         # forwards of the newest frame over the 31 cached frames (eager launches)
@@ -851,9 +860,9 @@ def main():
     ap.add_argument("--skip-kv", action="store_true")
     ap.add_argument("--skip-sweep", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=12.0)
-    ap.add_argument("--isolated", choices=["attention", "gemm", "cached"], default=None)
+    ap.add_argument("--isolated", choices=["attention", "gemm", "cached", "vae"], default=None)
     ap.add_argument("--case", default=None, help="--isolated attention: cases whose name contains this")
-    ap.add_argument("--batch", type=int, default=8, help="--isolated cached: sessions")
+    ap.add_argument("--batch", type=int, default=8, help="--isolated cached: sessions; --isolated vae: frames")
     ap.add_argument("--kv", default="fp8", choices=["bf16", "fp8", "int4", "progressive"],
                     help="--isolated cached: cache kind (progressive: 23 INT4 + 8 bf16 frames)")
     ap.add_argument("--M", type=int, default=36864)
