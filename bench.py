@@ -149,6 +149,84 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(mhz)}
 
 
+class NvmlClockSampler:
+    """Clocks during the timed region from NVML, polled every `period_s` by a thread of
+    this process (read-only queries: the SM clock, its maximum, power and the active
+    clock-event reasons).  It starts without the ~0.1 s start-up of an nvidia-smi
+    process, so a timed region of 20 steps (~90 ms) still gets tens of samples; samples
+    outside [mark_begin(), mark_end()] are dropped."""
+
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"),
+               ("hw_power_brake", "nvmlClocksEventReasonHwPowerBrakeSlowdown"))
+
+    def __init__(self, uuid, period_s=0.002):
+        import pynvml
+        self.nv = pynvml
+        pynvml.nvmlInit()
+        self.h = pynvml.nvmlDeviceGetHandleByUUID(uuid)
+        self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM))
+        self.period = period_s
+        self.samples = []
+        self.t0 = self.t1 = None
+        self.stop_flag = threading.Event()
+
+    def start(self):
+        self.thread = threading.Thread(target=self._run, daemon=True)
+        self.thread.start()
+
+    def _run(self):
+        nv = self.nv
+        get_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            nv.nvmlDeviceGetCurrentClocksThrottleReasons
+        while not self.stop_flag.is_set():
+            try:
+                t = time.perf_counter()
+                mhz = float(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+                watts = nv.nvmlDeviceGetPowerUsage(self.h) / 1000.0
+                bits = int(get_reasons(self.h))
+                self.samples.append((t, mhz, watts, bits))
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def mark_begin(self):
+        self.t0 = time.perf_counter()
+
+    def mark_end(self):
+        self.t1 = time.perf_counter()
+
+    def stop(self):
+        self.stop_flag.set()
+        self.thread.join(timeout=2)
+        inside = [x for x in self.samples if self.t0 is not None and self.t0 <= x[0] <= (self.t1 or x[0])]
+        reasons = set()
+        for _, _, _, bits in inside:
+            for name, const in self.REASONS:
+                if bits & getattr(self.nv, const, 0):
+                    reasons.add(name)
+        mhz = [x[1] for x in inside]
+        watts = [x[2] for x in inside]
+        try:
+            self.nv.nvmlShutdown()
+        except Exception:
+            pass
+        return {"sm_mhz": statistics.median(mhz) if mhz else None, "sm_max_mhz": self.max_mhz,
+                "power_w": statistics.median(watts) if watts else None,
+                "reasons": sorted(reasons), "samples": len(mhz), "source": "nvml",
+                "sm_mhz_min": min(mhz) if mhz else None}
+
+
+def clock_sampler(uuid):
+    """The NVML sampler where NVML answers, else the nvidia-smi one."""
+    try:
+        return NvmlClockSampler(uuid)
+    except Exception:
+        return ClockSampler(uuid)
+
+
 # ------------------------------------------------------------------------------ CPU baseline
 def cpu_model() -> str:
     try:
@@ -454,15 +532,19 @@ def run_ours(args, rank, world, local_rank):
         uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
     except Exception:
         pass
-    clocks = ClockSampler(uuid)
+    clocks = clock_sampler(uuid)
     clocks.start()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
+    if hasattr(clocks, "mark_begin"):
+        clocks.mark_begin()
     e0.record()
     for s in range(args.steps):
         run_step(s)
     e1.record()
     barrier()
+    if hasattr(clocks, "mark_end"):
+        clocks.mark_end()
     clk = clocks.stop()
     per_rank_ms = e0.elapsed_time(e1)
     ms_max = max_over_ranks(per_rank_ms, dist, dev)

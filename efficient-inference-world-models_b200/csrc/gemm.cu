@@ -310,11 +310,15 @@ void choose_tiles(int M, int N, int K, bool allow_split, int* bn, int* ctas, int
   const long long sms = num_sms();
   const int pairs = max_pairs<256, kEpiGateResid>();
   *splits = 1;
-  if (N % 256 == 0) {
-    // CTA pairs on 256 x 256 tiles (the chained launch's tiles) unless they run in fewer
-    // than four waves, the last of them under 45 % full: each SM stages half the B rows,
-    // so a pair tile costs the SM less operand traffic than any single-CTA tile, and from
-    // four waves on a partly filled last wave costs less than leaving the pairs
+  if (N % 256 == 0 && M >= 32 * kGemmBM) {
+    // CTA pairs on 256 x 256 tiles (the chained launch's tiles) from 4,096 rows on, unless
+    // they run in fewer than four waves, the last of them under 45 % full: each SM stages
+    // half the B rows, so a pair tile costs the SM less operand traffic than any
+    // single-CTA tile, and from four waves on a partly filled last wave costs less than
+    // leaving the pairs.  Below 4,096 rows (the incremental forward of 8-16 sessions:
+    // 1,152 and 2,304 rows) single CTAs measured faster in the whole forward (2.59 vs
+    // 2.64 ms at 8 sessions, 4.67 vs 4.83 ms at 16): there each projection is about one
+    // wave, and a 128-row tile keeps every SM busy where 256-row pair tiles leave half
     const long long pair_m = (M + 2 * kGemmBM - 1) / (2 * kGemmBM);
     const long long units = pair_m * (N / 256);
     const long long waves = (units + pairs - 1) / pairs;

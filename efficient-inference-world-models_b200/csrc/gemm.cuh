@@ -1048,8 +1048,9 @@ struct GemmOperands {
 };
 int make_gemm_operands(GemmOperands* g, const void* A, long long lda, const void* B, long long ldb,
                        int M, int N, int K, int bn, int ctas = 1);
-// Tile shape for an M x N x K projection on this GPU: CTA pairs on 256 x 256 tiles unless
-// they take fewer than four waves with the last under 45 % full; otherwise single CTAs
+// Tile shape for an M x N x K projection on this GPU: CTA pairs on 256 x 256 tiles from
+// 4,096 rows on, unless they take fewer than four waves with the last under 45 % full;
+// otherwise single CTAs
 // with the (tile N, K splits) of least estimated time (K splits only where allow_split:
 // the residual epilogue, whose reduce-add is linear in the accumulator).
 void choose_tiles(int M, int N, int K, bool allow_split, int* bn, int* ctas, int* splits);

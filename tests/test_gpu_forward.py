@@ -45,9 +45,13 @@ def rel_l2(a, b):
 # 32-frame window).  (2, 1, 32), (2, 1, 29), (2, 2, 17) and (2, 2, 32) run the
 # projections on CTA pairs as one chained launch per sub-block; 2 x 17 x 144 rows leave
 # the last pair tile ragged, and 29 x 144 rows (an odd frame count) leave a 32-row
-# quarter half past the end and a CTA of the last pair with no rows at all.
+# quarter half past the end and a CTA of the last pair with no rows at all.  (2, 1, 8),
+# (2, 1, 9), (2, 3, 5) and (2, 2, 8) (1,152 to 2,304 rows, the incremental forward's
+# sizes) run single-CTA projections with K-split residual GEMMs; 9 and 15 frames leave the
+# last 128-row block with 16 and 112 rows.
 @pytest.mark.parametrize("depth,B,T", [(16, 1, 4), (16, 1, 32), (2, 2, 3), (2, 1, 32), (2, 1, 29),
-                                       (1, 3, 1), (2, 2, 17), (2, 2, 32)])
+                                       (1, 3, 1), (2, 2, 17), (2, 2, 32), (2, 1, 8), (2, 1, 9),
+                                       (2, 3, 5), (2, 2, 8)])
 def test_forward_matches_oracle(pkg, cuda, depth, B, T):
     sd = state(pkg, depth)
     model = pkg.OasisDiTB200.from_state_dict(sd, device=cuda, depth=depth)

@@ -24,12 +24,14 @@ def rel_l2(a, b):
 
 # ----------------------------------------------------------------- GEMM (tcgen05)
 
-# (4608, 1024, 1024), (4500, 3072, 1024) and (1800, 4096, 256) run on CTA pairs (256-row
-# tiles); in the last two the final tile is ragged, in (1800, ...) the second CTA of the
-# last pair holds no valid row at all.
+# (4608, 1024, 1024), (4500, 3072, 1024) and (4196, 4096, 256) run on CTA pairs (256-row
+# tiles, from 4,096 rows on); in the last two the final tile is ragged, in (4196, ...) the
+# second CTA of the last pair holds no valid row at all.  (1800, 4096, 256) and
+# (2304, 1024, 4096) are single-CTA shapes of the incremental forward's size.
 @pytest.mark.parametrize("M,N,K", [(128, 256, 64), (200, 512, 1024), (576, 3072, 1024),
                                    (1000, 64, 4096), (4608, 1024, 1024), (130, 192, 128),
-                                   (4500, 3072, 1024), (1800, 4096, 256)])
+                                   (4500, 3072, 1024), (4196, 4096, 256), (1800, 4096, 256),
+                                   (2304, 1024, 4096)])
 def test_gemm_bf16_store(pkg, cuda, M, N, K):
     g = torch.Generator(device=cuda).manual_seed(M + N + K)
     A = torch.randn(M, K, device=cuda, generator=g).bfloat16()
@@ -43,7 +45,7 @@ def test_gemm_bf16_store(pkg, cuda, M, N, K):
     assert rel_l2(D.float(), ref) < 4e-3  # bf16 output rounding
 
 
-@pytest.mark.parametrize("M,N,K", [(256, 256, 256), (333, 128, 512), (1800, 4096, 256)])
+@pytest.mark.parametrize("M,N,K", [(256, 256, 256), (333, 128, 512), (1800, 4096, 256), (4196, 4096, 256)])
 def test_gemm_f32_bias(pkg, cuda, M, N, K):
     g = torch.Generator(device=cuda).manual_seed(7)
     A = torch.randn(M, K, device=cuda, generator=g).bfloat16()
