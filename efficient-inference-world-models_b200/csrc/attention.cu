@@ -619,7 +619,7 @@ __global__ void __launch_bounds__(kTpWarps * 32)
 // to the fp32 scores (s_j = scale_j q.c_j + zero_j sum(q)) and to the probabilities
 // (p'_j = p_j scale_j / max scale, plus sum_j p_j zero_j).  The frame's own key and value
 // (bf16 rows of the QKV output) are one more key on the CUDA cores.
-constexpr int kDecWarps = 8;
+constexpr int kDecWarps = 4;
 constexpr int kDecThreads = kDecWarps * 32;
 // Kinds of the decode kernel's template: one storage kind for every cached slot of a
 // tensor, or kDecMixed (per-slot kinds from the layout).
@@ -902,10 +902,14 @@ __device__ __forceinline__ float2 dec_scale(uint32_t raw, int kind, bool live) {
   return make_float2(1.0f, 0.0f);
 }
 
-// CTAs per SM the register budget is sized for: two for one storage kind per tensor;
-// mixed tensors keep their row kinds and three row pointers live, and take the registers
-// of one CTA (no spills) rather than spill inside the item loop
-__host__ __device__ constexpr int dec_min_ctas(int kk, int vk) { return kk == kDecMixed || vk == kDecMixed ? 1 : 2; }
+// CTAs (of 4 warps) per SM the register budget is sized for: four (128 registers) for one
+// storage kind per tensor; three (170) for two kind-uniform runs, which at 128 registers
+// spilled inside the item loop (163 without: 4.40 against 4.66 ms for the incremental
+// forward of 16 sessions over 23 INT4 + 8 bf16 frames); mixed tensors keep their row kinds
+// and three row pointers live and take two (255)
+__host__ __device__ constexpr int dec_min_ctas(int kk, int vk) {
+  return kk == kDecMixed || vk == kDecMixed ? 2 : (kk >= kDecSplit ? 3 : 4);
+}
 // storage kind of key position j under template kind code `code`
 __device__ __forceinline__ int dec_position_kind(int code, const DecodeTensor& d, int split, int j) {
   if (code == kDecMixed) return static_cast<int>((d.kinds >> (2 * j)) & 3ull);
