@@ -1254,6 +1254,369 @@ __global__ void __launch_bounds__(kDecThreads, dec_min_ctas(KK, VK))
   }
 }
 
+// ----------------------------------------------------------------------------------
+// one query frame over INT4 cached frames (all of them, or all but a first n-tile of bf16
+// frames): one warp per (session, token, 8 heads)
+// ----------------------------------------------------------------------------------
+// The per-head kernel above leaves 15 of the 16 rows of its score tile empty and runs the
+// softmax, the scale shuffles and the output on 4 of its 32 lanes; with INT4 codes that
+// scalar work, not HBM, sets its speed.  Here a warp takes 8 heads of a token at once.
+// Head hh's query is row hh of the A operand (the lanes of row group g = hh supply it,
+// every other row is zero) and its keys are the B columns, so the scores of all 8 heads
+// accumulate in one tile, row g holding head 8 hg + g; every lane quad then takes the
+// softmax, the scale folding and the live key of its own head.  P V runs per head as in
+// the per-head kernel (V^T the A operand, column 0 of B the head's P' row, fetched from
+// its lane quad by shuffle).  Fragment layouts, head-dim orders and the fp32 arithmetic
+// of each head are those of attn_decode_kernel, so both give the same bits.  Heads go in
+// pairs, the next head's rows loading while the current head's are used.
+// Layouts: kDhgInt4 - every position INT4 (keys and values); kDhgBf16Int4 - key positions
+// 0..7 bf16 (the newest frames of a progressive cache, placed first by the host), 8..31
+// INT4, the same for the values.  (With FP8 codes the per-head kernel is faster: there
+// the loads, not the instructions, bound it, and its per-head items keep more of them in
+// flight.)
+constexpr int kDhgWarps = 4;
+constexpr int kDhgThreads = kDhgWarps * 32;
+constexpr int kDhgInt4 = 0;
+constexpr int kDhgBf16Int4 = 1;
+
+template <int LAYOUT>
+__global__ void __launch_bounds__(kDhgThreads, 3)
+    attn_decode_hg_kernel(const __nv_bfloat16* __restrict__ qkv, __nv_bfloat16* __restrict__ out,
+                          const __grid_constant__ KvView kv, const __grid_constant__ DecodeLayout lay,
+                          int q_pos, int n_past, float scale_log2) {
+  pdl_trigger();
+  constexpr bool SPLIT = LAYOUT == kDhgBf16Int4;
+  constexpr int K0 = SPLIT ? OASIS_KV_BF16 : OASIS_KV_INT4;  // kind of n-tile 0 (positions 0..7)
+  constexpr int KW = 2, VW = 1;                              // INT4 words per key / value chunk
+  constexpr int K0W = SPLIT ? 8 : KW, V0W = SPLIT ? 4 : VW;  // the same for n-tile 0
+  constexpr uint32_t RB = dec_row_bytes(OASIS_KV_INT4), HB = dec_head_bytes(OASIS_KV_INT4);
+  constexpr uint32_t RB0 = dec_row_bytes(K0), HB0 = dec_head_bytes(K0);
+  const int lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
+  const KvTensor& tk = kv.t[0];
+  const KvTensor& tv = kv.t[1];
+  const DecodeTensor& dk = lay.t[0];
+  const DecodeTensor& dv = lay.t[1];
+  const uint8_t* kpool0 = SPLIT ? reinterpret_cast<const uint8_t*>(tk.bf16) : tk.int4;
+  const uint8_t* vpool0 = SPLIT ? reinterpret_cast<const uint8_t*>(tv.bf16) : tv.int4;
+
+  // This lane's rows (as attn_decode_kernel): key rows nt = 0..3 are key 8 nt + g, dims
+  // 16c..16c+15; value rows q = 0..7 are key 16 (q >> 2) + 2c + 8 ((q >> 1) & 1) + (q & 1),
+  // dims 8g..8g+7 (rows 0 and 1 lie in n-tile 0); score i is position 8 (i >> 1) + 2c +
+  // (i & 1) (scores 0 and 1 in n-tile 0).  Their slot offsets are read from the parameter
+  // space where they are used.
+  auto koff = [&](int nt) {
+    return nt == 0 ? dk.slot_page[g] * (OASIS_TOKENS * RB0) + c * (HB0 / 4)
+                   : dk.slot_page[8 * nt + g] * (OASIS_TOKENS * RB) + c * (HB / 4);
+  };
+  auto vpos = [&](int q) { return 16 * (q >> 2) + 2 * c + 8 * ((q >> 1) & 1) + (q & 1); };
+  auto voff = [&](int q) {
+    return q < 2 ? dv.slot_page[vpos(q)] * (OASIS_TOKENS * RB0) + g * (HB0 / 8)
+                 : dv.slot_page[vpos(q)] * (OASIS_TOKENS * RB) + g * (HB / 8);
+  };
+  auto spos = [&](int i) { return 8 * (i >> 1) + 2 * c + (i & 1); };
+  uint32_t smask = 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) smask |= ((lay.valid >> spos(i)) & 1u) << i;
+  const bool live_key = lay.live_kv && n_past <= q_pos;
+  const int items = lay.items;  // batch * 144 tokens * 2 head groups
+  const int warps_total = gridDim.x * kDhgWarps;
+  int it = blockIdx.x * kDhgWarps + (threadIdx.x >> 5);
+  pdl_wait();
+  if (it >= items) return;
+
+  struct KHead {  // one head's key words of this lane: n-tile 0, n-tiles 1..3
+    uint32_t n0[K0W];
+    uint32_t n[3][KW];
+  };
+  struct VHead {  // one head's value words of this lane: rows 0, 1 (n-tile 0), rows 2..7
+    uint32_t r0[2][V0W];
+    uint32_t r[6][VW];
+    uint32_t own[4];  // lanes c == 0: the frame's own value, dims 8g..8g+7
+  };
+  auto item_tok = [](int item) { return item >> 1; };
+  auto item_h0 = [](int item) { return 8 * (item & 1); };
+  // head h0's rows of the item's (session, token) in a pool of row bytes `rb`
+  auto row_base = [&](const uint8_t* pool, uint32_t pages, uint32_t rb, uint32_t hb, int item) {
+    const int tok = item_tok(item), p = tok % OASIS_TOKENS, b = tok / OASIS_TOKENS;
+    return pool + (static_cast<long long>(b) * pages * OASIS_TOKENS + p) * rb + item_h0(item) * hb;
+  };
+  auto load_k = [&](int item, int hh, KHead& k) {
+    const uint8_t* b0 = row_base(kpool0, dk.session_pages[K0], RB0, HB0, item) + hh * HB0;
+    const uint8_t* b = row_base(tk.int4, dk.session_pages[OASIS_KV_INT4], RB, HB, item) + hh * HB;
+#pragma unroll
+    for (int w = 0; w < K0W; ++w) k.n0[w] = 0u;
+    if ((lay.valid >> g) & 1u) {
+      const uint8_t* src = b0 + koff(0);
+      if constexpr (SPLIT) {
+        const uint4 x0 = ldg_stream_v4(src), x1 = ldg_stream_v4(src + 16);
+        k.n0[0] = x0.x; k.n0[1] = x0.y; k.n0[2] = x0.z; k.n0[3] = x0.w;
+        k.n0[4] = x1.x; k.n0[5] = x1.y; k.n0[6] = x1.z; k.n0[7] = x1.w;
+      } else {
+        const uint2 x = ldg_stream_v2(src);
+        k.n0[0] = x.x;
+        k.n0[1] = x.y;
+      }
+    }
+#pragma unroll
+    for (int nt = 1; nt < 4; ++nt) {
+      k.n[nt - 1][0] = k.n[nt - 1][1] = 0u;
+      if ((lay.valid >> (8 * nt + g)) & 1u) {
+        const uint2 x = ldg_stream_v2(b + koff(nt));
+        k.n[nt - 1][0] = x.x;
+        k.n[nt - 1][1] = x.y;
+      }
+    }
+  };
+  auto load_v = [&](int item, int hh, VHead& v) {
+    const uint8_t* b0 = row_base(vpool0, dv.session_pages[K0], RB0, HB0, item) + hh * HB0;
+    const uint8_t* b = row_base(tv.int4, dv.session_pages[OASIS_KV_INT4], RB, HB, item) + hh * HB;
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+#pragma unroll
+      for (int w = 0; w < V0W; ++w) v.r0[q][w] = 0u;
+      if ((lay.valid >> vpos(q)) & 1u) {
+        const uint8_t* src = b0 + voff(q);
+        if constexpr (SPLIT) {
+          const uint4 x = ldg_stream_v4(src);
+          v.r0[q][0] = x.x; v.r0[q][1] = x.y; v.r0[q][2] = x.z; v.r0[q][3] = x.w;
+        } else {
+          v.r0[q][0] = ldg_stream_u32(src);
+        }
+      }
+    }
+#pragma unroll
+    for (int q = 2; q < 8; ++q) {
+      v.r[q - 2][0] = 0u;
+      if ((lay.valid >> vpos(q)) & 1u) v.r[q - 2][0] = ldg_stream_u32(b + voff(q));
+    }
+    v.own[0] = v.own[1] = v.own[2] = v.own[3] = 0u;
+    if (c == 0 && live_key) {
+      const uint4 x = ldg_v4(qkv + static_cast<long long>(item_tok(item)) * kQkvLd + 2 * OASIS_HIDDEN +
+                             (item_h0(item) + hh) * 64 + 8 * g);
+      v.own[0] = x.x; v.own[1] = x.y; v.own[2] = x.z; v.own[3] = x.w;
+    }
+  };
+  // scale (| zero << 16) of score position i for the row head of an item: INT4 per
+  // (page, token, head); bf16 positions carry none
+  auto load_scales = [&](const KvTensor& t, const DecodeTensor& d, int item, uint32_t (&dst)[8]) {
+    const int tok = item_tok(item), p = tok % OASIS_TOKENS, b = tok / OASIS_TOKENS;
+    const long long e0 = dec_item_scale(d, OASIS_KV_INT4, b, p, item_h0(item) + g);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      dst[i] = 0u;
+      if ((!SPLIT || i >= 2) && ((smask >> i) & 1u)) {
+        const uint32_t so = dec_slot_scale(OASIS_KV_INT4, d.slot_page[spos(i)]);
+        dst[i] = ldg_u16(t.i4_scale + e0 + so) | (ldg_u16(t.i4_zero + e0 + so) << 16);
+      }
+    }
+  };
+  auto scale_of = [&](uint32_t raw, int i, bool live) {
+    return SPLIT && i < 2 ? dec_scale(raw, OASIS_KV_BF16, live) : dec_scale(raw, OASIS_KV_INT4, live);
+  };
+  // the row head's query (dims 16c..16c+15) and own key
+  uint32_t qraw[8], klraw[8], ksr[8], vsr[8];
+  auto load_q = [&](int item) {
+    const int tok = item_tok(item);
+    const __nv_bfloat16* row = qkv + static_cast<long long>(tok) * kQkvLd + (item_h0(item) + g) * 64 + 16 * c;
+    const uint4 a = ldg_v4(row), a1 = ldg_v4(row + 8);
+    qraw[0] = a.x; qraw[1] = a.y; qraw[2] = a.z; qraw[3] = a.w;
+    qraw[4] = a1.x; qraw[5] = a1.y; qraw[6] = a1.z; qraw[7] = a1.w;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) klraw[w] = 0u;
+    if (live_key) {
+      const uint4 k0 = ldg_v4(row + OASIS_HIDDEN), k1 = ldg_v4(row + OASIS_HIDDEN + 8);
+      klraw[0] = k0.x; klraw[1] = k0.y; klraw[2] = k0.z; klraw[3] = k0.w;
+      klraw[4] = k1.x; klraw[5] = k1.y; klraw[6] = k1.z; klraw[7] = k1.w;
+    }
+    load_scales(tk, dk, item, ksr);
+  };
+
+  KHead kh[2];
+  VHead vh[2];
+  load_q(it);
+  load_k(it, 0, kh[0]);
+  for (; it < items; it += warps_total) {
+    const int nx = it + warps_total;
+    const int tok = item_tok(it), h0 = item_h0(it);
+
+    // ---- the row head's query as A fragments (row g) in the nibble dim order
+    uint32_t qa[4][2];
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      qa[2 * k][0] = pack_f16x2(bf16_lo(qraw[4 * k]), bf16_lo(qraw[4 * k + 2]));
+      qa[2 * k][1] = pack_f16x2(bf16_hi(qraw[4 * k]), bf16_hi(qraw[4 * k + 2]));
+      qa[2 * k + 1][0] = pack_f16x2(bf16_lo(qraw[4 * k + 1]), bf16_lo(qraw[4 * k + 3]));
+      qa[2 * k + 1][1] = pack_f16x2(bf16_hi(qraw[4 * k + 1]), bf16_hi(qraw[4 * k + 3]));
+    }
+    float qsum = 0.0f;
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks) {
+      const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&qa[ks][0]));
+      const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&qa[ks][1]));
+      qsum += (f0.x + f0.y) + (f1.x + f1.y);
+    }
+    qsum += __shfl_xor_sync(0xffffffffu, qsum, 1);
+    qsum += __shfl_xor_sync(0xffffffffu, qsum, 2);
+    float s_live = -INFINITY;
+    if (live_key) {
+      float d = 0.0f;
+#pragma unroll
+      for (int w = 0; w < 8; ++w)
+        d = __fmaf_rn(bf16_hi(qraw[w]), bf16_hi(klraw[w]), __fmaf_rn(bf16_lo(qraw[w]), bf16_lo(klraw[w]), d));
+      d += __shfl_xor_sync(0xffffffffu, d, 1);
+      d += __shfl_xor_sync(0xffffffffu, d, 2);
+      s_live = d;
+    }
+
+    // ---- scores of the 8 heads in one tile: head hh's MMAs carry row hh of A only
+    float sacc[4][4];
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) sacc[nt][0] = sacc[nt][1] = sacc[nt][2] = sacc[nt][3] = 0.0f;
+    auto score_head = [&](int hh, const KHead& k) {
+      const bool mine = g == hh;
+      uint32_t a0[4], a2[4];
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks) {
+        a0[ks] = mine ? qa[ks][0] : 0u;
+        a2[ks] = mine ? qa[ks][1] : 0u;
+      }
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) {
+        if ((lay.valid >> (8 * nt)) & 0xFFu) {
+          uint32_t kbf[4][2];
+          if (nt == 0)
+            key_fragments<SPLIT ? kDecMixed : OASIS_KV_INT4, K0W>(k.n0, K0, kbf);
+          else
+            key_fragments<OASIS_KV_INT4, KW>(k.n[nt - 1], OASIS_KV_INT4, kbf);
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks)
+            mma_16816<false>(sacc[nt], a0[ks], 0u, a2[ks], 0u, kbf[ks][0], kbf[ks][1]);
+        }
+      }
+    };
+#pragma unroll 1
+    for (int hp = 0; hp < 8; hp += 2) {
+      load_k(it, hp + 1, kh[1]);
+      score_head(hp, kh[0]);
+      if (hp < 6) load_k(it, hp + 2, kh[0]);
+      score_head(hp + 1, kh[1]);
+    }
+    // the first head's values and the value scales load while the softmax runs
+    load_v(it, 0, vh[0]);
+    load_scales(tv, dv, it, vsr);
+
+    // ---- softmax of row g (head h0 + g) over the cached keys and the live key
+    float sc[8];
+    float mx = s_live;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float2 ks = scale_of(ksr[i], i, true);
+      const float sv = __fmaf_rn(sacc[i >> 1][i & 1], ks.x, ks.y * qsum);
+      sc[i] = (smask >> i) & 1u ? sv : -INFINITY;
+      mx = fmaxf(mx, sc[i]);
+    }
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    const float mxs = fmaxf(mx, -1e30f) * scale_log2;
+    float sum = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float pr = ex2_ftz(__fmaf_rn(sc[i], scale_log2, -mxs));
+      sum += pr;
+      sc[i] = bf16_round(pr);
+    }
+    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+    const float p_live = ex2_ftz(__fmaf_rn(s_live, scale_log2, -mxs));
+    sum += p_live;
+    const float pb_live = bf16_round(p_live);
+
+    // ---- P' = p * value multiplier / the row's largest multiplier, and sum p * zero
+    float vmax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) vmax = fmaxf(vmax, scale_of(vsr[i], i, (smask >> i) & 1u).x);
+    vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 1));
+    vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 2));
+    vmax = fmaxf(vmax, 1e-30f);
+    const float inv_vmax = 1.0f / vmax;
+    float corr = 0.0f;
+    uint32_t pbk[2][2];
+    {
+      float pv[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float2 vs = scale_of(vsr[i], i, (smask >> i) & 1u);
+        pv[i] = sc[i] * vs.x * inv_vmax;
+        corr = __fmaf_rn(sc[i], vs.y, corr);
+      }
+#pragma unroll
+      for (int kv2 = 0; kv2 < 2; ++kv2) {
+        pbk[kv2][0] = pack_f16x2(pv[4 * kv2], pv[4 * kv2 + 1]);
+        pbk[kv2][1] = pack_f16x2(pv[4 * kv2 + 2], pv[4 * kv2 + 3]);
+      }
+    }
+    corr += __shfl_xor_sync(0xffffffffu, corr, 1);
+    corr += __shfl_xor_sync(0xffffffffu, corr, 2);
+    const float inv = 1.0f / sum;
+
+    // ---- per head: O^T = V^T P'^T, then the live value, the multipliers and 1 / sum
+    auto pv_head = [&](int hh, const VHead& v) {
+      // column 0 of B: head hh's P' row from its lane quad (lanes 4 hh + c); the other
+      // columns (lanes g > 0) give output columns that are not read
+      uint32_t pb[2][2];
+#pragma unroll
+      for (int kv2 = 0; kv2 < 2; ++kv2) {
+        pb[kv2][0] = __shfl_sync(0xffffffffu, pbk[kv2][0], 4 * hh + c);
+        pb[kv2][1] = __shfl_sync(0xffffffffu, pbk[kv2][1], 4 * hh + c);
+      }
+      float oacc[4][4];
+#pragma unroll
+      for (int mo = 0; mo < 4; ++mo) oacc[mo][0] = oacc[mo][1] = oacc[mo][2] = oacc[mo][3] = 0.0f;
+#pragma unroll
+      for (int kv2 = 0; kv2 < 2; ++kv2) {
+        if (!((lay.valid >> (16 * kv2)) & 0xFFFFu)) continue;
+        uint32_t F[2][8];
+        if (kv2 == 0)  // rows 0, 1: n-tile 0; rows 2, 3: n-tile 1
+          value_fragments<SPLIT ? kDecMixed : OASIS_KV_INT4, V0W>(v.r0[0], v.r0[1], K0, K0, F[0]);
+        else
+          value_fragments<OASIS_KV_INT4, VW>(v.r[2], v.r[3], OASIS_KV_INT4, OASIS_KV_INT4, F[0]);
+        value_fragments<OASIS_KV_INT4, VW>(v.r[4 * kv2], v.r[4 * kv2 + 1], OASIS_KV_INT4, OASIS_KV_INT4, F[1]);
+#pragma unroll
+        for (int mo = 0; mo < 4; ++mo)
+          mma_16816<false>(oacc[mo], F[0][2 * mo], F[0][2 * mo + 1], F[1][2 * mo], F[1][2 * mo + 1], pb[kv2][0],
+                           pb[kv2][1]);
+      }
+      const float inv_h = __shfl_sync(0xffffffffu, inv, 4 * hh);
+      const float corr_h = __shfl_sync(0xffffffffu, corr, 4 * hh);
+      const float vmax_h = __shfl_sync(0xffffffffu, vmax, 4 * hh);
+      const float pl_h = __shfl_sync(0xffffffffu, pb_live, 4 * hh);
+      if (c == 0) {
+        uint32_t o[4];
+#pragma unroll
+        for (int mo = 0; mo < 4; ++mo) {
+          const float a0 = __fmaf_rn(vmax_h, oacc[mo][0], corr_h), a1 = __fmaf_rn(vmax_h, oacc[mo][2], corr_h);
+          o[mo] = pack_bf16x2(__fmaf_rn(pl_h, bf16_lo(v.own[mo]), a0) * inv_h,
+                              __fmaf_rn(pl_h, bf16_hi(v.own[mo]), a1) * inv_h);
+        }
+        *reinterpret_cast<uint4*>(out + static_cast<long long>(tok) * OASIS_HIDDEN + (h0 + hh) * 64 + 8 * g) =
+            make_uint4(o[0], o[1], o[2], o[3]);
+      }
+    };
+#pragma unroll 1
+    for (int hp = 0; hp < 8; hp += 2) {
+      load_v(it, hp + 1, vh[1]);
+      pv_head(hp, vh[0]);
+      if (hp < 6) {
+        load_v(it, hp + 2, vh[0]);
+      } else if (nx < items) {
+        load_q(nx);           // the next item's query, own key and key scales
+        load_k(nx, 0, kh[0]);  // and its first head's keys
+      }
+      pv_head(hp + 1, vh[1]);
+    }
+  }
+}
+
 // decode kernel for (key kind, value kind), each a storage kind or kDecMixed
 using DecodeKernel = void (*)(const __nv_bfloat16*, __nv_bfloat16*, const KvView, const DecodeLayout, int, int,
                               float);
@@ -1758,15 +2121,23 @@ int launch_attn_temporal(const void* qkv, const KvView& kv, int layer, void* out
         if (pos_slot[j] >= 0) d.slot_page[j] = static_cast<uint32_t>(layer * n_kind[pos_kind[which][j]] + t.index[pos_slot[j]]);
       }
     }
-    DecodeKernel kern = decode_kernel(uniform[0], uniform[1]);
+    // keys and values all INT4, or bf16 in n-tile 0 and INT4 after it: 8 heads per warp
+    const bool hg_int4 = uniform[0] == OASIS_KV_INT4 && uniform[1] == OASIS_KV_INT4;
+    const bool hg_split = uniform[0] == dec_split_code(OASIS_KV_BF16, OASIS_KV_INT4) && uniform[1] == uniform[0] &&
+                          lay.split == 8;
+    const bool hg = hg_int4 || hg_split;
+    DecodeKernel kern = !hg ? decode_kernel(uniform[0], uniform[1])
+                            : (hg_int4 ? attn_decode_hg_kernel<kDhgInt4> : attn_decode_hg_kernel<kDhgBf16Int4>);
+    const int threads = hg ? kDhgThreads : kDecThreads;
+    const int warps = hg ? kDhgWarps : kDecWarps;
+    if (hg) lay.items = batch * OASIS_TOKENS * (OASIS_HEADS / 8);
     int per_sm = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kDecThreads, 0) != cudaSuccess ||
-        per_sm < 1) {
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, 0) != cudaSuccess || per_sm < 1) {
       cudaGetLastError();
       per_sm = 1;
     }
-    const int ctas = std::min((lay.items + kDecWarps - 1) / kDecWarps, per_sm * num_sms());
-    cudaError_t e = launch_pdl(kern, dim3(ctas), dim3(kDecThreads), 0, stream,
+    const int ctas = std::min((lay.items + warps - 1) / warps, per_sm * num_sms());
+    cudaError_t e = launch_pdl(kern, dim3(ctas), dim3(threads), 0, stream,
                                static_cast<const __nv_bfloat16*>(qkv), static_cast<__nv_bfloat16*>(out),
                                kv, lay, q_pos0, n_past, kScaleLog2);
     if (e != cudaSuccess) return cuda_status(e, "attn_decode_kernel");

@@ -401,7 +401,11 @@ __device__ __forceinline__ bool ln_rows_phase(const EpiParams& ep, int M, unsign
   const int R = ((M + static_cast<int>(gridDim.x) - 1) / static_cast<int>(gridDim.x) + 3) & ~3;
   const int r_begin = static_cast<int>(blockIdx.x) * R;
   const int r_end = min(M, r_begin + R);
-  for (int row0 = r_begin + w * kLnRowsPerWarp; row0 < r_end; row0 += kEpiWarps * kLnRowsPerWarp) {
+  // rows per group: 4 where every warp gets at least one group of 4, else 2 or 1, so
+  // that all eight warps share a short row range (8 rows at 1,152 rows over 144 CTAs);
+  // groups of 1, 2 or 4 tile R (a multiple of 4) and never cross a frame or a block
+  const int gr = R >= kEpiWarps * kLnRowsPerWarp ? kLnRowsPerWarp : (R >= 2 * kEpiWarps ? 2 : 1);
+  for (int row0 = r_begin + w * gr; row0 < r_end; row0 += kEpiWarps * gr) {
     // the frame's shift/scale (written by an earlier kernel) load while the rows finish
     const long long f = row0 / OASIS_TOKENS;
     float4 a4[8], s4[8];
@@ -410,7 +414,7 @@ __device__ __forceinline__ bool ln_rows_phase(const EpiParams& ep, int M, unsign
     if (lane == 0) ok = wait_count_geq(ep.ln_count + row0 / kGemmBM, target);
     if (!__shfl_sync(0xffffffffu, ok, 0)) return false;
     __syncwarp();  // the acquire by lane 0 orders the whole warp's loads
-    const int nrows = min(kLnRowsPerWarp, r_end - row0);
+    const int nrows = min(gr, r_end - row0);
     const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(ep.out) +
                                                         static_cast<long long>(row0) * OASIS_HIDDEN);
     for (int r = 0; r < nrows; ++r)

@@ -263,6 +263,9 @@ def test_attn_window_from_cache(pkg, cuda, kinds, vkinds, q_frames, q_pos0):
     (["bf16"] * 31, ["fp8"] * 10 + ["bf16"] * 21),
     (["fp8"] * 2 + ["bf16"] * 29, ["fp8"] * 11 + ["bf16"] * 20),
     (["int4"] * 23 + ["bf16"] * 8, ["int4"] * 23 + ["bf16"] * 8),
+    # every slot INT4, and fewer bf16 slots than a key tile: the 8-heads-per-warp kernel
+    (["int4"] * 31, ["int4"] * 31),
+    (["int4"] * 10 + ["bf16"] * 5, ["int4"] * 10 + ["bf16"] * 5),
     # kinds interleaved: the kernel regroups the slots into kind-uniform key tiles
     (["int4", "bf16"] * 8, ["int4", "bf16"] * 8),
     (["fp8", "int4"] * 10 + ["bf16"], ["fp8"] * 20 + ["bf16"])])
@@ -281,6 +284,34 @@ def test_attn_decode_keys_values_in_own_tiers(pkg, cuda, kinds, vkinds):
     vp = v.float().reshape(B, P, TOK, 16, 64).permute(0, 2, 3, 1, 4).reshape(B * TOK, 16, P, 64)
     ref = _temporal_ref(new, B, 1, kp, vp, q_pos0=P)
     torch.cuda.synchronize()
+    assert rel_l2(out.float(), ref) < 1e-2
+
+
+@pytest.mark.parametrize("kinds,n_kv_extra", [(["int4"] * 31, 1), (["int4"] * 31, 0),
+                                               (["int4"] * 23 + ["bf16"] * 8, 1)])
+def test_attn_decode_int4_at_benchmark_batch(pkg, cuda, kinds, n_kv_extra):
+    """The INT4 and progressive (23 INT4 + 8 bf16) one-query-frame cases at 16 sessions, the
+    benchmark's batch (8 heads per warp, persistent grid with several items per warp), with
+    and without the frame's own key, vs fp32 SDPA on the dequantised cache."""
+    B, P = 16, len(kinds)
+    past = _kv_rows(B, P, cuda, 41)
+    cache = pkg.KVCacheB200(B, 1, kinds, device=cuda)
+    cache.store(past, layer=0)
+    new = _qkv(B, cuda, 42)
+    q_pos0 = P if n_kv_extra else P - 1
+    out = pkg.attn_temporal(new, batch=B, q_frames=1, q_pos0=q_pos0, n_past=P, n_kv=P + n_kv_extra, cache=cache,
+                            layer=0)
+    k, v = cache.load(0)
+    kp = k.float().reshape(B, P, TOK, 16, 64).permute(0, 2, 3, 1, 4).reshape(B * TOK, 16, P, 64)
+    vp = v.float().reshape(B, P, TOK, 16, 64).permute(0, 2, 3, 1, 4).reshape(B * TOK, 16, P, 64)
+    if n_kv_extra:
+        ref = _temporal_ref(new, B, 1, kp, vp, q_pos0=P)
+    else:
+        q = new.float().reshape(B, 1, TOK, 3, 16, 64)[:, :, :, 0].permute(0, 2, 3, 1, 4).reshape(B * TOK, 16, 1, 64)
+        ref = torch.nn.functional.scaled_dot_product_attention(q, kp, vp)
+        ref = ref.reshape(B, TOK, 16, 1, 64).permute(0, 3, 1, 2, 4).reshape(B * TOK, HID)
+    torch.cuda.synchronize()
+    assert torch.isfinite(out.float()).all()
     assert rel_l2(out.float(), ref) < 1e-2
 
 
