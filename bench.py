@@ -162,7 +162,7 @@ class NvmlClockSampler:
                ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"),
                ("hw_power_brake", "nvmlClocksEventReasonHwPowerBrakeSlowdown"))
 
-    def __init__(self, uuid, period_s=0.002):
+    def __init__(self, uuid, period_s=0.001):
         import pynvml
         self.nv = pynvml
         pynvml.nvmlInit()
@@ -181,13 +181,15 @@ class NvmlClockSampler:
         nv = self.nv
         get_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
             nv.nvmlDeviceGetCurrentClocksThrottleReasons
+        n, watts = 0, None
         while not self.stop_flag.is_set():
             try:
-                t = time.perf_counter()
                 mhz = float(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
-                watts = nv.nvmlDeviceGetPowerUsage(self.h) / 1000.0
                 bits = int(get_reasons(self.h))
-                self.samples.append((t, mhz, watts, bits))
+                if n % 10 == 0:  # the power reading is an average over a longer window anyway
+                    watts = nv.nvmlDeviceGetPowerUsage(self.h) / 1000.0
+                self.samples.append((time.perf_counter(), mhz, watts, bits))
+                n += 1
             except Exception:
                 pass
             time.sleep(self.period)
@@ -208,7 +210,7 @@ class NvmlClockSampler:
                 if bits & getattr(self.nv, const, 0):
                     reasons.add(name)
         mhz = [x[1] for x in inside]
-        watts = [x[2] for x in inside]
+        watts = [x[2] for x in inside if x[2] is not None]
         try:
             self.nv.nvmlShutdown()
         except Exception:
@@ -524,16 +526,18 @@ def run_ours(args, rank, world, local_rank):
             dist.barrier()
         torch.cuda.synchronize()
 
-    for s in range(max(3, args.warmup)):
-        run_step(s)
-    barrier()
     uuid = None
     try:
         uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
     except Exception:
         pass
+    # started before the warm-up steps, so it is polling steadily when the timed region
+    # begins; only the samples taken between mark_begin and mark_end are kept
     clocks = clock_sampler(uuid)
     clocks.start()
+    for s in range(max(3, args.warmup)):
+        run_step(s)
+    barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     if hasattr(clocks, "mark_begin"):
