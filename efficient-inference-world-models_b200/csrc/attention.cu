@@ -1279,12 +1279,14 @@ constexpr int kDhgThreads = kDhgWarps * 32;
 constexpr int kDhgInt4 = 0;
 constexpr int kDhgBf16Int4 = 1;
 
-template <int LAYOUT>
+template <int LAYOUT, int HPW>
 __global__ void __launch_bounds__(kDhgThreads, 3)
     attn_decode_hg_kernel(const __nv_bfloat16* __restrict__ qkv, __nv_bfloat16* __restrict__ out,
                           const __grid_constant__ KvView kv, const __grid_constant__ DecodeLayout lay,
                           int q_pos, int n_past, float scale_log2) {
   pdl_trigger();
+  static_assert(HPW == 4 || HPW == 8, "4 or 8 heads per warp");
+  constexpr int GROUPS = OASIS_HEADS / HPW;  // head groups of a token
   constexpr bool SPLIT = LAYOUT == kDhgBf16Int4;
   constexpr int K0 = SPLIT ? OASIS_KV_BF16 : OASIS_KV_INT4;  // kind of n-tile 0 (positions 0..7)
   constexpr int KW = 2, VW = 1;                              // INT4 words per key / value chunk
@@ -1318,7 +1320,7 @@ __global__ void __launch_bounds__(kDhgThreads, 3)
 #pragma unroll
   for (int i = 0; i < 8; ++i) smask |= ((lay.valid >> spos(i)) & 1u) << i;
   const bool live_key = lay.live_kv && n_past <= q_pos;
-  const int items = lay.items;  // batch * 144 tokens * 2 head groups
+  const int items = lay.items;  // batch * 144 tokens * GROUPS head groups
   const int warps_total = gridDim.x * kDhgWarps;
   int it = blockIdx.x * kDhgWarps + (threadIdx.x >> 5);
   pdl_wait();
@@ -1333,16 +1335,25 @@ __global__ void __launch_bounds__(kDhgThreads, 3)
     uint32_t r[6][VW];
     uint32_t own[4];  // lanes c == 0: the frame's own value, dims 8g..8g+7
   };
-  auto item_tok = [](int item) { return item >> 1; };
-  auto item_h0 = [](int item) { return 8 * (item & 1); };
+  auto item_tok = [](int item) { return item / GROUPS; };
+  auto item_h0 = [](int item) { return HPW * (item % GROUPS); };
   // head h0's rows of the item's (session, token) in a pool of row bytes `rb`
   auto row_base = [&](const uint8_t* pool, uint32_t pages, uint32_t rb, uint32_t hb, int item) {
     const int tok = item_tok(item), p = tok % OASIS_TOKENS, b = tok / OASIS_TOKENS;
     return pool + (static_cast<long long>(b) * pages * OASIS_TOKENS + p) * rb + item_h0(item) * hb;
   };
-  auto load_k = [&](int item, int hh, KHead& k) {
-    const uint8_t* b0 = row_base(kpool0, dk.session_pages[K0], RB0, HB0, item) + hh * HB0;
-    const uint8_t* b = row_base(tk.int4, dk.session_pages[OASIS_KV_INT4], RB, HB, item) + hh * HB;
+  struct Bases {  // head h0's rows of an item: keys and values, n-tile 0 and the INT4 n-tiles
+    const uint8_t *k0, *k, *v0, *v;
+  };
+  auto bases = [&](int item) {
+    return Bases{row_base(kpool0, dk.session_pages[K0], RB0, HB0, item),
+                 row_base(tk.int4, dk.session_pages[OASIS_KV_INT4], RB, HB, item),
+                 row_base(vpool0, dv.session_pages[K0], RB0, HB0, item),
+                 row_base(tv.int4, dv.session_pages[OASIS_KV_INT4], RB, HB, item)};
+  };
+  auto load_k = [&](const Bases& ib, int hh, KHead& k) {
+    const uint8_t* b0 = ib.k0 + hh * HB0;
+    const uint8_t* b = ib.k + hh * HB;
 #pragma unroll
     for (int w = 0; w < K0W; ++w) k.n0[w] = 0u;
     if ((lay.valid >> g) & 1u) {
@@ -1367,9 +1378,9 @@ __global__ void __launch_bounds__(kDhgThreads, 3)
       }
     }
   };
-  auto load_v = [&](int item, int hh, VHead& v) {
-    const uint8_t* b0 = row_base(vpool0, dv.session_pages[K0], RB0, HB0, item) + hh * HB0;
-    const uint8_t* b = row_base(tv.int4, dv.session_pages[OASIS_KV_INT4], RB, HB, item) + hh * HB;
+  auto load_v = [&](const Bases& ib, int item, int hh, VHead& v) {
+    const uint8_t* b0 = ib.v0 + hh * HB0;
+    const uint8_t* b = ib.v + hh * HB;
 #pragma unroll
     for (int q = 0; q < 2; ++q) {
 #pragma unroll
@@ -1400,7 +1411,7 @@ __global__ void __launch_bounds__(kDhgThreads, 3)
   // (page, token, head); bf16 positions carry none
   auto load_scales = [&](const KvTensor& t, const DecodeTensor& d, int item, uint32_t (&dst)[8]) {
     const int tok = item_tok(item), p = tok % OASIS_TOKENS, b = tok / OASIS_TOKENS;
-    const long long e0 = dec_item_scale(d, OASIS_KV_INT4, b, p, item_h0(item) + g);
+    const long long e0 = dec_item_scale(d, OASIS_KV_INT4, b, p, item_h0(item) + (g < HPW ? g : g - HPW));
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       dst[i] = 0u;
@@ -1417,7 +1428,9 @@ __global__ void __launch_bounds__(kDhgThreads, 3)
   uint32_t qraw[8], klraw[8], ksr[8], vsr[8];
   auto load_q = [&](int item) {
     const int tok = item_tok(item);
-    const __nv_bfloat16* row = qkv + static_cast<long long>(tok) * kQkvLd + (item_h0(item) + g) * 64 + 16 * c;
+    // lanes of row groups g >= HPW take head h0 + g - HPW: a valid row whose scores are never read
+    const int hr = item_h0(item) + (g < HPW ? g : g - HPW);
+    const __nv_bfloat16* row = qkv + static_cast<long long>(tok) * kQkvLd + hr * 64 + 16 * c;
     const uint4 a = ldg_v4(row), a1 = ldg_v4(row + 8);
     qraw[0] = a.x; qraw[1] = a.y; qraw[2] = a.z; qraw[3] = a.w;
     qraw[4] = a1.x; qraw[5] = a1.y; qraw[6] = a1.z; qraw[7] = a1.w;
@@ -1433,8 +1446,9 @@ __global__ void __launch_bounds__(kDhgThreads, 3)
 
   KHead kh[2];
   VHead vh[2];
+  Bases ib = bases(it);
   load_q(it);
-  load_k(it, 0, kh[0]);
+  load_k(ib, 0, kh[0]);
   for (; it < items; it += warps_total) {
     const int nx = it + warps_total;
     const int tok = item_tok(it), h0 = item_h0(it);
@@ -1495,14 +1509,14 @@ __global__ void __launch_bounds__(kDhgThreads, 3)
       }
     };
 #pragma unroll 1
-    for (int hp = 0; hp < 8; hp += 2) {
-      load_k(it, hp + 1, kh[1]);
+    for (int hp = 0; hp < HPW; hp += 2) {
+      load_k(ib, hp + 1, kh[1]);
       score_head(hp, kh[0]);
-      if (hp < 6) load_k(it, hp + 2, kh[0]);
+      if (hp < HPW - 2) load_k(ib, hp + 2, kh[0]);
       score_head(hp + 1, kh[1]);
     }
     // the first head's values and the value scales load while the softmax runs
-    load_v(it, 0, vh[0]);
+    load_v(ib, it, 0, vh[0]);
     load_scales(tv, dv, it, vsr);
 
     // ---- softmax of row g (head h0 + g) over the cached keys and the live key
@@ -1602,15 +1616,17 @@ __global__ void __launch_bounds__(kDhgThreads, 3)
             make_uint4(o[0], o[1], o[2], o[3]);
       }
     };
+    const Bases cur = ib;
 #pragma unroll 1
-    for (int hp = 0; hp < 8; hp += 2) {
-      load_v(it, hp + 1, vh[1]);
+    for (int hp = 0; hp < HPW; hp += 2) {
+      load_v(cur, it, hp + 1, vh[1]);
       pv_head(hp, vh[0]);
-      if (hp < 6) {
-        load_v(it, hp + 2, vh[0]);
+      if (hp < HPW - 2) {
+        load_v(cur, it, hp + 2, vh[0]);
       } else if (nx < items) {
-        load_q(nx);           // the next item's query, own key and key scales
-        load_k(nx, 0, kh[0]);  // and its first head's keys
+        ib = bases(nx);
+        load_q(nx);            // the next item's query, own key and key scales
+        load_k(ib, 0, kh[0]);  // and its first head's keys
       }
       pv_head(hp + 1, vh[1]);
     }
@@ -2126,11 +2142,15 @@ int launch_attn_temporal(const void* qkv, const KvView& kv, int layer, void* out
     const bool hg_split = uniform[0] == dec_split_code(OASIS_KV_BF16, OASIS_KV_INT4) && uniform[1] == uniform[0] &&
                           lay.split == 8;
     const bool hg = hg_int4 || hg_split;
+    // 8 heads per warp where the items fill at least two rounds of the resident warps
+    // (three 4-warp CTAs per SM), else 4 (twice the items: less idle time in the last round)
+    const bool hpw8 = batch * OASIS_TOKENS * 2 >= 2 * 3 * kDhgWarps * num_sms();
     DecodeKernel kern = !hg ? decode_kernel(uniform[0], uniform[1])
-                            : (hg_int4 ? attn_decode_hg_kernel<kDhgInt4> : attn_decode_hg_kernel<kDhgBf16Int4>);
+                        : hg_int4 ? (hpw8 ? attn_decode_hg_kernel<kDhgInt4, 8> : attn_decode_hg_kernel<kDhgInt4, 4>)
+                                  : (hpw8 ? attn_decode_hg_kernel<kDhgBf16Int4, 8> : attn_decode_hg_kernel<kDhgBf16Int4, 4>);
     const int threads = hg ? kDhgThreads : kDecThreads;
     const int warps = hg ? kDhgWarps : kDecWarps;
-    if (hg) lay.items = batch * OASIS_TOKENS * (OASIS_HEADS / 8);
+    if (hg) lay.items = batch * OASIS_TOKENS * (hpw8 ? 2 : 4);
     int per_sm = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, 0) != cudaSuccess || per_sm < 1) {
       cudaGetLastError();
