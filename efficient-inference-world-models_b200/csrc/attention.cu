@@ -1255,12 +1255,12 @@ __global__ void __launch_bounds__(kDecThreads, dec_min_ctas(KK, VK))
 }
 
 // ----------------------------------------------------------------------------------
-// one query frame over INT4 cached frames (all of them, or all but a first n-tile of bf16
-// frames): one warp per (session, token, 8 heads)
+// one query frame over FP8 or INT4 cached frames (all of them, or INT4 after a first
+// n-tile of bf16 frames): one warp per (session, token, 4 or 8 heads)
 // ----------------------------------------------------------------------------------
 // The per-head kernel above leaves 15 of the 16 rows of its score tile empty and runs the
-// softmax, the scale shuffles and the output on 4 of its 32 lanes; with INT4 codes that
-// scalar work, not HBM, sets its speed.  Here a warp takes 8 heads of a token at once.
+// softmax, the scale shuffles and the output on 4 of its 32 lanes; with FP8 / INT4 codes
+// that scalar work, not HBM, sets its speed.  Here a warp takes 4 or 8 heads of a token.
 // Head hh's query is row hh of the A operand (the lanes of row group g = hh supply it,
 // every other row is zero) and its keys are the B columns, so the scores of all 8 heads
 // accumulate in one tile, row g holding head 8 hg + g; every lane quad then takes the
@@ -1269,15 +1269,14 @@ __global__ void __launch_bounds__(kDecThreads, dec_min_ctas(KK, VK))
 // its lane quad by shuffle).  Fragment layouts, head-dim orders and the fp32 arithmetic
 // of each head are those of attn_decode_kernel, so both give the same bits.  Heads go in
 // pairs, the next head's rows loading while the current head's are used.
-// Layouts: kDhgInt4 - every position INT4 (keys and values); kDhgBf16Int4 - key positions
-// 0..7 bf16 (the newest frames of a progressive cache, placed first by the host), 8..31
-// INT4, the same for the values.  (With FP8 codes the per-head kernel is faster: there
-// the loads, not the instructions, bound it, and its per-head items keep more of them in
-// flight.)
+// Layouts: kDhgInt4 / kDhgFp8 - every position INT4 / FP8 (keys and values);
+// kDhgBf16Int4 - key positions 0..7 bf16 (the newest frames of a progressive cache, placed
+// first by the host), 8..31 INT4, the same for the values.
 constexpr int kDhgWarps = 4;
 constexpr int kDhgThreads = kDhgWarps * 32;
 constexpr int kDhgInt4 = 0;
 constexpr int kDhgBf16Int4 = 1;
+constexpr int kDhgFp8 = 2;
 
 template <int LAYOUT, int HPW>
 __global__ void __launch_bounds__(kDhgThreads, 3)
@@ -1288,18 +1287,23 @@ __global__ void __launch_bounds__(kDhgThreads, 3)
   static_assert(HPW == 4 || HPW == 8, "4 or 8 heads per warp");
   constexpr int GROUPS = OASIS_HEADS / HPW;  // head groups of a token
   constexpr bool SPLIT = LAYOUT == kDhgBf16Int4;
-  constexpr int K0 = SPLIT ? OASIS_KV_BF16 : OASIS_KV_INT4;  // kind of n-tile 0 (positions 0..7)
-  constexpr int KW = 2, VW = 1;                              // INT4 words per key / value chunk
+  constexpr int BK = LAYOUT == kDhgFp8 ? OASIS_KV_FP8 : OASIS_KV_INT4;  // kind of n-tiles 1..3
+  constexpr int K0 = SPLIT ? OASIS_KV_BF16 : BK;                         // kind of n-tile 0 (positions 0..7)
+  constexpr int KW = BK == OASIS_KV_FP8 ? 4 : 2, VW = BK == OASIS_KV_FP8 ? 2 : 1;  // words per key / value chunk
   constexpr int K0W = SPLIT ? 8 : KW, V0W = SPLIT ? 4 : VW;  // the same for n-tile 0
-  constexpr uint32_t RB = dec_row_bytes(OASIS_KV_INT4), HB = dec_head_bytes(OASIS_KV_INT4);
+  constexpr bool kNibble = BK == OASIS_KV_INT4;               // dim order of the keys (and query)
+  constexpr bool kZero = BK == OASIS_KV_INT4;                 // scales carry zeros
+  constexpr uint32_t RB = dec_row_bytes(BK), HB = dec_head_bytes(BK);
   constexpr uint32_t RB0 = dec_row_bytes(K0), HB0 = dec_head_bytes(K0);
   const int lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
   const KvTensor& tk = kv.t[0];
   const KvTensor& tv = kv.t[1];
   const DecodeTensor& dk = lay.t[0];
   const DecodeTensor& dv = lay.t[1];
-  const uint8_t* kpool0 = SPLIT ? reinterpret_cast<const uint8_t*>(tk.bf16) : tk.int4;
-  const uint8_t* vpool0 = SPLIT ? reinterpret_cast<const uint8_t*>(tv.bf16) : tv.int4;
+  const uint8_t* kpool = BK == OASIS_KV_FP8 ? tk.fp8 : tk.int4;
+  const uint8_t* vpool = BK == OASIS_KV_FP8 ? tv.fp8 : tv.int4;
+  const uint8_t* kpool0 = SPLIT ? reinterpret_cast<const uint8_t*>(tk.bf16) : kpool;
+  const uint8_t* vpool0 = SPLIT ? reinterpret_cast<const uint8_t*>(tv.bf16) : vpool;
 
   // This lane's rows (as attn_decode_kernel): key rows nt = 0..3 are key 8 nt + g, dims
   // 16c..16c+15; value rows q = 0..7 are key 16 (q >> 2) + 2c + 8 ((q >> 1) & 1) + (q & 1),
@@ -1347,9 +1351,9 @@ __global__ void __launch_bounds__(kDhgThreads, 3)
   };
   auto bases = [&](int item) {
     return Bases{row_base(kpool0, dk.session_pages[K0], RB0, HB0, item),
-                 row_base(tk.int4, dk.session_pages[OASIS_KV_INT4], RB, HB, item),
+                 row_base(kpool, dk.session_pages[BK], RB, HB, item),
                  row_base(vpool0, dv.session_pages[K0], RB0, HB0, item),
-                 row_base(tv.int4, dv.session_pages[OASIS_KV_INT4], RB, HB, item)};
+                 row_base(vpool, dv.session_pages[BK], RB, HB, item)};
   };
   auto load_k = [&](const Bases& ib, int hh, KHead& k) {
     const uint8_t* b0 = ib.k0 + hh * HB0;
@@ -1362,6 +1366,9 @@ __global__ void __launch_bounds__(kDhgThreads, 3)
         const uint4 x0 = ldg_stream_v4(src), x1 = ldg_stream_v4(src + 16);
         k.n0[0] = x0.x; k.n0[1] = x0.y; k.n0[2] = x0.z; k.n0[3] = x0.w;
         k.n0[4] = x1.x; k.n0[5] = x1.y; k.n0[6] = x1.z; k.n0[7] = x1.w;
+      } else if constexpr (BK == OASIS_KV_FP8) {
+        const uint4 x = ldg_stream_v4(src);
+        k.n0[0] = x.x; k.n0[1] = x.y; k.n0[2] = x.z; k.n0[3] = x.w;
       } else {
         const uint2 x = ldg_stream_v2(src);
         k.n0[0] = x.x;
@@ -1370,11 +1377,17 @@ __global__ void __launch_bounds__(kDhgThreads, 3)
     }
 #pragma unroll
     for (int nt = 1; nt < 4; ++nt) {
-      k.n[nt - 1][0] = k.n[nt - 1][1] = 0u;
+#pragma unroll
+      for (int w = 0; w < KW; ++w) k.n[nt - 1][w] = 0u;
       if ((lay.valid >> (8 * nt + g)) & 1u) {
-        const uint2 x = ldg_stream_v2(b + koff(nt));
-        k.n[nt - 1][0] = x.x;
-        k.n[nt - 1][1] = x.y;
+        if constexpr (BK == OASIS_KV_FP8) {
+          const uint4 x = ldg_stream_v4(b + koff(nt));
+          k.n[nt - 1][0] = x.x; k.n[nt - 1][1] = x.y; k.n[nt - 1][2] = x.z; k.n[nt - 1][3] = x.w;
+        } else {
+          const uint2 x = ldg_stream_v2(b + koff(nt));
+          k.n[nt - 1][0] = x.x;
+          k.n[nt - 1][1] = x.y;
+        }
       }
     }
   };
@@ -1390,6 +1403,10 @@ __global__ void __launch_bounds__(kDhgThreads, 3)
         if constexpr (SPLIT) {
           const uint4 x = ldg_stream_v4(src);
           v.r0[q][0] = x.x; v.r0[q][1] = x.y; v.r0[q][2] = x.z; v.r0[q][3] = x.w;
+        } else if constexpr (BK == OASIS_KV_FP8) {
+          const uint2 x = ldg_stream_v2(src);
+          v.r0[q][0] = x.x;
+          v.r0[q][1] = x.y;
         } else {
           v.r0[q][0] = ldg_stream_u32(src);
         }
@@ -1397,8 +1414,17 @@ __global__ void __launch_bounds__(kDhgThreads, 3)
     }
 #pragma unroll
     for (int q = 2; q < 8; ++q) {
-      v.r[q - 2][0] = 0u;
-      if ((lay.valid >> vpos(q)) & 1u) v.r[q - 2][0] = ldg_stream_u32(b + voff(q));
+#pragma unroll
+      for (int w = 0; w < VW; ++w) v.r[q - 2][w] = 0u;
+      if ((lay.valid >> vpos(q)) & 1u) {
+        if constexpr (BK == OASIS_KV_FP8) {
+          const uint2 x = ldg_stream_v2(b + voff(q));
+          v.r[q - 2][0] = x.x;
+          v.r[q - 2][1] = x.y;
+        } else {
+          v.r[q - 2][0] = ldg_stream_u32(b + voff(q));
+        }
+      }
     }
     v.own[0] = v.own[1] = v.own[2] = v.own[3] = 0u;
     if (c == 0 && live_key) {
@@ -1408,21 +1434,24 @@ __global__ void __launch_bounds__(kDhgThreads, 3)
     }
   };
   // scale (| zero << 16) of score position i for the row head of an item: INT4 per
-  // (page, token, head); bf16 positions carry none
+  // (page, token, head), FP8 per (page, head); bf16 positions carry none
   auto load_scales = [&](const KvTensor& t, const DecodeTensor& d, int item, uint32_t (&dst)[8]) {
     const int tok = item_tok(item), p = tok % OASIS_TOKENS, b = tok / OASIS_TOKENS;
-    const long long e0 = dec_item_scale(d, OASIS_KV_INT4, b, p, item_h0(item) + (g < HPW ? g : g - HPW));
+    const long long e0 = dec_item_scale(d, BK, b, p, item_h0(item) + (g < HPW ? g : g - HPW));
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       dst[i] = 0u;
       if ((!SPLIT || i >= 2) && ((smask >> i) & 1u)) {
-        const uint32_t so = dec_slot_scale(OASIS_KV_INT4, d.slot_page[spos(i)]);
-        dst[i] = ldg_u16(t.i4_scale + e0 + so) | (ldg_u16(t.i4_zero + e0 + so) << 16);
+        const uint32_t so = dec_slot_scale(BK, d.slot_page[spos(i)]);
+        if constexpr (BK == OASIS_KV_FP8)
+          dst[i] = ldg_u16(t.fp8_scale + e0 + so);
+        else
+          dst[i] = ldg_u16(t.i4_scale + e0 + so) | (ldg_u16(t.i4_zero + e0 + so) << 16);
       }
     }
   };
   auto scale_of = [&](uint32_t raw, int i, bool live) {
-    return SPLIT && i < 2 ? dec_scale(raw, OASIS_KV_BF16, live) : dec_scale(raw, OASIS_KV_INT4, live);
+    return SPLIT && i < 2 ? dec_scale(raw, OASIS_KV_BF16, live) : dec_scale(raw, BK, live);
   };
   // the row head's query (dims 16c..16c+15) and own key
   uint32_t qraw[8], klraw[8], ksr[8], vsr[8];
@@ -1453,24 +1482,34 @@ __global__ void __launch_bounds__(kDhgThreads, 3)
     const int nx = it + warps_total;
     const int tok = item_tok(it), h0 = item_h0(it);
 
-    // ---- the row head's query as A fragments (row g) in the nibble dim order
+    // ---- the row head's query as A fragments (row g) in the keys' dim order
     uint32_t qa[4][2];
+    if (!kNibble) {
 #pragma unroll
-    for (int k = 0; k < 2; ++k) {
-      qa[2 * k][0] = pack_f16x2(bf16_lo(qraw[4 * k]), bf16_lo(qraw[4 * k + 2]));
-      qa[2 * k][1] = pack_f16x2(bf16_hi(qraw[4 * k]), bf16_hi(qraw[4 * k + 2]));
-      qa[2 * k + 1][0] = pack_f16x2(bf16_lo(qraw[4 * k + 1]), bf16_lo(qraw[4 * k + 3]));
-      qa[2 * k + 1][1] = pack_f16x2(bf16_hi(qraw[4 * k + 1]), bf16_hi(qraw[4 * k + 3]));
+      for (int ks = 0; ks < 4; ++ks) {
+        qa[ks][0] = f16x2_bf16x2(qraw[2 * ks]);
+        qa[ks][1] = f16x2_bf16x2(qraw[2 * ks + 1]);
+      }
+    } else {
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        qa[2 * k][0] = pack_f16x2(bf16_lo(qraw[4 * k]), bf16_lo(qraw[4 * k + 2]));
+        qa[2 * k][1] = pack_f16x2(bf16_hi(qraw[4 * k]), bf16_hi(qraw[4 * k + 2]));
+        qa[2 * k + 1][0] = pack_f16x2(bf16_lo(qraw[4 * k + 1]), bf16_lo(qraw[4 * k + 3]));
+        qa[2 * k + 1][1] = pack_f16x2(bf16_hi(qraw[4 * k + 1]), bf16_hi(qraw[4 * k + 3]));
+      }
     }
     float qsum = 0.0f;
+    if (kZero) {
 #pragma unroll
-    for (int ks = 0; ks < 4; ++ks) {
-      const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&qa[ks][0]));
-      const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&qa[ks][1]));
-      qsum += (f0.x + f0.y) + (f1.x + f1.y);
+      for (int ks = 0; ks < 4; ++ks) {
+        const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&qa[ks][0]));
+        const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&qa[ks][1]));
+        qsum += (f0.x + f0.y) + (f1.x + f1.y);
+      }
+      qsum += __shfl_xor_sync(0xffffffffu, qsum, 1);
+      qsum += __shfl_xor_sync(0xffffffffu, qsum, 2);
     }
-    qsum += __shfl_xor_sync(0xffffffffu, qsum, 1);
-    qsum += __shfl_xor_sync(0xffffffffu, qsum, 2);
     float s_live = -INFINITY;
     if (live_key) {
       float d = 0.0f;
@@ -1499,9 +1538,9 @@ __global__ void __launch_bounds__(kDhgThreads, 3)
         if ((lay.valid >> (8 * nt)) & 0xFFu) {
           uint32_t kbf[4][2];
           if (nt == 0)
-            key_fragments<SPLIT ? kDecMixed : OASIS_KV_INT4, K0W>(k.n0, K0, kbf);
+            key_fragments<SPLIT ? kDecMixed : BK, K0W>(k.n0, K0, kbf);
           else
-            key_fragments<OASIS_KV_INT4, KW>(k.n[nt - 1], OASIS_KV_INT4, kbf);
+            key_fragments<BK, KW>(k.n[nt - 1], BK, kbf);
 #pragma unroll
           for (int ks = 0; ks < 4; ++ks)
             mma_16816<false>(sacc[nt], a0[ks], 0u, a2[ks], 0u, kbf[ks][0], kbf[ks][1]);
@@ -1525,7 +1564,8 @@ __global__ void __launch_bounds__(kDhgThreads, 3)
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const float2 ks = scale_of(ksr[i], i, true);
-      const float sv = __fmaf_rn(sacc[i >> 1][i & 1], ks.x, ks.y * qsum);
+      const float s = sacc[i >> 1][i & 1];
+      const float sv = kZero ? __fmaf_rn(s, ks.x, ks.y * qsum) : s * ks.x;
       sc[i] = (smask >> i) & 1u ? sv : -INFINITY;
       mx = fmaxf(mx, sc[i]);
     }
@@ -1561,7 +1601,7 @@ __global__ void __launch_bounds__(kDhgThreads, 3)
       for (int i = 0; i < 8; ++i) {
         const float2 vs = scale_of(vsr[i], i, (smask >> i) & 1u);
         pv[i] = sc[i] * vs.x * inv_vmax;
-        corr = __fmaf_rn(sc[i], vs.y, corr);
+        if (kZero) corr = __fmaf_rn(sc[i], vs.y, corr);
       }
 #pragma unroll
       for (int kv2 = 0; kv2 < 2; ++kv2) {
@@ -1569,8 +1609,10 @@ __global__ void __launch_bounds__(kDhgThreads, 3)
         pbk[kv2][1] = pack_f16x2(pv[4 * kv2 + 2], pv[4 * kv2 + 3]);
       }
     }
-    corr += __shfl_xor_sync(0xffffffffu, corr, 1);
-    corr += __shfl_xor_sync(0xffffffffu, corr, 2);
+    if (kZero) {
+      corr += __shfl_xor_sync(0xffffffffu, corr, 1);
+      corr += __shfl_xor_sync(0xffffffffu, corr, 2);
+    }
     const float inv = 1.0f / sum;
 
     // ---- per head: O^T = V^T P'^T, then the live value, the multipliers and 1 / sum
@@ -1591,10 +1633,10 @@ __global__ void __launch_bounds__(kDhgThreads, 3)
         if (!((lay.valid >> (16 * kv2)) & 0xFFFFu)) continue;
         uint32_t F[2][8];
         if (kv2 == 0)  // rows 0, 1: n-tile 0; rows 2, 3: n-tile 1
-          value_fragments<SPLIT ? kDecMixed : OASIS_KV_INT4, V0W>(v.r0[0], v.r0[1], K0, K0, F[0]);
+          value_fragments<SPLIT ? kDecMixed : BK, V0W>(v.r0[0], v.r0[1], K0, K0, F[0]);
         else
-          value_fragments<OASIS_KV_INT4, VW>(v.r[2], v.r[3], OASIS_KV_INT4, OASIS_KV_INT4, F[0]);
-        value_fragments<OASIS_KV_INT4, VW>(v.r[4 * kv2], v.r[4 * kv2 + 1], OASIS_KV_INT4, OASIS_KV_INT4, F[1]);
+          value_fragments<BK, VW>(v.r[2], v.r[3], BK, BK, F[0]);
+        value_fragments<BK, VW>(v.r[4 * kv2], v.r[4 * kv2 + 1], BK, BK, F[1]);
 #pragma unroll
         for (int mo = 0; mo < 4; ++mo)
           mma_16816<false>(oacc[mo], F[0][2 * mo], F[0][2 * mo + 1], F[1][2 * mo], F[1][2 * mo + 1], pb[kv2][0],
@@ -2137,16 +2179,19 @@ int launch_attn_temporal(const void* qkv, const KvView& kv, int layer, void* out
         if (pos_slot[j] >= 0) d.slot_page[j] = static_cast<uint32_t>(layer * n_kind[pos_kind[which][j]] + t.index[pos_slot[j]]);
       }
     }
-    // keys and values all INT4, or bf16 in n-tile 0 and INT4 after it: 8 heads per warp
+    // keys and values all FP8, all INT4, or bf16 in n-tile 0 and INT4 after it: 4 or 8
+    // heads per warp
     const bool hg_int4 = uniform[0] == OASIS_KV_INT4 && uniform[1] == OASIS_KV_INT4;
     const bool hg_split = uniform[0] == dec_split_code(OASIS_KV_BF16, OASIS_KV_INT4) && uniform[1] == uniform[0] &&
                           lay.split == 8;
-    const bool hg = hg_int4 || hg_split;
+    const bool hg_fp8 = uniform[0] == OASIS_KV_FP8 && uniform[1] == OASIS_KV_FP8;
+    const bool hg = hg_int4 || hg_split || hg_fp8;
     // 8 heads per warp where the items fill at least two rounds of the resident warps
     // (three 4-warp CTAs per SM), else 4 (twice the items: less idle time in the last round)
     const bool hpw8 = batch * OASIS_TOKENS * 2 >= 2 * 3 * kDhgWarps * num_sms();
     DecodeKernel kern = !hg ? decode_kernel(uniform[0], uniform[1])
                         : hg_int4 ? (hpw8 ? attn_decode_hg_kernel<kDhgInt4, 8> : attn_decode_hg_kernel<kDhgInt4, 4>)
+                        : hg_fp8  ? (hpw8 ? attn_decode_hg_kernel<kDhgFp8, 8> : attn_decode_hg_kernel<kDhgFp8, 4>)
                                   : (hpw8 ? attn_decode_hg_kernel<kDhgBf16Int4, 8> : attn_decode_hg_kernel<kDhgBf16Int4, 4>);
     const int threads = hg ? kDhgThreads : kDecThreads;
     const int warps = hg ? kDhgWarps : kDecWarps;
