@@ -417,13 +417,22 @@ __device__ __forceinline__ bool ln_rows_phase(const EpiParams& ep, int M, unsign
     const int nrows = min(gr, r_end - row0);
     const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(ep.out) +
                                                         static_cast<long long>(row0) * OASIS_HIDDEN);
-    for (int r = 0; r < nrows; ++r)
+    // rows in pairs, each pair one cp.async group: the second pair lands while the first
+    // is normalised (each lane copies, and later reads, only its own columns)
+    for (int r = 0; r < nrows; ++r) {
 #pragma unroll
-      for (int i = 0; i < 8; ++i)  // each lane copies (and later reads) its own columns
-        cp_async16(stage + r * 256 + lane + 32 * i, src + r * 256 + lane + 32 * i);
-    cp_async_wait_all();
-    ln_modulate_rows_smem(stage, nrows, a4, s4, ep.ln_out + static_cast<long long>(row0) * OASIS_HIDDEN,
-                          lane);
+      for (int i = 0; i < 8; ++i) cp_async16(stage + r * 256 + lane + 32 * i, src + r * 256 + lane + 32 * i);
+      if (r & 1 || r + 1 == nrows) cp_async_commit();
+    }
+    __nv_bfloat16* out0 = ep.ln_out + static_cast<long long>(row0) * OASIS_HIDDEN;
+#pragma unroll 1
+    for (int r0 = 0; r0 < nrows; r0 += 2) {
+      if (r0 + 2 < nrows)
+        cp_async_wait_group<1>();  // this pair has landed, the next may be in flight
+      else
+        cp_async_wait_group<0>();
+      ln_modulate_rows_smem(stage + r0 * 256, min(2, nrows - r0), a4, s4, out0 + r0 * OASIS_HIDDEN, lane);
+    }
     if (rows_done) {
       __syncwarp();
       if (lane == 0) red_release_add(rows_done + row0 / kGemmBM, static_cast<unsigned>(nrows));

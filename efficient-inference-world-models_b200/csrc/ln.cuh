@@ -11,7 +11,7 @@ namespace oasis {
 
 constexpr int kLnRowsPerWarp = 4;
 
-// shift/scale of one frame, in the lane's column layout
+// shift and 1 + scale of one frame, in the lane's column layout
 __device__ __forceinline__ void ln_load_modulation(const float* shift, const float* scale, int lane,
                                                    float4 (&a4)[8], float4 (&s4)[8]) {
   const float4* sh = reinterpret_cast<const float4*>(shift);
@@ -19,10 +19,17 @@ __device__ __forceinline__ void ln_load_modulation(const float* shift, const flo
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     a4[i] = sh[lane + 32 * i];
-    s4[i] = sc[lane + 32 * i];
+    const float4 s = sc[lane + 32 * i];
+    s4[i] = make_float4(1.0f + s.x, 1.0f + s.y, 1.0f + s.z, 1.0f + s.w);
   }
 }
 
+// y = ((x - mean) * rstd) * (1 + scale) + shift, the last product and sum fused
+__device__ __forceinline__ float ln_out(float d, float rstd, float ops, float shift) {
+  return __fmaf_rn(d * rstd, ops, shift);
+}
+
+// One row (lane holds columns 4 lane + 128 i); s4 holds 1 + scale (ln_load_modulation).
 __device__ __forceinline__ void ln_modulate_row(const float4 (&v)[8], const float4 (&a4)[8],
                                                 const float4 (&s4)[8], __nv_bfloat16* out_row,
                                                 int lane) {
@@ -32,11 +39,12 @@ __device__ __forceinline__ void ln_modulate_row(const float4 (&v)[8], const floa
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
   const float mean = sum * (1.0f / OASIS_HIDDEN);
+  float4 d[8];  // the centred row, kept for the output
   float sq = 0.0f;
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
-    const float a = v[i].x - mean, b = v[i].y - mean, c = v[i].z - mean, d = v[i].w - mean;
-    sq += (a * a + b * b) + (c * c + d * d);
+    d[i] = make_float4(v[i].x - mean, v[i].y - mean, v[i].z - mean, v[i].w - mean);
+    sq += (d[i].x * d[i].x + d[i].y * d[i].y) + (d[i].z * d[i].z + d[i].w * d[i].w);
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
@@ -46,18 +54,15 @@ __device__ __forceinline__ void ln_modulate_row(const float4 (&v)[8], const floa
   for (int i = 0; i < 8; ++i) {
     const float4 a = a4[i];
     const float4 s = s4[i];
-    const float y0 = (v[i].x - mean) * rstd * (1.0f + s.x) + a.x;
-    const float y1 = (v[i].y - mean) * rstd * (1.0f + s.y) + a.y;
-    const float y2 = (v[i].z - mean) * rstd * (1.0f + s.z) + a.z;
-    const float y3 = (v[i].w - mean) * rstd * (1.0f + s.w) + a.w;
-    o2[lane + 32 * i] = make_uint2(pack_bf16x2(y0, y1), pack_bf16x2(y2, y3));
+    o2[lane + 32 * i] = make_uint2(pack_bf16x2(ln_out(d[i].x, rstd, s.x, a.x), ln_out(d[i].y, rstd, s.y, a.y)),
+                                   pack_bf16x2(ln_out(d[i].z, rstd, s.z, a.z), ln_out(d[i].w, rstd, s.w, a.w)));
   }
 }
 
 // The same for rows staged in shared memory (row r at rows[r * 256 + lane + 32 i]),
 // two rows per pass with their reductions interleaved so the shuffle chains overlap;
-// shift/scale (a4/s4, ln_load_modulation) stay in registers.  Per row the arithmetic
-// is the sequence of ln_modulate_row.
+// shift and 1 + scale (a4/s4, ln_load_modulation) stay in registers.  Per row the
+// arithmetic is the sequence of ln_modulate_row.
 __device__ __forceinline__ void ln_modulate_rows_smem(const float4* rows, int nrows,
                                                       const float4 (&a4)[8], const float4 (&s4)[8],
                                                       __nv_bfloat16* out, int lane) {
@@ -82,10 +87,9 @@ __device__ __forceinline__ void ln_modulate_rows_smem(const float4* rows, int nr
       mean[r] = sum[r] * (1.0f / OASIS_HIDDEN);
       sq[r] = 0.0f;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float a = v[r][i].x - mean[r], b = v[r][i].y - mean[r], c = v[r][i].z - mean[r],
-                    d = v[r][i].w - mean[r];
-        sq[r] += (a * a + b * b) + (c * c + d * d);
+      for (int i = 0; i < 8; ++i) {  // v becomes the centred row
+        v[r][i] = make_float4(v[r][i].x - mean[r], v[r][i].y - mean[r], v[r][i].z - mean[r], v[r][i].w - mean[r]);
+        sq[r] += (v[r][i].x * v[r][i].x + v[r][i].y * v[r][i].y) + (v[r][i].z * v[r][i].z + v[r][i].w * v[r][i].w);
       }
     }
 #pragma unroll
@@ -101,11 +105,9 @@ __device__ __forceinline__ void ln_modulate_rows_smem(const float4* rows, int nr
       for (int i = 0; i < 8; ++i) {
         const float4 a = a4[i];
         const float4 s = s4[i];
-        const float y0 = (v[r][i].x - mean[r]) * rstd[r] * (1.0f + s.x) + a.x;
-        const float y1 = (v[r][i].y - mean[r]) * rstd[r] * (1.0f + s.y) + a.y;
-        const float y2 = (v[r][i].z - mean[r]) * rstd[r] * (1.0f + s.z) + a.z;
-        const float y3 = (v[r][i].w - mean[r]) * rstd[r] * (1.0f + s.w) + a.w;
-        o2[lane + 32 * i] = make_uint2(pack_bf16x2(y0, y1), pack_bf16x2(y2, y3));
+        const float4 d = v[r][i];
+        o2[lane + 32 * i] = make_uint2(pack_bf16x2(ln_out(d.x, rstd[r], s.x, a.x), ln_out(d.y, rstd[r], s.y, a.y)),
+                                       pack_bf16x2(ln_out(d.z, rstd[r], s.z, a.z), ln_out(d.w, rstd[r], s.w, a.w)));
       }
     }
   }
