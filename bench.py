@@ -596,18 +596,24 @@ def run_ours(args, rank, world, local_rank):
     # times; the families' times come from the last replay ----
     M = B * T * TOKENS
     fam_src = "graph"
-    n_prof = 1
+    n_prof = 5
     try:
+        # five captures of the step (each with its own timing events), each replayed twice:
+        # the family times are the mean over the second replays of the five graphs
         model.set_timing(B, T, True)
-        gt = torch.cuda.CUDAGraph()
-        with torch.cuda.stream(stream):
-            with torch.cuda.graph(gt, stream=stream):
-                step_body(1)
-        for _ in range(5):
-            gt.replay()
+        gts = []
+        for _ in range(n_prof):
+            gt = torch.cuda.CUDAGraph()
+            with torch.cuda.stream(stream):
+                with torch.cuda.graph(gt, stream=stream):
+                    step_body(1)
+            gts.append(gt)
+        for _ in range(2):
+            for gt in gts:
+                gt.replay()
         torch.cuda.synchronize()
         fam = model.get_timing(B, T)
-        del gt
+        del gts
     except Exception:  # eager fallback: events on the launching stream
         fam_src = "eager"
         model.set_timing(B, T, True)
