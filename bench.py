@@ -632,7 +632,9 @@ def run_ours(args, rank, world, local_rank):
     kv, sweep, lib = {}, [], None
     if rank == 0 and not args.skip_kv:
         kv = kv_configs(pkg, model, dev, g, peaks)
-    vae = {}
+    vae, rollout = {}, {}
+    if rank == 0 and not args.skip_kv:
+        rollout = rollout_bench(pkg, model, dev)
     if rank == 0 and not args.skip_sweep:
         sweep = attention_sweep(pkg, dev, peaks.get("hbm_gbs", 6650.0), reps=10)
         vae = vae_decode_bench(pkg, dev, peaks)
@@ -686,6 +688,7 @@ def run_ours(args, rank, world, local_rank):
             "kv_configs": kv,
             "attention_sweep": sweep,
             "vae_decode": vae,
+            "rollout": rollout,
         }
         print(json.dumps(line), flush=True)
     graphs.clear()
@@ -761,6 +764,38 @@ def kv_configs(pkg, model, dev, g, peaks):
             del gr, cache
         except Exception as e:
             out[name] = {"error": str(e)[:200]}
+    return out
+
+
+def rollout_bench(pkg, model, dev, frames=16, steps=SOLVER_STEPS):
+    """The public rollout API (`rollout_dpmpp`, CUDA graphs per frame) over a full 32-frame
+    window (31 prompt frames, then `frames` new ones, 5 DPM++ 2M steps each): every solver
+    step a full-window forward, or the first step of each frame full-window (rebuilding the
+    bf16 cache of the 31 past frames) and the other steps incremental forwards of the new
+    frame.  Frames/s of the second of two calls (graphs are captured inside each call)."""
+    out = {}
+    try:
+        g = torch.Generator().manual_seed(7)
+        prompt = torch.randn(1, WINDOW - 1, *FRAME, generator=g).to(dev)
+        acts = synthetic_actions(g, 1, WINDOW - 1 + frames).to(dev)
+        for name, use_cache in (("full_window_steps", False), ("cached_steps", True)):
+            ms = None
+            for _ in range(2):
+                torch.cuda.synchronize()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                pkg.rollout_dpmpp(model, prompt, acts, num_frames=frames, solver_steps=steps,
+                                  use_cache=use_cache, use_graph=True)
+                e1.record()
+                torch.cuda.synchronize()
+                ms = e0.elapsed_time(e1)
+            out[name] = {"frames_per_s": frames / (ms / 1000.0), "ms": ms, "frames": frames,
+                         "solver_steps": steps}
+        out["note"] = ("one session, window 32; causal temporal attention: the 31 context frames "
+                       "never see the new frame, so their outputs are the same at every solver "
+                       "step of a frame and the incremental steps skip only unused work")
+    except Exception as e:
+        out["error"] = str(e)[:200]
     return out
 
 
