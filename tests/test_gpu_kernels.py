@@ -106,6 +106,23 @@ def test_attn_temporal_bf16(pkg, cuda, B, T):
     assert rel_l2(out.float(), ref) < 1e-2
 
 
+@pytest.mark.parametrize("T,q_pos0,n_kv", [(8, 3, 5), (32, 0, 20), (17, 40, 17), (32, 7, 32)])
+def test_attn_temporal_full_window_offsets(pkg, cuda, T, q_pos0, n_kv):
+    """Full-window call (no cache) with the queries at window positions q_pos0.. and only
+    the first n_kv frames as keys: the causal mask takes both into account."""
+    B = 3
+    qkv = _qkv(B * T, cuda, 400 + T + q_pos0)
+    out = pkg.attn_temporal(qkv, batch=B, q_frames=T, q_pos0=q_pos0, n_kv=n_kv)
+    z = qkv.float().reshape(B, T, TOK, 3, 16, 64)
+    q, k, v = (z[:, :, :, i].permute(0, 2, 3, 1, 4).reshape(B * TOK, 16, T, 64) for i in range(3))
+    k, v = k[:, :, :n_kv].contiguous(), v[:, :, :n_kv].contiguous()
+    mask = torch.arange(n_kv, device=cuda)[None, :] <= (torch.arange(T, device=cuda) + q_pos0)[:, None]
+    ref = torch.nn.functional.scaled_dot_product_attention(q, k, v, attn_mask=mask)
+    ref = ref.reshape(B, TOK, 16, T, 64).permute(0, 3, 1, 2, 4).reshape(B * T * TOK, HID)
+    torch.cuda.synchronize()
+    assert rel_l2(out.float(), ref) < 1e-2
+
+
 # ----------------------------------------------------------------- KV cache quantisation
 
 def _kv_rows(B, F, cuda, seed, scale_per_frame=True):
