@@ -199,7 +199,8 @@ __global__ void __launch_bounds__(128) attn_vae_kernel(const __nv_bfloat16* __re
 // workspace layout of a decode of F frames (M = 576 F token rows)
 struct VaeLayout {
   size_t zin, resid, hbuf, qkv, attn, mlp, pred, cnt, total;
-  size_t cnt_words;  // LayerNorm-tail tile counters: 2 launches per block x ceil(M / 128)
+  size_t cnt_words;   // LayerNorm-tail tile counters: 2 launches per block x ceil(M / 128)
+  size_t flag_words;  // split-K order counters of one residual launch (<= 16 N tiles x 8 warps)
 };
 VaeLayout vae_layout(int F, int depth) {
   const size_t M = static_cast<size_t>(F) * kVaeTokens;
@@ -218,7 +219,10 @@ VaeLayout vae_layout(int F, int depth) {
   L.mlp = take(M * OASIS_MLP_HIDDEN * 2);
   L.pred = take(M * OASIS_VAE_PRED_LD * 4);
   L.cnt_words = static_cast<size_t>(2 * depth) * ((M + 127) / 128);
-  L.cnt = take(L.cnt_words * 4);
+  L.flag_words = ((M + 127) / 128) * (OASIS_HIDDEN / 64) * kEpiWarps;
+  // zeroed together per decode: the tile counters, then the split-K counters of every
+  // residual launch (out-proj and fc2 of each block)
+  L.cnt = take((L.cnt_words + static_cast<size_t>(2 * depth) * L.flag_words) * 4);
   L.total = off;
   return L;
 }
@@ -239,10 +243,17 @@ struct oasis_vae_plan {
 namespace oasis {
 namespace {
 
-int vae_proj(GemmOperands* g, const void* A, long long lda, const void* B, int M, int N, int K) {
+// A projection over the M token rows: tile shape from choose_tiles; the residual GEMMs
+// (out-proj, fc2) may split K, their splits' reduce-adds ordered by counters.
+int vae_proj(GemmOperands* g, const void* A, long long lda, const void* B, int M, int N, int K,
+             bool residual = false) {
   int bn = 256, ctas = 1, splits = 1;
-  choose_tiles(M, N, K, false, &bn, &ctas, &splits);
-  return make_gemm_operands(g, A, lda, B, K, M, N, K, bn, ctas);
+  choose_tiles(M, N, K, residual, &bn, &ctas, &splits);
+  if (int st = make_gemm_operands(g, A, lda, B, K, M, N, K, bn, ctas)) return st;
+  g->splits = splits;
+  if (split_flag_count(*g) > vae_layout(M / kVaeTokens, 1).flag_words)
+    return fail(OASIS_ERR_UNSUPPORTED, "oasis_vae_plan_create: split-K counters exceed their region");
+  return OASIS_OK;
 }
 
 int vae_plan_init(oasis_vae_plan* p, const oasis_vae_weights_t* w, int frames, void* workspace, size_t ws_bytes) {
@@ -267,11 +278,11 @@ int vae_plan_init(oasis_vae_plan* p, const oasis_vae_weights_t* w, int frames, v
     const oasis_vae_block_t& b = w->blk[i];
     st = vae_proj(&p->qkv[i], ws + L.hbuf, OASIS_HIDDEN, b.qkv_w, M, 3 * OASIS_HIDDEN, OASIS_HIDDEN);
     if (!st) st = set_gemm_output(&p->qkv[i], ws + L.qkv, 3 * OASIS_HIDDEN, false);
-    if (!st) st = vae_proj(&p->proj[i], ws + L.attn, OASIS_HIDDEN, b.proj_w, M, OASIS_HIDDEN, OASIS_HIDDEN);
+    if (!st) st = vae_proj(&p->proj[i], ws + L.attn, OASIS_HIDDEN, b.proj_w, M, OASIS_HIDDEN, OASIS_HIDDEN, true);
     if (!st) st = set_gemm_output(&p->proj[i], ws + L.resid, OASIS_HIDDEN, true);
     if (!st) st = vae_proj(&p->fc1[i], ws + L.hbuf, OASIS_HIDDEN, b.fc1_w, M, OASIS_MLP_HIDDEN, OASIS_HIDDEN);
     if (!st) st = set_gemm_output(&p->fc1[i], ws + L.mlp, OASIS_MLP_HIDDEN, false);
-    if (!st) st = vae_proj(&p->fc2[i], ws + L.mlp, OASIS_MLP_HIDDEN, b.fc2_w, M, OASIS_HIDDEN, OASIS_MLP_HIDDEN);
+    if (!st) st = vae_proj(&p->fc2[i], ws + L.mlp, OASIS_MLP_HIDDEN, b.fc2_w, M, OASIS_HIDDEN, OASIS_MLP_HIDDEN, true);
     if (!st) st = set_gemm_output(&p->fc2[i], ws + L.resid, OASIS_HIDDEN, true);
   }
   if (!st) st = vae_proj(&p->pred, ws + L.hbuf, OASIS_HIDDEN, w->pred_w, M, OASIS_VAE_PRED_LD, OASIS_HIDDEN);
@@ -292,7 +303,8 @@ int vae_run(oasis_vae_plan* p, const float* z, float* out, cudaStream_t s) {
   auto* hbuf = reinterpret_cast<__nv_bfloat16*>(ws + L.hbuf);
   auto* cnt = reinterpret_cast<unsigned int*>(ws + L.cnt);
   const size_t nblk = (static_cast<size_t>(M) + 127) / 128;
-  cudaError_t ce = cudaMemsetAsync(cnt, 0, L.cnt_words * 4, s);
+  unsigned int* flags = cnt + L.cnt_words;
+  cudaError_t ce = cudaMemsetAsync(cnt, 0, (L.cnt_words + static_cast<size_t>(2 * w.depth) * L.flag_words) * 4, s);
   if (ce != cudaSuccess) return cuda_status(ce, "cudaMemsetAsync(vae counters)");
 
   // latent projection into the fp32 residual, then the first LayerNorm (affine as
@@ -342,7 +354,7 @@ int vae_run(oasis_vae_plan* p, const float* z, float* out, cudaStream_t s) {
     eo.ln_scale = b.ln2_scale;
     eo.ln_mod_ld = 0;
     eo.ln_count = cnt + (2 * static_cast<size_t>(i)) * nblk;
-    eo.k_splits = 1;
+    eo.split_flags = flags + (2 * static_cast<size_t>(i)) * L.flag_words;
     if (int r = launch_gemm(p->proj[i], kEpiGateResid, eo, s)) return r;
     EpiParams e1{};
     e1.out = ws + L.mlp;
@@ -361,7 +373,7 @@ int vae_run(oasis_vae_plan* p, const float* z, float* out, cudaStream_t s) {
     e2.ln_scale = last ? w.norm_scale : w.blk[i + 1].ln1_scale;
     e2.ln_mod_ld = 0;
     e2.ln_count = cnt + (2 * static_cast<size_t>(i) + 1) * nblk;
-    e2.k_splits = 1;
+    e2.split_flags = flags + (2 * static_cast<size_t>(i) + 1) * L.flag_words;
     if (int r = launch_gemm(p->fc2[i], kEpiGateResid, e2, s)) return r;
   }
   EpiParams ep{};
