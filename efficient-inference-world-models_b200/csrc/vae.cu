@@ -53,39 +53,59 @@ __global__ void vae_unpatchify_kernel(const float* __restrict__ y, int ld, float
 // head, frame), one warp per 16 query rows; 64-key K/V tiles double-buffered through
 // shared memory by cp.async; S and P V on mma.sync (bf16, fp32 accumulation) with an
 // online softmax in registers.  q and k arrive post-RoPE from the QKV epilogue.
+// KG key groups of 4 warps split the 9 key blocks (group g takes blocks g, g + KG, ...),
+// each with its own K/V ring and named barrier; groups 1.. hand their running max, sum
+// and O to group 0, which merges them (the exact rescaling of the online softmax) and
+// writes the rows.  KG = 3 triples the warps per query row for a 1-frame decode, whose
+// 144 CTAs leave each SM one CTA; larger decodes run KG = 1.
 // ----------------------------------------------------------------------------------
 constexpr int kVaTile = 64 * 72;  // bf16 elements of a 64-row tile, rows padded to 72 (conflict-free ldmatrix)
-constexpr int kVaSmem = 5 * kVaTile * 2;  // Q + 2 stages x (K, V): 46,080 B
 constexpr int kVaBlocks = kVaeTokens / 64;  // 9 key blocks (and query blocks)
+constexpr int kVaGroupTiles = 4;            // per key group: 2 stages x (K, V)
+// Q + KG groups' rings: 46,080 B (KG = 1), 119,808 B (KG = 3)
+constexpr int va_smem(int kg) { return (1 + kVaGroupTiles * kg) * kVaTile * 2; }
+constexpr int kVaExFloats = 36;             // per thread: o[8][4], m0, m1, l0, l1
 
 __device__ __forceinline__ void va_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N>
 __device__ __forceinline__ void va_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+// barrier of key group g's 128 threads (id 0 is __syncthreads, the whole CTA when KG = 1)
+template <int KG>
+__device__ __forceinline__ void va_group_sync(int g) {
+  if constexpr (KG == 1)
+    __syncthreads();
+  else
+    asm volatile("bar.sync %0, 128;" ::"r"(1 + g) : "memory");
+}
 
-__global__ void __launch_bounds__(128) attn_vae_kernel(const __nv_bfloat16* __restrict__ qkv,
-                                                       __nv_bfloat16* __restrict__ out, float scale_log2) {
+template <int KG>
+__global__ void __launch_bounds__(128 * KG) attn_vae_kernel(const __nv_bfloat16* __restrict__ qkv,
+                                                            __nv_bfloat16* __restrict__ out, float scale_log2) {
+  static_assert(KG >= 1 && KG <= 3, "1..3 key groups");
   pdl_trigger();
   extern __shared__ __align__(16) uint8_t sm_va[];
   __nv_bfloat16* sq = reinterpret_cast<__nv_bfloat16*>(sm_va);
-  __nv_bfloat16* skv = sq + kVaTile;  // stage s: K at skv + 2s tiles, V at + (2s + 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
+  const int grp = warp >> 2, wq = warp & 3, gtid = tid & 127;
+  // this group's ring: stage s has K at skv + 2s tiles, V at + (2s + 1)
+  __nv_bfloat16* skv = sq + kVaTile + grp * kVaGroupTiles * kVaTile;
   const int g = lane >> 2, c = lane & 3;
   const int qb = blockIdx.x, h = blockIdx.y;
   const long long row0 = static_cast<long long>(blockIdx.z) * kVaeTokens;
   pdl_wait();
-  // a 64 x 64 tile: 64 rows x 8 chunks of 16 B, 4 chunks per thread
-  auto load_tile = [&](__nv_bfloat16* dst, int col0, int tok0) {
+  // a 64 x 64 tile: 64 rows x 8 chunks of 16 B, copied by `n` threads from thread `t0` on
+  auto load_tile = [&](__nv_bfloat16* dst, int col0, int tok0, int t0, int n) {
 #pragma unroll
-    for (int i = tid; i < 512; i += 128) {
+    for (int i = t0; i < 512; i += n) {
       const int r = i >> 3, ch = i & 7;
       cp_async16(dst + r * 72 + ch * 8, qkv + (row0 + tok0 + r) * (3 * OASIS_HIDDEN) + col0 + ch * 8);
     }
   };
   auto tile_addr = [&](const __nv_bfloat16* base, int row, int chunk) { return smem_u32(base + row * 72 + chunk * 8); };
 
-  load_tile(sq, h * 64, qb * 64);
-  load_tile(skv, OASIS_HIDDEN + h * 64, 0);
-  load_tile(skv + kVaTile, 2 * OASIS_HIDDEN + h * 64, 0);
+  load_tile(sq, h * 64, qb * 64, tid, 128 * KG);
+  load_tile(skv, OASIS_HIDDEN + h * 64, grp * 64, gtid, 128);
+  load_tile(skv + kVaTile, 2 * OASIS_HIDDEN + h * 64, grp * 64, gtid, 128);
   va_commit();
 
   uint32_t qa[4][4];
@@ -94,23 +114,25 @@ __global__ void __launch_bounds__(128) attn_vae_kernel(const __nv_bfloat16* __re
   for (int j = 0; j < 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.0f;
   float m0 = -1e30f, m1 = -1e30f, l0 = 0.0f, l1 = 0.0f;
 
-  for (int kb = 0; kb < kVaBlocks; ++kb) {
-    const int st = kb & 1;
-    if (kb + 1 < kVaBlocks) {
+  int st = 0;
+  for (int kb = grp; kb < kVaBlocks; kb += KG, st ^= 1) {
+    if (kb + KG < kVaBlocks) {
       __nv_bfloat16* nx = skv + 2 * (st ^ 1) * kVaTile;
-      load_tile(nx, OASIS_HIDDEN + h * 64, (kb + 1) * 64);
-      load_tile(nx + kVaTile, 2 * OASIS_HIDDEN + h * 64, (kb + 1) * 64);
+      load_tile(nx, OASIS_HIDDEN + h * 64, (kb + KG) * 64, gtid, 128);
+      load_tile(nx + kVaTile, 2 * OASIS_HIDDEN + h * 64, (kb + KG) * 64, gtid, 128);
       va_commit();
       va_wait<1>();  // this thread's copies of block kb (and of Q) have landed
     } else {
       va_wait<0>();
     }
-    __syncthreads();  // ... and every thread's
-    if (kb == 0) {
+    if (kb == grp) {
+      __syncthreads();  // Q (copied by every group) and each group's first block are in
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk)
-        ldsm_x4(tile_addr(sq, warp * 16 + (lane & 15), kk * 2 + (lane >> 4)), qa[kk][0], qa[kk][1], qa[kk][2],
+        ldsm_x4(tile_addr(sq, wq * 16 + (lane & 15), kk * 2 + (lane >> 4)), qa[kk][0], qa[kk][1], qa[kk][2],
                 qa[kk][3]);
+    } else {
+      va_group_sync<KG>(grp);  // ... and those of the group's other threads
     }
     const __nv_bfloat16* sk = skv + 2 * st * kVaTile;
     const __nv_bfloat16* sv = sk + kVaTile;
@@ -179,14 +201,47 @@ __global__ void __launch_bounds__(128) attn_vae_kernel(const __nv_bfloat16* __re
         mma_bf16_16816(o[jd + 1], pa, b2, b3);
       }
     }
-    __syncthreads();  // every warp is done with this stage before it is refilled
+    va_group_sync<KG>(grp);  // the group's warps are done with this stage before it is refilled
+  }
+  if constexpr (KG > 1) {
+    // groups 1.. leave their partial state in their own (now idle) ring; group 0 merges
+    float* ex = reinterpret_cast<float*>(skv) + (wq * 32 + lane) * kVaExFloats;
+    if (grp > 0) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        *reinterpret_cast<float4*>(ex + 4 * j) = make_float4(o[j][0], o[j][1], o[j][2], o[j][3]);
+      *reinterpret_cast<float4*>(ex + 32) = make_float4(m0, m1, l0, l1);
+    }
+    __syncthreads();
+    if (grp > 0) return;
+#pragma unroll
+    for (int q = 1; q < KG; ++q) {
+      const float* ey = reinterpret_cast<const float*>(sq + kVaTile + q * kVaGroupTiles * kVaTile) +
+                        (wq * 32 + lane) * kVaExFloats;
+      const float4 ml = *reinterpret_cast<const float4*>(ey + 32);
+      const float nm0 = fmaxf(m0, ml.x), nm1 = fmaxf(m1, ml.y);
+      const float a0 = exp2f((m0 - nm0) * scale_log2), b0 = exp2f((ml.x - nm0) * scale_log2);
+      const float a1 = exp2f((m1 - nm1) * scale_log2), b1 = exp2f((ml.y - nm1) * scale_log2);
+      m0 = nm0;
+      m1 = nm1;
+      l0 = l0 * a0 + ml.z * b0;
+      l1 = l1 * a1 + ml.w * b1;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float4 y = *reinterpret_cast<const float4*>(ey + 4 * j);
+        o[j][0] = o[j][0] * a0 + y.x * b0;
+        o[j][1] = o[j][1] * a0 + y.y * b0;
+        o[j][2] = o[j][2] * a1 + y.z * b1;
+        o[j][3] = o[j][3] * a1 + y.w * b1;
+      }
+    }
   }
   l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
   l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
   l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
   l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
   const float inv0 = 1.0f / l0, inv1 = 1.0f / l1;
-  const long long r0 = row0 + qb * 64 + warp * 16 + g;
+  const long long r0 = row0 + qb * 64 + wq * 16 + g;
   __nv_bfloat16* o_row0 = out + r0 * OASIS_HIDDEN + h * 64;
   __nv_bfloat16* o_row1 = o_row0 + 8 * OASIS_HIDDEN;
 #pragma unroll
@@ -324,7 +379,9 @@ int vae_run(oasis_vae_plan* p, const float* z, float* out, cudaStream_t s) {
   }
   static bool configured = false;
   if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(attn_vae_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kVaSmem);
+    cudaError_t e = cudaFuncSetAttribute(attn_vae_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, va_smem(1));
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(attn_vae_kernel<3>, cudaFuncAttributeMaxDynamicSharedMemorySize, va_smem(3));
     if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(attn_vae)");
     configured = true;
   }
@@ -339,9 +396,17 @@ int vae_run(oasis_vae_plan* p, const float* z, float* out, cudaStream_t s) {
     eq.rope_mod = kVaeTokens;
     eq.rope_add = 0;
     if (int r = launch_gemm(p->qkv[i], kEpiQkvRope, eq, s)) return r;
-    cudaError_t e = launch_pdl(attn_vae_kernel, dim3(kVaBlocks, OASIS_HEADS, p->frames), dim3(128), kVaSmem, s,
-                               reinterpret_cast<const __nv_bfloat16*>(ws + L.qkv),
-                               reinterpret_cast<__nv_bfloat16*>(ws + L.attn), 0.125f * 1.4426950408889634f);
+    // one frame (144 CTAs, one per SM): three key groups per CTA; from two frames on the
+    // 120 KB CTAs would take two waves, and single-group CTAs (4 per SM) fill the SMs
+    const bool split_keys = p->frames == 1;
+    const dim3 grid(kVaBlocks, OASIS_HEADS, p->frames);
+    const auto* q_in = reinterpret_cast<const __nv_bfloat16*>(ws + L.qkv);
+    auto* a_out = reinterpret_cast<__nv_bfloat16*>(ws + L.attn);
+    cudaError_t e = split_keys
+                        ? launch_pdl(attn_vae_kernel<3>, grid, dim3(3 * 128), va_smem(3), s, q_in, a_out,
+                                     0.125f * 1.4426950408889634f)
+                        : launch_pdl(attn_vae_kernel<1>, grid, dim3(128), va_smem(1), s, q_in, a_out,
+                                     0.125f * 1.4426950408889634f);
     if (e != cudaSuccess) return cuda_status(e, "attn_vae_kernel");
     EpiParams eo{};  // x += proj(attn) + b, then LayerNorm 2 into hbuf
     eo.out = resid;
