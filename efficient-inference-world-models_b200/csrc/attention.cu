@@ -356,9 +356,9 @@ __global__ void __launch_bounds__(kTpWarps * 32)
   uint8_t* sm_tp = TMA ? reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(sm_tp_raw) + 1023) &
                                                     ~static_cast<uintptr_t>(1023))
                        : sm_tp_raw;
-  uint64_t* tbar = reinterpret_cast<uint64_t*>(sm_tp + kTpTmaTiles);
+  uint64_t* tbar = reinterpret_cast<uint64_t*>(sm_tp + kTpTmaTiles);  // per head: Q+K, V
   if (TMA && threadIdx.x == 0) {
-    mbar_init(tbar, 1);
+    for (int i = 0; i < 2 * kTpWarps; ++i) mbar_init(&tbar[i], 1);
     mbar_fence_init();
     tma_prefetch_desc(&tm_qkv);
     tma_prefetch_desc(&tm_out);
@@ -382,13 +382,21 @@ __global__ void __launch_bounds__(kTpWarps * 32)
 
   if constexpr (TMA) {
     if (threadIdx.x == 0) {
-      mbar_arrive_expect_tx(tbar, kTpTmaTiles);
-      for (int hh = 0; hh < kTpWarps; ++hh)
-        for (int which = 0; which < 3; ++which)
-          tma_load_3d(sm_tp + (hh * 3 + which) * kTpTmaTile, &tm_qkv, tbar,
+      // each head's Q and K on one barrier, its V on a second, V last: a warp starts its
+      // scores once its own head's Q and K are in, while later heads and the values load
+      for (int hh = 0; hh < kTpWarps; ++hh) {
+        mbar_arrive_expect_tx(&tbar[2 * hh], 2 * kTpTmaTile);
+        for (int which = 0; which < 2; ++which)
+          tma_load_3d(sm_tp + (hh * 3 + which) * kTpTmaTile, &tm_qkv, &tbar[2 * hh],
                       which * OASIS_HIDDEN + (hg * kTpWarps + hh) * 64, p, b * q_frames);
+      }
+      for (int hh = 0; hh < kTpWarps; ++hh) {
+        mbar_arrive_expect_tx(&tbar[2 * hh + 1], kTpTmaTile);
+        tma_load_3d(sm_tp + (hh * 3 + 2) * kTpTmaTile, &tm_qkv, &tbar[2 * hh + 1],
+                    2 * OASIS_HIDDEN + (hg * kTpWarps + hh) * 64, p, b * q_frames);
+      }
     }
-    if (!mbar_wait(tbar, 0)) return;  // timeout recorded in the device error word
+    if (!mbar_wait(&tbar[2 * warp], 0)) return;  // timeout recorded in the device error word
   } else {
     uint8_t* raw = sm_tp + kTpTileBytes;  // [K | V] raw areas
     // ---- phase 1: every copy in flight (the 4 heads of one (session, token) are contiguous) ----
@@ -534,6 +542,9 @@ __global__ void __launch_bounds__(kTpWarps * 32)
     sum1 += __shfl_xor_sync(0xffffffffu, sum1, 1);
     sum1 += __shfl_xor_sync(0xffffffffu, sum1, 2);
 
+    if constexpr (TMA) {
+      if (mt == 0 && !mbar_wait(&tbar[2 * warp + 1], 0)) return;  // this head's V
+    }
     float o[8][4];
 #pragma unroll
     for (int j = 0; j < 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.0f;
