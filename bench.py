@@ -854,6 +854,38 @@ def rollout_bench(pkg, model, dev, frames=16, steps=SOLVER_STEPS):
     return out
 
 
+def replay_ms(fn, reps, dev):
+    """Mean device ms of one `fn()` call: three warm-up calls, then `reps` calls captured in
+    one CUDA graph and replayed once between CUDA events, so host launch cost (dozens of
+    launches per VAE decode) stays out of the figure.  Falls back to timed eager calls if
+    the capture fails.  Returns (ms, "graph" | "eager")."""
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    try:
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=torch.cuda.Stream(device=dev)):
+            for _ in range(reps):
+                fn()
+        gr.replay()
+        torch.cuda.synchronize()
+        e0.record()
+        gr.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        del gr
+        return e0.elapsed_time(e1) / reps, "graph"
+    except RuntimeError:
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / reps, "eager"
+
+
 def vae_decode_bench(pkg, dev, peaks, reps=10):
     """Latent decoder (`vae.decode`): the newest frame of a session (1 frame) and a whole
     32-frame window, frames/s with the tensor roofline of its projections + attention."""
@@ -864,19 +896,10 @@ def vae_decode_bench(pkg, dev, peaks, reps=10):
         for F in (1, 32):
             z = torch.randn(F, 576, 16, device=dev, generator=torch.Generator(device=dev).manual_seed(F))
             o = torch.empty(F, 3, 360, 640, device=dev)
-            for _ in range(3):
-                dec.decode(z, out=o)
-            torch.cuda.synchronize()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record()
-            for _ in range(reps):
-                dec.decode(z, out=o)
-            e1.record()
-            torch.cuda.synchronize()
-            ms = e0.elapsed_time(e1) / reps
+            ms, how = replay_ms(lambda: dec.decode(z, out=o), reps, dev)
             flop = F * 576 * 12 * 2 * (12 * 1024 * 1024) + F * 12 * 16 * 4 * 576 * 576 * 64
             out[f"frames_{F}"] = {"frames_per_s": F / (ms / 1e3), "ms": ms, "tflops": flop / ms / 1e9,
-                                  "frac_tensor": flop / ms / 1e9 / tpk}
+                                  "frac_tensor": flop / ms / 1e9 / tpk, "launch": how}
         del dec
         torch.cuda.empty_cache()
     except Exception as e:  # an extra line, never required
@@ -897,16 +920,7 @@ def attention_sweep(pkg, dev, hbm, reps=20, only=None):
         return only is None or only in case
 
     def timeit(fn):
-        for _ in range(3):
-            fn()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        torch.cuda.synchronize()
-        e0.record()
-        for _ in range(reps):
-            fn()
-        e1.record()
-        torch.cuda.synchronize()
-        return e0.elapsed_time(e1) / reps
+        return replay_ms(fn, reps, dev)[0]
 
     out = []
     for frames in (32, 256, 1024, 4096):
